@@ -1,0 +1,299 @@
+"""ctypes binding of libfirefly_b200.so (declared in include/firefly_b200.h).
+
+Every wrapper takes CUDA tensors, launches on the tensor's device and on
+torch's current stream of that device, and raises on a non-zero status:
+``ValueError`` for FF_ERR_INVALID_ARG / FF_ERR_UNSUPPORTED, ``RuntimeError``
+for FF_ERR_CUDA.  There is no CPU path: if the library is missing or a tensor
+is not on a CUDA device, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfirefly_b200.so"
+
+FF_OK = 0
+FF_ERR_INVALID_ARG = 1
+FF_ERR_UNSUPPORTED = 2
+FF_ERR_CUDA = 3
+FF_DEVICE_TIMEOUT = 0x1
+FF_DEVICE_BADARG = 0x2
+FF_DTYPE_F32 = 0
+FF_DTYPE_BF16 = 1
+FF_DTYPE_F16 = 2
+FF_OUT_S32 = 0
+FF_OUT_F32 = 1
+FF_OUT_BF16 = 2
+FF_OUT_BF16_ACCUM = 3
+
+# every symbol declared in include/firefly_b200.h, with its ctypes signature
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+_D = ctypes.c_double
+_U64 = ctypes.c_uint64
+SIGNATURES = {
+    "ff_version": (ctypes.c_char_p, []),
+    "ff_last_error": (ctypes.c_char_p, []),
+    "ff_num_sms": (_I, [_P]),
+    "ff_device_status": (_I, [_P, _I]),
+    "ff_quant_rows_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P]),
+    "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
+    "ff_transpose_i8": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P]),
+    "ff_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
+    "ff_colsum_ws_elems": (_I64, [_I64, _I64]),
+    "ff_colsum_bf16": (_I, [_P, _I64, _I64, _I64, _P, _P, _P]),
+    "ff_dqt_adamw8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
+                           _D, _D, _D, _D, _D, _D, _D, _D, _U64, _U64, _I64, _P, _P, _P, _P]),
+    "ff_update_int8_weight": (_I, [_P, _P, _I64, _P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library once; raise if it was not built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"firefly_b200 CUDA library not found at {LIB_PATH}; "
+                "build it with `python -m firefly_b200._build`"
+            )
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def version() -> str:
+    return lib().ff_version().decode()
+
+
+def _raise(rc: int, name: str) -> None:
+    msg = lib().ff_last_error().decode()
+    if rc in (FF_ERR_INVALID_ARG, FF_ERR_UNSUPPORTED):
+        raise ValueError(f"{name}: {msg}")
+    raise RuntimeError(f"{name} failed ({rc}): {msg}")
+
+
+def _call(name: str, *args) -> None:
+    rc = getattr(lib(), name)(*args)
+    if rc != FF_OK:
+        _raise(rc, name)
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("firefly_b200 kernels run on CUDA tensors only "
+                               f"(got a tensor on {t.device})")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    if dev is None:
+        raise ValueError("no tensor given")
+    return dev
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return FF_DTYPE_F32
+    if dt == torch.bfloat16:
+        return FF_DTYPE_BF16
+    if dt == torch.float16:
+        return FF_DTYPE_F16
+    raise ValueError(f"unsupported input dtype {dt}")
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def _rows_view(x: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """2-D tensor with unit column stride and its leading dimension."""
+    if x.dim() != 2:
+        raise ValueError(f"expected a 2-D tensor, got shape {tuple(x.shape)}")
+    if x.stride(1) != 1 or x.stride(0) < x.shape[1]:
+        x = x.contiguous()
+    return x, max(x.stride(0), x.shape[1])
+
+
+# ---------------------------------------------------------------------------
+# typed wrappers
+# ---------------------------------------------------------------------------
+def num_sms(device: torch.device | None = None) -> int:
+    out = ctypes.c_int(0)
+    with torch.cuda.device(device or torch.cuda.current_device()):
+        _call("ff_num_sms", ctypes.byref(out))
+    return out.value
+
+
+def device_status(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """Read (and by default clear) the device status word; synchronises the device."""
+    out = ctypes.c_uint32(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        _call("ff_device_status", ctypes.byref(out), int(clear))
+    return out.value
+
+
+def quant_rows(x: torch.Tensor, colmul: torch.Tensor | None = None, eps: float = 1e-8,
+               ldq: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row int8 quantiser.  Returns ``(q [R, ldq] int8, s [R] fp32)``."""
+    dev = _require_cuda(x, colmul)
+    x, ldx = _rows_view(x)
+    R, C = x.shape
+    if C == 0:
+        raise ValueError("cannot quantise rows of length 0")
+    ldq = C if ldq is None else ldq
+    q = torch.empty((R, ldq), dtype=torch.int8, device=dev)
+    s = torch.empty((R,), dtype=torch.float32, device=dev)
+    if colmul is not None:
+        colmul = colmul.to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        _call("ff_quant_rows_i8", _ptr(x), _dtype_code(x.dtype), R, C, ldx, _ptr(colmul),
+              float(eps), _ptr(q), ldq, _ptr(s), _stream(dev))
+    return q, s
+
+
+def quant_dual(x: torch.Tensor, row_colmul: torch.Tensor | None = None, eps: float = 1e-8,
+               rows: bool = True, cols: bool = True):
+    """Row codes ``[R, ldq]`` (ldq = round_up(C,16)) and transposed column codes
+    ``[C, ldqt]`` (ldqt = round_up(R,16)) with their scales.  Either part may be skipped
+    (returned as ``None``)."""
+    dev = _require_cuda(x, row_colmul)
+    x, ldx = _rows_view(x)
+    R, C = x.shape
+    if C == 0:
+        raise ValueError("cannot quantise rows of length 0")
+    ldq, ldqt = round_up(C, 16), round_up(max(R, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((R, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((R,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((C, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((C,), dtype=torch.float32, device=dev)
+    ws = torch.empty((R + C,), dtype=torch.float32, device=dev)
+    if row_colmul is not None:
+        row_colmul = row_colmul.to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        _call("ff_quant_dual_i8", _ptr(x), _dtype_code(x.dtype), R, C, ldx, _ptr(row_colmul),
+              float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols),
+              _ptr(ws), _stream(dev))
+    return q_rows, s_rows, q_cols, s_cols
+
+
+def transpose_i8(src: torch.Tensor, ldd: int | None = None) -> torch.Tensor:
+    """``[R, C]`` int8 -> ``[C, ldd]`` with ``ldd = round_up(R, 16)`` by default."""
+    dev = _require_cuda(src)
+    src, lds = _rows_view(src)
+    R, C = src.shape
+    ldd = round_up(max(R, 1), 16) if ldd is None else ldd
+    dst = torch.empty((C, ldd), dtype=torch.int8, device=dev)
+    with torch.cuda.device(dev):
+        _call("ff_transpose_i8", _ptr(src), R, C, lds, _ptr(dst), ldd, _stream(dev))
+    return dst
+
+
+def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | None = None,
+            scale_b: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+            out_kind: int = FF_OUT_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``D = epi(A[:, :k] · B[:, :k]ᵀ)``; A ``[M, lda]``, B ``[N, ldb]`` int8 (row stride 16k)."""
+    dev = _require_cuda(a, b, scale_a, scale_b, bias, out)
+    if a.dtype != torch.int8 or b.dtype != torch.int8:
+        raise ValueError("gemm_i8 operands must be int8")
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("gemm_i8 operands need unit column stride")
+    M, N = a.shape[0], b.shape[0]
+    lda, ldb = a.stride(0) if M > 1 else a.shape[1], b.stride(0) if N > 1 else b.shape[1]
+    odt = {FF_OUT_S32: torch.int32, FF_OUT_F32: torch.float32,
+           FF_OUT_BF16: torch.bfloat16, FF_OUT_BF16_ACCUM: torch.bfloat16}[out_kind]
+    if out is None:
+        if out_kind == FF_OUT_BF16_ACCUM:
+            raise ValueError("FF_OUT_BF16_ACCUM needs an existing output")
+        out = torch.empty((M, N), dtype=odt, device=dev)
+    if out.dtype != odt or out.shape[0] != M or out.shape[1] != N or out.stride(1) != 1:
+        raise ValueError("gemm_i8: output has the wrong dtype/shape/layout")
+    ldd = out.stride(0) if M > 1 else N
+    sa = None if scale_a is None else scale_a.to(torch.float32).contiguous()
+    sb = None if scale_b is None else scale_b.to(torch.float32).contiguous()
+    bb = None if bias is None else bias.to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        _call("ff_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
+              ldd, int(out_kind), M, N, int(k), _stream(dev))
+    return out
+
+
+def colsum_bf16(x: torch.Tensor) -> torch.Tensor:
+    """Deterministic fp32 column sums of a bf16 matrix, rounded to bf16."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    x, ldx = _rows_view(x)
+    R, C = x.shape
+    out = torch.empty((C,), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((int(lib().ff_colsum_ws_elems(R, C)),), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _call("ff_colsum_bf16", _ptr(x), R, C, ldx, _ptr(out), _ptr(ws), _stream(dev))
+    return out
+
+
+def dqt_adamw8(q: torch.Tensor, wscale: torch.Tensor, row_len: int, g: torch.Tensor,
+               m_q: torch.Tensor, m_absmax: torch.Tensor, v_q: torch.Tensor,
+               v_absmax: torch.Tensor, r_q: torch.Tensor, r_absmax: torch.Tensor, *,
+               lr: float, beta1: float, beta2: float, eps: float, wd: float, step: int,
+               sr_bias: float, seed: int, rng_offset: int = 0, elem_base: int = 0,
+               u: torch.Tensor | None = None, dec_s: torch.Tensor, dec_u: torch.Tensor,
+               block: int = 256) -> None:
+    """In-place fused DQT 8-bit AdamW update of one int8 weight (all tensors contiguous)."""
+    dev = _require_cuda(q, wscale, g, m_q, m_absmax, v_q, v_absmax, r_q, r_absmax, u, dec_s, dec_u)
+    numel = q.numel()
+    for name, t, dt in (("q", q, torch.int8), ("g", g, torch.bfloat16), ("m_q", m_q, torch.uint8),
+                        ("v_q", v_q, torch.uint8), ("r_q", r_q, torch.uint8)):
+        if t.dtype != dt or t.numel() != numel or not t.is_contiguous():
+            raise ValueError(f"dqt_adamw8: {name} must be a contiguous {dt} tensor of {numel} elements")
+    for name, t in (("m_absmax", m_absmax), ("v_absmax", v_absmax), ("r_absmax", r_absmax)):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < (numel + block - 1) // block:
+            raise ValueError(f"dqt_adamw8: {name} must be contiguous fp32 with one entry per block")
+    if u is not None and (u.dtype != torch.float32 or u.numel() != numel or not u.is_contiguous()):
+        raise ValueError("dqt_adamw8: u must be contiguous fp32 with one entry per element")
+    ws = wscale.to(torch.float32).contiguous()
+    bc1 = 1.0 - beta1 ** step
+    bc2 = 1.0 - beta2 ** step
+    with torch.cuda.device(dev):
+        _call("ff_dqt_adamw8", _ptr(q), _ptr(ws), int(row_len), int(elem_base), _ptr(g), _ptr(m_q),
+              _ptr(m_absmax), _ptr(v_q), _ptr(v_absmax), _ptr(r_q), _ptr(r_absmax), numel, block,
+              float(lr), float(beta1), float(beta2), float(eps), float(wd), bc1, bc2, float(sr_bias),
+              int(seed) & (2**64 - 1), int(step), int(rng_offset), _ptr(u), _ptr(dec_s), _ptr(dec_u),
+              _stream(dev))
+
+
+def update_int8_weight(w: torch.Tensor, dq: torch.Tensor) -> None:
+    dev = _require_cuda(w, dq)
+    if w.dtype != torch.int8 or not w.is_contiguous():
+        raise ValueError("update_int8_weight: int_weight must be contiguous int8")
+    dq = dq.to(torch.int32).contiguous()
+    if dq.numel() != w.numel():
+        raise ValueError("update_int8_weight: shape mismatch")
+    with torch.cuda.device(dev):
+        _call("ff_update_int8_weight", _ptr(w), _ptr(dq), w.numel(), _stream(dev))

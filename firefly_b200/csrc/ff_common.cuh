@@ -1,0 +1,143 @@
+// ff_common.cuh — shared helpers of the firefly_b200 C ABI (errors, status word,
+// bounded waits, element loads).  Compiled for sm_100a only.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/firefly_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "firefly_b200 is built for sm_100a only"
+#endif
+
+namespace ff {
+
+// ---------------------------------------------------------------------------
+// host-side error reporting
+// ---------------------------------------------------------------------------
+inline std::string& last_error_storage() {
+  static thread_local std::string s;
+  return s;
+}
+
+inline int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  last_error_storage() = buf;
+  return code;
+}
+
+inline int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return set_error(FF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return FF_OK;
+}
+
+#define FF_REQUIRE(cond, code, ...)            \
+  do {                                         \
+    if (!(cond)) return ::ff::set_error(code, __VA_ARGS__); \
+  } while (0)
+
+#define FF_CUDA_TRY(expr, what)                                               \
+  do {                                                                        \
+    cudaError_t _e = (expr);                                                  \
+    if (_e != cudaSuccess)                                                    \
+      return ::ff::set_error(FF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(_e)); \
+  } while (0)
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// device status word (one per device, lives in this library's module)
+// ---------------------------------------------------------------------------
+__device__ uint32_t g_status;
+
+__device__ __forceinline__ void raise_status(uint32_t bits) { atomicOr(&g_status, bits); }
+
+// ---------------------------------------------------------------------------
+// time-bounded waits
+// ---------------------------------------------------------------------------
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: no legitimate wait here comes close
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// element loads
+// ---------------------------------------------------------------------------
+template <int DT>
+struct Elem;
+template <>
+struct Elem<FF_DTYPE_F32> {
+  using T = float;
+  static __device__ __forceinline__ float to_f32(T v) { return v; }
+};
+template <>
+struct Elem<FF_DTYPE_BF16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float to_f32(T v) { return __bfloat162float(v); }
+};
+template <>
+struct Elem<FF_DTYPE_F16> {
+  using T = __half;
+  static __device__ __forceinline__ float to_f32(T v) { return __half2float(v); }
+};
+
+inline int dtype_size(int dt) { return dt == FF_DTYPE_F32 ? 4 : 2; }
+
+// load 8 consecutive elements starting at p as fp32 (16 B aligned for 2-byte types,
+// two 16 B loads for fp32)
+template <int DT>
+__device__ __forceinline__ void load8(const typename Elem<DT>::T* p, float (&v)[8]) {
+  if constexpr (DT == FF_DTYPE_F32) {
+    float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const typename Elem<DT>::T* e = reinterpret_cast<const typename Elem<DT>::T*>(&a);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = Elem<DT>::to_f32(e[j]);
+  }
+}
+
+// clamp(rint(v / s), -127, 127) with an IEEE divide: the quantiser of
+// fireflykernels.py:102-103 (torch.round is round-half-even)
+__device__ __forceinline__ int quant_code(float v, float s) {
+  float y = rintf(__fdiv_rn(v, s));
+  y = fminf(fmaxf(y, -127.f), 127.f);
+  return (y == y) ? (int)y : 0;
+}
+
+__device__ __forceinline__ float row_scale(float absmax, float eps) {
+  return __fdiv_rn(fmaxf(absmax, eps), 127.f);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) |
+         ((uint32_t)(d & 0xff) << 24);
+}
+
+}  // namespace ff

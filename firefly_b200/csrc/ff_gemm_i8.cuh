@@ -1,0 +1,543 @@
+// ff_gemm_i8.cuh — int8 x int8 -> int32 GEMM on the 5th-generation tensor cores.
+//
+//   acc[m, n] = sum_k A[m, k] * B[n, k]      (A: M x K, B: N x K, both K-contiguous)
+//   D[m, n]   = epilogue(acc)                (raw s32, or scaled fp32 / bf16 / bf16 add)
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer: 128 x 128 B tile of A and 256 x 128 B tile of B per
+//               stage into 128B-swizzled shared memory (4 stages, no multicast)
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 s32 accumulators) and
+//               issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32)
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, scale by the
+//               row/column fp32 scales (+bias), convert and store
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//
+// Every mbarrier wait is bounded by a time limit.  A wait that expires sets
+// FF_DEVICE_TIMEOUT in the device status word and an abort flag in shared
+// memory; all roles then leave their loops, in-flight TMA loads and MMAs are
+// drained with bounded waits, and TMEM is released before the CTA exits.
+#pragma once
+#include <cudaTypedefs.h>
+
+#include "ff_common.cuh"
+
+namespace ff {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes = int8 elements per stage along K (one 128 B swizzle row)
+constexpr int UMMA_K = 32;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;  // 16 KiB
+constexpr int B_BYTES = BN * BK;  // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int ACC_STAGES = 2;
+constexpr int TMEM_COLS = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int GROUP_M = 8;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128 B swizzle, 8-row core-matrix
+// groups 1024 B apart (SBO), LBO unused for swizzled K-major (encoded 1),
+// descriptor version 1 (bits 46-47), layout SWIZZLE_128B = 2 (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A and B signed int8
+// (bits 7-9 = 1, bits 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// bounded waits
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      raise_status(FF_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// drain wait used after an abort: ignores the abort flag, still time-bounded
+__device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_status(FF_DEVICE_TIMEOUT);
+      return;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tile order: groups of GROUP_M row-tiles walked column by column (L2 reuse of B)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int group = GROUP_M * tiles_n;
+  const int g = t / group;
+  const int first_m = g * GROUP_M;
+  const int gsz = min(tiles_m - first_m, GROUP_M);
+  const int r = t - g * group;
+  tm = first_m + r % gsz;
+  tn = r / gsz;
+}
+
+struct EpiParams {
+  const float* scale_a;
+  const float* scale_b;
+  const float* bias;
+  void* D;
+  int64_t ldd;
+  int64_t M, N;
+  int vec;  // 16-byte vector stores allowed
+};
+
+template <int OUT>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_t row, int64_t col0,
+                                               const EpiParams& p, float sa, int lane) {
+  // per-lane column operands, redistributed with shuffles (all lanes take part)
+  const int64_t mycol = col0 + lane;
+  float sbl = 1.f, bl = 0.f;
+  if constexpr (OUT != FF_OUT_S32) {
+    if (p.scale_b && mycol < p.N) sbl = __ldg(p.scale_b + mycol);
+    if (p.bias && mycol < p.N) bl = __ldg(p.bias + mycol);
+  }
+  float v[32];
+  if constexpr (OUT != FF_OUT_S32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float t = __int2float_rn((int)acc[j]);
+      if (p.scale_a) t = __fmul_rn(t, sa);
+      const float sb = __shfl_sync(0xffffffffu, sbl, j);
+      const float bj = __shfl_sync(0xffffffffu, bl, j);
+      if (p.scale_b) t = __fmul_rn(t, sb);
+      if (p.bias) t = __fadd_rn(t, bj);
+      v[j] = t;
+    }
+  }
+  if (row >= p.M) return;
+  const bool full = (col0 + 32 <= p.N) && p.vec;
+  if constexpr (OUT == FF_OUT_S32 || OUT == FF_OUT_F32) {
+    uint32_t* d = reinterpret_cast<uint32_t*>(p.D) + row * p.ldd + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        uint4 w;
+        if constexpr (OUT == FF_OUT_S32) {
+          w = make_uint4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        } else {
+          w = make_uint4(__float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
+                         __float_as_uint(v[j + 3]));
+        }
+        *reinterpret_cast<uint4*>(d + j) = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) {
+          if constexpr (OUT == FF_OUT_S32) d[j] = acc[j];
+          else d[j] = __float_as_uint(v[j]);
+        }
+      }
+    }
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        if constexpr (OUT == FF_OUT_BF16_ACCUM) {
+          uint4 o = *reinterpret_cast<const uint4*>(d + j);
+          const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&o);
+          __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(&w);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float add = __bfloat162float(__float2bfloat16_rn(v[j + e]));
+            nb[e] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(ob[e]), add));
+          }
+        } else {
+          __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(&w);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) nb[e] = __float2bfloat16_rn(v[j + e]);
+        }
+        *reinterpret_cast<uint4*>(d + j) = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) {
+          if constexpr (OUT == FF_OUT_BF16_ACCUM) {
+            const float add = __bfloat162float(__float2bfloat16_rn(v[j]));
+            d[j] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(d[j]), add));
+          } else {
+            d[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
+                   int tiles_m, int tiles_n, EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled tiles
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  const uint32_t sA = sbase;                    // STAGES x A_BYTES
+  const uint32_t sB = sbase + STAGES * A_BYTES;  // STAGES x B_BYTES
+  uint8_t* ctrl = smem + STAGES * STAGE_BYTES;
+  const uint32_t cbase = sbase + STAGES * STAGE_BYTES;
+  // barrier layout (8 bytes each)
+  auto full_bar = [&](int s) { return cbase + 8u * s; };
+  auto empty_bar = [&](int s) { return cbase + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * STAGES + ACC_STAGES + a); };
+  const uint32_t drain = cbase + 8u * (2 * STAGES + 2 * ACC_STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * STAGES + 2 * ACC_STAGES + 1));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = (int)((K + BK - 1) / BK);
+  const int total_tiles = tiles_m * tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < ACC_STAGES; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t used = 0, last_phase = 0;  // per-stage bit masks
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, tm * BM, full_bar(stage));
+          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, tn * BN, full_bar(stage));
+          used |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // make sure no TMA write into shared memory is still in flight at exit
+      for (int s = 0; s < STAGES; ++s)
+        if (used & (1u << s)) drain_bar(full_bar(s), (last_phase >> s) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * A_BYTES, b0 = sB + stage * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            tc_mma_i8(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), smem_desc_k_sw128(b0 + k * UMMA_K), idesc,
+                      (kb | k) != 0);
+          }
+          tc_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar(acc));
+        if (++acc == ACC_STAGES) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // wait until every MMA issued by this thread has finished (TMEM and smem reads)
+      tc_commit(drain);
+      drain_bar(drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int lg = warp & 3;  // TMEM lane group this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)tm * BM + lg * 32 + lane;
+      float sa = 1.f;
+      if constexpr (OUT != FF_OUT_S32) {
+        if (ep.scale_a && row < ep.M) sa = __ldg(ep.scale_a + row);
+      }
+      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t ncol_tile = min64(BN, ep.N - (int64_t)tn * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        if ((int64_t)c * 32 >= ncol_tile) break;
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_wait_ld();
+        epilogue_chunk<OUT>(r, row, (int64_t)tn * BN + c * 32, ep, sa, lane);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (++acc == ACC_STAGES) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FF_OK;
+}
+
+inline int num_sms_current() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+template <int OUT>
+inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
+                  const EpiParams& ep, int grid, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+                "ff_gemm_i8 smem attribute");
+    attr_set[dev] = true;
+  }
+  gemm_i8_kernel<OUT><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ma, mb, K, tiles_m, tiles_n, ep);
+  return check_launch("ff_gemm_i8");
+}
+
+}  // namespace gemm
+}  // namespace ff
+
+extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                          const float* scale_b, const float* bias, void* D, int64_t ldd, int out_kind, int64_t M,
+                          int64_t N, int64_t K, void* stream) {
+  using namespace ff;
+  using namespace ff::gemm;
+  FF_REQUIRE(M >= 0 && N >= 0 && K >= 1, FF_ERR_INVALID_ARG, "ff_gemm_i8: M=%lld N=%lld K=%lld", (long long)M,
+             (long long)N, (long long)K);
+  FF_REQUIRE(out_kind >= FF_OUT_S32 && out_kind <= FF_OUT_BF16_ACCUM, FF_ERR_INVALID_ARG,
+             "ff_gemm_i8: bad out_kind %d", out_kind);
+  if (M == 0 || N == 0) return FF_OK;
+  FF_REQUIRE(A && B && D, FF_ERR_INVALID_ARG, "ff_gemm_i8: null pointer");
+  FF_REQUIRE(lda >= K && ldb >= K && ldd >= N, FF_ERR_INVALID_ARG, "ff_gemm_i8: bad leading dims");
+  FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
+             "ff_gemm_i8: A/B need 16-byte alignment and lda/ldb multiples of 16 (lda=%lld ldb=%lld)",
+             (long long)lda, (long long)ldb);
+  FF_REQUIRE(M <= (int64_t)1 << 31 && N <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
+             "ff_gemm_i8: dimension too large");
+  const int64_t tm64 = (M + BM - 1) / BM, tn64 = (N + BN - 1) / BN;
+  FF_REQUIRE(tm64 * tn64 < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "ff_gemm_i8: too many tiles");
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, N, K, ldb, BN);
+  if (rc) return rc;
+  const int es = (out_kind == FF_OUT_BF16 || out_kind == FF_OUT_BF16_ACCUM) ? 2 : 4;
+  EpiParams ep;
+  ep.scale_a = scale_a;
+  ep.scale_b = scale_b;
+  ep.bias = bias;
+  ep.D = D;
+  ep.ldd = ldd;
+  ep.M = M;
+  ep.N = N;
+  ep.vec = aligned(D, 16) && ((ldd * es) % 16 == 0);
+  const int tiles_m = (int)tm64, tiles_n = (int)tn64;
+  const int total = tiles_m * tiles_n;
+  const int grid = min(total, num_sms_current());
+  cudaStream_t st = as_stream(stream);
+  switch (out_kind) {
+    case FF_OUT_S32: return launch<FF_OUT_S32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    case FF_OUT_F32: return launch<FF_OUT_F32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    case FF_OUT_BF16: return launch<FF_OUT_BF16>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    default: return launch<FF_OUT_BF16_ACCUM>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+  }
+}

@@ -1,0 +1,464 @@
+// ff_quant.cuh — int8 quantisers, int8 transpose and column sums (HBM-bound kernels).
+//
+// Quantiser math (fireflykernels.py:96-104, same as bitLinear.py:15-27):
+//   s = max(absmax, eps) / 127  (fp32, IEEE divide)
+//   q = clamp(rint(v / s), -127, 127)  (IEEE divide, round half to even)
+// Integer codes are bit-exact with the reference's torch CPU path.
+#pragma once
+#include "ff_common.cuh"
+
+namespace ff {
+
+// ---------------------------------------------------------------------------
+// K1: one warp per row.  Pass 1 reads the row for |x*colmul| max, pass 2
+// re-reads it (from L1/L2) and writes codes.  VEC path needs 16 B aligned rows.
+// ---------------------------------------------------------------------------
+template <int DT, bool VEC>
+__global__ void __launch_bounds__(256) quant_rows_kernel(
+    const typename Elem<DT>::T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+    const float* __restrict__ colmul, float eps, int8_t* __restrict__ q, int64_t ldq,
+    float* __restrict__ s) {
+  using T = typename Elem<DT>::T;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * ldx;
+  int8_t* qr = q + row * ldq;
+  float amax = 0.f;
+  if constexpr (VEC) {
+    const int64_t nvec = cols / 8;
+    for (int64_t i = lane; i < nvec; i += 32) {
+      float v[8];
+      load8<DT>(xr + i * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float t = colmul ? __fmul_rn(v[j], __ldg(colmul + i * 8 + j)) : v[j];
+        amax = fmaxf(amax, fabsf(t));
+      }
+    }
+    for (int64_t c = nvec * 8 + lane; c < cols; c += 32) {
+      float t = Elem<DT>::to_f32(xr[c]);
+      if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
+      amax = fmaxf(amax, fabsf(t));
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      float t = Elem<DT>::to_f32(xr[c]);
+      if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
+      amax = fmaxf(amax, fabsf(t));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float sc = row_scale(amax, eps);
+  if (lane == 0) s[row] = sc;
+  if constexpr (VEC) {
+    const int64_t nvec = cols / 8;
+    for (int64_t i = lane; i < nvec; i += 32) {
+      float v[8];
+      load8<DT>(xr + i * 8, v);
+      int c8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float t = colmul ? __fmul_rn(v[j], __ldg(colmul + i * 8 + j)) : v[j];
+        c8[j] = quant_code(t, sc);
+      }
+      uint2 w = make_uint2(pack4(c8[0], c8[1], c8[2], c8[3]), pack4(c8[4], c8[5], c8[6], c8[7]));
+      *reinterpret_cast<uint2*>(qr + i * 8) = w;
+    }
+    for (int64_t c = nvec * 8 + lane; c < ldq; c += 32) {
+      int code = 0;
+      if (c < cols) {
+        float t = Elem<DT>::to_f32(xr[c]);
+        if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
+        code = quant_code(t, sc);
+      }
+      qr[c] = (int8_t)code;
+    }
+  } else {
+    for (int64_t c = lane; c < ldq; c += 32) {
+      int code = 0;
+      if (c < cols) {
+        float t = Elem<DT>::to_f32(xr[c]);
+        if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
+        code = quant_code(t, sc);
+      }
+      qr[c] = (int8_t)code;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dual quantiser, pass A: raw absmax per row (of x*colmul) and per column (of x).
+// Tile: 256 rows x (128 threads * 8) columns.  Results are combined across
+// tiles with integer atomicMax on the (non-negative) fp32 bit patterns, which
+// is exact and order-independent.
+// ---------------------------------------------------------------------------
+constexpr int kDualARows = 256;
+constexpr int kDualAThreads = 128;
+
+template <int DT>
+__global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
+    const typename Elem<DT>::T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+    const float* __restrict__ colmul, bool want_rows, bool want_cols,
+    uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax) {
+  using T = typename Elem<DT>::T;
+  __shared__ float red[kDualARows][kDualAThreads / 32 + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * kDualAThreads * 8 + tid * 8;
+  const int64_t r0 = (int64_t)blockIdx.y * kDualARows;
+  const bool full = (c0 + 8 <= cols);
+  const bool vec_ok = ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
+                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  float cm[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cm[j] = (colmul && c0 + j < cols) ? __ldg(colmul + c0 + j) : 1.f;
+  float cmax[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cmax[j] = 0.f;
+  const int nr = (int)min64(kDualARows, rows - r0);
+  for (int i = 0; i < nr; ++i) {
+    const T* xr = x + (r0 + i) * ldx;
+    float v[8];
+    if (full && vec_ok) {
+      load8<DT>(xr + c0, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (c0 + j < cols) ? Elem<DT>::to_f32(xr[c0 + j]) : 0.f;
+    }
+    float rm = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      cmax[j] = fmaxf(cmax[j], fabsf(v[j]));
+      float t = colmul ? __fmul_rn(v[j], cm[j]) : v[j];
+      rm = fmaxf(rm, fabsf(t));
+    }
+    if (want_rows) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
+      if (lane == 0) red[i][warp] = rm;
+    }
+  }
+  if (want_cols) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (c0 + j < cols) atomicMax(col_amax + c0 + j, __float_as_uint(cmax[j]));
+  }
+  if (want_rows) {
+    __syncthreads();
+    for (int i = tid; i < nr; i += kDualAThreads) {
+      float m = red[i][0];
+#pragma unroll
+      for (int w = 1; w < kDualAThreads / 32; ++w) m = fmaxf(m, red[i][w]);
+      atomicMax(row_amax + r0 + i, __float_as_uint(m));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dual quantiser, pass B: 128 x 128 tiles.  Each thread owns 4 rows x 8 cols
+// (twice).  Row codes go straight to q_rows; column codes are packed 4 rows
+// per word into a shared-memory tile and written transposed (q_cols_t[c, r]).
+// ---------------------------------------------------------------------------
+constexpr int kTile = 128;
+
+template <int DT>
+__global__ void __launch_bounds__(256) dual_quant_kernel(
+    const typename Elem<DT>::T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+    const float* __restrict__ colmul, float eps, const uint32_t* __restrict__ row_amax,
+    const uint32_t* __restrict__ col_amax, int8_t* __restrict__ q_rows, int64_t ldq,
+    float* __restrict__ s_rows, int8_t* __restrict__ q_cols_t, int64_t ldqt,
+    float* __restrict__ s_cols) {
+  using T = typename Elem<DT>::T;
+  __shared__ uint32_t tileT[kTile][kTile / 4 + 1];  // [col][row/4]
+  __shared__ float srow[kTile], scol[kTile], cmul[kTile];
+  const int tid = threadIdx.x;
+  const int64_t C0 = (int64_t)blockIdx.x * kTile, R0 = (int64_t)blockIdx.y * kTile;
+  const bool do_rows = (q_rows != nullptr), do_cols = (q_cols_t != nullptr);
+  if (tid < kTile) {
+    const int64_t r = R0 + tid;
+    srow[tid] = (do_rows && r < rows) ? row_scale(__uint_as_float(row_amax[r]), eps) : 1.f;
+    if (do_rows && r < rows && blockIdx.x == 0) s_rows[r] = srow[tid];
+  } else {
+    const int k = tid - kTile;
+    const int64_t c = C0 + k;
+    scol[k] = (do_cols && c < cols) ? row_scale(__uint_as_float(col_amax[c]), eps) : 1.f;
+    cmul[k] = (colmul && c < cols) ? __ldg(colmul + c) : 1.f;
+    if (do_cols && c < cols && blockIdx.y == 0) s_cols[c] = scol[k];
+  }
+  __syncthreads();
+  const bool vec_ok = ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
+                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  const int cg = tid & 15;   // 8-column group
+  const int rg = tid >> 4;   // 4-row group (0..15), plus 16 for the second half
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int rb = (rg + half * 16) * 4;  // first row of this 4x8 micro-tile within the tile
+    const int cb = cg * 8;
+    const int64_t c = C0 + cb;
+    uint32_t colw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) colw[j] = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t r = R0 + rb + i;
+      float v[8];
+      if (r < rows) {
+        const T* xr = x + r * ldx;
+        if (vec_ok && c + 8 <= cols) {
+          load8<DT>(xr + c, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = (c + j < cols) ? Elem<DT>::to_f32(xr[c + j]) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      }
+      if (do_rows && r < rows && c < ldq) {
+        int code[8];
+        const float sr = srow[rb + i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) code[j] = quant_code(__fmul_rn(v[j], cmul[cb + j]), sr);
+        int8_t* qr = q_rows + r * ldq + c;
+        if (c + 8 <= ldq) {
+          *reinterpret_cast<uint2*>(qr) =
+              make_uint2(pack4(code[0], code[1], code[2], code[3]), pack4(code[4], code[5], code[6], code[7]));
+        } else {
+          for (int j = 0; c + j < ldq; ++j) qr[j] = (int8_t)code[j];
+        }
+      }
+      if (do_cols) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int code = (r < rows) ? quant_code(v[j], scol[cb + j]) : 0;
+          colw[j] |= (uint32_t)(code & 0xff) << (8 * i);
+        }
+      }
+    }
+    if (do_cols) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) tileT[cb + j][rb / 4] = colw[j];
+    }
+  }
+  if (!do_cols) return;
+  __syncthreads();
+  // write the transposed tile: 128 column-rows x 128 bytes, 16 B per thread-iteration
+  const int chunk = tid & 7;  // 16-byte chunk (4 words) of the 128-row span
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int k = (tid >> 3) + it * 32;  // column within tile
+    const int64_t c = C0 + k;
+    const int64_t r = R0 + chunk * 16;
+    if (c < cols && r < ldqt) {
+      uint4 w = make_uint4(tileT[k][chunk * 4 + 0], tileT[k][chunk * 4 + 1], tileT[k][chunk * 4 + 2],
+                           tileT[k][chunk * 4 + 3]);
+      *reinterpret_cast<uint4*>(q_cols_t + c * ldqt + r) = w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// int8 transpose through shared memory, 64 x 64 tiles (32 B-word packing)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) transpose_i8_kernel(const int8_t* __restrict__ src, int64_t rows,
+                                                           int64_t cols, int64_t lds, int8_t* __restrict__ dst,
+                                                           int64_t ldd) {
+  __shared__ int8_t t[64][64 + 4];
+  const int64_t R0 = (int64_t)blockIdx.y * 64, C0 = (int64_t)blockIdx.x * 64;
+  const int tid = threadIdx.x;
+  // load: 64 rows x 64 bytes, 16 bytes (as 4 words) per thread
+  {
+    const int r = tid >> 2, cb = (tid & 3) * 16;
+    const int64_t gr = R0 + r;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t gc = C0 + cb + j;
+      t[r][cb + j] = (gr < rows && gc < cols) ? src[gr * lds + gc] : (int8_t)0;
+    }
+  }
+  __syncthreads();
+  // store: dst row = source column, 64 bytes per dst row, 16 per thread
+  {
+    const int k = tid >> 2, rb = (tid & 3) * 16;
+    const int64_t gc = C0 + k;  // dst row
+    if (gc < cols) {
+      alignas(16) int8_t buf[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) buf[j] = t[rb + j][k];
+      const int64_t gr = R0 + rb;
+      int8_t* d = dst + gc * ldd + gr;
+      if (gr + 16 <= ldd && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+        *reinterpret_cast<uint4*>(d) = *reinterpret_cast<uint4*>(buf);
+      } else {
+        for (int j = 0; j < 16 && gr + j < ldd; ++j) d[j] = buf[j];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// deterministic column sums: stage 1 per 256-row chunk, stage 2 over chunks
+// ---------------------------------------------------------------------------
+constexpr int kColsumChunk = 256;
+
+__global__ void colsum_stage1(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+                              float* __restrict__ ws) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t ch = blockIdx.y;
+  if (c >= cols) return;
+  const int64_t r0 = ch * kColsumChunk, r1 = min64(rows, r0 + kColsumChunk);
+  float acc = 0.f;
+  for (int64_t r = r0; r < r1; ++r) acc += __bfloat162float(x[r * ldx + c]);
+  ws[ch * cols + c] = acc;
+}
+
+__global__ void colsum_stage2(const float* __restrict__ ws, int64_t nchunks, int64_t cols,
+                              __nv_bfloat16* __restrict__ out) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float acc = 0.f;
+  for (int64_t k = 0; k < nchunks; ++k) acc += ws[k * cols + c];
+  out[c] = __float2bfloat16_rn(acc);
+}
+
+__global__ void update_int8_weight_kernel(int8_t* __restrict__ w, const int32_t* __restrict__ dq, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    // int16 arithmetic as in the reference: int16(w) + int16(dq), then clamp
+    const int16_t v = (int16_t)((int16_t)w[i] + (int16_t)dq[i]);
+    w[i] = (int8_t)min(127, max(-127, (int)v));
+  }
+}
+
+}  // namespace ff
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" int ff_quant_rows_i8(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                                const float* colmul, float eps, int8_t* q, int64_t ldq, float* s,
+                                void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 1, FF_ERR_INVALID_ARG, "ff_quant_rows_i8: rows=%lld cols=%lld",
+             (long long)rows, (long long)cols);
+  FF_REQUIRE(ldx >= cols && ldq >= cols, FF_ERR_INVALID_ARG, "ff_quant_rows_i8: bad leading dims");
+  FF_REQUIRE(dtype == FF_DTYPE_F32 || dtype == FF_DTYPE_BF16 || dtype == FF_DTYPE_F16, FF_ERR_INVALID_ARG,
+             "ff_quant_rows_i8: bad dtype %d", dtype);
+  if (rows == 0) return FF_OK;
+  FF_REQUIRE(x && q && s, FF_ERR_INVALID_ARG, "ff_quant_rows_i8: null pointer");
+  const int es = dtype_size(dtype);
+  const bool vec = aligned(x, 16) && ((ldx * es) % 16 == 0) && aligned(q, 8) && (ldq % 8 == 0);
+  dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  cudaStream_t st = as_stream(stream);
+#define FF_QR(DT)                                                                                     \
+  if (vec)                                                                                            \
+    quant_rows_kernel<DT, true><<<grid, block, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, colmul, \
+                                                        eps, q, ldq, s);                              \
+  else                                                                                                \
+    quant_rows_kernel<DT, false><<<grid, block, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, colmul, \
+                                                         eps, q, ldq, s);
+  if (dtype == FF_DTYPE_F32) {
+    FF_QR(FF_DTYPE_F32)
+  } else if (dtype == FF_DTYPE_BF16) {
+    FF_QR(FF_DTYPE_BF16)
+  } else {
+    FF_QR(FF_DTYPE_F16)
+  }
+#undef FF_QR
+  return check_launch("ff_quant_rows_i8");
+}
+
+extern "C" int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                                const float* row_colmul, float eps, int8_t* q_rows, int64_t ldq,
+                                float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                                float* absmax_ws, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 1 && ldx >= cols, FF_ERR_INVALID_ARG,
+             "ff_quant_dual_i8: rows=%lld cols=%lld ldx=%lld", (long long)rows, (long long)cols, (long long)ldx);
+  FF_REQUIRE(dtype == FF_DTYPE_F32 || dtype == FF_DTYPE_BF16 || dtype == FF_DTYPE_F16, FF_ERR_INVALID_ARG,
+             "ff_quant_dual_i8: bad dtype %d", dtype);
+  const bool do_rows = q_rows != nullptr, do_cols = q_cols_t != nullptr;
+  FF_REQUIRE(do_rows || do_cols, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: nothing to do");
+  if (rows == 0) return FF_OK;
+  FF_REQUIRE(x && absmax_ws, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: null pointer");
+  if (do_rows) {
+    FF_REQUIRE(s_rows && ldq >= cols && ldq % 8 == 0 && aligned(q_rows, 8), FF_ERR_UNSUPPORTED,
+               "ff_quant_dual_i8: q_rows needs ldq>=cols, ldq%%8==0, 8-byte alignment");
+  }
+  if (do_cols) {
+    FF_REQUIRE(s_cols && ldqt >= rows && ldqt % 16 == 0 && aligned(q_cols_t, 16), FF_ERR_UNSUPPORTED,
+               "ff_quant_dual_i8: q_cols_t needs ldqt>=rows, ldqt%%16==0, 16-byte alignment");
+  }
+  cudaStream_t st = as_stream(stream);
+  uint32_t* row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  uint32_t* col_amax = row_amax + rows;
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(rows + cols), st), "ff_quant_dual_i8 memset");
+  dim3 gA((unsigned)((cols + kDualAThreads * 8 - 1) / (kDualAThreads * 8)), (unsigned)((rows + kDualARows - 1) / kDualARows));
+  const int64_t rspan = do_cols ? max64(rows, ldqt) : rows;
+  const int64_t cspan = do_rows ? max64(cols, ldq) : cols;
+  dim3 gB((unsigned)((cspan + kTile - 1) / kTile), (unsigned)((rspan + kTile - 1) / kTile));
+  FF_REQUIRE(gA.y < 65536 && gB.y < 65536, FF_ERR_UNSUPPORTED, "ff_quant_dual_i8: too many rows");
+#define FF_DQ(DT)                                                                                          \
+  dual_absmax_kernel<DT><<<gA, kDualAThreads, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, row_colmul, \
+                                                        do_rows, do_cols, row_amax, col_amax);             \
+  dual_quant_kernel<DT><<<gB, 256, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, row_colmul, eps,       \
+                                            row_amax, col_amax, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols);
+  if (dtype == FF_DTYPE_F32) {
+    FF_DQ(FF_DTYPE_F32)
+  } else if (dtype == FF_DTYPE_BF16) {
+    FF_DQ(FF_DTYPE_BF16)
+  } else {
+    FF_DQ(FF_DTYPE_F16)
+  }
+#undef FF_DQ
+  return check_launch("ff_quant_dual_i8");
+}
+
+extern "C" int ff_transpose_i8(const int8_t* src, int64_t rows, int64_t cols, int64_t lds, int8_t* dst,
+                               int64_t ldd, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 0 && lds >= cols && ldd >= rows, FF_ERR_INVALID_ARG,
+             "ff_transpose_i8: bad sizes");
+  if (rows == 0 || cols == 0) return FF_OK;
+  FF_REQUIRE(src && dst, FF_ERR_INVALID_ARG, "ff_transpose_i8: null pointer");
+  const int64_t rspan = max64(rows, ldd);
+  dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rspan + 63) / 64));
+  FF_REQUIRE(grid.y < 65536, FF_ERR_UNSUPPORTED, "ff_transpose_i8: too many rows");
+  transpose_i8_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, rows, cols, lds, dst, ldd);
+  return check_launch("ff_transpose_i8");
+}
+
+extern "C" int64_t ff_colsum_ws_elems(int64_t rows, int64_t cols) {
+  const int64_t nch = (rows + ff::kColsumChunk - 1) / ff::kColsumChunk;
+  return (nch > 0 ? nch : 1) * cols;
+}
+
+extern "C" int ff_colsum_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t ldx, uint16_t* out,
+                              float* ws, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 0 && ldx >= cols, FF_ERR_INVALID_ARG, "ff_colsum_bf16: bad sizes");
+  if (cols == 0) return FF_OK;
+  FF_REQUIRE(out && ws && (x || rows == 0), FF_ERR_INVALID_ARG, "ff_colsum_bf16: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int64_t nch = (rows + kColsumChunk - 1) / kColsumChunk;
+  if (nch == 0) {
+    FF_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(uint16_t) * cols, st), "ff_colsum_bf16 memset");
+    return FF_OK;
+  }
+  FF_REQUIRE(nch < 65536, FF_ERR_UNSUPPORTED, "ff_colsum_bf16: too many rows");
+  dim3 g1((unsigned)((cols + 255) / 256), (unsigned)nch);
+  colsum_stage1<<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, ldx, ws);
+  colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(ws, nch, cols,
+                                                                reinterpret_cast<__nv_bfloat16*>(out));
+  return check_launch("ff_colsum_bf16");
+}
+
+extern "C" int ff_update_int8_weight(int8_t* w, const int32_t* dq, int64_t n, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(n >= 0, FF_ERR_INVALID_ARG, "ff_update_int8_weight: n < 0");
+  if (n == 0) return FF_OK;
+  FF_REQUIRE(w && dq, FF_ERR_INVALID_ARG, "ff_update_int8_weight: null pointer");
+  const int64_t blocks = min64((n + 255) / 256, 148 * 16);
+  update_int8_weight_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(w, dq, n);
+  return check_launch("ff_update_int8_weight");
+}

@@ -1,0 +1,176 @@
+/*
+ * firefly_b200.h — C ABI of the FireFly INT8 training hot path on NVIDIA B200 (sm_100a).
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types.  Every entry
+ * point is asynchronous on `stream` (a cudaStream_t passed as void*; NULL is
+ * the legacy default stream), performs no host synchronisation, allocates no
+ * device memory, and returns FF_OK or an FF_ERR_* code.  On error,
+ * ff_last_error() returns a message for the calling thread.
+ *
+ * Device pointers must point to memory of the current device.  All matrices
+ * are row-major with an explicit leading dimension in ELEMENTS.
+ *
+ * Kernel-side waits (mbarrier / pipeline waits) are bounded in time; when one
+ * gives up, the kernel records FF_DEVICE_TIMEOUT in the per-device status word
+ * (ff_device_status) and returns instead of hanging.
+ *
+ * Reference: fumitoshi0524/FireFly (pure PyTorch).  Each entry point names the
+ * reference function it replaces.
+ */
+#ifndef FIREFLY_B200_H
+#define FIREFLY_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FF_API __attribute__((visibility("default")))
+#else
+#define FF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FF_OK 0
+#define FF_ERR_INVALID_ARG 1  /* null pointer, negative size, bad leading dimension */
+#define FF_ERR_UNSUPPORTED 2  /* shape/alignment the kernel does not handle */
+#define FF_ERR_CUDA 3         /* a CUDA runtime/driver call failed */
+
+/* bits of the per-device status word */
+#define FF_DEVICE_TIMEOUT 0x1u  /* a bounded in-kernel wait expired */
+#define FF_DEVICE_BADARG 0x2u   /* a kernel-side argument check failed */
+
+/* element types of floating-point inputs */
+#define FF_DTYPE_F32 0
+#define FF_DTYPE_BF16 1
+#define FF_DTYPE_F16 2
+
+/* GEMM output kinds */
+#define FF_OUT_S32 0        /* raw int32 accumulators */
+#define FF_OUT_F32 1        /* fp32  ((acc * sa[m]) * sb[n]) + bias[n] */
+#define FF_OUT_BF16 2       /* bf16 of the fp32 value above */
+#define FF_OUT_BF16_ACCUM 3 /* D = bf16(f32(D) + f32(bf16(value)))  (grad-cache add) */
+
+/* Library version string, e.g. "firefly_b200 0.1.0 sm_100a". */
+FF_API const char* ff_version(void);
+
+/* Message of the last error on this host thread ("" if none). */
+FF_API const char* ff_last_error(void);
+
+/* Number of SMs of the current device (used for persistent grids). */
+FF_API int ff_num_sms(int* out);
+
+/*
+ * Per-device status word (FF_DEVICE_* bits) written by kernels.  Reading it
+ * synchronises the device.  `clear` != 0 resets it to 0 after reading.
+ * No reference counterpart (the reference has no kernels of its own).
+ */
+FF_API int ff_device_status(uint32_t* out, int clear);
+
+/*
+ * Per-row absmax int8 quantiser.
+ * Replaces fireflykernels.py:96-104 quantize_fp_to_int8 (and bitLinear.py:15-27):
+ *   s[r] = max(max_c |x[r,c]*colmul[c]|, eps) / 127        (fp32, IEEE divide)
+ *   q[r,c] = clamp(rint((x[r,c]*colmul[c]) / s[r]), -127, 127)   (round half even)
+ * x: rows x cols of `dtype` with leading dim ldx.  colmul: NULL or fp32[cols].
+ * q: int8 rows x ldq (ldq >= cols; entries cols..ldq-1 are written as 0).
+ * s: fp32[rows].  rows == 0 is a no-op; cols must be >= 1.
+ * Used per token on activations (the forward's activation quantiser).
+ */
+FF_API int ff_quant_rows_i8(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                     const float* colmul, float eps, int8_t* q, int64_t ldq, float* s,
+                     void* stream);
+
+/*
+ * Row + column quantiser of one matrix in two passes (backward operands).
+ * Row part: exactly ff_quant_rows_i8 (with optional colmul) into q_rows/s_rows.
+ * Column part: the same quantiser applied to each COLUMN of x (no colmul),
+ *   s_cols[c] = max(max_r |x[r,c]|, eps)/127, codes written TRANSPOSED:
+ *   q_cols_t[c, r] (int8, leading dim ldqt >= rows; r in rows..ldqt-1 written as 0).
+ * q_rows/s_rows may be NULL (column part only); q_cols_t/s_cols may be NULL
+ * (row part only).  absmax_ws: fp32 workspace of rows + cols elements
+ * (caller-owned device memory; contents on return are the raw absmax values).
+ * Replaces the bf16 operand preparation of fireflykernels.py:164-193
+ * (x2d.to(bf16) saved for backward, go_bf16, int_weight*weight_scale).
+ */
+FF_API int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                     const float* row_colmul, float eps,
+                     int8_t* q_rows, int64_t ldq, float* s_rows,
+                     int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                     float* absmax_ws, void* stream);
+
+/*
+ * int8 transpose: dst[c, r] = src[r, c] for r < rows, c < cols; dst entries
+ * r in rows..ldd-1 are written 0.  Builds the K-major copy of W (Wᵀ) that
+ * the dX GEMM reads; the reference keeps per-handle weight layouts in
+ * _cached_weight_transform (fireflykernels.py:64-90).
+ */
+FF_API int ff_transpose_i8(const int8_t* src, int64_t rows, int64_t cols, int64_t lds,
+                    int8_t* dst, int64_t ldd, void* stream);
+
+/*
+ * int8 tensor-core GEMM (tcgen05 kind::i8, int32 accumulation in TMEM).
+ *   acc[m,n] = sum_k A[m,k] * B[n,k]    A: M x K (lda), B: N x K (ldb), both K-contiguous
+ *   D[m,n]   = epilogue(acc) per out_kind (FF_OUT_*), D leading dim ldd.
+ * scale_a: NULL or fp32[M]; scale_b: NULL or fp32[N]; bias: NULL or fp32[N].
+ * Requirements: A, B 16-byte aligned; lda, ldb multiples of 16; K >= 1.
+ * Replaces the GEMMs of fireflykernels.py:167 (forward), :191 (dX), :193 (dW)
+ * and the dead cuBLASLt path igemmlt + mm_dequant (fireflykernels.py:132-156).
+ */
+FF_API int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+               const float* scale_a, const float* scale_b, const float* bias,
+               void* D, int64_t ldd, int out_kind, int64_t M, int64_t N, int64_t K,
+               void* stream);
+
+/*
+ * Column sums of a bf16 matrix in fp32, rounded to bf16: db[c] = bf16(sum_r x[r,c]).
+ * Deterministic (fixed reduction order).  ws: fp32 workspace of
+ * ff_colsum_ws_elems(rows, cols) elements.  Replaces go_bf16.sum(dim=0)
+ * (fireflykernels.py:200).
+ */
+FF_API int64_t ff_colsum_ws_elems(int64_t rows, int64_t cols);
+FF_API int ff_colsum_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t ldx,
+                   uint16_t* out, float* ws, void* stream);
+
+/*
+ * Fused DQT-SR 8-bit AdamW update of one int8 weight tensor (one BitLinear).
+ * Replaces FireFlyOptim.step's bit-module loop body fireflyoptim.py:137-209
+ * together with update_int8_weight_ (fireflykernels.py:218-223) and the
+ * mu-law codecs (fireflyoptim.py:22-80).  Per element (fp32 math):
+ *   decode m (signed), v (unsigned), r (signed) from uint8 codes * block absmax;
+ *   m = b1*m + (1-b1)*g;  v = b2*v + (1-b2)*g*g;
+ *   a = (m/bc1) / (sqrt(v/bc2) + eps);   ws = max(wscale[row], eps)
+ *   r += -lr*(a + wd*q*ws)/ws;
+ *   dq = sign(r)*(floor|r| + [u < clamp(frac|r| + tanh(a)*sr_bias*sign(r), 0, 1)])
+ *   q = clamp(q+dq, -127, 127);  r -= dq;
+ *   re-encode r, m, v per block of `block` elements (new block absmax, clamp 1e-12).
+ * Hyperparameters are doubles (python floats); each is rounded to fp32 where
+ * the reference's torch op rounds it (1-beta is formed in double first).
+ * numel elements of q/g/m/v/r; block must be 256; row_len = elements per
+ * weight row (wscale index = (elem_base + i) / row_len).  bc1 = 1-b1^t,
+ * bc2 = 1-b2^t for the step t being taken.
+ * Uniforms: u != NULL -> u[i] (fp32, element i); u == NULL -> Philox4x32-10
+ * keyed by (seed, step) at global element index rng_offset + i.
+ * dec_s / dec_u: fp32[256] decode tables (x_norm of each code).
+ * elem_base: element index of element 0 within its weight (0 unless a shard).
+ */
+FF_API int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base,
+                  const uint16_t* g, uint8_t* m_q, float* m_absmax, uint8_t* v_q,
+                  float* v_absmax, uint8_t* r_q, float* r_absmax, int64_t numel,
+                  int64_t block, double lr, double beta1, double beta2, double eps, double wd,
+                  double bc1, double bc2, double sr_bias, uint64_t seed, uint64_t step,
+                  int64_t rng_offset, const float* u, const float* dec_s,
+                  const float* dec_u, void* stream);
+
+/*
+ * update_int8_weight_ (fireflykernels.py:218-223): w = clamp(int16(w) + dq, -127, 127).
+ * dq: int32[n].
+ */
+FF_API int ff_update_int8_weight(int8_t* w, const int32_t* dq, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FIREFLY_B200_H */

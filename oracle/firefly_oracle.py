@@ -1,0 +1,334 @@
+"""CPU oracle for the FireFly INT8 training hot path.  TEST INFRASTRUCTURE ONLY.
+
+This module is the checker.  Only ``tests/``, ``__graft_entry__.smoke()`` and
+the CPU-baseline leg of ``bench.py`` may import it; the product path
+(``firefly_b200``) never does, and fails loudly if its CUDA library is missing.
+
+It restates the reference algorithm (fumitoshi0524/FireFly) in numpy:
+
+* ``quantize_rows``           fireflykernels.py:96-104 (``quantize_fp_to_int8``)
+* ``quantize_cols_t``         the same math applied per column, codes transposed
+                              (the dW operands of the int8 backward)
+* ``gemm_i8`` + ``dequant``   int32 accumulation and the scale epilogue, the
+                              structure of ``_forward_bnb`` fireflykernels.py:132-156
+* ``linear_forward`` / ``linear_backward``
+                              BitLinear through int8 GEMMs: Y = X Wᵀ, dX = dY W,
+                              dW = dYᵀ X (fireflykernels.py:164-210 define the ops)
+* ``encode_signed`` …         mu-law 8-bit blockwise codecs fireflyoptim.py:8-80
+* ``dqt_adamw8_step``         FireFlyOptim bit-module update fireflyoptim.py:136-209
+* ``philox_uniforms``         the counter-based uniforms the GPU optimizer draws
+
+Rounding model.  Every reference op is evaluated in fp32 with correct rounding:
+``+ - * /`` are IEEE fp32, ``sqrt/exp/log1p/tanh`` are computed in fp64 and
+rounded once to fp32.  The two fused multiply-adds that torch's CPU kernels
+perform (``add_(g, alpha=…)`` and ``addcmul_``, fireflyoptim.py:175-176) are
+modelled as FMAs.  torch's own CPU transcendental and sqrt kernels are within
+about one ulp of this, so the oracle reproduces the reference's int8 codes
+exactly and its 8-bit optimizer codes to within one code on a tiny fraction of
+elements; ``tests/test_oracle_golden.py`` pins both against fixtures produced
+by running the reference (``tests/golden/make_golden.py``).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+_MU = F32(255.0)
+_INV_LN1P_MU = F32(1.0 / 5.545177444479562)  # fireflyoptim.py:10
+
+
+# --------------------------------------------------------------------------
+# bf16 helpers (bf16 is carried as uint16 bit patterns)
+# --------------------------------------------------------------------------
+def f32_to_bf16_bits(x) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 (what ``tensor.to(torch.bfloat16)`` does)."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    r = ((b.astype(np.uint64) + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, np.uint16(0x7FC0), r)
+
+
+def bf16_bits_to_f32(h) -> np.ndarray:
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(x) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+def _f64fn(fn, x):
+    return fn(np.asarray(x, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def _fma(a, b, c):
+    """fp32 fused multiply-add, rounded once (fp64 holds a*b exactly)."""
+    a64 = np.asarray(a, np.float32).astype(np.float64)
+    b64 = np.asarray(b, np.float32).astype(np.float64)
+    c64 = np.asarray(c, np.float32).astype(np.float64)
+    return (a64 * b64 + c64).astype(np.float32)
+
+
+# --------------------------------------------------------------------------
+# a1: per-row absmax int8 quantiser
+# --------------------------------------------------------------------------
+def quantize_rows(w, eps: float = 1e-8, colmul=None):
+    """fireflykernels.py:96-104: ``s = max(|w|_row, eps)/127``, ``q = clamp(rint(w/s), ±127)``.
+
+    ``colmul`` (optional, fp32 per column) multiplies ``w`` elementwise first;
+    the backward uses it to fold the per-output weight scale into dY.
+    """
+    w = np.asarray(w, dtype=np.float32)
+    if w.ndim != 2:
+        raise ValueError(f"weight must be 2D [out_features, in_features], got {w.shape}")
+    if colmul is not None:
+        w = w * np.asarray(colmul, np.float32)[None, :]
+    if w.shape[1] == 0:
+        raise ValueError("cannot quantise rows of length 0")
+    absmax = np.abs(w).max(axis=1, keepdims=True) if w.shape[0] else np.zeros((0, 1), F32)
+    scale = np.maximum(absmax, F32(eps)) / F32(127.0)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = np.clip(np.rint(w / scale), -127, 127)
+    q = np.where(np.isnan(q), 0, q).astype(np.int8)
+    return q, scale[:, 0].astype(np.float32)
+
+
+def quantize_cols_t(x, eps: float = 1e-8):
+    """Per-column version of ``quantize_rows``: returns codes transposed ``[C, R]`` and ``s[C]``."""
+    q, s = quantize_rows(np.asarray(x, np.float32).T, eps)
+    return q, s
+
+
+# --------------------------------------------------------------------------
+# int8 GEMM + epilogue
+# --------------------------------------------------------------------------
+def gemm_i8(a, b) -> np.ndarray:
+    """Exact ``A[M,K] · B[N,K]ᵀ`` accumulation of int8 codes, returned as int64.
+
+    fp64 BLAS is exact here: every product and partial sum is an integer below 2^53.
+    """
+    a = np.asarray(a, np.int8)
+    b = np.asarray(b, np.int8)
+    return np.rint(a.astype(np.float64) @ b.astype(np.float64).T).astype(np.int64)
+
+
+def dequant(acc, scale_a=None, scale_b=None, bias=None) -> np.ndarray:
+    """Epilogue: ``((f32(acc) * sa[m]) * sb[n]) + bias[n]`` in fp32, each op rounded."""
+    v = np.asarray(acc).astype(np.float32)
+    if scale_a is not None:
+        v = v * np.asarray(scale_a, np.float32)[:, None]
+    if scale_b is not None:
+        v = v * np.asarray(scale_b, np.float32)[None, :]
+    if bias is not None:
+        v = v + np.asarray(bias, np.float32)[None, :]
+    return v
+
+
+# --------------------------------------------------------------------------
+# BitLinear through int8 GEMMs
+# --------------------------------------------------------------------------
+def linear_forward(x, q_w, s_w, bias=None, eps: float = 1e-8):
+    """Y = X·W_effᵀ (+b) with per-token int8 activations.  Returns (y_bf16_bits, q_x, s_x, acc)."""
+    q_x, s_x = quantize_rows(x, eps)
+    acc = gemm_i8(q_x, q_w)
+    y = dequant(acc, s_x, s_w, bias)
+    return f32_to_bf16_bits(y), q_x, s_x, acc
+
+
+def linear_backward(x, dy, q_w, s_w, has_bias=False, eps: float = 1e-8, grad_cache=None):
+    """int8 backward of ``fireflykernels.py:184-210``.
+
+    * dX: quantise ``g = dY ⊙ s_w`` per token, ``dX = s_g[t] · (q_g · q_w)`` (contracts over O).
+    * dW: quantise dY and X per column over tokens, ``dW = s_dy[o]·s_x[k]·(q_dyᵀ · q_xᵀᵀ)``.
+      Added to ``grad_cache`` like ``_BIT_GRAD_CACHE`` (bf16 add of the bf16-rounded term).
+    * db: fp32 column sum of dY, rounded to bf16.
+    Returns dict with bf16 bit patterns for dx, gw, db and the intermediate codes.
+    """
+    x = np.asarray(x, np.float32)
+    dyf = bf16_bits_to_f32(dy) if np.asarray(dy).dtype == np.uint16 else np.asarray(dy, np.float32)
+    q_g, s_g = quantize_rows(dyf, eps, colmul=s_w)
+    acc_dx = gemm_i8(q_g, np.ascontiguousarray(np.asarray(q_w, np.int8).T))
+    dx = dequant(acc_dx, s_g, None)
+    q_dyt, s_dy = quantize_cols_t(dyf, eps)
+    q_xt, s_xc = quantize_cols_t(x, eps)
+    acc_dw = gemm_i8(q_dyt, q_xt)
+    gw = f32_to_bf16_bits(dequant(acc_dw, s_dy, s_xc))
+    if grad_cache is not None:
+        gw = f32_to_bf16_bits(bf16_bits_to_f32(grad_cache) + bf16_bits_to_f32(gw))
+    out = {
+        "dx": f32_to_bf16_bits(dx), "gw": gw,
+        "q_g": q_g, "s_g": s_g, "acc_dx": acc_dx,
+        "q_dyt": q_dyt, "s_dy": s_dy, "q_xt": q_xt, "s_xc": s_xc, "acc_dw": acc_dw,
+    }
+    if has_bias:
+        out["db"] = f32_to_bf16_bits(dyf.astype(np.float64).sum(axis=0).astype(np.float32))
+    return out
+
+
+# --------------------------------------------------------------------------
+# mu-law 8-bit blockwise codecs (fireflyoptim.py:8-80)
+# --------------------------------------------------------------------------
+def _blocks(x, bs):
+    flat = np.asarray(x, np.float32).ravel()
+    n = flat.size
+    nb = (n + bs - 1) // bs
+    pad = np.zeros(nb * bs, np.float32)
+    pad[:n] = flat
+    return pad.reshape(nb, bs), n
+
+
+def encode_signed(x, bs: int = 256):
+    """fireflyoptim.py:22-36. Returns (uint8 codes shaped like x, fp32 absmax[nblocks])."""
+    blocks, n = _blocks(x, bs)
+    absmax = np.maximum(np.abs(blocks).max(axis=1), F32(1e-12))
+    xn = np.clip(blocks / absmax[:, None], F32(-1.0), F32(1.0))
+    comp = (np.sign(xn) * _f64fn(np.log1p, _MU * np.abs(xn))) * _INV_LN1P_MU
+    q = np.clip(np.rint(comp * F32(127.0)), -127, 127).astype(np.int16)
+    codes = (q.ravel()[:n] + 128).astype(np.uint8)
+    return codes.reshape(np.shape(x)), absmax.astype(np.float32)
+
+
+def encode_unsigned(x, bs: int = 256):
+    """fireflyoptim.py:53-67 (absmax is the plain block max, not |x|)."""
+    blocks, n = _blocks(x, bs)
+    absmax = np.maximum(blocks.max(axis=1), F32(1e-12))
+    xn = np.clip(blocks / absmax[:, None], F32(0.0), F32(1.0))
+    comp = _f64fn(np.log1p, _MU * xn) * _INV_LN1P_MU
+    q = np.clip(np.rint(comp * F32(255.0)), 0, 255)
+    codes = q.ravel()[:n].astype(np.uint8)
+    return codes.reshape(np.shape(x)), absmax.astype(np.float32)
+
+
+def decode_table_signed() -> np.ndarray:
+    """x_norm for each signed code, fireflyoptim.py:47-48 (absmax factor excluded)."""
+    y = np.clip((np.arange(256, dtype=np.float32) - F32(128.0)) / F32(127.0), F32(-1), F32(1))
+    return (np.sign(y) * (_f64fn(np.exp, np.abs(y) / _INV_LN1P_MU) - F32(1.0))) / _MU
+
+
+def decode_table_unsigned() -> np.ndarray:
+    """x_norm for each unsigned code, fireflyoptim.py:77-78."""
+    y = np.clip(np.arange(256, dtype=np.float32) / F32(255.0), F32(0), F32(1))
+    return (_f64fn(np.exp, y / _INV_LN1P_MU) - F32(1.0)) / _MU
+
+
+def _decode(codes, absmax, bs, table):
+    c = np.asarray(codes, np.uint8).ravel()
+    n = c.size
+    xn = table[c]
+    blk = np.arange(n) // bs
+    return (xn * np.asarray(absmax, np.float32)[blk]).reshape(np.shape(codes))
+
+
+def decode_signed(codes, absmax, bs: int = 256):
+    """fireflyoptim.py:39-50."""
+    return _decode(codes, absmax, bs, decode_table_signed())
+
+
+def decode_unsigned(codes, absmax, bs: int = 256):
+    """fireflyoptim.py:70-80."""
+    return _decode(codes, absmax, bs, decode_table_unsigned())
+
+
+def init_state(shape, bs: int = 256) -> dict:
+    """Zero-initialised 8-bit states, fireflyoptim.py:142-161."""
+    z = np.zeros(shape, np.float32)
+    m_q, m_a = encode_signed(z, bs)
+    v_q, v_a = encode_unsigned(z, bs)
+    r_q, r_a = encode_signed(z, bs)
+    return {"step": 0, "m_q": m_q, "m_absmax": m_a, "v_q": v_q, "v_absmax": v_a,
+            "r_q": r_q, "r_absmax": r_a}
+
+
+# --------------------------------------------------------------------------
+# DQT-SR 8-bit AdamW step (fireflyoptim.py:136-209)
+# --------------------------------------------------------------------------
+def dqt_adamw8_step(q, ws, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.1,
+                    sr_bias=0.15, bs=256, u=None):
+    """One bit-module update.  ``g`` is the fp32 (bf16-valued) gradient ``[O, K]``.
+
+    Returns ``(q_new, state_new)``; ``state`` is not modified.  ``u`` are the
+    uniforms of ``torch.rand_like`` (fireflyoptim.py:192), shape ``[O, K]``.
+    """
+    q = np.asarray(q, np.int8)
+    g = np.asarray(g, np.float32)
+    shape = q.shape
+    m = decode_signed(state["m_q"], state["m_absmax"], bs)
+    v = decode_unsigned(state["v_q"], state["v_absmax"], bs)
+    r = decode_signed(state["r_q"], state["r_absmax"], bs)
+    t = int(state["step"]) + 1
+    m = _fma(g, F32(1.0 - beta1), m * F32(beta1))
+    v = _fma(F32(1.0 - beta2) * g, g, v * F32(beta2))
+    m_hat = m / F32(1.0 - beta1 ** t)
+    v_hat = v / F32(1.0 - beta2 ** t)
+    ws_c = np.maximum(np.asarray(ws, np.float32).reshape(-1, 1), F32(eps))
+    if len(shape) == 1:
+        ws_c = ws_c.reshape(-1)
+    iw = q.astype(np.float32)
+    adam = m_hat / (_f64fn(np.sqrt, v_hat) + F32(eps))
+    dwe = F32(-lr) * (adam + (F32(wd) * iw) * ws_c)
+    r = r + dwe / ws_c
+    abs_r = np.abs(r)
+    base = np.floor(abs_r)
+    frac = abs_r - base
+    sgn = np.sign(r).astype(np.float32)
+    bias = (_f64fn(np.tanh, adam) * F32(sr_bias)) * sgn
+    fb = np.clip(frac + bias, F32(0.0), F32(1.0))
+    if u is None:
+        raise ValueError("the oracle needs the uniforms")
+    extra = (np.asarray(u, np.float32) < fb).astype(np.float32)
+    dq = (sgn * (base + extra)).astype(np.int32)
+    if np.any(dq != 0):
+        q = np.clip(q.astype(np.int16) + dq.astype(np.int16), -127, 127).astype(np.int8)
+        r = r - dq.astype(np.float32)
+    r_q, r_a = encode_signed(r, bs)
+    m_q, m_a = encode_signed(m, bs)
+    v_q, v_a = encode_unsigned(v, bs)
+    return q, {"step": t, "m_q": m_q, "m_absmax": m_a, "v_q": v_q, "v_absmax": v_a,
+               "r_q": r_q, "r_absmax": r_a}
+
+
+# --------------------------------------------------------------------------
+# Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11) counter-based uniforms
+# --------------------------------------------------------------------------
+_PHILOX_M0 = np.uint64(0xD2511F53)
+_PHILOX_M1 = np.uint64(0xCD9E8D57)
+_PHILOX_W0 = np.uint32(0x9E3779B9)
+_PHILOX_W1 = np.uint32(0xBB67AE85)
+
+
+def philox4x32_10(c0, c1, c2, c3, k0, k1):
+    """Vectorised Philox4x32 with 10 rounds; all arguments uint32 arrays/scalars."""
+    c0, c1, c2, c3 = (np.asarray(c, np.uint32).copy() for c in (c0, c1, c2, c3))
+    k0, k1 = int(k0) & 0xFFFFFFFF, int(k1) & 0xFFFFFFFF
+    for _ in range(10):
+        p0 = _PHILOX_M0 * c0.astype(np.uint64)
+        p1 = _PHILOX_M1 * c2.astype(np.uint64)
+        hi0, lo0 = (p0 >> np.uint64(32)).astype(np.uint32), p0.astype(np.uint32)
+        hi1, lo1 = (p1 >> np.uint64(32)).astype(np.uint32), p1.astype(np.uint32)
+        c0, c1, c2, c3 = hi1 ^ c1 ^ np.uint32(k0), lo1, hi0 ^ c3 ^ np.uint32(k1), lo0
+        k0 = (k0 + int(_PHILOX_W0)) & 0xFFFFFFFF
+        k1 = (k1 + int(_PHILOX_W1)) & 0xFFFFFFFF
+    return c0, c1, c2, c3
+
+
+def philox_uniforms(numel: int, seed: int, step: int, elem_offset: int = 0) -> np.ndarray:
+    """Uniforms in (0,1) for global elements ``[elem_offset, elem_offset+numel)``.
+
+    Element ``e`` uses Philox call ``e // 8`` (counter ``(e//8 lo, e//8 hi, step lo, step hi)``,
+    key ``(seed lo, seed hi)``) and 16-bit lane ``e % 8`` of its 128-bit output
+    (word ``(e%8)//2``, low half first); ``u = (h + 0.5) / 65536``.
+    """
+    if numel == 0:
+        return np.zeros(0, np.float32)
+    e = np.arange(elem_offset, elem_offset + numel, dtype=np.uint64)
+    call = np.unique(e // np.uint64(8))
+    lo = (call & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    hi = (call >> np.uint64(32)).astype(np.uint32)
+    s_lo = np.uint32(step & 0xFFFFFFFF)
+    s_hi = np.uint32((step >> 32) & 0xFFFFFFFF)
+    w = philox4x32_10(lo, hi, np.full_like(lo, s_lo), np.full_like(lo, s_hi),
+                      np.uint32(seed & 0xFFFFFFFF), np.uint32((seed >> 32) & 0xFFFFFFFF))
+    words = np.stack(w, axis=1)  # [ncalls, 4]
+    halves = np.stack([words & 0xFFFF, words >> 16], axis=2).reshape(-1, 8)  # [ncalls, 8]
+    idx = (e // np.uint64(8) - call[0]).astype(np.int64)
+    h = halves[idx, (e % np.uint64(8)).astype(np.int64)].astype(np.float32)
+    return (h + F32(0.5)) * F32(1.0 / 65536.0)

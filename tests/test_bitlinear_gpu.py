@@ -1,0 +1,134 @@
+"""BitLinear forward/backward through the int8 tensor-core path against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import firefly_b200 as ff
+from firefly_b200 import fireflykernels as fk
+from oracle import firefly_oracle as O
+from tests._util import assert_close_rel, bf16_bits, bf16_ulp_diff, from_bf16_bits, load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+REL = 1e-3
+
+
+def _layer(K, O_, bias, seed):
+    torch.manual_seed(seed)
+    layer = ff.BitLinear(K, O_, bias=bias)
+    w = torch.randn(O_, K, generator=torch.Generator().manual_seed(seed)) * 0.02
+    q, s = ff.quantize_fp_to_int8(w)
+    layer.int_weight.copy_(q)
+    layer.weight_scale.copy_(s)
+    if bias:
+        with torch.no_grad():
+            layer.bias.copy_(torch.randn(O_, generator=torch.Generator().manual_seed(seed + 1)) * 0.1)
+    return layer.to(DEV)
+
+
+@pytest.mark.parametrize("T,K,O_,bias,xdt", [
+    (256, 1024, 1024, False, torch.float32),   # the single-layer config
+    (48, 64, 32, True, torch.bfloat16),
+    (37, 100, 70, True, torch.float32),        # K and O not multiples of 16, ragged T
+    (1, 16, 16, False, torch.bfloat16),
+])
+def test_forward_backward_match_oracle(T, K, O_, bias, xdt):
+    layer = _layer(K, O_, bias, seed=T + K)
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(T, K, generator=g)).to(xdt)
+    dy = torch.randn(T, O_, generator=g).to(torch.bfloat16)
+    xd = x.to(DEV).requires_grad_(True)
+    y = layer(xd)
+    assert y.dtype == torch.bfloat16 and y.shape == (T, O_)
+    y.backward(dy.to(DEV))
+    q = layer.int_weight.cpu().numpy()
+    s = layer.weight_scale.cpu().numpy()
+    b = layer.bias.detach().cpu().numpy() if bias else None
+    y_o, *_ = O.linear_forward(x.float().numpy(), q, s, b)
+    # same fp32 epilogue as the oracle: bf16 outputs identical
+    np.testing.assert_array_equal(bf16_bits(y), y_o)
+    out = O.linear_backward(x.float().numpy(), bf16_bits(dy), q, s, has_bias=bias)
+    assert xd.grad.dtype == xdt
+    np.testing.assert_array_equal(bf16_bits(xd.grad.to(torch.bfloat16)), out["dx"])
+    gw = layer.consume_weight_grad()
+    assert gw.dtype == torch.bfloat16 and gw.shape == (O_, K)
+    np.testing.assert_array_equal(bf16_bits(gw), out["gw"])
+    assert layer.consume_weight_grad() is None
+    if bias:
+        assert bf16_ulp_diff(bf16_bits(layer.bias.grad), out["db"]).max() <= 1
+
+
+def test_grad_cache_accumulates_across_micro_batches():
+    layer = _layer(96, 80, False, seed=1)
+    g = torch.Generator().manual_seed(2)
+    xs = [torch.randn(64, 96, generator=g) for _ in range(2)]
+    dys = [torch.randn(64, 80, generator=g).to(torch.bfloat16) for _ in range(2)]
+    cache = None
+    q, s = layer.int_weight.cpu().numpy(), layer.weight_scale.cpu().numpy()
+    for x, dy in zip(xs, dys):
+        y = layer(x.to(DEV).requires_grad_(True))
+        y.backward(dy.to(DEV))
+        out = O.linear_backward(x.numpy(), bf16_bits(dy), q, s, grad_cache=cache)
+        cache = out["gw"]
+    np.testing.assert_array_equal(bf16_bits(layer.consume_weight_grad()), cache)
+
+
+def test_three_d_input_and_errors():
+    layer = _layer(32, 48, False, seed=3)
+    x = torch.randn(2, 5, 32, device=DEV)
+    y = layer(x)
+    assert y.shape == (2, 5, 48)
+    with pytest.raises(ValueError):
+        layer(torch.randn(4, 31, device=DEV))
+    with pytest.raises(RuntimeError):
+        layer(torch.randn(4, 32))  # CPU input, CUDA module
+    # no-grad forward does not leave a gradient behind
+    with torch.no_grad():
+        layer(x)
+    assert layer.consume_weight_grad() is None
+
+
+def test_accuracy_against_live_bf16_reference():
+    """The reference computes in bf16 (fireflykernels.py:164-210); the int8 path stays close."""
+    z = load_golden("linear_bf16.npz")
+    for c in ("fp32", "bias_bf16"):
+        x = torch.from_numpy(z[c + "_x"])
+        if bool(z[c + "_xisbf16"]):
+            x = x.to(torch.bfloat16)
+        q, s = torch.from_numpy(z[c + "_q"]), torch.from_numpy(z[c + "_s"])
+        O_, K = q.shape
+        layer = ff.BitLinear(K, O_, bias=bool(z[c + "_bias"].size)).to(DEV)
+        layer.int_weight.copy_(q)
+        layer.weight_scale.copy_(s)
+        if layer.bias is not None:
+            with torch.no_grad():
+                layer.bias.copy_(torch.from_numpy(z[c + "_bias"]))
+        y = layer(x.to(DEV))
+        y_ref = from_bf16_bits(z[c + "_y"]).float()
+        rel = (y.float().cpu() - y_ref).norm() / y_ref.norm()
+        assert rel < 0.02, (c, float(rel))
+
+
+def test_state_dict_reregisters_handle():
+    a = _layer(16, 16, False, seed=4)
+    b = _layer(16, 16, False, seed=5)
+    ha, hb = a._registered_handle, b._registered_handle
+    assert ha != hb
+    b.load_state_dict(a.state_dict())
+    assert b._registered_handle == ha
+    assert hb not in fk._REGISTERED_HANDLES
+    assert torch.equal(a.int_weight, b.int_weight)
+
+
+def test_weight_cache_invalidated_by_optimizer():
+    layer = _layer(64, 48, False, seed=6)
+    x = torch.randn(32, 64, device=DEV, requires_grad=True)
+    opt = ff.FireFlyOptim([torch.nn.Parameter(torch.zeros(1, device=DEV))], lr=5e-2, bit_modules=[layer])
+    for _ in range(3):
+        y = layer(x)
+        y.backward(torch.ones_like(y))
+        x.grad = None
+        opt.step()
+        # the transposed weight used by the next dX GEMM must be the updated weight
+        wt = fk._weight_transposed(layer._registered_handle, layer.int_weight)
+        np.testing.assert_array_equal(wt.cpu().numpy()[:, :48], layer.int_weight.cpu().numpy().T)

@@ -1,0 +1,126 @@
+"""tcgen05 int8 GEMM against the oracle: int32 accumulators bit-exact, dequantised outputs
+within 1e-3 relative (bf16: or within one bf16 step of the rounded oracle)."""
+import numpy as np
+import pytest
+import torch
+
+from firefly_b200 import _capi
+from oracle import firefly_oracle as O
+from tests._util import assert_close_rel, bf16_bits
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+REL = 1e-3
+
+
+def _operands(M, N, K, seed, ld_pad=0):
+    g = torch.Generator().manual_seed(seed)
+    lda = (K + 15) // 16 * 16 + ld_pad
+    a = torch.zeros(M, lda, dtype=torch.int8)
+    b = torch.zeros(N, lda, dtype=torch.int8)
+    a[:, :K] = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    b[:, :K] = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    # garbage in the padding must not leak into the sums
+    if lda > K:
+        a[:, K:] = 77
+        b[:, K:] = -55
+    sa = torch.empty(M).uniform_(1e-3, 1e-2, generator=g)
+    sb = torch.empty(N).uniform_(1e-3, 1e-2, generator=g)
+    bias = torch.randn(N, generator=g)
+    return a, b, sa, sb, bias
+
+
+SHAPES = [
+    (1, 1, 1),
+    (128, 256, 128),
+    (16, 512, 1024),
+    (200, 300, 1000),
+    (129, 257, 129),
+    (256, 1024, 1024),
+    (1024, 1024, 1024),
+    (130, 8192, 256),
+    (513, 200, 4096),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_s32_bit_exact(M, N, K):
+    a, b, *_ = _operands(M, N, K, seed=M + N + K, ld_pad=16 if K % 3 == 0 else 0)
+    d = _capi.gemm_i8(a.to(DEV), b.to(DEV), K, out_kind=_capi.FF_OUT_S32)
+    want = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
+    np.testing.assert_array_equal(d.cpu().numpy().astype(np.int64), want)
+    assert _capi.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (200, 300, 1000), (256, 1024, 1024), (129, 257, 4096)])
+def test_gemm_f32_and_bf16_epilogue(M, N, K):
+    a, b, sa, sb, bias = _operands(M, N, K, seed=3 * M + K)
+    acc = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
+    want = O.dequant(acc, sa.numpy(), sb.numpy(), bias.numpy())
+    ad, bd = a.to(DEV), b.to(DEV)
+    d32 = _capi.gemm_i8(ad, bd, K, sa.to(DEV), sb.to(DEV), bias.to(DEV), out_kind=_capi.FF_OUT_F32)
+    # same fp32 operation order as the oracle: identical results expected
+    np.testing.assert_array_equal(d32.cpu().numpy(), want)
+    d16 = _capi.gemm_i8(ad, bd, K, sa.to(DEV), sb.to(DEV), bias.to(DEV), out_kind=_capi.FF_OUT_BF16)
+    want16 = O.f32_to_bf16_bits(want)
+    np.testing.assert_array_equal(bf16_bits(d16), want16)
+    # scale_a only (the dX epilogue)
+    d = _capi.gemm_i8(ad, bd, K, sa.to(DEV), None, None, out_kind=_capi.FF_OUT_F32)
+    np.testing.assert_array_equal(d.cpu().numpy(), O.dequant(acc, sa.numpy()))
+    assert_close_rel(d.cpu().numpy(), O.dequant(acc, sa.numpy()), REL, "scale_a only")
+
+
+def test_gemm_bf16_accumulate():
+    M, N, K = 300, 520, 700
+    a, b, sa, sb, _ = _operands(M, N, K, seed=5)
+    g = torch.Generator().manual_seed(6)
+    old = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    d = old.clone().to(DEV)
+    _capi.gemm_i8(a.to(DEV), b.to(DEV), K, sa.to(DEV), sb.to(DEV), out_kind=_capi.FF_OUT_BF16_ACCUM, out=d)
+    acc = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
+    term = O.round_bf16(O.dequant(acc, sa.numpy(), sb.numpy()))
+    want = O.f32_to_bf16_bits(old.float().numpy() + term)
+    np.testing.assert_array_equal(bf16_bits(d), want)
+
+
+def test_gemm_strided_output_and_misaligned_n():
+    M, N, K = 70, 45, 96
+    a, b, sa, sb, bias = _operands(M, N, K, seed=8)
+    big = torch.zeros(M, 64, dtype=torch.float32, device=DEV)
+    out = big[:, 3:3 + N]
+    _capi.gemm_i8(a.to(DEV), b.to(DEV), K, sa.to(DEV), sb.to(DEV), bias.to(DEV), out_kind=_capi.FF_OUT_F32, out=out)
+    acc = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
+    np.testing.assert_array_equal(out.cpu().numpy(), O.dequant(acc, sa.numpy(), sb.numpy(), bias.numpy()))
+    assert (big[:, :3] == 0).all() and (big[:, 3 + N:] == 0).all()
+
+
+def test_gemm_rejects_bad_layout():
+    a = torch.zeros(4, 24, dtype=torch.int8, device=DEV)
+    b = torch.zeros(4, 32, dtype=torch.int8, device=DEV)
+    with pytest.raises(ValueError):
+        _capi.gemm_i8(a, b, 24, out_kind=_capi.FF_OUT_S32)  # lda = 24 is not a multiple of 16
+    with pytest.raises(ValueError):
+        _capi.gemm_i8(b, b, 0, out_kind=_capi.FF_OUT_S32)
+
+
+def test_gemm_large_square_checksum():
+    """8192^3 (the headline size): exact int32 checked through size-independent properties.
+
+    acc = A·Bᵀ; for all-ones x, (A·Bᵀ)·x = A·(Bᵀ·x) checked in int64 on the host, and a
+    random sample of entries is recomputed exactly."""
+    M = N = K = 8192
+    g = torch.Generator(device=DEV).manual_seed(0)
+    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8, device=DEV)
+    b = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8, device=DEV)
+    d = _capi.gemm_i8(a, b, K, out_kind=_capi.FF_OUT_S32)
+    row_sums = d.to(torch.int64).sum(dim=1)
+    bt_ones = b.to(torch.int64).sum(dim=0)  # Bᵀ·1, [K]
+    want = (a.to(torch.int64) * bt_ones[None, :]).sum(dim=1)
+    assert torch.equal(row_sums, want)
+    idx = torch.randint(0, M, (64,), generator=torch.Generator().manual_seed(1))
+    jdx = torch.randint(0, N, (64,), generator=torch.Generator().manual_seed(2))
+    ai = a[idx.to(DEV)].to(torch.int64).cpu()
+    bj = b[jdx.to(DEV)].to(torch.int64).cpu()
+    sub = d[idx.to(DEV)][:, jdx.to(DEV)].to(torch.int64).cpu()
+    assert torch.equal(sub, ai @ bj.T)
+    assert _capi.device_status() == 0
