@@ -54,6 +54,13 @@ SIGNATURES = {
 
 _lib = None
 
+# Instrumentation for benchmarks: number of this library's kernels launched so far,
+# and an optional list that collects (start_event, end_event, ops) per GEMM launch.
+LAUNCHES = 0
+GEMM_EVENTS: list | None = None
+_KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_transpose_i8": 1, "ff_gemm_i8": 1,
+                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
+
 
 def lib() -> ctypes.CDLL:
     """Load the CUDA library once; raise if it was not built."""
@@ -85,9 +92,11 @@ def _raise(rc: int, name: str) -> None:
 
 
 def _call(name: str, *args) -> None:
+    global LAUNCHES
     rc = getattr(lib(), name)(*args)
     if rc != FF_OK:
         _raise(rc, name)
+    LAUNCHES += _KERNELS_PER_CALL.get(name, 0)
 
 
 def _ptr(t: torch.Tensor | None):
@@ -239,8 +248,15 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | No
     sb = None if scale_b is None else scale_b.to(torch.float32).contiguous()
     bb = None if bias is None else bias.to(torch.float32).contiguous()
     with torch.cuda.device(dev):
+        ev = None
+        if GEMM_EVENTS is not None and M > 0 and N > 0:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         _call("ff_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
               ldd, int(out_kind), M, N, int(k), _stream(dev))
+        if ev is not None:
+            ev[1].record()
+            GEMM_EVENTS.append((ev[0], ev[1], 2 * M * N * int(k)))
     return out
 
 

@@ -42,10 +42,18 @@ _INV_LN1P_MU = F32(1.0 / 5.545177444479562)  # fireflyoptim.py:10
 # --------------------------------------------------------------------------
 def f32_to_bf16_bits(x) -> np.ndarray:
     """Round-to-nearest-even fp32 -> bf16 (what ``tensor.to(torch.bfloat16)`` does)."""
-    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
-    nan = np.isnan(np.asarray(x, dtype=np.float32))
-    r = ((b.astype(np.uint64) + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
-    return np.where(nan, np.uint16(0x7FC0), r)
+    f = np.ascontiguousarray(x, dtype=np.float32)
+    b = f.view(np.uint32)
+    t = b >> 16
+    t &= 1
+    t += 0x7FFF
+    t += b  # no uint32 overflow for finite values; NaN patterns are replaced below
+    t >>= 16
+    r = t.astype(np.uint16)
+    nan = np.isnan(f)
+    if nan.any():
+        r[nan] = 0x7FC0
+    return r
 
 
 def bf16_bits_to_f32(h) -> np.ndarray:
@@ -102,13 +110,15 @@ def quantize_cols_t(x, eps: float = 1e-8):
 # int8 GEMM + epilogue
 # --------------------------------------------------------------------------
 def gemm_i8(a, b) -> np.ndarray:
-    """Exact ``A[M,K] · B[N,K]ᵀ`` accumulation of int8 codes, returned as int64.
-
-    fp64 BLAS is exact here: every product and partial sum is an integer below 2^53.
-    """
+    """Exact ``A[M,K] · B[N,K]ᵀ`` accumulation of int8 codes, returned as int64."""
     a = np.asarray(a, np.int8)
     b = np.asarray(b, np.int8)
-    return np.rint(a.astype(np.float64) @ b.astype(np.float64).T).astype(np.int64)
+    # K chunks of 1024: every partial sum is an integer below 2^24, exact in fp32 BLAS;
+    # chunks are summed in fp64 (exact below 2^53)
+    acc = np.zeros((a.shape[0], b.shape[0]), np.float64)
+    for k0 in range(0, a.shape[1], 1024):
+        acc += a[:, k0:k0 + 1024].astype(np.float32) @ b[:, k0:k0 + 1024].astype(np.float32).T
+    return np.rint(acc).astype(np.int64)
 
 
 def dequant(acc, scale_a=None, scale_b=None, bias=None) -> np.ndarray:
