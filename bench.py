@@ -56,7 +56,43 @@ def parse_args():
     ap.add_argument("--adamw-params", type=float, default=6.7e9)
     ap.add_argument("--no-sub", action="store_true", help="skip the GEMM sweep and the AdamW sub-benchmarks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "mlp"],
+                    help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
+
+
+def kernel_case(args):
+    """One launch of one kernel on a case sized for an ncu capture (a few GB at most)."""
+    import torch
+
+    from firefly_b200 import _capi
+    from firefly_b200.fireflyoptim import _tables_on
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel_case.startswith("gemm"):
+        M, N, K = (8192, 8192, 8192) if args.kernel_case == "gemm8192" else (16, 8192, 8192)
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        sa, sb = torch.rand(M, device=dev) * 1e-2, torch.rand(N, device=dev) * 1e-2
+        _capi.gemm_i8(a, b, K, sa, sb, out_kind=_capi.FF_OUT_BF16)
+    elif args.kernel_case == "adamw":
+        n = 268435456
+        q = torch.randint(-127, 128, (n,), dtype=torch.int8, device=dev, generator=g)
+        grad = torch.empty(n, dtype=torch.bfloat16, device=dev).normal_(0, 1e-3, generator=g)
+        c = [torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g) for _ in range(3)]
+        am = [torch.empty(n // 256, device=dev).uniform_(1e-4, 1e-2, generator=g) for _ in range(3)]
+        ws = torch.empty(n // 4096, device=dev).uniform_(1e-4, 1e-3, generator=g)
+        dec_s, dec_u = _tables_on(dev)
+        _capi.dqt_adamw8(q, ws, 4096, grad, c[0], am[0], c[1], am[1], c[2], am[2], lr=1e-3, beta1=0.9,
+                         beta2=0.999, eps=1e-8, wd=0.01, step=3, sr_bias=0.15, seed=1, dec_s=dec_s, dec_u=dec_u)
+    elif args.kernel_case == "quant":
+        x = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
+        cm = torch.rand(11008, device=dev) * 1e-3
+        _capi.quant_dual(x, row_colmul=cm)
+    torch.cuda.synchronize()
+    assert _capi.device_status() == 0
+    print("ok", args.kernel_case)
 
 
 # ---------------------------------------------------------------------------
@@ -373,6 +409,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if args.kernel_case:
+        kernel_case(args)
+        return
 
     import datetime
 
@@ -394,12 +433,14 @@ def main():
     mods = [model.gate, model.up, model.down]
     opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
-    x = torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16)
+    # the block input is an activation of the model: it needs a gradient (dX is part of the step)
+    x = torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(True)
     dy = torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16)
 
     def step(xi, dyi):
         y = model(xi)
         y.backward(dyi)
+        xi.grad = None
         opt.step()
         return y
 
@@ -441,9 +482,9 @@ def main():
     g_ops = [o for _, _, o in gemm_events]
 
     # ---- e2e: host inputs copied in, loss read back, every step
-    xh = x.cpu().pin_memory()
+    xh = x.detach().cpu().pin_memory()
     dyh = dy.cpu().pin_memory()
-    xd, dyd = torch.empty_like(x), torch.empty_like(dy)
+    xd, dyd = torch.empty_like(x).requires_grad_(True), torch.empty_like(dy)
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     e2e_steps = max(3, args.steps // 2)
     barrier()
@@ -451,7 +492,8 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(e2e_steps):
-        xd.copy_(xh, non_blocking=True)
+        with torch.no_grad():
+            xd.copy_(xh, non_blocking=True)
         dyd.copy_(dyh, non_blocking=True)
         y = step(xd, dyd)
         loss = (y[-1].float() * dyd[-1].float()).sum()  # the step's scalar result
@@ -512,7 +554,7 @@ def main():
             "l2": "inputs larger than L2 (step working set > 126 MB)",
         },
         "e2e": {"value": T * world * e2e_steps / e2e_sec, "unit": "tokens/s",
-                "h2d_bytes_per_step": int(x.numel() * 2 + dy.numel() * 2), "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": int(xh.numel() * 2 + dyh.numel() * 2), "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
         "roofline": {
             "kernel": "ff_gemm_i8 (tcgen05 kind::i8)", "bound": "tensor",

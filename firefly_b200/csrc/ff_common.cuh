@@ -131,6 +131,25 @@ __device__ __forceinline__ int quant_code(float v, float s) {
   return (y == y) ? (int)y : 0;
 }
 
+// The same code as quant_code(v, s), computed from inv_s = 1/s (round-to-nearest).
+// y = v * inv_s is within 1.5 ulp of the IEEE quotient v / s, so rint(y) equals
+// rint(v / s) except when y lies within a few ulps of a half-integer; only then is
+// the exact division done.  Rounding uses the 1.5*2^23 magic add (round half to
+// even on the FMA pipe, no float-to-int conversion unit op).
+__device__ __forceinline__ int quant_code_fast(float v, float s, float inv_s) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float y = fminf(fmaxf(__fmul_rn(v, inv_s), -128.f), 128.f);
+  float t = __fadd_rn(y, kMagic);
+  const float r = __fsub_rn(t, kMagic);
+  const float dist = fabsf(fabsf(__fsub_rn(y, r)) - 0.5f);
+  if (dist <= 4.8e-7f * fabsf(y)) {  // near a tie: decide with the correctly rounded quotient
+    y = fminf(fmaxf(__fdiv_rn(v, s), -128.f), 128.f);
+    t = __fadd_rn(y, kMagic);
+  }
+  const int code = __float_as_int(t) - 0x4B400000;
+  return min(127, max(-127, code));
+}
+
 __device__ __forceinline__ float row_scale(float absmax, float eps) {
   return __fdiv_rn(fmaxf(absmax, eps), 127.f);
 }

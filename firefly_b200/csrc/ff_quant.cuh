@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float sc = row_scale(amax, eps);
+  const float isc = __frcp_rn(sc);
   if (lane == 0) s[row] = sc;
   if constexpr (VEC) {
     const int64_t nvec = cols / 8;
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float t = colmul ? __fmul_rn(v[j], __ldg(colmul + i * 8 + j)) : v[j];
-        c8[j] = quant_code(t, sc);
+        c8[j] = quant_code_fast(t, sc, isc);
       }
       uint2 w = make_uint2(pack4(c8[0], c8[1], c8[2], c8[3]), pack4(c8[4], c8[5], c8[6], c8[7]));
       *reinterpret_cast<uint2*>(qr + i * 8) = w;
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code(t, sc);
+        code = quant_code_fast(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code(t, sc);
+        code = quant_code_fast(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -90,12 +91,15 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 
 // ---------------------------------------------------------------------------
 // Dual quantiser, pass A: raw absmax per row (of x*colmul) and per column (of x).
-// Tile: 256 rows x (128 threads * 8) columns.  Results are combined across
-// tiles with integer atomicMax on the (non-negative) fp32 bit patterns, which
-// is exact and order-independent.
+// CTA: 256 threads, tile of 128 rows x 1024 columns.  Threads 0-127 take the
+// even rows, 128-255 the odd rows; each thread owns 8 columns (16 B of bf16)
+// and keeps 4 row loads in flight.  Partial maxima are combined through shared
+// memory, then across CTAs with integer atomicMax on the (non-negative) fp32 bit
+// patterns, which is exact and order-independent.
 // ---------------------------------------------------------------------------
-constexpr int kDualARows = 256;
-constexpr int kDualAThreads = 128;
+constexpr int kDualARows = 128;
+constexpr int kDualAThreads = 256;
+constexpr int kDualACols = 1024;
 
 template <int DT>
 __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
@@ -103,12 +107,14 @@ __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
     const float* __restrict__ colmul, bool want_rows, bool want_cols,
     uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax) {
   using T = typename Elem<DT>::T;
-  __shared__ float red[kDualARows][kDualAThreads / 32 + 1];
+  __shared__ float red[kDualARows][9];            // per row: 8 warps' partial maxima
+  __shared__ float cred[kDualACols];               // odd-row half's column maxima
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t c0 = (int64_t)blockIdx.x * kDualAThreads * 8 + tid * 8;
+  const int half = tid >> 7, ct = tid & 127;
+  const int64_t c0 = (int64_t)blockIdx.x * kDualACols + ct * 8;
   const int64_t r0 = (int64_t)blockIdx.y * kDualARows;
   const bool full = (c0 + 8 <= cols);
-  const bool vec_ok = ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
+  const bool vec_ok = full && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
                       ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   float cm[8];
 #pragma unroll
@@ -117,39 +123,55 @@ __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
 #pragma unroll
   for (int j = 0; j < 8; ++j) cmax[j] = 0.f;
   const int nr = (int)min64(kDualARows, rows - r0);
-  for (int i = 0; i < nr; ++i) {
-    const T* xr = x + (r0 + i) * ldx;
-    float v[8];
-    if (full && vec_ok) {
-      load8<DT>(xr + c0, v);
-    } else {
+  constexpr int U = 4;
+  for (int i0 = half; i0 < kDualARows; i0 += 2 * U) {
+    float v[U][8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (c0 + j < cols) ? Elem<DT>::to_f32(xr[c0 + j]) : 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + 2 * u;
+      if (i < nr) {
+        const T* xr = x + (r0 + i) * ldx;
+        if (vec_ok) {
+          load8<DT>(xr + c0, v[u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[u][j] = (c0 + j < cols) ? Elem<DT>::to_f32(xr[c0 + j]) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
+      }
     }
-    float rm = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float rm = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        cmax[j] = fmaxf(cmax[j], fabsf(v[u][j]));
+        rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(v[u][j], cm[j]) : v[u][j]));
+      }
+      if (want_rows) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
+        if (lane == 0) red[i0 + 2 * u][warp & 3] = rm;
+      }
+    }
+  }
+  if (want_cols && half == 1) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cred[ct * 8 + j] = cmax[j];
+  }
+  __syncthreads();
+  if (want_cols && half == 0) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      cmax[j] = fmaxf(cmax[j], fabsf(v[j]));
-      float t = colmul ? __fmul_rn(v[j], cm[j]) : v[j];
-      rm = fmaxf(rm, fabsf(t));
+      const float m = fmaxf(cmax[j], cred[ct * 8 + j]);
+      if (c0 + j < cols) atomicMax(col_amax + c0 + j, __float_as_uint(m));
     }
-    if (want_rows) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
-      if (lane == 0) red[i][warp] = rm;
-    }
-  }
-  if (want_cols) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (c0 + j < cols) atomicMax(col_amax + c0 + j, __float_as_uint(cmax[j]));
   }
   if (want_rows) {
-    __syncthreads();
     for (int i = tid; i < nr; i += kDualAThreads) {
-      float m = red[i][0];
-#pragma unroll
-      for (int w = 1; w < kDualAThreads / 32; ++w) m = fmaxf(m, red[i][w]);
+      const float m = fmaxf(fmaxf(red[i][0], red[i][1]), fmaxf(red[i][2], red[i][3]));
       atomicMax(row_amax + r0 + i, __float_as_uint(m));
     }
   }
@@ -170,19 +192,23 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
     float* __restrict__ s_rows, int8_t* __restrict__ q_cols_t, int64_t ldqt,
     float* __restrict__ s_cols) {
   using T = typename Elem<DT>::T;
-  __shared__ uint32_t tileT[kTile][kTile / 4 + 1];  // [col][row/4]
-  __shared__ float srow[kTile], scol[kTile], cmul[kTile];
+  // [col][row/4] words; word w of column c is stored at (w + c + c/32) mod 32, which
+  // keeps both the column-wise writes and the row-wise reads nearly conflict-free
+  __shared__ uint32_t tileT[kTile][kTile / 4];
+  __shared__ float srow[kTile], scol[kTile], cmul[kTile], isrow[kTile], iscol[kTile];
   const int tid = threadIdx.x;
   const int64_t C0 = (int64_t)blockIdx.x * kTile, R0 = (int64_t)blockIdx.y * kTile;
   const bool do_rows = (q_rows != nullptr), do_cols = (q_cols_t != nullptr);
   if (tid < kTile) {
     const int64_t r = R0 + tid;
     srow[tid] = (do_rows && r < rows) ? row_scale(__uint_as_float(row_amax[r]), eps) : 1.f;
+    isrow[tid] = __frcp_rn(srow[tid]);
     if (do_rows && r < rows && blockIdx.x == 0) s_rows[r] = srow[tid];
   } else {
     const int k = tid - kTile;
     const int64_t c = C0 + k;
     scol[k] = (do_cols && c < cols) ? row_scale(__uint_as_float(col_amax[c]), eps) : 1.f;
+    iscol[k] = __frcp_rn(scol[k]);
     cmul[k] = (colmul && c < cols) ? __ldg(colmul + c) : 1.f;
     if (do_cols && c < cols && blockIdx.y == 0) s_cols[c] = scol[k];
   }
@@ -217,9 +243,9 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
       }
       if (do_rows && r < rows && c < ldq) {
         int code[8];
-        const float sr = srow[rb + i];
+        const float sr = srow[rb + i], isr = isrow[rb + i];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) code[j] = quant_code(__fmul_rn(v[j], cmul[cb + j]), sr);
+        for (int j = 0; j < 8; ++j) code[j] = quant_code_fast(__fmul_rn(v[j], cmul[cb + j]), sr, isr);
         int8_t* qr = q_rows + r * ldq + c;
         if (c + 8 <= ldq) {
           *reinterpret_cast<uint2*>(qr) =
@@ -231,14 +257,17 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
       if (do_cols) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int code = (r < rows) ? quant_code(v[j], scol[cb + j]) : 0;
+          const int code = (r < rows) ? quant_code_fast(v[j], scol[cb + j], iscol[cb + j]) : 0;
           colw[j] |= (uint32_t)(code & 0xff) << (8 * i);
         }
       }
     }
     if (do_cols) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) tileT[cb + j][rb / 4] = colw[j];
+      for (int j = 0; j < 8; ++j) {
+        const int c = cb + j;
+        tileT[c][(rb / 4 + c + (c >> 5)) & 31] = colw[j];
+      }
     }
   }
   if (!do_cols) return;
@@ -251,8 +280,9 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
     const int64_t c = C0 + k;
     const int64_t r = R0 + chunk * 16;
     if (c < cols && r < ldqt) {
-      uint4 w = make_uint4(tileT[k][chunk * 4 + 0], tileT[k][chunk * 4 + 1], tileT[k][chunk * 4 + 2],
-                           tileT[k][chunk * 4 + 3]);
+      const int rot = k + (k >> 5);
+      uint4 w = make_uint4(tileT[k][(chunk * 4 + 0 + rot) & 31], tileT[k][(chunk * 4 + 1 + rot) & 31],
+                           tileT[k][(chunk * 4 + 2 + rot) & 31], tileT[k][(chunk * 4 + 3 + rot) & 31]);
       *reinterpret_cast<uint4*>(q_cols_t + c * ldqt + r) = w;
     }
   }
@@ -393,7 +423,7 @@ extern "C" int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t 
   uint32_t* row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
   uint32_t* col_amax = row_amax + rows;
   FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(rows + cols), st), "ff_quant_dual_i8 memset");
-  dim3 gA((unsigned)((cols + kDualAThreads * 8 - 1) / (kDualAThreads * 8)), (unsigned)((rows + kDualARows - 1) / kDualARows));
+  dim3 gA((unsigned)((cols + kDualACols - 1) / kDualACols), (unsigned)((rows + kDualARows - 1) / kDualARows));
   const int64_t rspan = do_cols ? max64(rows, ldqt) : rows;
   const int64_t cspan = do_rows ? max64(cols, ldq) : cols;
   dim3 gB((unsigned)((cspan + kTile - 1) / kTile), (unsigned)((rspan + kTile - 1) / kTile));
