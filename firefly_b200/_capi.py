@@ -43,6 +43,7 @@ SIGNATURES = {
     "ff_device_status": (_I, [_P, _I]),
     "ff_quant_rows_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P]),
     "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
+    "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_transpose_i8": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P]),
     "ff_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "ff_colsum_ws_elems": (_I64, [_I64, _I64]),
@@ -58,7 +59,8 @@ _lib = None
 # and an optional list that collects (start_event, end_event, ops) per GEMM launch.
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
-_KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_transpose_i8": 1, "ff_gemm_i8": 1,
+_KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
+                     "ff_transpose_i8": 1, "ff_gemm_i8": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
 
 

@@ -100,6 +100,31 @@ FF_API int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols
                      int8_t* q_cols_t, int64_t ldqt, float* s_cols,
                      float* absmax_ws, void* stream);
 
+/* Largest rows + cols that ff_quant_dual_i8_noalloc accepts (its scratch: 1 MiB of fp32). */
+#define FF_NOALLOC_DUAL_MAX_ELEMS 262144
+
+/*
+ * ff_quant_dual_i8 for callers that cannot allocate device memory: same
+ * arguments and results, minus absmax_ws.  No counterpart in the reference.
+ *
+ * Who needs it: a host runtime whose device memory is all handed out by its own
+ * pool allocator (cudaMalloc from inside it would take memory the pool has
+ * reserved and is not freed back through the pool), and callers on a pipelined
+ * step that cannot afford cudaMalloc's implicit device-wide synchronisation.
+ * The absmax scratch is a static array inside this library (FF_NOALLOC_DUAL_MAX_ELEMS
+ * floats, held on every GPU that loads the library until the process exits);
+ * rows + cols above that limit return FF_ERR_UNSUPPORTED.  The first call on a
+ * device looks up the array's device address (a runtime call, no allocation),
+ * so make that first call before any stream capture.  All calls share the
+ * array: calls whose kernels overlap on the GPU (different streams, no ordering)
+ * race on it and must be serialised by the caller.  The call allocates nothing
+ * (no cudaMalloc, cudaFree or allocating library routine).
+ */
+FF_API int ff_quant_dual_i8_noalloc(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                                    const float* row_colmul, float eps,
+                                    int8_t* q_rows, int64_t ldq, float* s_rows,
+                                    int8_t* q_cols_t, int64_t ldqt, float* s_cols, void* stream);
+
 /*
  * int8 transpose: dst[c, r] = src[r, c] for r < rows, c < cols; dst entries
  * r in rows..ldd-1 are written 0.  Builds the K-major copy of W (Wᵀ) that
