@@ -150,6 +150,17 @@ __device__ __forceinline__ int quant_code_fast(float v, float s, float inv_s) {
   return min(127, max(-127, code));
 }
 
+// quant_code_fast when |v| <= 127 * s is known (s computed from the absmax of the very
+// values being quantised): |v / s| <= 127, so no clamp is needed before or after rounding.
+__device__ __forceinline__ int quant_code_bounded(float v, float s, float inv_s) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float y = __fmul_rn(v, inv_s);
+  float t = __fadd_rn(y, kMagic);
+  const float dist = fabsf(fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) - 0.5f);
+  if (dist <= 4.8e-7f * fabsf(y)) t = __fadd_rn(__fdiv_rn(v, s), kMagic);
+  return __float_as_int(t) - 0x4B400000;
+}
+
 __device__ __forceinline__ float row_scale(float absmax, float eps) {
   return __fdiv_rn(fmaxf(absmax, eps), 127.f);
 }

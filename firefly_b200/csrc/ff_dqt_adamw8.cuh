@@ -32,7 +32,12 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kBlock = 256;
 constexpr int kRep = 16;                  // table replicas: lanes l and l+16 share one
 constexpr int kTabWords = 256 * kRep;     // one replicated table
-constexpr int kSmemBytes = 2 * kTabWords * 4;
+constexpr int kTabBytes = 2 * kTabWords * 4;
+// per warp, two stages of one block's inputs, filled by 1-D bulk (TMA) copies:
+// g (512 B) | q (256) | m (256) | v (256) | r (256) | u (1024, parity mode only)
+constexpr int kStageBytes = 512 + 4 * 256 + 1024;
+constexpr int kStageOffQ = 512, kStageOffM = 768, kStageOffV = 1024, kStageOffR = 1280, kStageOffU = 1536;
+constexpr int kSmemBytes = kTabBytes + kWarps * 2 * kStageBytes + kWarps * 2 * 8;
 constexpr float kMagic = 12582912.0f;     // 1.5 * 2^23
 
 struct Params {
@@ -53,10 +58,49 @@ struct Params {
   uint32_t seed_lo, seed_hi, step_lo, step_hi;
   int64_t rng_offset;
   int64_t row_step, in_row_step;  // grid-stride advance in (rows, elements within a row)
+  int bulk;                       // all arrays 16-byte aligned: stage inputs with bulk copies
   const float* u;
   const float* dec_s;
   const float* dec_u;
 };
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void bar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar));
+}
+__device__ __forceinline__ void bar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// time-bounded wait; false (and FF_DEVICE_TIMEOUT raised) if the copies never landed
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+  if (bar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!bar_try(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_status(FF_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+// 1-D bulk copy global -> shared (no multicast), completion counted on `bar`
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
 
 // Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3", SC'11)
 __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
@@ -119,12 +163,14 @@ __device__ __forceinline__ float div_nr(float x, float d, float inv_d) {
   return __fmaf_rn(r, inv_d, q0);
 }
 
-// sqrt(x) from rsqrt.approx with one residual correction (x >= 0; x == 0 gives 0)
+// sqrt(x) from rsqrt.approx with one residual correction, x >= 0.  Arguments below
+// 1e-37 (whose square roots are far below any eps added to them) use rsqrt(1e-37), so
+// x == 0 gives exactly 0 without a select.
 __device__ __forceinline__ float sqrt_nr(float x) {
-  const float rs = rsqrt_approx(x);
-  const float s0 = x == 0.f ? 0.f : __fmul_rn(x, rs);
+  const float rs = rsqrt_approx(fmaxf(x, 1e-37f));
+  const float s0 = __fmul_rn(x, rs);
   const float e = __fmaf_rn(-s0, s0, x);
-  return x == 0.f ? 0.f : __fmaf_rn(e, __fmul_rn(0.5f, rs), s0);
+  return __fmaf_rn(e, __fmul_rn(0.5f, rs), s0);
 }
 
 // exact int <-> float for small integers on the FMA/ALU pipes
@@ -137,28 +183,105 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// low bytes of four ints -> one word (byte permutes)
 __device__ __forceinline__ uint32_t pack_codes(const int (&c)[8], int base) {
-  return (uint32_t)(c[base] & 0xff) | ((uint32_t)(c[base + 1] & 0xff) << 8) |
-         ((uint32_t)(c[base + 2] & 0xff) << 16) | ((uint32_t)(c[base + 3] & 0xff) << 24);
+  const uint32_t lo = __byte_perm((uint32_t)c[base], (uint32_t)c[base + 1], 0x0040);
+  const uint32_t hi = __byte_perm((uint32_t)c[base + 2], (uint32_t)c[base + 3], 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
 }
+
+// ---------------------------------------------------------------------------
+// packed fp32 pairs: Blackwell's f32x2 add/sub/mul/fma issue two fp32 ops per
+// instruction (the kernel is bound by instruction issue, not by the FMA pipe)
+// ---------------------------------------------------------------------------
+struct f2 {
+  uint64_t v;
+};
+__device__ __forceinline__ f2 mk2(float a, float b) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ f2 splat(float a) { return mk2(a, a); }
+__device__ __forceinline__ void un2(f2 x, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x.v)); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 add2_rm(f2 a, f2 b) {
+  f2 r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+// x / d with nd = -d and id ~ 1/d: q0 = x*id, r = x - q0*d (exact), q = q0 + r*id
+__device__ __forceinline__ f2 div2(f2 x, f2 nd, f2 id) {
+  const f2 q0 = mul2(x, id);
+  return fma2(fma2(q0, nd, x), id, q0);
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xFFu; }
 
 template <bool HAS_U, bool SMALL_ROWS>
 __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
-  extern __shared__ float tab[];  // [2][256 codes][kRep]
+  extern __shared__ __align__(128) float tab[];  // [2][256 codes][kRep], then staging, then barriers
   float* tabS = tab;
   float* tabU = tab + kTabWords;
+  uint8_t* stage_base = reinterpret_cast<uint8_t*>(tab) + kTabBytes;
+  const int warp = threadIdx.x >> 5;
+  uint8_t* my_stage = stage_base + warp * 2 * kStageBytes;
+  const uint32_t bar0 = smem_addr(stage_base + kWarps * 2 * kStageBytes) + warp * 16;
   for (int i = threadIdx.x; i < kTabWords; i += kThreads) {
     tabS[i] = __ldg(p.dec_s + i / kRep);
     tabU[i] = __ldg(p.dec_u + i / kRep);
   }
+  if ((threadIdx.x & 31) == 0) {
+    bar_init(bar0);
+    bar_init(bar0 + 8);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int slot = lane & (kRep - 1);
+  const uint32_t stage_bytes_tx = 512 + 4 * 256 + (HAS_U ? 1024 : 0);
+  // lane 0 stages block b (a full block) into stage s
+  auto prefetch = [&](int64_t b, int s) {
+    const uint32_t dst = smem_addr(my_stage + s * kStageBytes), bar = bar0 + 8 * s;
+    const int64_t e = b * kBlock;
+    bar_expect(bar, stage_bytes_tx);
+    bulk_g2s(dst, p.g + e, 512, bar);
+    bulk_g2s(dst + kStageOffQ, p.q + e, 256, bar);
+    bulk_g2s(dst + kStageOffM, p.m_q + e, 256, bar);
+    bulk_g2s(dst + kStageOffV, p.v_q + e, 256, bar);
+    bulk_g2s(dst + kStageOffR, p.r_q + e, 256, bar);
+    if constexpr (HAS_U) bulk_g2s(dst + kStageOffU, p.u + e, 1024, bar);
+  };
+  const int64_t full_blocks = p.numel / kBlock;  // blocks [0, full_blocks) have 256 elements
   const int64_t nblocks = (p.numel + kBlock - 1) / kBlock;
   const int64_t wstride = (int64_t)gridDim.x * kWarps;
   const float eps = p.eps;
   const int64_t last_row = (p.elem_base + p.numel - 1) / p.row_len;
-  int64_t blk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  // loop-invariant pairs
+  const f2 b1 = splat(p.beta1), b2 = splat(p.beta2), omb1 = splat(p.omb1), omb2 = splat(p.omb2);
+  const f2 nbc1 = splat(-p.bc1), nbc2 = splat(-p.bc2), ibc1 = splat(p.ibc1), ibc2 = splat(p.ibc2);
+  const f2 eps2 = splat(eps), nlr = splat(p.neg_lr), wd2 = splat(p.wd), magic2 = splat(kMagic);
+  const f2 half2 = splat(0.5f), mone2 = splat(-1.f);
+  int64_t blk = (int64_t)blockIdx.x * kWarps + warp;
   // weight row of this lane's first element, advanced incrementally (no division per block)
   int64_t row, in_row;
   {
@@ -166,54 +289,73 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
     row = ge / p.row_len;
     in_row = ge - row * p.row_len;
   }
-  for (; blk < nblocks; blk += wstride) {
+  if (p.bulk && lane == 0 && blk < full_blocks) prefetch(blk, 0);
+  for (int it = 0; blk < nblocks; blk += wstride, ++it) {
     const int64_t e0 = blk * kBlock + lane * 8;
     const int nvalid = (int)max64(0, min64(8, p.numel - e0));
-    float g[8];
-    int qv[8], mc[8], vc[8], rc[8];
-    if (nvalid == 8) {
-      const uint4 gw = __ldg(reinterpret_cast<const uint4*>(p.g + e0));
-      const uint2 qw = *reinterpret_cast<const uint2*>(p.q + e0);
-      const uint2 mw = *reinterpret_cast<const uint2*>(p.m_q + e0);
-      const uint2 vw = *reinterpret_cast<const uint2*>(p.v_q + e0);
-      const uint2 rw = *reinterpret_cast<const uint2*>(p.r_q + e0);
-      const uint32_t gws[4] = {gw.x, gw.y, gw.z, gw.w};
+    const int stg = it & 1;
+    const bool staged = p.bulk && blk < full_blocks;
+    // stage the next block while this one is computed (its stage was consumed last iteration)
+    if (p.bulk && lane == 0 && blk + wstride < full_blocks) prefetch(blk + wstride, stg ^ 1);
+    const float am = __ldg(p.m_absmax + blk), av = __ldg(p.v_absmax + blk), ar = __ldg(p.r_absmax + blk);
+    // ---------------- inputs as packed words: g (bf16 pairs), q/m/v/r (bytes)
+    uint32_t gw[4], qw[2], mw[2], vw[2], rw[2];
+    float u[HAS_U ? 8 : 1];
+    if (staged) {
+      if (!bar_wait(bar0 + 8 * stg, (it >> 1) & 1)) return;  // copies lost: status raised
+      const uint8_t* sb = my_stage + stg * kStageBytes;
+      const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
+      const uint2 q2 = *reinterpret_cast<const uint2*>(sb + kStageOffQ + lane * 8);
+      const uint2 m2 = *reinterpret_cast<const uint2*>(sb + kStageOffM + lane * 8);
+      const uint2 v2 = *reinterpret_cast<const uint2*>(sb + kStageOffV + lane * 8);
+      const uint2 r2 = *reinterpret_cast<const uint2*>(sb + kStageOffR + lane * 8);
+      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
+      qw[0] = q2.x; qw[1] = q2.y; mw[0] = m2.x; mw[1] = m2.y;
+      vw[0] = v2.x; vw[1] = v2.y; rw[0] = r2.x; rw[1] = r2.y;
+      if constexpr (HAS_U) {
+        const float4 u0 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32);
+        const float4 u1 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32 + 16);
+        u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w;
+        u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
+      }
+      __syncwarp();  // every lane has its inputs: the stage may be refilled next iteration
+    } else if (nvalid == 8) {
+      const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(p.g + e0));
+      const uint2 q2 = *reinterpret_cast<const uint2*>(p.q + e0);
+      const uint2 m2 = *reinterpret_cast<const uint2*>(p.m_q + e0);
+      const uint2 v2 = *reinterpret_cast<const uint2*>(p.v_q + e0);
+      const uint2 r2 = *reinterpret_cast<const uint2*>(p.r_q + e0);
+      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
+      qw[0] = q2.x; qw[1] = q2.y; mw[0] = m2.x; mw[1] = m2.y;
+      vw[0] = v2.x; vw[1] = v2.y; rw[0] = r2.x; rw[1] = r2.y;
+      if constexpr (HAS_U) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        g[j] = __uint_as_float((j & 1) ? (gws[j >> 1] & 0xFFFF0000u) : (gws[j >> 1] << 16));
-        const int sh = (j & 3) * 8;
-        const uint32_t qwj = j < 4 ? qw.x : qw.y, mwj = j < 4 ? mw.x : mw.y;
-        const uint32_t vwj = j < 4 ? vw.x : vw.y, rwj = j < 4 ? rw.x : rw.y;
-        qv[j] = (int)(int8_t)((qwj >> sh) & 0xff);
-        mc[j] = (int)((mwj >> sh) & 0xff);
-        vc[j] = (int)((vwj >> sh) & 0xff);
-        rc[j] = (int)((rwj >> sh) & 0xff);
+        for (int j = 0; j < 8; ++j) u[j] = __ldg(p.u + e0 + j);
       }
     } else {
+      // ragged tail of the last block: missing elements get g = 0, q = 0 and the zero
+      // codes (m, r: 128; v: 0), which the update maps to zeros (ignored by the absmax)
+      gw[0] = gw[1] = gw[2] = gw[3] = 0u;
+      qw[0] = qw[1] = 0u;
+      mw[0] = mw[1] = rw[0] = rw[1] = 0x80808080u;
+      vw[0] = vw[1] = 0u;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const bool ok = j < nvalid;
-        g[j] = ok ? __uint_as_float((uint32_t)p.g[e0 + j] << 16) : 0.f;
-        qv[j] = ok ? (int)p.q[e0 + j] : 0;
-        mc[j] = ok ? (int)p.m_q[e0 + j] : 128;
-        vc[j] = ok ? (int)p.v_q[e0 + j] : 0;
-        rc[j] = ok ? (int)p.r_q[e0 + j] : 128;
+        if (j < nvalid) {
+          const int sh = 8 * (j & 3), w = j >> 2;
+          gw[j >> 1] |= (uint32_t)p.g[e0 + j] << (16 * (j & 1));
+          qw[w] |= ((uint32_t)(uint8_t)p.q[e0 + j]) << sh;
+          mw[w] = (mw[w] & ~(0xFFu << sh)) | ((uint32_t)p.m_q[e0 + j] << sh);
+          vw[w] |= (uint32_t)p.v_q[e0 + j] << sh;
+          rw[w] = (rw[w] & ~(0xFFu << sh)) | ((uint32_t)p.r_q[e0 + j] << sh);
+        }
+        if constexpr (HAS_U) u[j] = j < nvalid ? __ldg(p.u + e0 + j) : 2.f;
       }
     }
-    const float am = __ldg(p.m_absmax + blk), av = __ldg(p.v_absmax + blk), ar = __ldg(p.r_absmax + blk);
-    float u[8];
-    if constexpr (HAS_U) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) u[j] = j < nvalid ? __ldg(p.u + e0 + j) : 2.f;
-    } else {
-      uint32_t w[4];
+    uint32_t rw4[4];  // Philox output: 16 bits per element
+    if constexpr (!HAS_U) {
       const uint64_t call = (uint64_t)(p.rng_offset + e0) >> 3;
-      philox4x32_10((uint32_t)call, (uint32_t)(call >> 32), p.step_lo, p.step_hi, p.seed_lo, p.seed_hi, w);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t h = (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
-        u[j] = __fmul_rn(__fsub_rn(__int_as_float(0x4B000000 | h), 8388608.f) + 0.5f, 1.0f / 65536.0f);
-      }
+      philox4x32_10((uint32_t)call, (uint32_t)(call >> 32), p.step_lo, p.step_hi, p.seed_lo, p.seed_hi, rw4);
     }
     // weight-row scales: with row_len >= 8 the 8 elements span at most two rows
     const int64_t ra = min64(row, last_row), rb = min64(row + 1, last_row);
@@ -221,89 +363,150 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
     const float wsa = fmaxf(__ldg(p.wscale + ra), eps);
     const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
     const float iwsa = __frcp_rn(wsa), iwsb = __frcp_rn(wsb);
-    float mn[8], vn[8], rn[8];
+    const f2 am2 = splat(am), av2 = splat(av), ar2 = splat(ar);
+    f2 mn[4], vn[4], rn[4];
     int qn[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float ws = j < jsw ? wsa : wsb, iws = j < jsw ? iwsa : iwsb;
+    for (int pp = 0; pp < 4; ++pp) {
+      const int j0 = 2 * pp, j1 = 2 * pp + 1;
+      const int w = pp >> 1, k0 = j0 & 3, k1 = j1 & 3;
+      // weight-row scale of both elements
+      float ws0 = j0 < jsw ? wsa : wsb, ws1 = j1 < jsw ? wsa : wsb;
+      float iws0 = j0 < jsw ? iwsa : iwsb, iws1 = j1 < jsw ? iwsa : iwsb;
       if constexpr (SMALL_ROWS) {  // rows shorter than 8 elements: one division per element
-        ws = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j, p.numel - 1)) / p.row_len, last_row)), eps);
-        iws = __frcp_rn(ws);
+        ws0 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j0, p.numel - 1)) / p.row_len, last_row)), eps);
+        ws1 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j1, p.numel - 1)) / p.row_len, last_row)), eps);
+        iws0 = __frcp_rn(ws0);
+        iws1 = __frcp_rn(ws1);
       }
-      float m = __fmul_rn(tabS[mc[j] * kRep + slot], am);
-      float v = __fmul_rn(tabU[vc[j] * kRep + slot], av);
-      float r = __fmul_rn(tabS[rc[j] * kRep + slot], ar);
-      const float gj = g[j];
-      m = __fmaf_rn(gj, p.omb1, __fmul_rn(m, p.beta1));
-      v = __fmaf_rn(__fmul_rn(p.omb2, gj), gj, __fmul_rn(v, p.beta2));
-      // the residual update below loses its leading digits when dq is subtracted, so
-      // this chain follows the reference's rounding step by step (fireflyoptim.py:177-184)
-      const float mh = div_nr(m, p.bc1, p.ibc1);
-      const float vh = div_nr(v, p.bc2, p.ibc2);
-      const float den = __fadd_rn(sqrt_nr(vh), eps);
-      const float a = div_nr(mh, den, rcp_approx(den));
-      const float qf = small_int_to_float(qv[j]);
-      const float dwe = __fmul_rn(p.neg_lr, __fadd_rn(a, __fmul_rn(__fmul_rn(p.wd, qf), ws)));
-      r = __fadd_rn(r, div_nr(dwe, ws, iws));
-      const float absr = fabsf(r);
-      float base;
-      if (absr < 4194304.f) {  // floor via the magic add (exact below 2^22)
-        base = __fsub_rn(__fadd_rn(__fsub_rn(absr, 0.5f), kMagic), kMagic);
-        if (__fadd_rn(base, 1.f) <= absr) base = __fadd_rn(base, 1.f);
+      const f2 ws = mk2(ws0, ws1), nws = mk2(-ws0, -ws1), iws = mk2(iws0, iws1);
+      // decode (fireflyoptim.py:39-80): table value * block absmax
+      const f2 g = mk2(__uint_as_float(gw[pp] << 16), __uint_as_float(gw[pp] & 0xFFFF0000u));
+      f2 m = mul2(mk2(tabS[byte_of(mw[w], k0) * kRep + slot], tabS[byte_of(mw[w], k1) * kRep + slot]), am2);
+      f2 v = mul2(mk2(tabU[byte_of(vw[w], k0) * kRep + slot], tabU[byte_of(vw[w], k1) * kRep + slot]), av2);
+      f2 r = mul2(mk2(tabS[byte_of(rw[w], k0) * kRep + slot], tabS[byte_of(rw[w], k1) * kRep + slot]), ar2);
+      // Adam moments (fireflyoptim.py:175-178); the chain below follows the reference's
+      // rounding step by step because the residual loses its leading digits when dq is
+      // subtracted (fireflyoptim.py:177-184)
+      m = fma2(g, omb1, mul2(m, b1));
+      v = fma2(mul2(omb2, g), g, mul2(v, b2));
+      const f2 mh = div2(m, nbc1, ibc1);
+      const f2 vh = div2(v, nbc2, ibc2);
+      float vh0, vh1;
+      un2(vh, vh0, vh1);
+      // sqrt from rsqrt.approx with one residual correction; arguments below 1e-37 (square
+      // roots far below eps) use rsqrt(1e-37) so that sqrt(0) = 0 exactly
+      const f2 rs = mk2(rsqrt_approx(fmaxf(vh0, 1e-37f)), rsqrt_approx(fmaxf(vh1, 1e-37f)));
+      const f2 s0 = mul2(vh, rs);
+      const f2 sq = fma2(fma2(s0, mul2(s0, mone2), vh), mul2(rs, half2), s0);
+      const f2 den = add2(sq, eps2);
+      float d0, d1;
+      un2(den, d0, d1);
+      const f2 a = div2(mh, mul2(den, mone2), mk2(rcp_approx(d0), rcp_approx(d1)));
+      // DQT residual (fireflyoptim.py:180-184)
+      const int q0 = (int)(int8_t)byte_of(qw[w], k0), q1 = (int)(int8_t)byte_of(qw[w], k1);
+      const f2 qf = sub2(mk2(__int_as_float(0x4B400000 + q0), __int_as_float(0x4B400000 + q1)), magic2);
+      const f2 dwe = mul2(nlr, add2(a, mul2(mul2(wd2, qf), ws)));
+      r = add2(r, div2(dwe, nws, iws));
+      // momentum-biased stochastic rounding (fireflyoptim.py:186-198)
+      float r0, r1, a0, a1;
+      un2(r, r0, r1);
+      un2(a, a0, a1);
+      // |r| is clamped to 2^21 (far above any reachable residual) so that the floor and the
+      // integer conversion below are exact magic-number adds
+      const f2 absr = mk2(fminf(fabsf(r0), 2097152.f), fminf(fabsf(r1), 2097152.f));
+      const f2 base = sub2(add2_rm(absr, magic2), magic2);  // floor(|r|)
+      const f2 frac = sub2(absr, base);
+      float fr0, fr1, bs0, bs1;
+      un2(frac, fr0, fr1);
+      un2(base, bs0, bs1);
+      float uj[2];
+      if constexpr (HAS_U) {
+        uj[0] = u[j0];
+        uj[1] = u[j1];
       } else {
-        base = floorf(absr);
+        const uint32_t wd_ = rw4[pp];
+        uj[0] = __fmul_rn(__fadd_rn(__fsub_rn(__int_as_float(0x4B000000 | (wd_ & 0xFFFFu)), 8388608.f), 0.5f),
+                          1.0f / 65536.0f);
+        uj[1] = __fmul_rn(__fadd_rn(__fsub_rn(__int_as_float(0x4B000000 | (wd_ >> 16)), 8388608.f), 0.5f),
+                          1.0f / 65536.0f);
       }
-      const float frac = __fsub_rn(absr, base);
-      const float sgn = r > 0.f ? 1.f : (r < 0.f ? -1.f : 0.f);
-      float fb = frac;
-      if (p.sr_bias != 0.f) {
-        fb = __fadd_rn(frac, __fmul_rn(__fmul_rn(tanh_approx(a), p.sr_bias), sgn));
-        // tanh.approx is good to ~5e-4: near the decision use an accurate tanh
-        if (fabsf(__fsub_rn(u[j], fb)) < 2e-4f)
-          fb = __fadd_rn(frac, __fmul_rn(__fmul_rn(tanh_accurate(a), p.sr_bias), sgn));
+      const float rr[2] = {r0, r1}, aa[2] = {a0, a1}, fr[2] = {fr0, fr1}, bs[2] = {bs0, bs1};
+      float dqf[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float fb = fr[e];
+        if (p.sr_bias != 0.f) {
+          // bias = tanh(a) * sr_bias * sign(r), sign(0) = 0
+          const float tb = rr[e] != 0.f ? __fmul_rn(tanh_approx(aa[e]), p.sr_bias) : 0.f;
+          fb = __fadd_rn(fr[e], copysignf(tb, tb * rr[e]));
+          // tanh.approx is good to ~5e-4: near the decision use an accurate tanh
+          if (fabsf(__fsub_rn(uj[e], fb)) < 2e-4f) {
+            const float tb2 = rr[e] != 0.f ? __fmul_rn(tanh_accurate(aa[e]), p.sr_bias) : 0.f;
+            fb = __fadd_rn(fr[e], copysignf(tb2, tb2 * rr[e]));
+          }
+        }
+        const float extra = (uj[e] < fb) ? 1.f : 0.f;   // u in (0,1): same as u < clamp(fb, 0, 1)
+        dqf[e] = copysignf(__fadd_rn(bs[e], extra), rr[e]);  // sign(r) * (floor|r| + extra)
       }
-      fb = fminf(fmaxf(fb, 0.f), 1.f);
-      const float extra = (u[j] < fb) ? 1.f : 0.f;
-      const float dqf = fminf(fmaxf(__fmul_rn(sgn, __fadd_rn(base, extra)), -2097152.f), 2097152.f);
-      if (j < nvalid) {
-        qn[j] = max(-127, min(127, qv[j] + rne_int(dqf)));
-        r = __fsub_rn(r, dqf);
-      } else {
-        qn[j] = 0;
-        r = 0.f;
-        m = 0.f;
-        v = 0.f;
-      }
-      mn[j] = m;
-      vn[j] = v;
-      rn[j] = r;
+      qn[j0] = max(-127, min(127, q0 + rne_int(dqf[0])));
+      qn[j1] = max(-127, min(127, q1 + rne_int(dqf[1])));
+      rn[pp] = sub2(r, mk2(dqf[0], dqf[1]));
+      mn[pp] = m;
+      vn[pp] = v;
     }
     // ---------------- block absmax and re-encode (mu-law, fireflyoptim.py:22-67)
     float xm = 0.f, xv = 0.f, xr = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      xm = fmaxf(xm, fabsf(mn[j]));
-      xv = fmaxf(xv, vn[j]);
-      xr = fmaxf(xr, fabsf(rn[j]));
+    for (int pp = 0; pp < 4; ++pp) {
+      float a0, a1;
+      un2(mn[pp], a0, a1);
+      xm = fmaxf(xm, fmaxf(fabsf(a0), fabsf(a1)));
+      un2(vn[pp], a0, a1);
+      xv = fmaxf(xv, fmaxf(a0, a1));
+      un2(rn[pp], a0, a1);
+      xr = fmaxf(xr, fmaxf(fabsf(a0), fabsf(a1)));
     }
     xm = fmaxf(warp_max(xm), 1e-12f);
     xv = fmaxf(warp_max(xv), 1e-12f);
     xr = fmaxf(warp_max(xr), 1e-12f);
-    const float ixm = __frcp_rn(xm), ixv = __frcp_rn(xv), ixr = __frcp_rn(xr);
+    const f2 ixm = splat(__frcp_rn(xm)), ixv = splat(__frcp_rn(xv)), ixr = splat(__frcp_rn(xr));
+    const f2 c255 = splat(255.f), one2 = splat(1.f), k127 = splat(15.875f), k255 = splat(31.875f);
     int cm[8], cv[8], cr[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float nm = fminf(fabsf(__fmul_rn(mn[j], ixm)), 1.f);
-      const float nr = fminf(fabsf(__fmul_rn(rn[j], ixr)), 1.f);
-      const float nv = fminf(fmaxf(__fmul_rn(vn[j], ixv), 0.f), 1.f);
-      const float lm = __fmul_rn(lg2_approx(__fmaf_rn(255.f, nm, 1.f)), 15.875f);
-      const float lr = __fmul_rn(lg2_approx(__fmaf_rn(255.f, nr, 1.f)), 15.875f);
-      const float lv = __fmul_rn(lg2_approx(__fmaf_rn(255.f, nv, 1.f)), 31.875f);
-      cm[j] = min(255, max(1, rne_int(__fadd_rn(copysignf(lm, mn[j]), 128.f))));
-      cr[j] = min(255, max(1, rne_int(__fadd_rn(copysignf(lr, rn[j]), 128.f))));
-      cv[j] = min(255, max(0, rne_int(lv)));
+    for (int pp = 0; pp < 4; ++pp) {
+      float x0, x1, y0, y1;
+      // signed m and r: code = 128 + sign(x) * rint(127/8 * log2(1 + 255 |x|/absmax))
+      un2(mul2(mn[pp], ixm), x0, x1);
+      un2(mul2(rn[pp], ixr), y0, y1);
+      const f2 tm = fma2(c255, mk2(fminf(fabsf(x0), 1.f), fminf(fabsf(x1), 1.f)), one2);
+      const f2 tr = fma2(c255, mk2(fminf(fabsf(y0), 1.f), fminf(fabsf(y1), 1.f)), one2);
+      float tm0, tm1, tr0, tr1;
+      un2(tm, tm0, tm1);
+      un2(tr, tr0, tr1);
+      float lm0, lm1, lr0, lr1;
+      un2(mul2(mk2(lg2_approx(tm0), lg2_approx(tm1)), k127), lm0, lm1);
+      un2(mul2(mk2(lg2_approx(tr0), lg2_approx(tr1)), k127), lr0, lr1);
+      // 0 <= l <= 127 (log2 of at most 256 is 8): rounding with +128 folded into the magic add
+      const f2 sm = add2(mk2(copysignf(lm0, x0), copysignf(lm1, x1)), splat(kMagic + 128.f));
+      const f2 sr = add2(mk2(copysignf(lr0, y0), copysignf(lr1, y1)), splat(kMagic + 128.f));
+      float s0, s1;
+      un2(sm, s0, s1);
+      cm[2 * pp] = __float_as_int(s0) - 0x4B400000;
+      cm[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
+      un2(sr, s0, s1);
+      cr[2 * pp] = __float_as_int(s0) - 0x4B400000;
+      cr[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
+      // unsigned v: code = rint(255/8 * log2(1 + 255 v/absmax))
+      un2(mul2(vn[pp], ixv), x0, x1);
+      const f2 tv = fma2(c255, mk2(fminf(fmaxf(x0, 0.f), 1.f), fminf(fmaxf(x1, 0.f), 1.f)), one2);
+      un2(tv, x0, x1);
+      un2(add2(mul2(mk2(lg2_approx(x0), lg2_approx(x1)), k255), magic2), s0, s1);
+      cv[2 * pp] = __float_as_int(s0) - 0x4B400000;
+      cv[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
     }
     if (nvalid == 8) {
+      // generic-proxy stores; the bulk copies only ever read other blocks
       *reinterpret_cast<uint2*>(p.q + e0) = make_uint2(pack_codes(qn, 0), pack_codes(qn, 4));
       *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(pack_codes(cm, 0), pack_codes(cm, 4));
       *reinterpret_cast<uint2*>(p.v_q + e0) = make_uint2(pack_codes(cv, 0), pack_codes(cv, 4));
@@ -387,6 +590,7 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   p.u = u;
   p.dec_s = dec_s;
   p.dec_u = dec_u;
+  p.bulk = aligned(q, 16) && aligned(m_q, 16) && aligned(v_q, 16) && aligned(r_q, 16) && (!u || aligned(u, 16));
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_set[64] = {false};

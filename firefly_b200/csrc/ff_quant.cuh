@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float t = colmul ? __fmul_rn(v[j], __ldg(colmul + i * 8 + j)) : v[j];
-        c8[j] = quant_code_fast(t, sc, isc);
+        c8[j] = quant_code_bounded(t, sc, isc);
       }
       uint2 w = make_uint2(pack4(c8[0], c8[1], c8[2], c8[3]), pack4(c8[4], c8[5], c8[6], c8[7]));
       *reinterpret_cast<uint2*>(qr + i * 8) = w;
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code_fast(t, sc, isc);
+        code = quant_code_bounded(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code_fast(t, sc, isc);
+        code = quant_code_bounded(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -213,51 +213,61 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
     if (do_cols && c < cols && blockIdx.y == 0) s_cols[c] = scol[k];
   }
   __syncthreads();
-  const bool vec_ok = ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
-                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   const int cg = tid & 15;   // 8-column group
   const int rg = tid >> 4;   // 4-row group (0..15), plus 16 for the second half
+  const int cb = cg * 8;
+  const int64_t c = C0 + cb;
+  const bool vec_ok = (c + 8 <= cols) && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
+                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  const bool row_store = do_rows && c < ldq;
+  float cmv[8], scv[8], iscv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    cmv[j] = cmul[cb + j];
+    scv[j] = scol[cb + j];
+    iscv[j] = iscol[cb + j];
+  }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int rb = (rg + half * 16) * 4;  // first row of this 4x8 micro-tile within the tile
-    const int cb = cg * 8;
-    const int64_t c = C0 + cb;
     uint32_t colw[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) colw[j] = 0u;
+    const T* xr = x + (R0 + rb) * ldx + c;
+    int8_t* qr = q_rows + (R0 + rb) * ldq + c;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 4; ++i, xr += ldx, qr += ldq) {
       const int64_t r = R0 + rb + i;
       float v[8];
       if (r < rows) {
-        const T* xr = x + r * ldx;
-        if (vec_ok && c + 8 <= cols) {
-          load8<DT>(xr + c, v);
+        if (vec_ok) {
+          load8<DT>(xr, v);
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] = (c + j < cols) ? Elem<DT>::to_f32(xr[c + j]) : 0.f;
+          for (int j = 0; j < 8; ++j) v[j] = (c + j < cols) ? Elem<DT>::to_f32(xr[j]) : 0.f;
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = 0.f;
       }
-      if (do_rows && r < rows && c < ldq) {
+      if (row_store && r < rows) {
         int code[8];
         const float sr = srow[rb + i], isr = isrow[rb + i];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) code[j] = quant_code_fast(__fmul_rn(v[j], cmul[cb + j]), sr, isr);
-        int8_t* qr = q_rows + r * ldq + c;
+        for (int j = 0; j < 8; ++j) code[j] = quant_code_bounded(__fmul_rn(v[j], cmv[j]), sr, isr);
         if (c + 8 <= ldq) {
           *reinterpret_cast<uint2*>(qr) =
               make_uint2(pack4(code[0], code[1], code[2], code[3]), pack4(code[4], code[5], code[6], code[7]));
         } else {
-          for (int j = 0; c + j < ldq; ++j) qr[j] = (int8_t)code[j];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (c + j < ldq) qr[j] = (int8_t)code[j];
         }
       }
       if (do_cols) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int code = (r < rows) ? quant_code_fast(v[j], scol[cb + j], iscol[cb + j]) : 0;
+          const int code = quant_code_bounded(v[j], scv[j], iscv[j]);  // v = 0 past the last row
           colw[j] |= (uint32_t)(code & 0xff) << (8 * i);
         }
       }
@@ -265,8 +275,8 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
     if (do_cols) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = cb + j;
-        tileT[c][(rb / 4 + c + (c >> 5)) & 31] = colw[j];
+        const int cc = cb + j;
+        tileT[cc][(rb / 4 + cc + (cc >> 5)) & 31] = colw[j];
       }
     }
   }
@@ -277,13 +287,13 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int k = (tid >> 3) + it * 32;  // column within tile
-    const int64_t c = C0 + k;
+    const int64_t cc = C0 + k;
     const int64_t r = R0 + chunk * 16;
-    if (c < cols && r < ldqt) {
+    if (cc < cols && r < ldqt) {
       const int rot = k + (k >> 5);
       uint4 w = make_uint4(tileT[k][(chunk * 4 + 0 + rot) & 31], tileT[k][(chunk * 4 + 1 + rot) & 31],
                            tileT[k][(chunk * 4 + 2 + rot) & 31], tileT[k][(chunk * 4 + 3 + rot) & 31]);
-      *reinterpret_cast<uint4*>(q_cols_t + c * ldqt + r) = w;
+      *reinterpret_cast<uint4*>(q_cols_t + cc * ldqt + r) = w;
     }
   }
 }

@@ -165,6 +165,37 @@ def _as_float_input(x: torch.Tensor) -> torch.Tensor:
     return x.float()
 
 
+# The activation codes of the last quantised input.  Two BitLinear layers that read the
+# same tensor (the gate and up projections of a SwiGLU block) quantise it once.  The entry
+# holds a reference to the tensor, so its storage cannot be reused while cached, and is
+# keyed by storage, offset, shape, strides, dtype and the in-place version counter.
+_ACT_CACHE: dict = {}
+
+
+def _act_key(x: torch.Tensor, with_cols: bool):
+    return (x.untyped_storage().data_ptr(), x.storage_offset(), tuple(x.shape), tuple(x.stride()),
+            x.dtype, x._version, with_cols, x.device)
+
+
+def _quantize_activation(x: torch.Tensor, with_cols: bool):
+    key = _act_key(x, with_cols)
+    hit = _ACT_CACHE.get("entry")
+    if hit is not None and hit[0] == key:
+        return hit[2]
+    if with_cols:
+        codes = _capi.quant_dual(x)
+    else:
+        K = x.shape[1]
+        q, s = _capi.quant_rows(x, ldq=_capi.round_up(K, 16))
+        codes = (q, s, None, None)
+    _ACT_CACHE["entry"] = (key, x, codes)
+    return codes
+
+
+def clear_activation_cache() -> None:
+    _ACT_CACHE.clear()
+
+
 class Int8LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2d, int_weight, weight_scale, bias, handle):
@@ -183,11 +214,9 @@ class Int8LinearFn(torch.autograd.Function):
         y = torch.empty((T, O), dtype=torch.bfloat16, device=x.device)
         saved_xt = saved_sx = None
         if T > 0:
+            q_x, s_x, q_xt, s_xc = _quantize_activation(x, with_cols=need_grad)
             if need_grad:
-                q_x, s_x, q_xt, s_xc = _capi.quant_dual(x)
                 saved_xt, saved_sx = q_xt, s_xc
-            else:
-                q_x, s_x = _capi.quant_rows(x, ldq=_capi.round_up(K, 16))
             w_op = _weight_operand(handle, int_weight)
             _capi.gemm_i8(q_x, w_op, K, scale_a=s_x, scale_b=ws, bias=b,
                           out_kind=_capi.FF_OUT_BF16, out=y)
