@@ -237,7 +237,9 @@ __device__ __forceinline__ f2 div2(f2 x, f2 nd, f2 id) {
 
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xFFu; }
 
-template <bool HAS_U, bool SMALL_ROWS>
+// ROWS: 0 = row_len a multiple of 8 (a lane's 8 elements share one weight row),
+//       1 = row_len >= 8 (they span at most two rows), 2 = row_len < 8
+template <bool HAS_U, int ROWS>
 __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
   extern __shared__ __align__(128) float tab[];  // [2][256 codes][kRep], then staging, then barriers
   float* tabS = tab;
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
     }
     // weight-row scales: with row_len >= 8 the 8 elements span at most two rows
     const int64_t ra = min64(row, last_row), rb = min64(row + 1, last_row);
-    const int jsw = SMALL_ROWS ? 8 : (int)min64(8, p.row_len - in_row);  // j >= jsw: next row
+    const int jsw = ROWS != 1 ? 8 : (int)min64(8, p.row_len - in_row);  // j >= jsw: next row
     const float wsa = fmaxf(__ldg(p.wscale + ra), eps);
     const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
     const float iwsa = __frcp_rn(wsa), iwsb = __frcp_rn(wsb);
@@ -373,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
       // weight-row scale of both elements
       float ws0 = j0 < jsw ? wsa : wsb, ws1 = j1 < jsw ? wsa : wsb;
       float iws0 = j0 < jsw ? iwsa : iwsb, iws1 = j1 < jsw ? iwsa : iwsb;
-      if constexpr (SMALL_ROWS) {  // rows shorter than 8 elements: one division per element
+      if constexpr (ROWS == 2) {  // rows shorter than 8 elements: one division per element
         ws0 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j0, p.numel - 1)) / p.row_len, last_row)), eps);
         ws1 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j1, p.numel - 1)) / p.row_len, last_row)), eps);
         iws0 = __frcp_rn(ws0);
@@ -471,39 +473,35 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
     xv = fmaxf(warp_max(xv), 1e-12f);
     xr = fmaxf(warp_max(xr), 1e-12f);
     const f2 ixm = splat(__frcp_rn(xm)), ixv = splat(__frcp_rn(xv)), ixr = splat(__frcp_rn(xr));
-    const f2 c255 = splat(255.f), one2 = splat(1.f), k127 = splat(15.875f), k255 = splat(31.875f);
+    const f2 k127 = splat(15.875f), k255 = splat(31.875f);
     int cm[8], cv[8], cr[8];
+    // |x| / absmax can exceed 1 by an ulp (absmax is the largest |x|); log2(256 + tiny) * 127/8
+    // still rounds to 127 (255 for v), so no clamps are needed.  v is never negative.
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-      float x0, x1, y0, y1;
-      // signed m and r: code = 128 + sign(x) * rint(127/8 * log2(1 + 255 |x|/absmax))
+      float x0, x1, y0, y1, z0, z1;
       un2(mul2(mn[pp], ixm), x0, x1);
       un2(mul2(rn[pp], ixr), y0, y1);
-      const f2 tm = fma2(c255, mk2(fminf(fabsf(x0), 1.f), fminf(fabsf(x1), 1.f)), one2);
-      const f2 tr = fma2(c255, mk2(fminf(fabsf(y0), 1.f), fminf(fabsf(y1), 1.f)), one2);
-      float tm0, tm1, tr0, tr1;
-      un2(tm, tm0, tm1);
-      un2(tr, tr0, tr1);
-      float lm0, lm1, lr0, lr1;
-      un2(mul2(mk2(lg2_approx(tm0), lg2_approx(tm1)), k127), lm0, lm1);
-      un2(mul2(mk2(lg2_approx(tr0), lg2_approx(tr1)), k127), lr0, lr1);
-      // 0 <= l <= 127 (log2 of at most 256 is 8): rounding with +128 folded into the magic add
-      const f2 sm = add2(mk2(copysignf(lm0, x0), copysignf(lm1, x1)), splat(kMagic + 128.f));
-      const f2 sr = add2(mk2(copysignf(lr0, y0), copysignf(lr1, y1)), splat(kMagic + 128.f));
+      un2(mul2(vn[pp], ixv), z0, z1);
+      // signed m and r: code = 128 + sign(x) * rint(127/8 * log2(1 + 255 |x|/absmax))
+      float lm0, lm1, lr0, lr1, lv0, lv1;
+      un2(mul2(mk2(lg2_approx(__fmaf_rn(255.f, fabsf(x0), 1.f)), lg2_approx(__fmaf_rn(255.f, fabsf(x1), 1.f))), k127),
+          lm0, lm1);
+      un2(mul2(mk2(lg2_approx(__fmaf_rn(255.f, fabsf(y0), 1.f)), lg2_approx(__fmaf_rn(255.f, fabsf(y1), 1.f))), k127),
+          lr0, lr1);
+      // unsigned v: code = rint(255/8 * log2(1 + 255 v/absmax)), +magic folded in
+      un2(fma2(mk2(lg2_approx(__fmaf_rn(255.f, z0, 1.f)), lg2_approx(__fmaf_rn(255.f, z1, 1.f))), k255, magic2),
+          lv0, lv1);
+      // rounding with +128 folded into the magic add
       float s0, s1;
-      un2(sm, s0, s1);
+      un2(add2(mk2(copysignf(lm0, x0), copysignf(lm1, x1)), splat(kMagic + 128.f)), s0, s1);
       cm[2 * pp] = __float_as_int(s0) - 0x4B400000;
       cm[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
-      un2(sr, s0, s1);
+      un2(add2(mk2(copysignf(lr0, y0), copysignf(lr1, y1)), splat(kMagic + 128.f)), s0, s1);
       cr[2 * pp] = __float_as_int(s0) - 0x4B400000;
       cr[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
-      // unsigned v: code = rint(255/8 * log2(1 + 255 v/absmax))
-      un2(mul2(vn[pp], ixv), x0, x1);
-      const f2 tv = fma2(c255, mk2(fminf(fmaxf(x0, 0.f), 1.f), fminf(fmaxf(x1, 0.f), 1.f)), one2);
-      un2(tv, x0, x1);
-      un2(add2(mul2(mk2(lg2_approx(x0), lg2_approx(x1)), k255), magic2), s0, s1);
-      cv[2 * pp] = __float_as_int(s0) - 0x4B400000;
-      cv[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
+      cv[2 * pp] = __float_as_int(lv0) - 0x4B400000;
+      cv[2 * pp + 1] = __float_as_int(lv1) - 0x4B400000;
     }
     if (nvalid == 8) {
       // generic-proxy stores; the bulk copies only ever read other blocks
@@ -595,14 +593,12 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   cudaGetDevice(&dev);
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    FF_CUDA_TRY(cudaFuncSetAttribute(dqt_adamw8_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes), "ff_dqt_adamw8 smem attribute");
-    FF_CUDA_TRY(cudaFuncSetAttribute(dqt_adamw8_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes), "ff_dqt_adamw8 smem attribute");
-    FF_CUDA_TRY(cudaFuncSetAttribute(dqt_adamw8_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes), "ff_dqt_adamw8 smem attribute");
-    FF_CUDA_TRY(cudaFuncSetAttribute(dqt_adamw8_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes), "ff_dqt_adamw8 smem attribute");
+    const void* fns[] = {(const void*)dqt_adamw8_kernel<true, 0>, (const void*)dqt_adamw8_kernel<true, 1>,
+                         (const void*)dqt_adamw8_kernel<true, 2>, (const void*)dqt_adamw8_kernel<false, 0>,
+                         (const void*)dqt_adamw8_kernel<false, 1>, (const void*)dqt_adamw8_kernel<false, 2>};
+    for (const void* fn : fns)
+      FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                  "ff_dqt_adamw8 smem attribute");
     attr_set[dev] = true;
   }
   const int64_t nblocks = (numel + kBlock - 1) / kBlock;
@@ -614,13 +610,18 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   p.row_step = stride_elems / row_len;
   p.in_row_step = stride_elems % row_len;
   cudaStream_t st = as_stream(stream);
-  const bool small = row_len < 8;
+  // a lane's 8 elements start at a multiple of 8 of the weight when elem_base is one
+  const int rows_mode = (row_len % 8 == 0 && elem_base % 8 == 0) ? 0 : (row_len >= 8 ? 1 : 2);
+#define FF_DQT_LAUNCH(HU, RM) dqt_adamw8_kernel<HU, RM><<<grid, kThreads, kSmemBytes, st>>>(p)
   if (u) {
-    if (small) dqt_adamw8_kernel<true, true><<<grid, kThreads, kSmemBytes, st>>>(p);
-    else dqt_adamw8_kernel<true, false><<<grid, kThreads, kSmemBytes, st>>>(p);
+    if (rows_mode == 0) FF_DQT_LAUNCH(true, 0);
+    else if (rows_mode == 1) FF_DQT_LAUNCH(true, 1);
+    else FF_DQT_LAUNCH(true, 2);
   } else {
-    if (small) dqt_adamw8_kernel<false, true><<<grid, kThreads, kSmemBytes, st>>>(p);
-    else dqt_adamw8_kernel<false, false><<<grid, kThreads, kSmemBytes, st>>>(p);
+    if (rows_mode == 0) FF_DQT_LAUNCH(false, 0);
+    else if (rows_mode == 1) FF_DQT_LAUNCH(false, 1);
+    else FF_DQT_LAUNCH(false, 2);
   }
+#undef FF_DQT_LAUNCH
   return check_launch("ff_dqt_adamw8");
 }
