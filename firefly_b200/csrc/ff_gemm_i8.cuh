@@ -438,6 +438,253 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// 2-CTA variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).  Each CTA stages its own
+// 128 rows of A and its own 128 rows of B (no multicast); the leader (rank 0)
+// issues the MMAs, which read both CTAs' shared memory and write each CTA's
+// 128 x 256 accumulator into that CTA's TMEM.  Per CTA this halves the B tile
+// traffic of the 1-CTA kernel (32 KB instead of 48 KB of smem fill per k-block).
+//
+// Barriers: full[s] lives in the leader and completes when both CTAs' TMA loads
+// of stage s landed (the leader arms it with both CTAs' bytes); empty[s] and
+// tfull[a] live in both CTAs and are signalled by the leader's tcgen05.commit
+// with multicast to both; tempty[a] lives in the leader and counts the 8
+// epilogue warps of the pair.  All waits are time-bounded.
+// ---------------------------------------------------------------------------
+constexpr int C2_BM = 128;        // rows of A per CTA (256 per pair)
+constexpr int C2_BN = 256;        // columns of the pair's tile (128 rows of B per CTA)
+constexpr int C2_BN_CTA = 128;
+constexpr int C2_STAGES = 6;
+constexpr int C2_A_BYTES = C2_BM * BK;      // 16 KiB
+constexpr int C2_B_BYTES = C2_BN_CTA * BK;  // 16 KiB
+constexpr int C2_STAGE_BYTES = C2_A_BYTES + C2_B_BYTES;
+constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory, completion counted on a barrier of the
+// leader CTA of the pair (no multicast)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leader_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   bar),
+               "h"(mask)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
+                        int tiles_m, int tiles_n, EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  const uint32_t sA = sbase;                       // C2_STAGES x C2_A_BYTES
+  const uint32_t sB = sbase + C2_STAGES * C2_A_BYTES;  // C2_STAGES x C2_B_BYTES
+  uint8_t* ctrl = smem + C2_STAGES * C2_STAGE_BYTES;
+  const uint32_t cbase = sbase + C2_STAGES * C2_STAGE_BYTES;
+  auto full_bar = [&](int s) { return cbase + 8u * s; };
+  auto empty_bar = [&](int s) { return cbase + 8u * (C2_STAGES + s); };
+  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * C2_STAGES + a); };
+  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * C2_STAGES + ACC_STAGES + a); };
+  const uint32_t drain = cbase + 8u * (2 * C2_STAGES + 2 * ACC_STAGES);
+  const uint32_t done_bar = drain + 8u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * C2_STAGES + 2 * ACC_STAGES + 2));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * C2_STAGES + 2 * ACC_STAGES + 2) + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const uint32_t peer = rank ^ 1u;
+  const int num_kb = (int)((K + BK - 1) / BK);
+  const int total_tiles = tiles_m * tiles_n;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C2_STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < ACC_STAGES; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);
+    }
+    mbar_init(drain, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lbar = mapa_shared(full_bar(stage), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C2_STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * C2_A_BYTES, &tmA, kb * BK, tm * (2 * C2_BM) + (int)rank * C2_BM, lbar);
+          tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK, tn * C2_BN + (int)rank * C2_BN_CTA, lbar);
+          if (++stage == C2_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(2 * C2_BM, C2_BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
+        if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C2_BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * C2_A_BYTES, b0 = sB + stage * C2_B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), smem_desc_k_sw128(b0 + k * UMMA_K), idesc,
+                           (kb | k) != 0);
+          }
+          tc_commit_pair(empty_bar(stage));  // frees the stage in both CTAs
+          if (++stage == C2_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(tfull_bar(acc));  // accumulator ready in both CTAs
+        if (++acc == ACC_STAGES) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      tc_commit(drain);  // every MMA of this thread has finished
+      drain_bar(drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int lg = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < total_tiles; t += num_pairs) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
+      float sa = 1.f;
+      if constexpr (OUT != FF_OUT_S32) {
+        if (ep.scale_a && row < ep.M) sa = __ldg(ep.scale_a + row);
+      }
+      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(acc * C2_BN);
+      const int64_t ncol_tile = min64(C2_BN, ep.N - (int64_t)tn * C2_BN);
+#pragma unroll 1
+      for (int c = 0; c < C2_BN / 32; ++c) {
+        if ((int64_t)c * 32 >= ncol_tile) break;
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_wait_ld();
+        epilogue_chunk<OUT>(r, row, (int64_t)tn * C2_BN + c * 32, ep, sa, lane);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(tempty_bar(acc), 0));
+      if (++acc == ACC_STAGES) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) spin_ns(20000);  // let any TMA load still in flight land before the CTA exits
+  // neither CTA frees TMEM before the other is done with the pair's allocation
+  if (threadIdx.x == 32) {
+    mbar_arrive_remote(mapa_shared(done_bar, peer));
+    drain_bar(done_bar, 0);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -493,6 +740,65 @@ inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int t
   return check_launch("ff_gemm_i8");
 }
 
+template <int OUT>
+inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
+                       const EpiParams& ep, int max_pairs, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_2cta_kernel<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C2_SMEM_BYTES),
+                "ff_gemm_i8 2-CTA smem attribute");
+    attr_set[dev] = true;
+  }
+  const int pairs = min(tiles_m * tiles_n, max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = C2_SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT>, ma, mb, K, tiles_m, tiles_n, ep),
+              "ff_gemm_i8 2-CTA launch");
+  return check_launch("ff_gemm_i8 (2-CTA)");
+}
+
+// clusters of two 2-CTA GEMM CTAs that fit on the device at once (cached per device)
+inline int max_pairs_current() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!cache[dev]) {
+    cudaFuncSetAttribute(gemm_i8_2cta_kernel<FF_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         C2_SMEM_BYTES);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = C2_SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_2cta_kernel<FF_OUT_BF16>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cache[dev] = n > 0 ? n : -1;
+  }
+  return cache[dev] > 0 ? cache[dev] : 0;
+}
+
 }  // namespace gemm
 }  // namespace ff
 
@@ -515,10 +821,9 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
              "ff_gemm_i8: dimension too large");
   const int64_t tm64 = (M + BM - 1) / BM, tn64 = (N + BN - 1) / BN;
   FF_REQUIRE(tm64 * tn64 < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "ff_gemm_i8: too many tiles");
+  cudaStream_t st = as_stream(stream);
   CUtensorMap ma, mb;
   int rc = make_map(&ma, A, M, K, lda, BM);
-  if (rc) return rc;
-  rc = make_map(&mb, B, N, K, ldb, BN);
   if (rc) return rc;
   const int es = (out_kind == FF_OUT_BF16 || out_kind == FF_OUT_BF16_ACCUM) ? 2 : 4;
   EpiParams ep;
@@ -530,10 +835,24 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
   ep.M = M;
   ep.N = N;
   ep.vec = aligned(D, 16) && ((ldd * es) % 16 == 0);
+  // large problems: 256 x 256 tiles on CTA pairs (cta_group::2)
+  const int max_pairs = (M >= 256 && N >= 256) ? max_pairs_current() : 0;
+  if (max_pairs > 0) {
+    rc = make_map(&mb, B, N, K, ldb, C2_BN_CTA);
+    if (rc) return rc;
+    const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((N + C2_BN - 1) / C2_BN);
+    switch (out_kind) {
+      case FF_OUT_S32: return launch_2cta<FF_OUT_S32>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_F32: return launch_2cta<FF_OUT_F32>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      default: return launch_2cta<FF_OUT_BF16_ACCUM>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+    }
+  }
+  rc = make_map(&mb, B, N, K, ldb, BN);
+  if (rc) return rc;
   const int tiles_m = (int)tm64, tiles_n = (int)tn64;
   const int total = tiles_m * tiles_n;
   const int grid = min(total, num_sms_current());
-  cudaStream_t st = as_stream(stream);
   switch (out_kind) {
     case FF_OUT_S32: return launch<FF_OUT_S32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
     case FF_OUT_F32: return launch<FF_OUT_F32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
