@@ -265,28 +265,30 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
   }
 }
 
-template <int OUT>
+template <int OUT, int BN_, int STAGES_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
                    int tiles_m, int tiles_n, EpiParams ep) {
   extern __shared__ uint8_t smem_raw[];
+  constexpr int B_BYTES_ = BN_ * BK, STAGE_BYTES_ = A_BYTES + B_BYTES_;
+  constexpr int TMEM_COLS_ = ACC_STAGES * BN_ < 32 ? 32 : ACC_STAGES * BN_;
   // 1024-byte alignment for the 128B-swizzled tiles
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   const uint32_t sbase = raw_addr + pad;
-  const uint32_t sA = sbase;                    // STAGES x A_BYTES
-  const uint32_t sB = sbase + STAGES * A_BYTES;  // STAGES x B_BYTES
-  uint8_t* ctrl = smem + STAGES * STAGE_BYTES;
-  const uint32_t cbase = sbase + STAGES * STAGE_BYTES;
+  const uint32_t sA = sbase;                    // STAGES_ x A_BYTES
+  const uint32_t sB = sbase + STAGES_ * A_BYTES;  // STAGES_ x B_BYTES_
+  uint8_t* ctrl = smem + STAGES_ * STAGE_BYTES_;
+  const uint32_t cbase = sbase + STAGES_ * STAGE_BYTES_;
   // barrier layout (8 bytes each)
   auto full_bar = [&](int s) { return cbase + 8u * s; };
-  auto empty_bar = [&](int s) { return cbase + 8u * (STAGES + s); };
-  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * STAGES + a); };
-  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * STAGES + ACC_STAGES + a); };
-  const uint32_t drain = cbase + 8u * (2 * STAGES + 2 * ACC_STAGES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * STAGES + 2 * ACC_STAGES + 1));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 4);
+  auto empty_bar = [&](int s) { return cbase + 8u * (STAGES_ + s); };
+  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * STAGES_ + a); };
+  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * STAGES_ + ACC_STAGES + a); };
+  const uint32_t drain = cbase + 8u * (2 * STAGES_ + 2 * ACC_STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * STAGES_ + 2 * ACC_STAGES + 1));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * STAGES_ + 2 * ACC_STAGES + 1) + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int total_tiles = tiles_m * tiles_n;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < STAGES_; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -310,7 +312,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
+                 "r"(TMEM_COLS_)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -334,26 +336,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES_);
           tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, tm * BM, full_bar(stage));
-          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, tn * BN, full_bar(stage));
+          tma_load_2d(sB + stage * B_BYTES_, &tmB, kb * BK, tn * BN_, full_bar(stage));
           used |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
+          if (++stage == STAGES_) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
       // make sure no TMA write into shared memory is still in flight at exit
-      for (int s = 0; s < STAGES; ++s)
+      for (int s = 0; s < STAGES_; ++s)
         if (used & (1u << s)) drain_bar(full_bar(s), (last_phase >> s) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(BM, BN);
+      constexpr uint32_t idesc = idesc_i8(BM, BN_);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -362,21 +364,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN_);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!wait_bar(full_bar(stage), phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = sA + stage * A_BYTES, b0 = sB + stage * B_BYTES;
+          const uint32_t a0 = sA + stage * A_BYTES, b0 = sB + stage * B_BYTES_;
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             tc_mma_i8(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), smem_desc_k_sw128(b0 + k * UMMA_K), idesc,
                       (kb | k) != 0);
           }
           tc_commit(empty_bar(stage));
-          if (++stage == STAGES) {
+          if (++stage == STAGES_) {
             stage = 0;
             phase ^= 1u;
           }
@@ -408,15 +410,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (OUT != FF_OUT_S32) {
         if (ep.scale_a && row < ep.M) sa = __ldg(ep.scale_a + row);
       }
-      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(acc * BN);
-      const int64_t ncol_tile = min64(BN, ep.N - (int64_t)tn * BN);
+      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(acc * BN_);
+      const int64_t ncol_tile = min64(BN_, ep.N - (int64_t)tn * BN_);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BN_ / 32; ++c) {
         if ((int64_t)c * 32 >= ncol_tile) break;
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
         tmem_wait_ld();
-        epilogue_chunk<OUT>(r, row, (int64_t)tn * BN + c * 32, ep, sa, lane);
+        epilogue_chunk<OUT>(r, row, (int64_t)tn * BN_ + c * 32, ep, sa, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS_)
                  : "memory");
   }
 }
@@ -725,20 +727,26 @@ inline int num_sms_current() {
   return cache[dev];
 }
 
-template <int OUT>
+template <int OUT, int BN_, int STAGES_>
 inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
                   const EpiParams& ep, int grid, cudaStream_t st) {
+  constexpr int smem = STAGES_ * (A_BYTES + BN_ * BK) + 1024 + 256;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT, BN_, STAGES_>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem),
                 "ff_gemm_i8 smem attribute");
     attr_set[dev] = true;
   }
-  gemm_i8_kernel<OUT><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ma, mb, K, tiles_m, tiles_n, ep);
+  gemm_i8_kernel<OUT, BN_, STAGES_><<<grid, NUM_THREADS, smem, st>>>(ma, mb, K, tiles_m, tiles_n, ep);
   return check_launch("ff_gemm_i8");
 }
+
+// narrow tiles (128 x 64, 8 stages) for problems that 128 x 256 tiles cannot spread over the SMs
+constexpr int NARROW_BN = 64;
+constexpr int NARROW_STAGES = 8;
 
 template <int OUT>
 inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
@@ -835,9 +843,19 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
   ep.M = M;
   ep.N = N;
   ep.vec = aligned(D, 16) && ((ldd * es) % 16 == 0);
-  // large problems: 256 x 256 tiles on CTA pairs (cta_group::2)
+  // Tile configuration by a small cost model: waves x work per SM per tile / relative
+  // efficiency, for 256 x 256 tiles on CTA pairs (cta_group::2), 128 x 256 tiles and
+  // 128 x 64 tiles (the narrow tiles spread small and skinny problems over the SMs).
+  const int nsm = num_sms_current();
   const int max_pairs = (M >= 256 && N >= 256) ? max_pairs_current() : 0;
-  if (max_pairs > 0) {
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t wide_tiles = tm64 * tn64;
+  const int64_t narrow_tiles = tm64 * ((N + 63) / 64);
+  auto waves = [](int64_t tiles, int64_t slots) { return (double)((tiles + slots - 1) / slots); };
+  const double cost_pair = max_pairs > 0 ? waves(pair_tiles, max_pairs) * 4.0 : 1e300;
+  const double cost_wide = waves(wide_tiles, nsm) * 4.0 / 0.9;
+  const double cost_narrow = waves(narrow_tiles, nsm) * 1.0 / 0.6;
+  if (cost_pair <= cost_wide && cost_pair <= cost_narrow) {
     rc = make_map(&mb, B, N, K, ldb, C2_BN_CTA);
     if (rc) return rc;
     const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((N + C2_BN - 1) / C2_BN);
@@ -848,15 +866,30 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
       default: return launch_2cta<FF_OUT_BF16_ACCUM>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
     }
   }
-  rc = make_map(&mb, B, N, K, ldb, BN);
+  if (cost_wide <= cost_narrow) {  // 128 x 256 tiles, one CTA each
+    rc = make_map(&mb, B, N, K, ldb, BN);
+    if (rc) return rc;
+    const int tiles_m = (int)tm64, tiles_n = (int)tn64;
+    const int grid = min(tiles_m * tiles_n, nsm);
+    switch (out_kind) {
+      case FF_OUT_S32: return launch<FF_OUT_S32, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_F32: return launch<FF_OUT_F32, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_BF16: return launch<FF_OUT_BF16, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      default: return launch<FF_OUT_BF16_ACCUM, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    }
+  }
+  // small or skinny problems: 128 x 64 tiles (skinny M streams B at HBM speed over many SMs)
+  rc = make_map(&mb, B, N, K, ldb, NARROW_BN);
   if (rc) return rc;
-  const int tiles_m = (int)tm64, tiles_n = (int)tn64;
-  const int total = tiles_m * tiles_n;
-  const int grid = min(total, num_sms_current());
+  const int tiles_m = (int)tm64, tiles_n = (int)((N + NARROW_BN - 1) / NARROW_BN);
+  FF_REQUIRE((int64_t)tiles_m * tiles_n < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "ff_gemm_i8: too many tiles");
+  const int grid = min(tiles_m * tiles_n, nsm);
   switch (out_kind) {
-    case FF_OUT_S32: return launch<FF_OUT_S32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    case FF_OUT_F32: return launch<FF_OUT_F32>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    case FF_OUT_BF16: return launch<FF_OUT_BF16>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    default: return launch<FF_OUT_BF16_ACCUM>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    case FF_OUT_S32: return launch<FF_OUT_S32, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    case FF_OUT_F32: return launch<FF_OUT_F32, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    case FF_OUT_BF16:
+      return launch<FF_OUT_BF16, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+    default:
+      return launch<FF_OUT_BF16_ACCUM, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
   }
 }

@@ -40,6 +40,8 @@ SHAPES = [
     (1024, 1024, 1024),
     (130, 8192, 256),
     (513, 200, 4096),
+    (130, 18944, 512),    # 128 x 256 tiles, one CTA each
+    (2600, 2600, 1000),   # 256 x 256 tiles on CTA pairs, ragged M, N and K
 ]
 
 
@@ -52,7 +54,8 @@ def test_gemm_s32_bit_exact(M, N, K):
     assert _capi.device_status() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (200, 300, 1000), (256, 1024, 1024), (129, 257, 4096)])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (200, 300, 1000), (256, 1024, 1024), (129, 257, 4096),
+                                   (130, 18944, 512), (2600, 2600, 1000)])
 def test_gemm_f32_and_bf16_epilogue(M, N, K):
     a, b, sa, sb, bias = _operands(M, N, K, seed=3 * M + K)
     acc = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
@@ -70,8 +73,8 @@ def test_gemm_f32_and_bf16_epilogue(M, N, K):
     assert_close_rel(d.cpu().numpy(), O.dequant(acc, sa.numpy()), REL, "scale_a only")
 
 
-def test_gemm_bf16_accumulate():
-    M, N, K = 300, 520, 700
+@pytest.mark.parametrize("M,N,K", [(300, 520, 700), (2600, 2600, 1000)])
+def test_gemm_bf16_accumulate(M, N, K):
     a, b, sa, sb, _ = _operands(M, N, K, seed=5)
     g = torch.Generator().manual_seed(6)
     old = torch.randn(M, N, generator=g).to(torch.bfloat16)
