@@ -269,9 +269,13 @@ def dqt_adamw8_step(q, ws, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd
     v = _fma(F32(1.0 - beta2) * g, g, v * F32(beta2))
     m_hat = m / F32(1.0 - beta1 ** t)
     v_hat = v / F32(1.0 - beta2 ** t)
-    ws_c = np.maximum(np.asarray(ws, np.float32).reshape(-1, 1), F32(eps))
-    if len(shape) == 1:
-        ws_c = ws_c.reshape(-1)
+    ws = np.asarray(ws, np.float32)
+    if ws.shape == shape:  # one scale per element (a flat piece of a weight)
+        ws_c = np.maximum(ws, F32(eps))
+    else:  # one scale per row
+        ws_c = np.maximum(ws.reshape(-1, 1), F32(eps))
+        if len(shape) == 1:
+            ws_c = ws_c.reshape(-1)
     iw = q.astype(np.float32)
     adam = m_hat / (_f64fn(np.sqrt, v_hat) + F32(eps))
     dwe = F32(-lr) * (adam + (F32(wd) * iw) * ws_c)
@@ -294,6 +298,20 @@ def dqt_adamw8_step(q, ws, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd
     v_q, v_a = encode_unsigned(v, bs)
     return q, {"step": t, "m_q": m_q, "m_absmax": m_a, "v_q": v_q, "v_absmax": v_a,
                "r_q": r_q, "r_absmax": r_a}
+
+
+def dqt_adamw8_segment(q, ws_rows, row_len, elem_base, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8,
+                       wd=0.1, sr_bias=0.15, u, bs=256):
+    """``dqt_adamw8_step`` on a flat piece of one weight: elements ``[elem_base, elem_base+n)``
+    of a weight whose rows are ``row_len`` long and whose per-row scales are ``ws_rows``.
+    ``elem_base`` must be a multiple of ``bs`` (blocks are those of the whole weight)."""
+    q = np.asarray(q, np.int8).ravel()
+    n = q.size
+    rows = (elem_base + np.arange(n)) // int(row_len)
+    ws_elem = np.asarray(ws_rows, np.float32)[rows]
+    st = {k: (np.asarray(v).ravel() if k.endswith("_q") else v) for k, v in state.items()}
+    return dqt_adamw8_step(q, ws_elem, np.asarray(g, np.float32).ravel(), st, lr=lr, beta1=beta1, beta2=beta2,
+                           eps=eps, wd=wd, sr_bias=sr_bias, bs=bs, u=np.asarray(u, np.float32).ravel())
 
 
 # --------------------------------------------------------------------------
