@@ -425,6 +425,9 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
+        # keep stdout to the one JSON line (NCCL's version banner would precede it)
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     d, f, T = args.d_model, args.ffn, args.tokens
     torch.manual_seed(1234 + rank)
