@@ -90,6 +90,21 @@ def kernel_case(args):
         x = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
         cm = torch.rand(11008, device=dev) * 1e-3
         _capi.quant_dual(x, row_colmul=cm)
+    elif args.kernel_case == "mlp":
+        # two training steps of the benchmark block; profile the second (skip the first's launches)
+        from firefly_b200.distributed import ZeroFireFlyOptim
+        from firefly_b200.swiglu import SwiGLUMLP
+
+        model = SwiGLUMLP(args.d_model, args.ffn).to(dev)
+        model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
+        opt = ZeroFireFlyOptim([model.gate, model.up, model.down], lr=1e-3, weight_decay=0.01, seed=7)
+        x = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+        dy = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(2):
+            y = model(x)
+            y.backward(dy)
+            x.grad = None
+            opt.step()
     torch.cuda.synchronize()
     assert _capi.device_status() == 0
     print("ok", args.kernel_case)
@@ -388,6 +403,17 @@ def adamw_bench(dev, params: float, peak_gbs: float):
             "bytes_per_param": ADAMW_BYTES_PER_PARAM, "frac_of_measured_hbm": round(gbs / peak_gbs, 3)}
 
 
+def load_traffic():
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu capture."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -481,8 +507,9 @@ def main():
     if world > 1:
         dist.all_reduce(sec_t, op=dist.ReduceOp.MAX)
     sec = float(sec_t.item())
-    g_ms = [a.elapsed_time(b) for a, b, _ in gemm_events]
-    g_ops = [o for _, _, o in gemm_events]
+    g_ms = [a.elapsed_time(b) for a, b, _, _ in gemm_events]
+    g_ops = [o for _, _, o, _ in gemm_events]
+    alg_bytes = sum(b for _, _, _, b in gemm_events)
 
     # ---- e2e: every step's inputs copied from pinned host memory, the loss read back.
     # The copy of step i+1's inputs (side stream, two device buffers) overlaps step i.
@@ -585,7 +612,8 @@ def main():
         "roofline": {
             "kernel": "ff_gemm_i8 (tcgen05 kind::i8)", "bound": "tensor",
             "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s", "frac": achieved / int8_peak if achieved else None,
-            "traffic": None,
+            "traffic": load_traffic().get("ff_gemm_i8 swiglu_mlp_train_step", {}).get("bytes_per_launch"),
+            "traffic_algorithmic": alg_bytes / max(len(g_ms), 1) if g_ms else None,
             "note": ("int8 ops (2*M*N*K) per launch / mean CUDA-event launch time in the timed region; "
                      "peak = 2 x measured sustained cuBLAS bf16 (MEASURED_PEAKS.json), the B200 int8 rate "
                      f"being twice bf16; frac of nominal 4.5 POPS = {achieved / NOMINAL_INT8_TOPS:.3f}"

@@ -56,7 +56,7 @@ SIGNATURES = {
 _lib = None
 
 # Instrumentation for benchmarks: number of this library's kernels launched so far,
-# and an optional list that collects (start_event, end_event, ops) per GEMM launch.
+# and an optional list that collects (start_event, end_event, ops, algorithmic bytes) per GEMM launch.
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
@@ -258,7 +258,8 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | No
               ldd, int(out_kind), M, N, int(k), _stream(dev))
         if ev is not None:
             ev[1].record()
-            GEMM_EVENTS.append((ev[0], ev[1], 2 * M * N * int(k)))
+            byts = M * int(k) + N * int(k) + M * N * out.element_size() * (2 if out_kind == FF_OUT_BF16_ACCUM else 1)
+            GEMM_EVENTS.append((ev[0], ev[1], 2 * M * N * int(k), byts))
     return out
 
 
