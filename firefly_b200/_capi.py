@@ -46,6 +46,7 @@ SIGNATURES = {
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_transpose_i8": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P]),
     "ff_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
+    "ff_gemm_i8_kn": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "ff_colsum_ws_elems": (_I64, [_I64, _I64]),
     "ff_colsum_bf16": (_I, [_P, _I64, _I64, _I64, _P, _P, _P]),
     "ff_dqt_adamw8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
@@ -60,7 +61,7 @@ _lib = None
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
-                     "ff_transpose_i8": 1, "ff_gemm_i8": 1,
+                     "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
 
 
@@ -228,15 +229,27 @@ def transpose_i8(src: torch.Tensor, ldd: int | None = None) -> torch.Tensor:
 
 def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | None = None,
             scale_b: torch.Tensor | None = None, bias: torch.Tensor | None = None,
-            out_kind: int = FF_OUT_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``D = epi(A[:, :k] · B[:, :k]ᵀ)``; A ``[M, lda]``, B ``[N, ldb]`` int8 (row stride 16k)."""
+            out_kind: int = FF_OUT_BF16, out: torch.Tensor | None = None, b_kn_cols: int | None = None) -> torch.Tensor:
+    """``D = epi(A[:, :k] · B[:, :k]ᵀ)``; A ``[M, lda]``, B ``[N, ldb]`` int8 (row stride 16k).
+
+    With ``b_kn_cols = N`` the B operand is instead a K x N row-major matrix ``b[:k, :N]``
+    (``ff_gemm_i8_kn``): ``D = epi(A[:, :k] · B[:k, :N])``.
+    """
     dev = _require_cuda(a, b, scale_a, scale_b, bias, out)
     if a.dtype != torch.int8 or b.dtype != torch.int8:
         raise ValueError("gemm_i8 operands must be int8")
     if a.stride(1) != 1 or b.stride(1) != 1:
         raise ValueError("gemm_i8 operands need unit column stride")
-    M, N = a.shape[0], b.shape[0]
-    lda, ldb = a.stride(0) if M > 1 else a.shape[1], b.stride(0) if N > 1 else b.shape[1]
+    M = a.shape[0]
+    lda = a.stride(0) if M > 1 else a.shape[1]
+    if b_kn_cols is None:
+        N = b.shape[0]
+        ldb = b.stride(0) if N > 1 else b.shape[1]
+        fn = "ff_gemm_i8"
+    else:
+        N = int(b_kn_cols)
+        ldb = b.stride(0) if b.shape[0] > 1 else b.shape[1]
+        fn = "ff_gemm_i8_kn"
     odt = {FF_OUT_S32: torch.int32, FF_OUT_F32: torch.float32,
            FF_OUT_BF16: torch.bfloat16, FF_OUT_BF16_ACCUM: torch.bfloat16}[out_kind]
     if out is None:
@@ -254,7 +267,7 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | No
         if GEMM_EVENTS is not None and M > 0 and N > 0:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        _call("ff_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
+        _call(fn, _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
               ldd, int(out_kind), M, N, int(k), _stream(dev))
         if ev is not None:
             ev[1].record()

@@ -122,6 +122,13 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// Shared-memory matrix descriptor of an MN-major operand tile in 128 B swizzle: each k row
+// holds 128 bytes of N, 8-row groups 1024 B apart (SBO), 128-column N chunks `lbo` bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 // Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A and B signed int8
 // (bits 7-9 = 1, bits 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
 __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
@@ -265,7 +272,8 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
   }
 }
 
-template <int OUT, int BN_, int STAGES_>
+// BMN: B is given MN-major (a K x N row-major matrix) instead of K-major (N x K)
+template <int OUT, int BN_, int STAGES_, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
                    int tiles_m, int tiles_n, EpiParams ep) {
@@ -338,7 +346,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES_);
           tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, tm * BM, full_bar(stage));
-          tma_load_2d(sB + stage * B_BYTES_, &tmB, kb * BK, tn * BN_, full_bar(stage));
+          if constexpr (!BMN) {
+            tma_load_2d(sB + stage * B_BYTES_, &tmB, kb * BK, tn * BN_, full_bar(stage));
+          } else {  // 128 k rows x 128 N bytes per box
+#pragma unroll
+            for (int cchunk = 0; cchunk < BN_ / 128; ++cchunk)
+              tma_load_2d(sB + stage * B_BYTES_ + cchunk * (128 * BK), &tmB, tn * BN_ + cchunk * 128, kb * BK,
+                          full_bar(stage));
+          }
           used |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES_) {
@@ -355,7 +370,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(BM, BN_);
+      static_assert(!BMN || BN_ % 128 == 0, "MN-major B needs 128-column chunks");
+      constexpr uint32_t idesc = idesc_i8(BM, BN_) | (BMN ? (1u << 16) : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -374,8 +390,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a0 = sA + stage * A_BYTES, b0 = sB + stage * B_BYTES_;
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            tc_mma_i8(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), smem_desc_k_sw128(b0 + k * UMMA_K), idesc,
-                      (kb | k) != 0);
+            const uint64_t bdesc = BMN ? smem_desc_mn_sw128(b0 + k * UMMA_K * 128, 128 * BK)
+                                       : smem_desc_k_sw128(b0 + k * UMMA_K);
+            tc_mma_i8(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), bdesc, idesc, (kb | k) != 0);
           }
           tc_commit(empty_bar(stage));
           if (++stage == STAGES_) {
@@ -510,7 +527,7 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
   }
 }
 
-template <int OUT>
+template <int OUT, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
                         int tiles_m, int tiles_n, EpiParams ep) {
@@ -584,7 +601,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t lbar = mapa_shared(full_bar(stage), 0);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C2_STAGE_BYTES);
           tma_load_2d_pair(sA + stage * C2_A_BYTES, &tmA, kb * BK, tm * (2 * C2_BM) + (int)rank * C2_BM, lbar);
-          tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK, tn * C2_BN + (int)rank * C2_BN_CTA, lbar);
+          if constexpr (!BMN) {
+            tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK, tn * C2_BN + (int)rank * C2_BN_CTA, lbar);
+          } else {  // this CTA's 128 columns of B: 128 k rows x 128 N bytes
+            tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, tn * C2_BN + (int)rank * C2_BN_CTA, kb * BK, lbar);
+          }
           if (++stage == C2_STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -596,7 +617,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (rank == 0 && lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(2 * C2_BM, C2_BN);
+      constexpr uint32_t idesc = idesc_i8(2 * C2_BM, C2_BN) | (BMN ? (1u << 16) : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -615,8 +636,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a0 = sA + stage * C2_A_BYTES, b0 = sB + stage * C2_B_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), smem_desc_k_sw128(b0 + k * UMMA_K), idesc,
-                           (kb | k) != 0);
+            const uint64_t bdesc = BMN ? smem_desc_mn_sw128(b0 + k * UMMA_K * 128, 128 * BK)
+                                       : smem_desc_k_sw128(b0 + k * UMMA_K);
+            tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), bdesc, idesc, (kb | k) != 0);
           }
           tc_commit_pair(empty_bar(stage));  // frees the stage in both CTAs
           if (++stage == C2_STAGES) {
@@ -727,7 +749,7 @@ inline int num_sms_current() {
   return cache[dev];
 }
 
-template <int OUT, int BN_, int STAGES_>
+template <int OUT, int BN_, int STAGES_, bool BMN>
 inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
                   const EpiParams& ep, int grid, cudaStream_t st) {
   constexpr int smem = STAGES_ * (A_BYTES + BN_ * BK) + 1024 + 256;
@@ -735,12 +757,12 @@ inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int t
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT, BN_, STAGES_>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem),
+    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT, BN_, STAGES_, BMN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                 "ff_gemm_i8 smem attribute");
     attr_set[dev] = true;
   }
-  gemm_i8_kernel<OUT, BN_, STAGES_><<<grid, NUM_THREADS, smem, st>>>(ma, mb, K, tiles_m, tiles_n, ep);
+  gemm_i8_kernel<OUT, BN_, STAGES_, BMN><<<grid, NUM_THREADS, smem, st>>>(ma, mb, K, tiles_m, tiles_n, ep);
   return check_launch("ff_gemm_i8");
 }
 
@@ -748,14 +770,14 @@ inline int launch(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int t
 constexpr int NARROW_BN = 64;
 constexpr int NARROW_STAGES = 8;
 
-template <int OUT>
+template <int OUT, bool BMN>
 inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
                        const EpiParams& ep, int max_pairs, cudaStream_t st) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_2cta_kernel<OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_2cta_kernel<OUT, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C2_SMEM_BYTES),
                 "ff_gemm_i8 2-CTA smem attribute");
     attr_set[dev] = true;
@@ -773,7 +795,7 @@ inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT>, ma, mb, K, tiles_m, tiles_n, ep),
+  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, K, tiles_m, tiles_n, ep),
               "ff_gemm_i8 2-CTA launch");
   return check_launch("ff_gemm_i8 (2-CTA)");
 }
@@ -784,7 +806,7 @@ inline int max_pairs_current() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (!cache[dev]) {
-    cudaFuncSetAttribute(gemm_i8_2cta_kernel<FF_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_i8_2cta_kernel<FF_OUT_BF16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          C2_SMEM_BYTES);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
@@ -798,7 +820,7 @@ inline int max_pairs_current() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_2cta_kernel<FF_OUT_BF16>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_2cta_kernel<FF_OUT_BF16, false>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -807,28 +829,25 @@ inline int max_pairs_current() {
   return cache[dev] > 0 ? cache[dev] : 0;
 }
 
-}  // namespace gemm
-}  // namespace ff
-
-extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
-                          const float* scale_b, const float* bias, void* D, int64_t ldd, int out_kind, int64_t M,
-                          int64_t N, int64_t K, void* stream) {
-  using namespace ff;
-  using namespace ff::gemm;
-  FF_REQUIRE(M >= 0 && N >= 0 && K >= 1, FF_ERR_INVALID_ARG, "ff_gemm_i8: M=%lld N=%lld K=%lld", (long long)M,
+// One GEMM, any layout of B: BMN == false -> B is N x K (ldb), BMN == true -> B is K x N (ldb).
+template <bool BMN>
+inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                         const float* scale_a, const float* scale_b, const float* bias, void* D, int64_t ldd,
+                         int out_kind, int64_t M, int64_t N, int64_t K, void* stream) {
+  FF_REQUIRE(M >= 0 && N >= 0 && K >= 1, FF_ERR_INVALID_ARG, "%s: M=%lld N=%lld K=%lld", name, (long long)M,
              (long long)N, (long long)K);
-  FF_REQUIRE(out_kind >= FF_OUT_S32 && out_kind <= FF_OUT_BF16_ACCUM, FF_ERR_INVALID_ARG,
-             "ff_gemm_i8: bad out_kind %d", out_kind);
+  FF_REQUIRE(out_kind >= FF_OUT_S32 && out_kind <= FF_OUT_BF16_ACCUM, FF_ERR_INVALID_ARG, "%s: bad out_kind %d", name,
+             out_kind);
   if (M == 0 || N == 0) return FF_OK;
-  FF_REQUIRE(A && B && D, FF_ERR_INVALID_ARG, "ff_gemm_i8: null pointer");
-  FF_REQUIRE(lda >= K && ldb >= K && ldd >= N, FF_ERR_INVALID_ARG, "ff_gemm_i8: bad leading dims");
+  FF_REQUIRE(A && B && D, FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE(lda >= K && ldb >= (BMN ? N : K) && ldd >= N, FF_ERR_INVALID_ARG, "%s: bad leading dims", name);
   FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
-             "ff_gemm_i8: A/B need 16-byte alignment and lda/ldb multiples of 16 (lda=%lld ldb=%lld)",
+             "%s: A/B need 16-byte alignment and lda/ldb multiples of 16 (lda=%lld ldb=%lld)", name,
              (long long)lda, (long long)ldb);
   FF_REQUIRE(M <= (int64_t)1 << 31 && N <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
-             "ff_gemm_i8: dimension too large");
+             "%s: dimension too large", name);
   const int64_t tm64 = (M + BM - 1) / BM, tn64 = (N + BN - 1) / BN;
-  FF_REQUIRE(tm64 * tn64 < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "ff_gemm_i8: too many tiles");
+  FF_REQUIRE(tm64 * tn64 < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "%s: too many tiles", name);
   cudaStream_t st = as_stream(stream);
   CUtensorMap ma, mb;
   int rc = make_map(&ma, A, M, K, lda, BM);
@@ -845,7 +864,8 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
   ep.vec = aligned(D, 16) && ((ldd * es) % 16 == 0);
   // Tile configuration by a small cost model: waves x work per SM per tile / relative
   // efficiency, for 256 x 256 tiles on CTA pairs (cta_group::2), 128 x 256 tiles and
-  // 128 x 64 tiles (the narrow tiles spread small and skinny problems over the SMs).
+  // 128 x 64 tiles (the narrow tiles spread small and skinny problems over the SMs; not
+  // offered for an MN-major B, which is staged in 128-column chunks).
   const int nsm = num_sms_current();
   const int max_pairs = (M >= 256 && N >= 256) ? max_pairs_current() : 0;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
@@ -854,42 +874,69 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
   auto waves = [](int64_t tiles, int64_t slots) { return (double)((tiles + slots - 1) / slots); };
   const double cost_pair = max_pairs > 0 ? waves(pair_tiles, max_pairs) * 4.0 : 1e300;
   const double cost_wide = waves(wide_tiles, nsm) * 4.0 / 0.9;
-  const double cost_narrow = waves(narrow_tiles, nsm) * 1.0 / 0.6;
+  const double cost_narrow = BMN ? 1e300 : waves(narrow_tiles, nsm) * 1.0 / 0.6;
+  // B maps: K-major boxes are (128 K bytes) x (rows of N); MN-major boxes are (128 N bytes) x (128 K rows)
+  auto map_b = [&](int n_rows_per_box) {
+    return BMN ? make_map(&mb, B, K, N, ldb, BK) : make_map(&mb, B, N, K, ldb, n_rows_per_box);
+  };
   if (cost_pair <= cost_wide && cost_pair <= cost_narrow) {
-    rc = make_map(&mb, B, N, K, ldb, C2_BN_CTA);
+    rc = map_b(C2_BN_CTA);
     if (rc) return rc;
     const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((N + C2_BN - 1) / C2_BN);
     switch (out_kind) {
-      case FF_OUT_S32: return launch_2cta<FF_OUT_S32>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_F32: return launch_2cta<FF_OUT_F32>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      default: return launch_2cta<FF_OUT_BF16_ACCUM>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
     }
   }
   if (cost_wide <= cost_narrow) {  // 128 x 256 tiles, one CTA each
-    rc = make_map(&mb, B, N, K, ldb, BN);
+    rc = map_b(BN);
     if (rc) return rc;
     const int tiles_m = (int)tm64, tiles_n = (int)tn64;
     const int grid = min(tiles_m * tiles_n, nsm);
     switch (out_kind) {
-      case FF_OUT_S32: return launch<FF_OUT_S32, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-      case FF_OUT_F32: return launch<FF_OUT_F32, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-      case FF_OUT_BF16: return launch<FF_OUT_BF16, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-      default: return launch<FF_OUT_BF16_ACCUM, BN, STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_S32: return launch<FF_OUT_S32, BN, STAGES, BMN>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_F32: return launch<FF_OUT_F32, BN, STAGES, BMN>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_BF16: return launch<FF_OUT_BF16, BN, STAGES, BMN>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      default: return launch<FF_OUT_BF16_ACCUM, BN, STAGES, BMN>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
     }
   }
-  // small or skinny problems: 128 x 64 tiles (skinny M streams B at HBM speed over many SMs)
-  rc = make_map(&mb, B, N, K, ldb, NARROW_BN);
-  if (rc) return rc;
-  const int tiles_m = (int)tm64, tiles_n = (int)((N + NARROW_BN - 1) / NARROW_BN);
-  FF_REQUIRE((int64_t)tiles_m * tiles_n < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "ff_gemm_i8: too many tiles");
-  const int grid = min(tiles_m * tiles_n, nsm);
-  switch (out_kind) {
-    case FF_OUT_S32: return launch<FF_OUT_S32, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    case FF_OUT_F32: return launch<FF_OUT_F32, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    case FF_OUT_BF16:
-      return launch<FF_OUT_BF16, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
-    default:
-      return launch<FF_OUT_BF16_ACCUM, NARROW_BN, NARROW_STAGES>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+  if constexpr (!BMN) {
+    // small or skinny problems: 128 x 64 tiles (skinny M streams B at HBM speed over many SMs)
+    rc = map_b(NARROW_BN);
+    if (rc) return rc;
+    const int tiles_m = (int)tm64, tiles_n = (int)((N + NARROW_BN - 1) / NARROW_BN);
+    FF_REQUIRE((int64_t)tiles_m * tiles_n < ((int64_t)1 << 31), FF_ERR_UNSUPPORTED, "%s: too many tiles", name);
+    const int grid = min(tiles_m * tiles_n, nsm);
+    switch (out_kind) {
+      case FF_OUT_S32:
+        return launch<FF_OUT_S32, NARROW_BN, NARROW_STAGES, false>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_F32:
+        return launch<FF_OUT_F32, NARROW_BN, NARROW_STAGES, false>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      case FF_OUT_BF16:
+        return launch<FF_OUT_BF16, NARROW_BN, NARROW_STAGES, false>(ma, mb, K, tiles_m, tiles_n, ep, grid, st);
+      default:
+        return launch<FF_OUT_BF16_ACCUM, NARROW_BN, NARROW_STAGES, false>(ma, mb, K, tiles_m, tiles_n, ep, grid,
+                                                                          st);
+    }
   }
+  return set_error(FF_ERR_UNSUPPORTED, "%s: no tile configuration", name);
+}
+
+}  // namespace gemm
+}  // namespace ff
+
+extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                          const float* scale_b, const float* bias, void* D, int64_t ldd, int out_kind, int64_t M,
+                          int64_t N, int64_t K, void* stream) {
+  return ff::gemm::gemm_dispatch<false>("ff_gemm_i8", A, lda, B, ldb, scale_a, scale_b, bias, D, ldd, out_kind, M, N,
+                                        K, stream);
+}
+
+extern "C" int ff_gemm_i8_kn(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                             const float* scale_b, const float* bias, void* D, int64_t ldd, int out_kind, int64_t M,
+                             int64_t N, int64_t K, void* stream) {
+  return ff::gemm::gemm_dispatch<true>("ff_gemm_i8_kn", A, lda, B, ldb, scale_a, scale_b, bias, D, ldd, out_kind, M,
+                                       N, K, stream);
 }

@@ -91,7 +91,7 @@ def set_grad_slot(handle: int, slot: torch.Tensor | None) -> None:
 # ---------------------------------------------------------------------------
 # Weight-layout cache (the role of _BNB_WCACHE, fireflykernels.py:64-90)
 # ---------------------------------------------------------------------------
-# handle -> {"key": (version, ptr, torch_version), "wk": K-padded codes, "wt": Wᵀ codes}
+# handle -> {"key_k": (version, ptr, torch_version, shape), "wk": codes padded to a 16-multiple row}
 _W_CACHE: dict[int, dict] = {}
 _W_VERSION: dict[int, int] = {}
 
@@ -106,7 +106,9 @@ def _weight_key(handle: int, w: torch.Tensor):
 
 
 def _weight_operand(handle: int, w: torch.Tensor) -> torch.Tensor:
-    """W as a GEMM B operand ``[O, ldk]`` with ``ldk % 16 == 0`` (W itself when it already is)."""
+    """W as a GEMM operand ``[O, ldk]`` with ``ldk % 16 == 0`` (W itself when it already is).
+
+    The forward reads it as the N x K operand, the dX GEMM as the K x N operand."""
     O, K = w.shape
     if K % 16 == 0 and w.is_contiguous():
         return w
@@ -118,16 +120,6 @@ def _weight_operand(handle: int, w: torch.Tensor) -> torch.Tensor:
         wk[:, :K].copy_(w)
         ent["wk"], ent["key_k"] = wk, key
     return ent["wk"]
-
-
-def _weight_transposed(handle: int, w: torch.Tensor) -> torch.Tensor:
-    """Wᵀ codes ``[K, round_up(O,16)]`` (the K-major B operand of the dX GEMM)."""
-    ent = _W_CACHE.setdefault(handle, {})
-    key = _weight_key(handle, w)
-    if ent.get("key_t") != key:
-        ent["wt"] = _capi.transpose_i8(w)
-        ent["key_t"] = key
-    return ent["wt"]
 
 
 # ---------------------------------------------------------------------------
@@ -247,8 +239,9 @@ class Int8LinearFn(torch.autograd.Function):
             return grad_in, None, None, db, None
         q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=ws, rows=need_dx, cols=True)
         if need_dx:
-            wt = _weight_transposed(ctx.handle, int_weight)
-            grad_in = _capi.gemm_i8(q_g, wt, O, scale_a=s_g, out_kind=_capi.FF_OUT_BF16)
+            # dX = dY·W contracts over O: W [O, K] is read directly as the K x N operand
+            w_op = _weight_operand(ctx.handle, int_weight)
+            grad_in = _capi.gemm_i8(q_g, w_op, O, scale_a=s_g, out_kind=_capi.FF_OUT_BF16, b_kn_cols=K)
         # dW = dYᵀ X, accumulated in the epilogue (fireflykernels.py:193-198)
         _weight_grad_gemm(ctx.handle, q_dyt, s_dy, q_xt, s_xc, O, K, T, dy.device)
         grad_bias = _capi.colsum_bf16(dy) if ctx.has_bias else None

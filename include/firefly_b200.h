@@ -149,6 +149,17 @@ FF_API int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb
                void* stream);
 
 /*
+ * ff_gemm_i8 with B given as a K x N row-major matrix (N contiguous, leading dim ldb >= N,
+ * ldb a multiple of 16): acc[m,n] = sum_k A[m,k] * B[k,n].  B is staged MN-major, so the
+ * dX GEMM reads the int8 weight W[O, K_in] directly as its K x N operand (no transposed
+ * copy).  Replaces torch.matmul(go_bf16, w_bf16) at fireflykernels.py:191.
+ */
+FF_API int ff_gemm_i8_kn(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                         const float* scale_a, const float* scale_b, const float* bias,
+                         void* D, int64_t ldd, int out_kind, int64_t M, int64_t N, int64_t K,
+                         void* stream);
+
+/*
  * Column sums of a bf16 matrix in fp32, rounded to bf16: db[c] = bf16(sum_r x[r,c]).
  * Deterministic (fixed reduction order).  ws: fp32 workspace of
  * ff_colsum_ws_elems(rows, cols) elements.  Replaces go_bf16.sum(dim=0)

@@ -121,14 +121,20 @@ def test_state_dict_reregisters_handle():
 
 
 def test_weight_cache_invalidated_by_optimizer():
-    layer = _layer(64, 48, False, seed=6)
-    x = torch.randn(32, 64, device=DEV, requires_grad=True)
+    """K = 70 is not a multiple of 16: the GEMMs read a padded copy of W, which must follow
+    every optimizer update (the role of _invalidate_weight_cache, fireflyoptim.py:198)."""
+    layer = _layer(70, 48, False, seed=6)
+    x = torch.randn(32, 70, device=DEV, requires_grad=True)
     opt = ff.FireFlyOptim([torch.nn.Parameter(torch.zeros(1, device=DEV))], lr=5e-2, bit_modules=[layer])
+    q, s = layer.int_weight.cpu().numpy(), layer.weight_scale.cpu().numpy()
     for _ in range(3):
         y = layer(x)
-        y.backward(torch.ones_like(y))
+        dy = torch.randn_like(y)
+        y.backward(dy)
+        out = O.linear_backward(x.detach().cpu().numpy(), bf16_bits(dy), q, s)
+        np.testing.assert_array_equal(bf16_bits(x.grad.to(torch.bfloat16)), out["dx"])
         x.grad = None
         opt.step()
-        # the transposed weight used by the next dX GEMM must be the updated weight
-        wt = fk._weight_transposed(layer._registered_handle, layer.int_weight)
-        np.testing.assert_array_equal(wt.cpu().numpy()[:, :48], layer.int_weight.cpu().numpy().T)
+        q = layer.int_weight.cpu().numpy()
+        wk = fk._weight_operand(layer._registered_handle, layer.int_weight)
+        np.testing.assert_array_equal(wk.cpu().numpy()[:, :70], q)

@@ -127,3 +127,23 @@ def test_gemm_large_square_checksum():
     sub = d[idx.to(DEV)][:, jdx.to(DEV)].to(torch.int64).cpu()
     assert torch.equal(sub, ai @ bj.T)
     assert _capi.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (200, 300, 1000), (8192, 4096, 1100), (2600, 2600, 1000),
+                                   (130, 18944, 512), (64, 96, 70)])
+def test_gemm_kn_layout_bit_exact(M, N, K):
+    """B given K x N row-major (the dX GEMM reads W [O, K_in] this way): MN-major staging."""
+    g = torch.Generator().manual_seed(M + 3 * N + K)
+    ldb = (N + 15) // 16 * 16
+    a = torch.zeros(M, (K + 15) // 16 * 16, dtype=torch.int8)
+    a[:, :K] = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    b = torch.zeros(K, ldb, dtype=torch.int8)
+    b[:, :N] = torch.randint(-127, 128, (K, N), generator=g, dtype=torch.int8)
+    b[:, N:] = 99  # padding columns must not leak
+    sa = torch.empty(M).uniform_(1e-3, 1e-2, generator=g)
+    d = _capi.gemm_i8(a.to(DEV), b.to(DEV), K, out_kind=_capi.FF_OUT_S32, b_kn_cols=N)
+    acc = O.gemm_i8(a[:, :K].numpy(), np.ascontiguousarray(b[:, :N].numpy().T))
+    np.testing.assert_array_equal(d.cpu().numpy().astype(np.int64), acc)
+    d16 = _capi.gemm_i8(a.to(DEV), b.to(DEV), K, sa.to(DEV), out_kind=_capi.FF_OUT_BF16, b_kn_cols=N)
+    np.testing.assert_array_equal(bf16_bits(d16), O.f32_to_bf16_bits(O.dequant(acc, sa.numpy())))
+    assert _capi.device_status() == 0
