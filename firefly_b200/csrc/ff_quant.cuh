@@ -9,6 +9,67 @@
 
 namespace ff {
 
+// 8 consecutive input elements held in their storage format (16 B for 2-byte types,
+// 32 B for fp32): loads are issued first, conversion happens when values are used.
+template <int DT>
+struct Raw8;
+template <>
+struct Raw8<FF_DTYPE_BF16> {
+  uint4 w;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { w = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ void from_local(const __nv_bfloat16* p) { w = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void zero() { w = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ float get(int j) const {
+    const uint32_t x = j < 2 ? w.x : (j < 4 ? w.y : (j < 6 ? w.z : w.w));
+    return __uint_as_float((j & 1) ? (x & 0xFFFF0000u) : (x << 16));
+  }
+};
+template <>
+struct Raw8<FF_DTYPE_F16> {
+  uint4 w;
+  __device__ __forceinline__ void load(const __half* p) { w = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ void from_local(const __half* p) { w = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void zero() { w = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ float get(int j) const {
+    const uint32_t x = j < 2 ? w.x : (j < 4 ? w.y : (j < 6 ? w.z : w.w));
+    return __half2float(__ushort_as_half((unsigned short)((j & 1) ? (x >> 16) : (x & 0xFFFFu))));
+  }
+};
+template <>
+struct Raw8<FF_DTYPE_F32> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void from_local(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ float get(int j) const {
+    const float4& h = j < 4 ? a : b;
+    const int k = j & 3;
+    return k == 0 ? h.x : (k == 1 ? h.y : (k == 2 ? h.z : h.w));
+  }
+};
+
+// 8 elements starting at column c of row xr (vector load when allowed, else guarded scalars)
+template <int DT>
+__device__ __forceinline__ void load_raw8(Raw8<DT>& r, const typename Elem<DT>::T* xr, int64_t c, int64_t cols,
+                                          bool vec) {
+  if (vec) {
+    r.load(xr + c);
+  } else {
+    // slow path: build the storage-format vector from guarded scalar loads (a local
+    // array, read back with generic loads: the non-coherent global path does not apply)
+    alignas(16) typename Elem<DT>::T tmp[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tmp[j] = (c + j < cols) ? xr[c + j] : typename Elem<DT>::T(0.f);
+    r.from_local(tmp);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // K1: one warp per row.  Pass 1 reads the row for |x*colmul| max, pass 2
 // re-reads it (from L1/L2) and writes codes.  VEC path needs 16 B aligned rows.
@@ -100,6 +161,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 constexpr int kDualARows = 128;
 constexpr int kDualAThreads = 256;
 constexpr int kDualACols = 1024;
+constexpr int kDualAU = 8;  // rows of 16 B in flight per thread
 
 template <int DT>
 __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
@@ -107,15 +169,14 @@ __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
     const float* __restrict__ colmul, bool want_rows, bool want_cols,
     uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax) {
   using T = typename Elem<DT>::T;
-  __shared__ float red[kDualARows][9];            // per row: 8 warps' partial maxima
-  __shared__ float cred[kDualACols];               // odd-row half's column maxima
+  __shared__ float red[kDualARows][5];   // per row: 4 warps' partial maxima
+  __shared__ float cred[kDualACols];     // odd-row half's column maxima
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = tid >> 7, ct = tid & 127;
   const int64_t c0 = (int64_t)blockIdx.x * kDualACols + ct * 8;
   const int64_t r0 = (int64_t)blockIdx.y * kDualARows;
-  const bool full = (c0 + 8 <= cols);
-  const bool vec_ok = full && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
-                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  const bool vec = (c0 + 8 <= cols) && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   float cm[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) cm[j] = (colmul && c0 + j < cols) ? __ldg(colmul + c0 + j) : 1.f;
@@ -123,32 +184,24 @@ __global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
 #pragma unroll
   for (int j = 0; j < 8; ++j) cmax[j] = 0.f;
   const int nr = (int)min64(kDualARows, rows - r0);
-  constexpr int U = 4;
-  for (int i0 = half; i0 < kDualARows; i0 += 2 * U) {
-    float v[U][8];
+  const T* xbase = x + r0 * ldx;
+#pragma unroll 1
+  for (int i0 = half; i0 < kDualARows; i0 += 2 * kDualAU) {
+    Raw8<DT> v[kDualAU];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < kDualAU; ++u) {
       const int i = i0 + 2 * u;
-      if (i < nr) {
-        const T* xr = x + (r0 + i) * ldx;
-        if (vec_ok) {
-          load8<DT>(xr + c0, v[u]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[u][j] = (c0 + j < cols) ? Elem<DT>::to_f32(xr[c0 + j]) : 0.f;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
-      }
+      if (i < nr) load_raw8<DT>(v[u], xbase + (int64_t)i * ldx, c0, cols, vec);
+      else v[u].zero();
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < kDualAU; ++u) {
       float rm = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        cmax[j] = fmaxf(cmax[j], fabsf(v[u][j]));
-        rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(v[u][j], cm[j]) : v[u][j]));
+        const float e = v[u].get(j);
+        cmax[j] = fmaxf(cmax[j], fabsf(e));
+        rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(e, cm[j]) : e));
       }
       if (want_rows) {
 #pragma unroll
@@ -227,29 +280,31 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
     scv[j] = scol[cb + j];
     iscv[j] = iscol[cb + j];
   }
+  // issue all eight row loads of this thread (two 4 x 8 micro-tiles) before any math
+  Raw8<DT> raw[2][4];
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int rb = (rg + half * 16) * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t r = R0 + rb + i;
+      if (r < rows) load_raw8<DT>(raw[half][i], x + r * ldx, c, cols, vec_ok);
+      else raw[half][i].zero();
+    }
+  }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int rb = (rg + half * 16) * 4;  // first row of this 4x8 micro-tile within the tile
     uint32_t colw[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) colw[j] = 0u;
-    const T* xr = x + (R0 + rb) * ldx + c;
     int8_t* qr = q_rows + (R0 + rb) * ldq + c;
 #pragma unroll
-    for (int i = 0; i < 4; ++i, xr += ldx, qr += ldq) {
+    for (int i = 0; i < 4; ++i, qr += ldq) {
       const int64_t r = R0 + rb + i;
       float v[8];
-      if (r < rows) {
-        if (vec_ok) {
-          load8<DT>(xr, v);
-        } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] = (c + j < cols) ? Elem<DT>::to_f32(xr[j]) : 0.f;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.f;
-      }
+      for (int j = 0; j < 8; ++j) v[j] = raw[half][i].get(j);
       if (row_store && r < rows) {
         int code[8];
         const float sr = srow[rb + i], isr = isrow[rb + i];
