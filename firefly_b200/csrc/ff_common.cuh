@@ -150,6 +150,30 @@ __device__ __forceinline__ int quant_code_fast(float v, float s, float inv_s) {
   return min(127, max(-127, code));
 }
 
+// quant_code(v, s) from inv_s = RN(1/s) without a divide: q0 = RN(v * inv_s), the residual
+// v - q0*s is exact in one FMA, and RN(q0 + residual * inv_s) is the correctly rounded
+// quotient RN(v / s) (Markstein's division theorem for a correctly rounded reciprocal).
+// |v| <= 127 * s is assumed (s computed from the absmax of the values being quantised),
+// so |v / s| <= 127 and no clamp is needed; rounding is the 1.5*2^23 magic add.
+__device__ __forceinline__ int quant_code_nr(float v, float s, float inv_s) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float q0 = __fmul_rn(v, inv_s);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, v), inv_s, q0);
+  return __float_as_int(__fadd_rn(q, kMagic)) - 0x4B400000;
+}
+
+// The code of quant_code_bounded without its exact fallback: returns rint(v * inv_s) and
+// sets `tie` when the result may differ from rint(v / s) (y within a few ulps of a
+// half-integer); the caller then recomputes with quant_code.
+__device__ __forceinline__ int quant_code_flagged(float v, float inv_s, bool& tie) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float y = __fmul_rn(v, inv_s);
+  const float t = __fadd_rn(y, kMagic);
+  const float dist = fabsf(fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) - 0.5f);
+  tie |= (dist <= 4.8e-7f * fabsf(y));
+  return __float_as_int(t) - 0x4B400000;
+}
+
 // quant_code_fast when |v| <= 127 * s is known (s computed from the absmax of the very
 // values being quantised): |v / s| <= 127, so no clamp is needed before or after rounding.
 __device__ __forceinline__ int quant_code_bounded(float v, float s, float inv_s) {

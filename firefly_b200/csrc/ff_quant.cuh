@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float t = colmul ? __fmul_rn(v[j], __ldg(colmul + i * 8 + j)) : v[j];
-        c8[j] = quant_code_bounded(t, sc, isc);
+        c8[j] = quant_code_nr(t, sc, isc);
       }
       uint2 w = make_uint2(pack4(c8[0], c8[1], c8[2], c8[3]), pack4(c8[4], c8[5], c8[6], c8[7]));
       *reinterpret_cast<uint2*>(qr + i * 8) = w;
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code_bounded(t, sc, isc);
+        code = quant_code_nr(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
       if (c < cols) {
         float t = Elem<DT>::to_f32(xr[c]);
         if (colmul) t = __fmul_rn(t, __ldg(colmul + c));
-        code = quant_code_bounded(t, sc, isc);
+        code = quant_code_nr(t, sc, isc);
       }
       qr[c] = (int8_t)code;
     }
@@ -302,29 +302,26 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i, qr += ldq) {
       const int64_t r = R0 + rb + i;
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = raw[half][i].get(j);
-      if (row_store && r < rows) {
+      if (do_rows) {
         int code[8];
         const float sr = srow[rb + i], isr = isrow[rb + i];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) code[j] = quant_code_bounded(__fmul_rn(v[j], cmv[j]), sr, isr);
-        if (c + 8 <= ldq) {
-          *reinterpret_cast<uint2*>(qr) =
-              make_uint2(pack4(code[0], code[1], code[2], code[3]), pack4(code[4], code[5], code[6], code[7]));
-        } else {
+        for (int j = 0; j < 8; ++j) code[j] = quant_code_nr(__fmul_rn(raw[half][i].get(j), cmv[j]), sr, isr);
+        if (row_store && r < rows) {
+          if (c + 8 <= ldq) {
+            *reinterpret_cast<uint2*>(qr) =
+                make_uint2(pack4(code[0], code[1], code[2], code[3]), pack4(code[4], code[5], code[6], code[7]));
+          } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (c + j < ldq) qr[j] = (int8_t)code[j];
+            for (int j = 0; j < 8; ++j)
+              if (c + j < ldq) qr[j] = (int8_t)code[j];
+          }
         }
       }
       if (do_cols) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int code = quant_code_bounded(v[j], scv[j], iscv[j]);  // v = 0 past the last row
-          colw[j] |= (uint32_t)(code & 0xff) << (8 * i);
-        }
+        for (int j = 0; j < 8; ++j)  // rows past the end hold zeros: code 0
+          colw[j] |= (uint32_t)(quant_code_nr(raw[half][i].get(j), scv[j], iscv[j]) & 0xff) << (8 * i);
       }
     }
     if (do_cols) {
