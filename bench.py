@@ -5,7 +5,8 @@
 
 One step = one training step of a BitLinear SwiGLU MLP block at Llama-7B shapes
 (d_model 4096, ffn 11008, 8192 tokens per GPU, bf16 activations, weights
-N(0, 0.02) quantised per row): forward, backward with an upstream gradient
+N(0, 0.02) quantised per row; gate and up are the two halves of one 4096 -> 22016
+BitLinear, down is 11008 -> 4096): forward, backward with an upstream gradient
 ~N(0,1), and the 8-bit DQT AdamW step (lr 1e-3, betas 0.9/0.999, eps 1e-8,
 wd 0.01, block 256).  With N GPUs (torchrun, one rank per GPU, NCCL) every
 rank runs its own 8192 tokens, gradients are reduce-scattered, the optimizer
@@ -56,7 +57,8 @@ def parse_args():
     ap.add_argument("--adamw-params", type=float, default=6.7e9)
     ap.add_argument("--no-sub", action="store_true", help="skip the GEMM sweep and the AdamW sub-benchmarks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "mlp"],
+    ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
+                                              "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -90,6 +92,13 @@ def kernel_case(args):
         x = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
         cm = torch.rand(11008, device=dev) * 1e-3
         _capi.quant_dual(x, row_colmul=cm)
+    elif args.kernel_case in ("swiglu", "swiglu_bwd"):
+        gu = (torch.randn(8192, 2 * 11008, device=dev, generator=g) * 2).to(torch.bfloat16)
+        if args.kernel_case == "swiglu":
+            _capi.swiglu_quant(gu)
+        else:
+            dh = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
+            _capi.swiglu_bwd_quant(dh, gu, colmul=torch.rand(2 * 11008, device=dev) * 1e-3)
     elif args.kernel_case == "mlp":
         # two training steps of the benchmark block; profile the second (skip the first's launches)
         from firefly_b200.distributed import ZeroFireFlyOptim
@@ -97,7 +106,7 @@ def kernel_case(args):
 
         model = SwiGLUMLP(args.d_model, args.ffn).to(dev)
         model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
-        opt = ZeroFireFlyOptim([model.gate, model.up, model.down], lr=1e-3, weight_decay=0.01, seed=7)
+        opt = ZeroFireFlyOptim([model.gate_up, model.down], lr=1e-3, weight_decay=0.01, seed=7)
         x = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
         dy = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16)
         for _ in range(2):
@@ -193,8 +202,7 @@ class CpuStepModel:
         self.d, self.f, self.tokens = d, f, tokens
         self.params_total = 2 * d * f + f * d
         rng = self.rng = np.random.default_rng(0)
-        self.qg, self.sg = O.quantize_rows(rng.standard_normal((f, d)).astype(np.float32) * 0.02)
-        self.qu, self.su = O.quantize_rows(rng.standard_normal((f, d)).astype(np.float32) * 0.02)
+        self.qgu, self.sgu = O.quantize_rows(rng.standard_normal((2 * f, d)).astype(np.float32) * 0.02)
         self.qd, self.sd = O.quantize_rows(rng.standard_normal((d, f)).astype(np.float32) * 0.02)
         self.n = max(param_sample // 4096, 1) * 4096
         self.q, self.ws = O.quantize_rows(rng.standard_normal((self.n // 4096, 4096)).astype(np.float32) * 0.02)
@@ -209,19 +217,7 @@ class CpuStepModel:
         x = O.round_bf16(self.rng.standard_normal((t, self.d)).astype(np.float32))
         dy = O.f32_to_bf16_bits(self.rng.standard_normal((t, self.d)).astype(np.float32))
         t0 = time.perf_counter()
-        g_bits, *_ = O.linear_forward(x, self.qg, self.sg)
-        u_bits, *_ = O.linear_forward(x, self.qu, self.su)
-        g = O.bf16_bits_to_f32(g_bits)
-        u = O.bf16_bits_to_f32(u_bits)
-        sig = (1.0 / (1.0 + np.exp(-g.astype(np.float64)))).astype(np.float32)
-        h = O.round_bf16(g * sig * u)
-        O.linear_forward(h, self.qd, self.sd)
-        out_d = O.linear_backward(h, dy, self.qd, self.sd)
-        dh = O.bf16_bits_to_f32(out_d["dx"])
-        dgate = O.f32_to_bf16_bits(dh * u * (sig * (1 + g * (1 - sig))))
-        dup = O.f32_to_bf16_bits(dh * g * sig)
-        O.linear_backward(x, dgate, self.qg, self.sg)
-        O.linear_backward(x, dup, self.qu, self.su)
+        O.swiglu_mlp_step(x, dy, self.qgu, self.sgu, self.qd, self.sd)
         dt = time.perf_counter() - t0
         if record:
             self.fb_times.append((t, dt))
@@ -459,7 +455,7 @@ def main():
     torch.manual_seed(1234 + rank)
     model = SwiGLUMLP(d, f).to(dev)
     model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
-    mods = [model.gate, model.up, model.down]
+    mods = [model.gate_up, model.down]
     opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     # the block input is an activation of the model: it needs a gradient (dX is part of the step)

@@ -44,6 +44,10 @@ SIGNATURES = {
     "ff_quant_rows_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P]),
     "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
+    "ff_swiglu_selftest": (_I, [_P, _P, _P]),
+    "ff_swiglu_quant_i8": (_I, [_P, _P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P]),
+    "ff_swiglu_bwd_quant_i8": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _I64, _P, _P,
+                                    _I64, _P, _P, _P]),
     "ff_transpose_i8": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P]),
     "ff_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "ff_gemm_i8_kn": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
@@ -61,6 +65,7 @@ _lib = None
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
+                     "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
 
@@ -213,6 +218,98 @@ def quant_dual(x: torch.Tensor, row_colmul: torch.Tensor | None = None, eps: flo
               float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols),
               _ptr(ws), _stream(dev))
     return q_rows, s_rows, q_cols, s_cols
+
+
+_SWIGLU_CHECKED: set[int] = set()
+
+
+def swiglu_selftest(device: torch.device | None = None) -> tuple[int, int, int | None]:
+    """``(mismatches, ieee_inputs, first_mismatch)`` of the exhaustive check of the SwiGLU
+    kernels' branch-free arithmetic over all 65536 bf16 inputs on ``device`` (synchronises);
+    ``first_mismatch`` is the smallest mismatching bf16 bit pattern or None."""
+    mism, ieee, first = ctypes.c_uint32(0), ctypes.c_uint32(0), ctypes.c_uint32(0)
+    with torch.cuda.device(device or torch.cuda.current_device()):
+        _call("ff_swiglu_selftest", ctypes.byref(mism), ctypes.byref(ieee), ctypes.byref(first))
+    return int(mism.value), int(ieee.value), (None if first.value == 0xFFFFFFFF else int(first.value))
+
+
+def _require_swiglu_math(dev: torch.device) -> None:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx in _SWIGLU_CHECKED:
+        return
+    mism, _, first = swiglu_selftest(torch.device("cuda", idx))
+    if mism:
+        raise RuntimeError(f"SwiGLU kernels' arithmetic differs from IEEE fp32 on cuda:{idx} for {mism} "
+                           f"bf16 inputs (first: 0x{first:04x}); the fused SwiGLU path cannot be used")
+    _SWIGLU_CHECKED.add(idx)
+
+
+def _swiglu_halves(gu: torch.Tensor):
+    """The gate and up halves ``[T, f]`` of a bf16 ``[T, 2f]`` projection output."""
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2 or gu.shape[1] % 2:
+        raise ValueError(f"expected a bf16 [T, 2f] gate/up output, got {gu.dtype} {tuple(gu.shape)}")
+    gu, ld = _rows_view(gu)
+    return gu, ld, gu.shape[1] // 2
+
+
+def swiglu_quant(gu: torch.Tensor, eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """Dual codes of ``h = silu(g) * u`` (bf16 as torch forms it) for ``gu = [g | u]``.
+
+    Returns ``quant_dual(h)``'s four outputs and h itself (bf16 ``[T, f]``)."""
+    dev = _require_cuda(gu)
+    _require_swiglu_math(dev)
+    gu, ld, F = _swiglu_halves(gu)
+    T = gu.shape[0]
+    ldq, ldqt = round_up(F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((F,), dtype=torch.float32, device=dev)
+    ldh = round_up(F, 8)
+    h = torch.empty((T, ldh), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + F,), dtype=torch.float32, device=dev)
+    u = gu[:, F:]
+    with torch.cuda.device(dev):
+        _call("ff_swiglu_quant_i8", _ptr(gu), _ptr(u), ld, T, F, float(eps), _ptr(h), ldh, _ptr(q_rows), ldq,
+              _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols), _ptr(ws), _stream(dev))
+    return q_rows, s_rows, q_cols, s_cols, h[:, :F]
+
+
+def swiglu_bwd_quant(dh: torch.Tensor, gu: torch.Tensor, colmul: torch.Tensor | None = None,
+                     eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """Dual codes of the ``[T, 2f]`` gradient ``[dg | du]`` of ``gu`` given ``dh = dL/dh``.
+
+    Returns ``quant_dual([dg | du], row_colmul=colmul)``'s four outputs (row codes
+    ``[T, round_up(2f, 16)]``, column codes ``[2f, round_up(T, 16)]``) and ``[dg | du]``
+    itself (bf16 ``[T, 2f]``)."""
+    dev = _require_cuda(dh, gu, colmul)
+    _require_swiglu_math(dev)
+    gu, ld, F = _swiglu_halves(gu)
+    if dh.dtype != torch.bfloat16 or tuple(dh.shape) != (gu.shape[0], F):
+        raise ValueError(f"dh must be bf16 [{gu.shape[0]}, {F}], got {dh.dtype} {tuple(dh.shape)}")
+    dh, ldh = _rows_view(dh)
+    T = gu.shape[0]
+    ldq, ldqt = round_up(2 * F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((2 * F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((2 * F,), dtype=torch.float32, device=dev)
+    dgu = torch.empty((T, 2 * F), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + 2 * F,), dtype=torch.float32, device=dev)
+    if colmul is not None:
+        colmul = colmul.to(torch.float32).contiguous()
+    u = gu[:, F:]
+    with torch.cuda.device(dev):
+        _call("ff_swiglu_bwd_quant_i8", _ptr(dh), ldh, _ptr(gu), _ptr(u), ld, T, F, _ptr(colmul),
+              float(eps), _ptr(dgu), 2 * F, _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols),
+              _ptr(ws), _stream(dev))
+    return q_rows, s_rows, q_cols, s_cols, dgu
 
 
 def transpose_i8(src: torch.Tensor, ldd: int | None = None) -> torch.Tensor:

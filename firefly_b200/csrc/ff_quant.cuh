@@ -71,6 +71,206 @@ __device__ __forceinline__ void load_raw8(Raw8<DT>& r, const typename Elem<DT>::
 }
 
 // ---------------------------------------------------------------------------
+// Element sources of the dual quantiser's absmax pass.  A source turns raw row loads
+// into the values of its NOUT column panels; the plain source is the input itself, the
+// SwiGLU sources compute the activation (or its gradients) from the GEMM outputs and
+// have the pass store them (bf16) for the quantiser pass.  Every source maps all-zero
+// raw inputs (rows and columns past the end are loaded as zeros) to the value 0.
+// ---------------------------------------------------------------------------
+template <int DT>
+struct PlainSrc {
+  static constexpr int NOUT = 1;
+  static constexpr bool kPreloadBoth = true;  // small raw: keep all 8 rows of a thread in flight
+  static constexpr bool kStore = false;       // pass A never writes the values back
+  static constexpr int kMinBlocks = 2;        // pass A blocks per SM the registers must allow
+  static constexpr int kRowsInFlight = 8;     // pass A rows loaded per thread before the math
+  using T = typename Elem<DT>::T;
+  const T* x;
+  int64_t ld;
+  struct Raw {
+    Raw8<DT> v;
+    __device__ __forceinline__ void zero() { v.zero(); }
+  };
+  __device__ __forceinline__ bool vec(int64_t c, int64_t cols) const {
+    return (c + 8 <= cols) && ((ld * (int64_t)sizeof(T)) % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  }
+  __device__ __forceinline__ void load(Raw& r, int64_t row, int64_t c, int64_t cols, bool v) const {
+    load_raw8<DT>(r.v, x + row * ld, c, cols, v);
+  }
+  __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[0][j] = r.v.get(j);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// SwiGLU arithmetic.  torch evaluates, per element x of the gate (a bf16 value, fp32 math):
+//   silu(x)        = x / (1 + exp(-x))                         (IEEE divide)
+//   sigmoid(x)     = 1 / (1 + exp(-x))                         (IEEE divide)
+//   silu_backward  = d * sigmoid * (1 + x * (1 - sigmoid))
+// The IEEE divide is a branch around a slow path, which serialises the kernels that
+// evaluate it per element.  swiglu_fast computes the same values without branches:
+//   den = 1 + expf(-x)                    (the same expf as torch)
+//   s   = y + y * (1 - den * y)           y = rcp.approx(den): one Newton-Raphson step
+//   q   = q0 + s * (x - den * q0)         q0 = x * s: one residual correction
+// (Markstein's correction steps for reciprocal and quotient, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).
+// x is a bf16 value, so the inputs form a finite set of 65536 values: swiglu_selftest_kernel
+// checks s == RN(1/den) and q == RN(x/den) for every one of them on the running device
+// (ff_swiglu_selftest; the Python layer runs it once per device before the first SwiGLU
+// call and refuses to continue on a device where it fails).  Inputs outside the range of the fast path (x <= -87: den >= 2^126, where 1/den is
+// subnormal and rcp.approx flushes it; x not finite) set `rare` and are recomputed with the
+// IEEE operations by the caller.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+struct SwigluMath {
+  float den, s, q;  // 1 + exp(-x), RN(1/den), RN(x/den)
+};
+__device__ __forceinline__ SwigluMath swiglu_fast(float x, bool& rare) {
+  SwigluMath m;
+  m.den = __fadd_rn(1.f, expf(-x));
+  const float y = rcp_approx_ftz(m.den);
+  m.s = __fmaf_rn(__fmaf_rn(-m.den, y, 1.f), y, y);
+  const float q0 = __fmul_rn(x, m.s);
+  m.q = __fmaf_rn(__fmaf_rn(-m.den, q0, x), m.s, q0);
+  m.q = x == 0.f ? x : m.q;  // the correction turns -0 into +0; x / den keeps the sign of a zero
+  // the reciprocal step is exact except for an all-ones significand (Markstein's exception)
+  rare |= !(x > -87.f && x < INFINITY) || ((__float_as_uint(m.den) & 0x7FFFFFu) == 0x7FFFFFu);
+  return m;
+}
+__device__ __forceinline__ SwigluMath swiglu_exact(float x) {
+  SwigluMath m;
+  m.den = __fadd_rn(1.f, expf(-x));
+  m.s = __fdiv_rn(1.f, m.den);
+  m.q = __fdiv_rn(x, m.den);
+  return m;
+}
+// h = bf16(bf16(silu(g)) * u)
+__device__ __forceinline__ float swiglu_h(const SwigluMath& m, float u) { return bf16r(__fmul_rn(bf16r(m.q), u)); }
+// dg = bf16(silu_backward(bf16(dh * u), g)), du = bf16(dh * bf16(silu(g)))
+__device__ __forceinline__ float swiglu_dg(const SwigluMath& m, float x, float dh, float u) {
+  const float ds = bf16r(__fmul_rn(dh, u));
+  return bf16r(__fmul_rn(__fmul_rn(ds, m.s), __fmaf_rn(x, __fsub_rn(1.f, m.s), 1.f)));
+}
+__device__ __forceinline__ float swiglu_du(const SwigluMath& m, float dh) { return bf16r(__fmul_rn(dh, bf16r(m.q))); }
+
+// every bf16 bit pattern x: fast path (where it applies) against the IEEE operations;
+// counts[0] = mismatches, counts[1] = inputs routed to the IEEE path, counts[2] = smallest
+// mismatching bf16 bit pattern (0xFFFFFFFF if none)
+__global__ void swiglu_selftest_kernel(uint32_t* counts) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 65536u) return;
+  const float x = __uint_as_float(i << 16);
+  bool rare = false;
+  const SwigluMath f = swiglu_fast(x, rare);
+  if (rare) {
+    atomicAdd(counts + 1, 1u);
+    return;
+  }
+  const SwigluMath e = swiglu_exact(x);
+  if (__float_as_uint(f.s) != __float_as_uint(e.s) || __float_as_uint(f.q) != __float_as_uint(e.q) ||
+      __float_as_uint(f.den) != __float_as_uint(e.den)) {
+    atomicAdd(counts, 1u);
+    atomicMin(counts + 2, i);
+  }
+}
+
+// h = bf16(bf16(silu(g)) * u): the SwiGLU activation between the gate/up and down projections
+struct SwigluSrc {
+  static constexpr int NOUT = 1;
+  static constexpr bool kPreloadBoth = false;
+  static constexpr bool kStore = true;  // pass A writes h (bf16) for pass B
+  static constexpr int kMinBlocks = 3;
+  static constexpr int kRowsInFlight = 4;
+  const __nv_bfloat16* g;
+  const __nv_bfloat16* u;
+  int64_t ld;
+  struct Raw {
+    Raw8<FF_DTYPE_BF16> g, u;
+    __device__ __forceinline__ void zero() {
+      g.zero();
+      u.zero();
+    }
+  };
+  __device__ __forceinline__ bool vec(int64_t c, int64_t cols) const {
+    return (c + 8 <= cols) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(g) & 15) == 0) &&
+           ((reinterpret_cast<uintptr_t>(u) & 15) == 0);
+  }
+  __device__ __forceinline__ void load(Raw& r, int64_t row, int64_t c, int64_t cols, bool v) const {
+    load_raw8<FF_DTYPE_BF16>(r.g, g + row * ld, c, cols, v);
+    load_raw8<FF_DTYPE_BF16>(r.u, u + row * ld, c, cols, v);
+  }
+  // all 8 values of a raw vector: branch-free, then the rare inputs again with IEEE ops
+  __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
+    bool rare = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[0][j] = swiglu_h(swiglu_fast(r.g.get(j), rare), r.u.get(j));
+    if (__builtin_expect(rare, 0)) {
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) out[0][j] = swiglu_h(swiglu_exact(r.g.get(j)), r.u.get(j));
+    }
+  }
+};
+
+// gradients of h = silu(g) * u given dh, as torch's autograd forms them in bf16; the two
+// are the column panels [dg | du] of one gradient matrix (gate and up share one projection):
+//   panel 0: dg = bf16(silu_backward(bf16(dh * u), g))
+//   panel 1: du = bf16(dh * bf16(silu(g)))
+struct SwigluBwdSrc {
+  static constexpr int NOUT = 2;
+  static constexpr bool kPreloadBoth = false;
+  static constexpr bool kStore = true;  // pass A writes [dg | du] (bf16) for pass B
+  static constexpr int kMinBlocks = 2;
+  static constexpr int kRowsInFlight = 2;
+  const __nv_bfloat16* dh;  // [rows, ldh]
+  const __nv_bfloat16* g;   // [rows, ld]
+  const __nv_bfloat16* u;   // [rows, ld]
+  int64_t ldh, ld;
+  struct Raw {
+    Raw8<FF_DTYPE_BF16> dh, g, u;
+    __device__ __forceinline__ void zero() {
+      dh.zero();
+      g.zero();
+      u.zero();
+    }
+  };
+  __device__ __forceinline__ bool vec(int64_t c, int64_t cols) const {
+    return (c + 8 <= cols) && (ld % 8 == 0) && (ldh % 8 == 0) && ((reinterpret_cast<uintptr_t>(dh) & 15) == 0) &&
+           ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((reinterpret_cast<uintptr_t>(u) & 15) == 0);
+  }
+  __device__ __forceinline__ void load(Raw& r, int64_t row, int64_t c, int64_t cols, bool v) const {
+    load_raw8<FF_DTYPE_BF16>(r.dh, dh + row * ldh, c, cols, v);
+    load_raw8<FF_DTYPE_BF16>(r.g, g + row * ld, c, cols, v);
+    load_raw8<FF_DTYPE_BF16>(r.u, u + row * ld, c, cols, v);
+  }
+  __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
+    bool rare = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x = r.g.get(j), d = r.dh.get(j);
+      const SwigluMath m = swiglu_fast(x, rare);
+      out[0][j] = swiglu_dg(m, x, d, r.u.get(j));
+      out[1][j] = swiglu_du(m, d);
+    }
+    if (__builtin_expect(rare, 0)) {
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) {
+        const float x = r.g.get(j), d = r.dh.get(j);
+        const SwigluMath m = swiglu_exact(x);
+        out[0][j] = swiglu_dg(m, x, d, r.u.get(j));
+        out[1][j] = swiglu_du(m, d);
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
 // K1: one warp per row.  Pass 1 reads the row for |x*colmul| max, pass 2
 // re-reads it (from L1/L2) and writes codes.  VEC path needs 16 B aligned rows.
 // ---------------------------------------------------------------------------
@@ -161,66 +361,97 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(
 constexpr int kDualARows = 128;
 constexpr int kDualAThreads = 256;
 constexpr int kDualACols = 1024;
-constexpr int kDualAU = 8;  // rows of 16 B in flight per thread
 
-template <int DT>
-__global__ void __launch_bounds__(kDualAThreads) dual_absmax_kernel(
-    const typename Elem<DT>::T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
-    const float* __restrict__ colmul, bool want_rows, bool want_cols,
-    uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax) {
-  using T = typename Elem<DT>::T;
+template <class Src>
+__global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_kernel(Src src, int64_t rows, int64_t cols,
+                                                                    const float* __restrict__ colmul, bool want_rows,
+                                                                    bool want_cols, uint32_t* __restrict__ row_amax,
+                                                                    uint32_t* __restrict__ col_amax,
+                                                                    __nv_bfloat16* __restrict__ store, int64_t lds) {
+  constexpr int NO = Src::NOUT;
+  constexpr int U = Src::kRowsInFlight;
   __shared__ float red[kDualARows][5];   // per row: 4 warps' partial maxima
-  __shared__ float cred[kDualACols];     // odd-row half's column maxima
+  __shared__ float cred[NO][kDualACols];  // odd-row half's column maxima
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = tid >> 7, ct = tid & 127;
   const int64_t c0 = (int64_t)blockIdx.x * kDualACols + ct * 8;
   const int64_t r0 = (int64_t)blockIdx.y * kDualARows;
-  const bool vec = (c0 + 8 <= cols) && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
-                   ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-  float cm[8];
+  const bool vec = src.vec(c0, cols);
+  const bool vec_store = store && (c0 + 8 <= cols) && (lds % 8 == 0) && (cols % 8 == 0 || NO == 1) &&
+                         ((reinterpret_cast<uintptr_t>(store) & 15) == 0);
+  float cm[NO][8], cmax[NO][8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) cm[j] = (colmul && c0 + j < cols) ? __ldg(colmul + c0 + j) : 1.f;
-  float cmax[8];
+  for (int o = 0; o < NO; ++o)
 #pragma unroll
-  for (int j = 0; j < 8; ++j) cmax[j] = 0.f;
+    for (int j = 0; j < 8; ++j) {
+      cm[o][j] = (colmul && c0 + j < cols) ? __ldg(colmul + o * cols + c0 + j) : 1.f;
+      cmax[o][j] = 0.f;
+    }
   const int nr = (int)min64(kDualARows, rows - r0);
-  const T* xbase = x + r0 * ldx;
 #pragma unroll 1
-  for (int i0 = half; i0 < kDualARows; i0 += 2 * kDualAU) {
-    Raw8<DT> v[kDualAU];
+  for (int i0 = half; i0 < kDualARows; i0 += 2 * U) {
+    typename Src::Raw v[U];
 #pragma unroll
-    for (int u = 0; u < kDualAU; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int i = i0 + 2 * u;
-      if (i < nr) load_raw8<DT>(v[u], xbase + (int64_t)i * ldx, c0, cols, vec);
+      if (i < nr) src.load(v[u], r0 + i, c0, cols, vec);
       else v[u].zero();
     }
 #pragma unroll
-    for (int u = 0; u < kDualAU; ++u) {
+    for (int u = 0; u < U; ++u) {
       float rm = 0.f;
+      float ev[NO][8];
+      src.eval8(v[u], ev);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float e = v[u].get(j);
-        cmax[j] = fmaxf(cmax[j], fabsf(e));
-        rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(e, cm[j]) : e));
+#pragma unroll
+        for (int o = 0; o < NO; ++o) {
+          const float e = ev[o][j];  // columns past the end were loaded as zeros: value 0
+          cmax[o][j] = fmaxf(cmax[o][j], fabsf(e));
+          rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(e, cm[o][j]) : e));
+        }
+      }
+      const int i = i0 + 2 * u;
+      if (Src::kStore && store && i < nr) {  // the values as bf16 (they are bf16 already): panel o at column o*cols
+#pragma unroll
+        for (int o = 0; o < NO; ++o) {
+          __nv_bfloat16* dst = store + (r0 + i) * lds + o * cols + c0;
+          if (vec_store) {
+            uint4 w;
+            w.x = (__float_as_uint(ev[o][0]) >> 16) | (__float_as_uint(ev[o][1]) & 0xFFFF0000u);
+            w.y = (__float_as_uint(ev[o][2]) >> 16) | (__float_as_uint(ev[o][3]) & 0xFFFF0000u);
+            w.z = (__float_as_uint(ev[o][4]) >> 16) | (__float_as_uint(ev[o][5]) & 0xFFFF0000u);
+            w.w = (__float_as_uint(ev[o][6]) >> 16) | (__float_as_uint(ev[o][7]) & 0xFFFF0000u);
+            *reinterpret_cast<uint4*>(dst) = w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (c0 + j < cols) dst[j] = __float2bfloat16_rn(ev[o][j]);
+          }
+        }
       }
       if (want_rows) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
+        for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
         if (lane == 0) red[i0 + 2 * u][warp & 3] = rm;
       }
     }
   }
   if (want_cols && half == 1) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) cred[ct * 8 + j] = cmax[j];
+    for (int o = 0; o < NO; ++o)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cred[o][ct * 8 + j] = cmax[o][j];
   }
   __syncthreads();
   if (want_cols && half == 0) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float m = fmaxf(cmax[j], cred[ct * 8 + j]);
-      if (c0 + j < cols) atomicMax(col_amax + c0 + j, __float_as_uint(m));
-    }
+    for (int o = 0; o < NO; ++o)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float m = fmaxf(cmax[o][j], cred[o][ct * 8 + j]);
+        if (c0 + j < cols) atomicMax(col_amax + o * cols + c0 + j, __float_as_uint(m));
+      }
   }
   if (want_rows) {
     for (int i = tid; i < nr; i += kDualAThreads) {
@@ -460,6 +691,56 @@ extern "C" int ff_quant_rows_i8(const void* x, int dtype, int64_t rows, int64_t 
   return check_launch("ff_quant_rows_i8");
 }
 
+namespace ff {
+// Pass A over one source (absmax_ws: rows + NOUT*cols floats, cleared here); with `store`
+// the source's values are also written as bf16, panel o at columns o*cols.. of store.
+template <class Src>
+int launch_pass_a(const char* name, const Src& src, int64_t rows, int64_t cols, const float* colmul,
+                  bool do_rows, bool do_cols, float* absmax_ws, __nv_bfloat16* store, int64_t lds,
+                  cudaStream_t st) {
+  uint32_t* row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(rows + Src::NOUT * cols), st), name);
+  dim3 gA((unsigned)((cols + kDualACols - 1) / kDualACols), (unsigned)((rows + kDualARows - 1) / kDualARows));
+  FF_REQUIRE(gA.y < 65536, FF_ERR_UNSUPPORTED, "%s: too many rows", name);
+  dual_absmax_kernel<Src><<<gA, kDualAThreads, 0, st>>>(src, rows, cols, colmul, do_rows, do_cols, row_amax,
+                                                         row_amax + rows, store, lds);
+  return check_launch(name);
+}
+
+// Pass B over a matrix x of type DT whose absmax values pass A left in absmax_ws.
+template <int DT>
+int launch_pass_b(const char* name, const typename Elem<DT>::T* x, int64_t rows, int64_t cols, int64_t ldx,
+                  const float* colmul, float eps, int8_t* q_rows, int64_t ldq, float* s_rows, int8_t* q_cols_t,
+                  int64_t ldqt, float* s_cols, const float* absmax_ws, cudaStream_t st) {
+  const uint32_t* row_amax = reinterpret_cast<const uint32_t*>(absmax_ws);
+  const int64_t rspan = q_cols_t ? max64(rows, ldqt) : rows;
+  const int64_t cspan = q_rows ? max64(cols, ldq) : cols;
+  dim3 gB((unsigned)((cspan + kTile - 1) / kTile), (unsigned)((rspan + kTile - 1) / kTile));
+  FF_REQUIRE(gB.y < 65536, FF_ERR_UNSUPPORTED, "%s: too many rows", name);
+  dual_quant_kernel<DT><<<gB, 256, 0, st>>>(x, rows, cols, ldx, colmul, eps, row_amax, row_amax + rows, q_rows,
+                                            ldq, s_rows, q_cols_t, ldqt, s_cols);
+  return check_launch(name);
+}
+
+// shared argument checks of the dual quantisers' outputs
+inline int check_dual_outputs(const char* name, int64_t rows, int64_t cols, const int8_t* q_rows,
+                              int64_t ldq, const float* s_rows, const int8_t* q_cols_t, int64_t ldqt,
+                              const float* s_cols, const float* absmax_ws) {
+  const bool do_rows = q_rows != nullptr, do_cols = q_cols_t != nullptr;
+  FF_REQUIRE(do_rows || do_cols, FF_ERR_INVALID_ARG, "%s: nothing to do", name);
+  FF_REQUIRE(absmax_ws, FF_ERR_INVALID_ARG, "%s: null workspace", name);
+  if (do_rows) {
+    FF_REQUIRE(s_rows && ldq >= cols && ldq % 8 == 0 && aligned(q_rows, 8), FF_ERR_UNSUPPORTED,
+               "%s: q_rows needs ldq>=cols, ldq%%8==0, 8-byte alignment", name);
+  }
+  if (do_cols) {
+    FF_REQUIRE(s_cols && ldqt >= rows && ldqt % 16 == 0 && aligned(q_cols_t, 16), FF_ERR_UNSUPPORTED,
+               "%s: q_cols_t needs ldqt>=rows, ldqt%%16==0, 16-byte alignment", name);
+  }
+  return FF_OK;
+}
+}  // namespace ff
+
 extern "C" int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
                                 const float* row_colmul, float eps, int8_t* q_rows, int64_t ldq,
                                 float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols,
@@ -469,41 +750,99 @@ extern "C" int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t 
              "ff_quant_dual_i8: rows=%lld cols=%lld ldx=%lld", (long long)rows, (long long)cols, (long long)ldx);
   FF_REQUIRE(dtype == FF_DTYPE_F32 || dtype == FF_DTYPE_BF16 || dtype == FF_DTYPE_F16, FF_ERR_INVALID_ARG,
              "ff_quant_dual_i8: bad dtype %d", dtype);
-  const bool do_rows = q_rows != nullptr, do_cols = q_cols_t != nullptr;
-  FF_REQUIRE(do_rows || do_cols, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: nothing to do");
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: nothing to do");
   if (rows == 0) return FF_OK;
-  FF_REQUIRE(x && absmax_ws, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: null pointer");
-  if (do_rows) {
-    FF_REQUIRE(s_rows && ldq >= cols && ldq % 8 == 0 && aligned(q_rows, 8), FF_ERR_UNSUPPORTED,
-               "ff_quant_dual_i8: q_rows needs ldq>=cols, ldq%%8==0, 8-byte alignment");
-  }
-  if (do_cols) {
-    FF_REQUIRE(s_cols && ldqt >= rows && ldqt % 16 == 0 && aligned(q_cols_t, 16), FF_ERR_UNSUPPORTED,
-               "ff_quant_dual_i8: q_cols_t needs ldqt>=rows, ldqt%%16==0, 16-byte alignment");
-  }
+  FF_REQUIRE(x, FF_ERR_INVALID_ARG, "ff_quant_dual_i8: null input");
+  const int rc = check_dual_outputs("ff_quant_dual_i8", rows, cols, q_rows, ldq, s_rows, q_cols_t, ldqt,
+                                    s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
   cudaStream_t st = as_stream(stream);
-  uint32_t* row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
-  uint32_t* col_amax = row_amax + rows;
-  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(rows + cols), st), "ff_quant_dual_i8 memset");
-  dim3 gA((unsigned)((cols + kDualACols - 1) / kDualACols), (unsigned)((rows + kDualARows - 1) / kDualARows));
-  const int64_t rspan = do_cols ? max64(rows, ldqt) : rows;
-  const int64_t cspan = do_rows ? max64(cols, ldq) : cols;
-  dim3 gB((unsigned)((cspan + kTile - 1) / kTile), (unsigned)((rspan + kTile - 1) / kTile));
-  FF_REQUIRE(gA.y < 65536 && gB.y < 65536, FF_ERR_UNSUPPORTED, "ff_quant_dual_i8: too many rows");
 #define FF_DQ(DT)                                                                                          \
-  dual_absmax_kernel<DT><<<gA, kDualAThreads, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, row_colmul, \
-                                                        do_rows, do_cols, row_amax, col_amax);             \
-  dual_quant_kernel<DT><<<gB, 256, 0, st>>>((const Elem<DT>::T*)x, rows, cols, ldx, row_colmul, eps,       \
-                                            row_amax, col_amax, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols);
-  if (dtype == FF_DTYPE_F32) {
-    FF_DQ(FF_DTYPE_F32)
-  } else if (dtype == FF_DTYPE_BF16) {
-    FF_DQ(FF_DTYPE_BF16)
-  } else {
-    FF_DQ(FF_DTYPE_F16)
+  {                                                                                                      \
+    const auto* xt = (const Elem<DT>::T*)x;                                                              \
+    const int ra = launch_pass_a("ff_quant_dual_i8", PlainSrc<DT>{xt, ldx}, rows, cols, row_colmul,      \
+                                 q_rows != nullptr, q_cols_t != nullptr, absmax_ws, nullptr, 0, st);     \
+    if (ra != FF_OK) return ra;                                                                          \
+    return launch_pass_b<DT>("ff_quant_dual_i8", xt, rows, cols, ldx, row_colmul, eps, q_rows, ldq,      \
+                             s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);                             \
   }
+  if (dtype == FF_DTYPE_F32) FF_DQ(FF_DTYPE_F32)
+  if (dtype == FF_DTYPE_BF16) FF_DQ(FF_DTYPE_BF16)
+  FF_DQ(FF_DTYPE_F16)
 #undef FF_DQ
-  return check_launch("ff_quant_dual_i8");
+}
+
+extern "C" int ff_swiglu_quant_i8(const uint16_t* g, const uint16_t* u, int64_t ld, int64_t rows, int64_t cols,
+                                  float eps, uint16_t* h, int64_t ldh, int8_t* q_rows, int64_t ldq, float* s_rows,
+                                  int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 1 && ld >= cols && ldh >= cols, FF_ERR_INVALID_ARG,
+             "ff_swiglu_quant_i8: rows=%lld cols=%lld ld=%lld ldh=%lld", (long long)rows, (long long)cols,
+             (long long)ld, (long long)ldh);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "ff_swiglu_quant_i8: nothing to do");
+  if (rows == 0) return FF_OK;
+  FF_REQUIRE(g && u && h, FF_ERR_INVALID_ARG, "ff_swiglu_quant_i8: null input or h");
+  int rc = check_dual_outputs("ff_swiglu_quant_i8", rows, cols, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols,
+                              absmax_ws);
+  if (rc != FF_OK) return rc;
+  cudaStream_t st = as_stream(stream);
+  auto* hb = reinterpret_cast<__nv_bfloat16*>(h);
+  const SwigluSrc src{reinterpret_cast<const __nv_bfloat16*>(g), reinterpret_cast<const __nv_bfloat16*>(u), ld};
+  rc = launch_pass_a("ff_swiglu_quant_i8", src, rows, cols, nullptr, q_rows != nullptr, q_cols_t != nullptr,
+                     absmax_ws, hb, ldh, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>("ff_swiglu_quant_i8", hb, rows, cols, ldh, nullptr, eps, q_rows, ldq, s_rows,
+                                      q_cols_t, ldqt, s_cols, absmax_ws, st);
+}
+
+extern "C" int ff_swiglu_bwd_quant_i8(const uint16_t* dh, int64_t ldh, const uint16_t* g, const uint16_t* u,
+                                      int64_t ld, int64_t rows, int64_t cols, const float* colmul, float eps,
+                                      uint16_t* dgu, int64_t lddgu, int8_t* q_rows, int64_t ldq, float* s_rows,
+                                      int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws,
+                                      void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 1 && ld >= cols && ldh >= cols && lddgu >= 2 * cols, FF_ERR_INVALID_ARG,
+             "ff_swiglu_bwd_quant_i8: rows=%lld cols=%lld ld=%lld ldh=%lld lddgu=%lld", (long long)rows,
+             (long long)cols, (long long)ld, (long long)ldh, (long long)lddgu);
+  FF_REQUIRE(cols % 8 == 0, FF_ERR_UNSUPPORTED, "ff_swiglu_bwd_quant_i8: cols=%lld must be a multiple of 8",
+             (long long)cols);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "ff_swiglu_bwd_quant_i8: nothing to do");
+  if (rows == 0) return FF_OK;
+  FF_REQUIRE(dh && g && u && dgu, FF_ERR_INVALID_ARG, "ff_swiglu_bwd_quant_i8: null input or dgu");
+  int rc = check_dual_outputs("ff_swiglu_bwd_quant_i8", rows, 2 * cols, q_rows, ldq, s_rows, q_cols_t, ldqt,
+                              s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
+  cudaStream_t st = as_stream(stream);
+  auto* db = reinterpret_cast<__nv_bfloat16*>(dgu);
+  const SwigluBwdSrc src{reinterpret_cast<const __nv_bfloat16*>(dh), reinterpret_cast<const __nv_bfloat16*>(g),
+                         reinterpret_cast<const __nv_bfloat16*>(u), ldh, ld};
+  rc = launch_pass_a("ff_swiglu_bwd_quant_i8", src, rows, cols, colmul, q_rows != nullptr, q_cols_t != nullptr,
+                     absmax_ws, db, lddgu, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>("ff_swiglu_bwd_quant_i8", db, rows, 2 * cols, lddgu, colmul, eps, q_rows,
+                                      ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
+}
+
+namespace ff {
+__device__ uint32_t g_swiglu_selftest[3];
+}
+
+extern "C" int ff_swiglu_selftest(uint32_t* mismatches, uint32_t* ieee_inputs, uint32_t* first_mismatch) {
+  using namespace ff;
+  FF_REQUIRE(mismatches && ieee_inputs && first_mismatch, FF_ERR_INVALID_ARG, "ff_swiglu_selftest: null pointer");
+  const uint32_t zero[3] = {0u, 0u, 0xFFFFFFFFu};
+  FF_CUDA_TRY(cudaMemcpyToSymbol(g_swiglu_selftest, zero, sizeof(zero)), "ff_swiglu_selftest");
+  uint32_t* counts = nullptr;
+  FF_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&counts), g_swiglu_selftest), "ff_swiglu_selftest");
+  swiglu_selftest_kernel<<<256, 256>>>(counts);
+  const int rc = check_launch("ff_swiglu_selftest");
+  if (rc != FF_OK) return rc;
+  uint32_t out[3];
+  FF_CUDA_TRY(cudaMemcpyFromSymbol(out, g_swiglu_selftest, sizeof(out)), "ff_swiglu_selftest");
+  *mismatches = out[0];
+  *ieee_inputs = out[1];
+  *first_mismatch = out[2];
+  return FF_OK;
 }
 
 extern "C" int ff_transpose_i8(const int8_t* src, int64_t rows, int64_t cols, int64_t lds, int8_t* dst,

@@ -126,6 +126,59 @@ FF_API int ff_quant_dual_i8_noalloc(const void* x, int dtype, int64_t rows, int6
                                     int8_t* q_cols_t, int64_t ldqt, float* s_cols, void* stream);
 
 /*
+ * Exhaustive check of the SwiGLU kernels' branch-free arithmetic on the current
+ * device: for every bf16 value x, 1/(1+exp(-x)) and x/(1+exp(-x)) as the kernels
+ * compute them must equal the IEEE fp32 divides torch uses.  *mismatches = number of
+ * inputs where they differ (must be 0 before ff_swiglu_quant_i8 / ff_swiglu_bwd_quant_i8
+ * results can be trusted; run it once per device), *ieee_inputs = inputs the kernels
+ * route to the IEEE operations instead (x <= -87, non-finite x, and x whose
+ * 1 + exp(-x) has an all-ones significand), *first_mismatch = the smallest mismatching
+ * bf16 bit pattern (0xFFFFFFFF when none).  Synchronous (it waits for the device), on
+ * the legacy default stream.
+ */
+FF_API int ff_swiglu_selftest(uint32_t* mismatches, uint32_t* ieee_inputs, uint32_t* first_mismatch);
+
+/*
+ * SwiGLU activation fused with the dual quantiser: computes
+ *   h[r,c] = bf16(bf16(silu(g[r,c])) * u[r,c]),  silu(x) = x / (1 + exp(-x))  (fp32)
+ * exactly as torch's bf16 F.silu(g) * u does, writes it to h (bf16, leading dim ldh)
+ * while taking its row and column absmax in the same pass, then quantises h exactly
+ * as ff_quant_dual_i8 quantises a bf16 matrix (no colmul).  g, u: bf16 rows x cols
+ * with the common leading dim ld (the gate and up halves of one [rows, 2*cols]
+ * projection output: u = g + cols).  Outputs and absmax_ws (rows + cols floats) as
+ * ff_quant_dual_i8.  Two kernels; g and u are read once.  Requires a passing
+ * ff_swiglu_selftest on the device.
+ * Replaces, on the SwiGLU MLP block built from BitLinear layers, the elementwise
+ * silu and mul between the projections plus the down projection's input
+ * quantisation (fireflykernels.py:164-167 applied to h).
+ */
+FF_API int ff_swiglu_quant_i8(const uint16_t* g, const uint16_t* u, int64_t ld, int64_t rows, int64_t cols,
+                              float eps, uint16_t* h, int64_t ldh, int8_t* q_rows, int64_t ldq, float* s_rows,
+                              int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws, void* stream);
+
+/*
+ * Backward of the SwiGLU activation fused with the dual quantiser of the gate/up
+ * projection's output gradient.  With dh the gradient of h (bf16, leading dim ldh)
+ * and g, u as in ff_swiglu_quant_i8, the gradient of the [rows, 2*cols] projection
+ * output is the two column panels, formed in bf16 exactly as torch's autograd
+ * forms them for F.silu(g) * u:
+ *   panel 0 (gate): dg = bf16(bf16(dh*u) * s * (1 + g*(1 - s))),  s = 1/(1 + exp(-g))
+ *   panel 1 (up):   du = bf16(dh * bf16(silu(g)))
+ * It is written to dgu (bf16 [rows, lddgu], lddgu >= 2*cols) while its absmax values
+ * are taken, then quantised exactly as ff_quant_dual_i8 quantises the bf16 matrix
+ * dgu with row_colmul = colmul (NULL or fp32[2*cols], the projection's weight
+ * scales): q_rows [rows, ldq >= 2*cols], s_rows [rows], q_cols_t [2*cols, ldqt],
+ * s_cols [2*cols]; absmax_ws rows + 2*cols floats.  cols must be a multiple of 8.
+ * Requires a passing ff_swiglu_selftest on the device.
+ * Replaces torch's mul/silu backward between the down projection's dX and the
+ * gate/up projection's backward operand preparation (fireflykernels.py:184-193).
+ */
+FF_API int ff_swiglu_bwd_quant_i8(const uint16_t* dh, int64_t ldh, const uint16_t* g, const uint16_t* u,
+                                  int64_t ld, int64_t rows, int64_t cols, const float* colmul, float eps,
+                                  uint16_t* dgu, int64_t lddgu, int8_t* q_rows, int64_t ldq, float* s_rows,
+                                  int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws, void* stream);
+
+/*
  * int8 transpose: dst[c, r] = src[r, c] for r < rows, c < cols; dst entries
  * r in rows..ldd-1 are written 0.  Builds the K-major copy of W (Wᵀ) that
  * the dX GEMM reads; the reference keeps per-handle weight layouts in

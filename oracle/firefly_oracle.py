@@ -17,6 +17,10 @@ It restates the reference algorithm (fumitoshi0524/FireFly) in numpy:
 * ``encode_signed`` …         mu-law 8-bit blockwise codecs fireflyoptim.py:8-80
 * ``dqt_adamw8_step``         FireFlyOptim bit-module update fireflyoptim.py:136-209
 * ``philox_uniforms``         the counter-based uniforms the GPU optimizer draws
+* ``swiglu_forward`` / ``swiglu_backward`` / ``swiglu_mlp_step``
+                              the SwiGLU MLP block of BitLinear layers (the benchmark
+                              workload; the reference has no model code): torch's
+                              bf16 silu, mul and their autograd formulas
 
 Rounding model.  Every reference op is evaluated in fp32 with correct rounding:
 ``+ - * /`` are IEEE fp32, ``sqrt/exp/log1p/tanh`` are computed in fp64 and
@@ -131,6 +135,57 @@ def dequant(acc, scale_a=None, scale_b=None, bias=None) -> np.ndarray:
     if bias is not None:
         v = v + np.asarray(bias, np.float32)[None, :]
     return v
+
+
+# --------------------------------------------------------------------------
+# SwiGLU activation between BitLinear layers (bf16 tensors, as torch computes them)
+# --------------------------------------------------------------------------
+def _sigmoid_parts(g):
+    """``(1 + exp(-g), 1 / (1 + exp(-g)))`` in fp32, exp rounded once from fp64."""
+    g = np.asarray(g, np.float32)
+    den = (F32(1.0) + _f64fn(np.exp, -g)).astype(np.float32)
+    return den, (F32(1.0) / den).astype(np.float32)
+
+
+def swiglu_forward(g, u):
+    """``h = bf16(bf16(silu(g)) * u)`` for bf16-valued fp32 arrays g, u (torch's F.silu(g) * u)."""
+    g = np.asarray(g, np.float32)
+    den, _ = _sigmoid_parts(g)
+    silu = round_bf16(g / den)
+    return round_bf16(silu * np.asarray(u, np.float32))
+
+
+def swiglu_backward(dh, g, u):
+    """``(dg, du)`` of ``h = silu(g) * u`` as torch's autograd forms them in bf16:
+    ``du = bf16(dh * bf16(silu(g)))`` and ``dg = bf16(ds * s * (1 + g * (1 - s)))`` with
+    ``ds = bf16(dh * u)``, ``s = 1 / (1 + exp(-g))`` (the last term one FMA)."""
+    dh, g, u = (np.asarray(a, np.float32) for a in (dh, g, u))
+    den, sg = _sigmoid_parts(g)
+    ds = round_bf16(dh * u)
+    dg = round_bf16((ds * sg).astype(np.float32) * _fma(g, (F32(1.0) - sg).astype(np.float32), F32(1.0)))
+    du = round_bf16(dh * round_bf16(g / den))
+    return dg, du
+
+
+def swiglu_mlp_step(x, dy, q_gu, s_gu, q_d, s_d, eps: float = 1e-8):
+    """Forward + backward of ``y = down(silu(g) * u)``, ``[g | u] = gate_up(x)``.
+
+    ``q_gu [2f, d]`` holds the gate rows then the up rows.  Returns a dict with y, dx
+    and both weight gradients (bf16 bit patterns) and the intermediate codes."""
+    x = np.asarray(x, np.float32)
+    f = q_d.shape[1]
+    gu_bits, q_x, s_x, _ = linear_forward(x, q_gu, s_gu, eps=eps)
+    gu = bf16_bits_to_f32(gu_bits)
+    g, u = gu[:, :f], gu[:, f:]
+    h = swiglu_forward(g, u)
+    y_bits, q_h, s_h, _ = linear_forward(h, q_d, s_d, eps=eps)
+    bd = linear_backward(h, dy, q_d, s_d, eps=eps)
+    dh = bf16_bits_to_f32(bd["dx"])
+    dg, du = swiglu_backward(dh, g, u)
+    bgu = linear_backward(x, np.concatenate([dg, du], axis=1), q_gu, s_gu, eps=eps)
+    return {"y": y_bits, "dx": bgu["dx"], "gw_gu": bgu["gw"], "gw_d": bd["gw"], "gu": gu_bits,
+            "q_h": q_h, "s_h": s_h, "q_dgu": bgu["q_g"], "s_dgu": bgu["s_g"],
+            "q_dgut": bgu["q_dyt"], "s_dguc": bgu["s_dy"]}
 
 
 # --------------------------------------------------------------------------
