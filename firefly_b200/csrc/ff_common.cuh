@@ -194,4 +194,63 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(d & 0xff) << 24);
 }
 
+// ---------------------------------------------------------------------------
+// packed fp32 pairs: Blackwell's f32x2 add/sub/mul/fma issue two IEEE fp32 ops per
+// instruction (for kernels bound by instruction issue, not by the FMA pipe)
+// ---------------------------------------------------------------------------
+struct f2 {
+  uint64_t v;
+};
+__device__ __forceinline__ f2 mk2(float a, float b) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ f2 splat(float a) { return mk2(a, a); }
+__device__ __forceinline__ void un2(f2 x, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x.v)); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 add2_rm(f2 a, f2 b) {
+  f2 r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+
+// low bytes of four words packed into one word (byte k = low byte of the k-th argument)
+__device__ __forceinline__ uint32_t pack_lo4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+// word w with its byte k (0..3) replaced by the low byte of t
+template <int K>
+__device__ __forceinline__ uint32_t put_byte(uint32_t w, uint32_t t) {
+  constexpr uint32_t sel = K == 0 ? 0x3214u : K == 1 ? 0x3240u : K == 2 ? 0x3410u : 0x4210u;
+  return __byte_perm(w, t, sel);
+}
+// quant_code_nr on a pair, returning the magic-number words (low byte = the int8 code)
+__device__ __forceinline__ f2 quant_words_nr2(f2 v, f2 neg_s, f2 inv_s) {
+  const f2 q0 = mul2(v, inv_s);
+  return add2(fma2(fma2(q0, neg_s, v), inv_s, q0), splat(12582912.0f));
+}
+__device__ __forceinline__ void words2(f2 x, uint32_t& a, uint32_t& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(x.v));
+}
+
 }  // namespace ff

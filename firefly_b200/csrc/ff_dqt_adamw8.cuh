@@ -190,45 +190,6 @@ __device__ __forceinline__ uint32_t pack_codes(const int (&c)[8], int base) {
   return __byte_perm(lo, hi, 0x5410);
 }
 
-// ---------------------------------------------------------------------------
-// packed fp32 pairs: Blackwell's f32x2 add/sub/mul/fma issue two fp32 ops per
-// instruction (the kernel is bound by instruction issue, not by the FMA pipe)
-// ---------------------------------------------------------------------------
-struct f2 {
-  uint64_t v;
-};
-__device__ __forceinline__ f2 mk2(float a, float b) {
-  f2 r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ f2 splat(float a) { return mk2(a, a); }
-__device__ __forceinline__ void un2(f2 x, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x.v)); }
-__device__ __forceinline__ f2 add2(f2 a, f2 b) {
-  f2 r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 add2_rm(f2 a, f2 b) {
-  f2 r;
-  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
-  f2 r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
-  f2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
-  f2 r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
-  return r;
-}
 // x / d with nd = -d and id ~ 1/d: q0 = x*id, r = x - q0*d (exact), q = q0 + r*id
 __device__ __forceinline__ f2 div2(f2 x, f2 nd, f2 id) {
   const f2 q0 = mul2(x, id);

@@ -23,6 +23,13 @@ struct Raw8<FF_DTYPE_BF16> {
     const uint32_t x = j < 2 ? w.x : (j < 4 ? w.y : (j < 6 ? w.z : w.w));
     return __uint_as_float((j & 1) ? (x & 0xFFFF0000u) : (x << 16));
   }
+  __device__ __forceinline__ uint32_t word(int p) const {  // elements 2p (low half), 2p+1
+    return p == 0 ? w.x : (p == 1 ? w.y : (p == 2 ? w.z : w.w));
+  }
+  __device__ __forceinline__ f2 pair(int p) const {
+    const uint32_t x = word(p);
+    return mk2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
+  }
 };
 template <>
 struct Raw8<FF_DTYPE_F16> {
@@ -34,6 +41,7 @@ struct Raw8<FF_DTYPE_F16> {
     const uint32_t x = j < 2 ? w.x : (j < 4 ? w.y : (j < 6 ? w.z : w.w));
     return __half2float(__ushort_as_half((unsigned short)((j & 1) ? (x >> 16) : (x & 0xFFFFu))));
   }
+  __device__ __forceinline__ f2 pair(int p) const { return mk2(get(2 * p), get(2 * p + 1)); }
 };
 template <>
 struct Raw8<FF_DTYPE_F32> {
@@ -52,6 +60,7 @@ struct Raw8<FF_DTYPE_F32> {
     const int k = j & 3;
     return k == 0 ? h.x : (k == 1 ? h.y : (k == 2 ? h.z : h.w));
   }
+  __device__ __forceinline__ f2 pair(int p) const { return mk2(get(2 * p), get(2 * p + 1)); }
 };
 
 // 8 elements starting at column c of row xr (vector load when allowed, else guarded scalars)
@@ -84,6 +93,7 @@ struct PlainSrc {
   static constexpr bool kStore = false;       // pass A never writes the values back
   static constexpr int kMinBlocks = 2;        // pass A blocks per SM the registers must allow
   static constexpr int kRowsInFlight = 8;     // pass A rows loaded per thread before the math
+  static constexpr bool kWords = DT == FF_DTYPE_BF16;  // values available as bf16x2 words
   using T = typename Elem<DT>::T;
   const T* x;
   int64_t ld;
@@ -100,6 +110,14 @@ struct PlainSrc {
   __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
 #pragma unroll
     for (int j = 0; j < 8; ++j) out[0][j] = r.v.get(j);
+  }
+  __device__ __forceinline__ void eval_words(const Raw& r, uint32_t (&w)[NOUT][4]) const {
+    if constexpr (DT == FF_DTYPE_BF16) {
+      w[0][0] = r.v.w.x;
+      w[0][1] = r.v.w.y;
+      w[0][2] = r.v.w.z;
+      w[0][3] = r.v.w.w;
+    }
   }
 };
 
@@ -128,20 +146,57 @@ __device__ __forceinline__ float rcp_approx_ftz(float x) {
   return y;
 }
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// bf16x2 words: element 2k in the low half, 2k+1 in the high half
+__device__ __forceinline__ uint32_t pack_bf16x2(f2 v) {
+  float a, b;
+  un2(v, a, b);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ f2 unpack_bf16x2(uint32_t w) {
+  return mk2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t abs_bf16x2(uint32_t w) { return w & 0x7FFF7FFFu; }
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 struct SwigluMath {
   float den, s, q;  // 1 + exp(-x), RN(1/den), RN(x/den)
 };
+// x / den has the sign of x (the correction step would turn -0 into +0)
+__device__ __forceinline__ float sign_of(float v, float x) { return copysignf(v, x); }
 __device__ __forceinline__ SwigluMath swiglu_fast(float x, bool& rare) {
   SwigluMath m;
   m.den = __fadd_rn(1.f, expf(-x));
   const float y = rcp_approx_ftz(m.den);
   m.s = __fmaf_rn(__fmaf_rn(-m.den, y, 1.f), y, y);
   const float q0 = __fmul_rn(x, m.s);
-  m.q = __fmaf_rn(__fmaf_rn(-m.den, q0, x), m.s, q0);
-  m.q = x == 0.f ? x : m.q;  // the correction turns -0 into +0; x / den keeps the sign of a zero
-  // the reciprocal step is exact except for an all-ones significand (Markstein's exception)
-  rare |= !(x > -87.f && x < INFINITY) || ((__float_as_uint(m.den) & 0x7FFFFFu) == 0x7FFFFFu);
+  m.q = sign_of(__fmaf_rn(__fmaf_rn(-m.den, q0, x), m.s, q0), x);
+  rare |= !(m.den < 0x1p126f) || !(x < INFINITY);
+  return m;
+}
+// the same on a pair of inputs (f32x2 arithmetic); s and q as pairs
+struct SwigluMath2 {
+  f2 s, q;
+};
+__device__ __forceinline__ SwigluMath2 swiglu_fast2(float x0, float x1, bool& rare) {
+  const f2 x = mk2(x0, x1), one = splat(1.f);
+  const float e0 = expf(-x0), e1 = expf(-x1);
+  const f2 e = mk2(e0, e1);
+  const f2 nden = sub2(splat(-1.f), e);  // -(1 + e), rounded as 1 + e
+  float d0, d1;
+  un2(add2(one, e), d0, d1);
+  const f2 y = mk2(rcp_approx_ftz(d0), rcp_approx_ftz(d1));
+  SwigluMath2 m;
+  m.s = fma2(fma2(nden, y, one), y, y);
+  const f2 q0 = mul2(x, m.s);
+  float q0a, q0b;
+  un2(fma2(fma2(nden, q0, x), m.s, q0), q0a, q0b);
+  m.q = mk2(sign_of(q0a, x0), sign_of(q0b, x1));
+  rare |= !(d0 < 0x1p126f) || !(d1 < 0x1p126f) || !(x0 < INFINITY) || !(x1 < INFINITY);
   return m;
 }
 __device__ __forceinline__ SwigluMath swiglu_exact(float x) {
@@ -188,6 +243,7 @@ struct SwigluSrc {
   static constexpr bool kStore = true;  // pass A writes h (bf16) for pass B
   static constexpr int kMinBlocks = 3;
   static constexpr int kRowsInFlight = 4;
+  static constexpr bool kWords = true;
   const __nv_bfloat16* g;
   const __nv_bfloat16* u;
   int64_t ld;
@@ -206,14 +262,23 @@ struct SwigluSrc {
     load_raw8<FF_DTYPE_BF16>(r.g, g + row * ld, c, cols, v);
     load_raw8<FF_DTYPE_BF16>(r.u, u + row * ld, c, cols, v);
   }
-  // all 8 values of a raw vector: branch-free, then the rare inputs again with IEEE ops
-  __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
+  // the 8 values of a raw vector as bf16x2 words: branch-free, then again with the IEEE
+  // operations when an input is outside the fast path's range
+  __device__ __forceinline__ void eval_words(const Raw& r, uint32_t (&w)[NOUT][4]) const {
     bool rare = false;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) out[0][j] = swiglu_h(swiglu_fast(r.g.get(j), rare), r.u.get(j));
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t gw = r.g.word(p);
+      const SwigluMath2 m = swiglu_fast2(__uint_as_float(gw << 16), __uint_as_float(gw & 0xFFFF0000u), rare);
+      w[0][p] = pack_bf16x2(mul2(unpack_bf16x2(pack_bf16x2(m.q)), unpack_bf16x2(r.u.word(p))));
+    }
     if (__builtin_expect(rare, 0)) {
 #pragma unroll 1
-      for (int j = 0; j < 8; ++j) out[0][j] = swiglu_h(swiglu_exact(r.g.get(j)), r.u.get(j));
+      for (int p = 0; p < 4; ++p) {
+        const float h0 = swiglu_h(swiglu_exact(r.g.get(2 * p)), r.u.get(2 * p));
+        const float h1 = swiglu_h(swiglu_exact(r.g.get(2 * p + 1)), r.u.get(2 * p + 1));
+        w[0][p] = pack_bf16x2(mk2(h0, h1));
+      }
     }
   }
 };
@@ -228,6 +293,7 @@ struct SwigluBwdSrc {
   static constexpr bool kStore = true;  // pass A writes [dg | du] (bf16) for pass B
   static constexpr int kMinBlocks = 2;
   static constexpr int kRowsInFlight = 2;
+  static constexpr bool kWords = true;
   const __nv_bfloat16* dh;  // [rows, ldh]
   const __nv_bfloat16* g;   // [rows, ld]
   const __nv_bfloat16* u;   // [rows, ld]
@@ -249,22 +315,31 @@ struct SwigluBwdSrc {
     load_raw8<FF_DTYPE_BF16>(r.g, g + row * ld, c, cols, v);
     load_raw8<FF_DTYPE_BF16>(r.u, u + row * ld, c, cols, v);
   }
-  __device__ __forceinline__ void eval8(const Raw& r, float (&out)[NOUT][8]) const {
+  __device__ __forceinline__ void eval_words(const Raw& r, uint32_t (&w)[NOUT][4]) const {
     bool rare = false;
+    const f2 one = splat(1.f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float x = r.g.get(j), d = r.dh.get(j);
-      const SwigluMath m = swiglu_fast(x, rare);
-      out[0][j] = swiglu_dg(m, x, d, r.u.get(j));
-      out[1][j] = swiglu_du(m, d);
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t gw = r.g.word(p);
+      const f2 x = unpack_bf16x2(gw), d = unpack_bf16x2(r.dh.word(p));
+      const SwigluMath2 m = swiglu_fast2(__uint_as_float(gw << 16), __uint_as_float(gw & 0xFFFF0000u), rare);
+      const f2 ds = unpack_bf16x2(pack_bf16x2(mul2(d, unpack_bf16x2(r.u.word(p)))));
+      w[0][p] = pack_bf16x2(mul2(mul2(ds, m.s), fma2(x, sub2(one, m.s), one)));
+      w[1][p] = pack_bf16x2(mul2(d, unpack_bf16x2(pack_bf16x2(m.q))));
     }
     if (__builtin_expect(rare, 0)) {
 #pragma unroll 1
-      for (int j = 0; j < 8; ++j) {
-        const float x = r.g.get(j), d = r.dh.get(j);
-        const SwigluMath m = swiglu_exact(x);
-        out[0][j] = swiglu_dg(m, x, d, r.u.get(j));
-        out[1][j] = swiglu_du(m, d);
+      for (int p = 0; p < 4; ++p) {
+        float dg[2], du[2];
+        for (int k = 0; k < 2; ++k) {
+          const int j = 2 * p + k;
+          const float x = r.g.get(j), d = r.dh.get(j);
+          const SwigluMath m = swiglu_exact(x);
+          dg[k] = swiglu_dg(m, x, d, r.u.get(j));
+          du[k] = swiglu_du(m, d);
+        }
+        w[0][p] = pack_bf16x2(mk2(dg[0], dg[1]));
+        w[1][p] = pack_bf16x2(mk2(du[0], du[1]));
       }
     }
   }
@@ -363,14 +438,14 @@ constexpr int kDualAThreads = 256;
 constexpr int kDualACols = 1024;
 
 template <class Src>
-__global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_kernel(Src src, int64_t rows, int64_t cols,
-                                                                    const float* __restrict__ colmul, bool want_rows,
-                                                                    bool want_cols, uint32_t* __restrict__ row_amax,
-                                                                    uint32_t* __restrict__ col_amax,
-                                                                    __nv_bfloat16* __restrict__ store, int64_t lds) {
+__global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_kernel(
+    Src src, int64_t rows, int64_t cols, const float* __restrict__ colmul, bool want_rows, bool want_cols,
+    uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax, __nv_bfloat16* __restrict__ store,
+    int64_t lds) {
   constexpr int NO = Src::NOUT;
   constexpr int U = Src::kRowsInFlight;
-  __shared__ float red[kDualARows][5];   // per row: 4 warps' partial maxima
+  constexpr bool W = Src::kWords;
+  __shared__ float red[kDualARows][5];    // per row: 4 warps' partial maxima
   __shared__ float cred[NO][kDualACols];  // odd-row half's column maxima
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = tid >> 7, ct = tid & 127;
@@ -379,14 +454,24 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
   const bool vec = src.vec(c0, cols);
   const bool vec_store = store && (c0 + 8 <= cols) && (lds % 8 == 0) && (cols % 8 == 0 || NO == 1) &&
                          ((reinterpret_cast<uintptr_t>(store) & 15) == 0);
-  float cm[NO][8], cmax[NO][8];
+  // colmul of this thread's 8 columns (pairs), and the column maxima: bf16x2 words of |v|
+  // for word sources (the values are bf16, so their maximum is too), fp32 otherwise
+  f2 cm2[NO][4];
+  float cmax[NO][W ? 1 : 8];
+  uint32_t cmaxw[NO][W ? 4 : 1];
 #pragma unroll
-  for (int o = 0; o < NO; ++o)
+  for (int o = 0; o < NO; ++o) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      cm[o][j] = (colmul && c0 + j < cols) ? __ldg(colmul + o * cols + c0 + j) : 1.f;
-      cmax[o][j] = 0.f;
+    for (int q = 0; q < 4; ++q) {
+      const int64_t c = c0 + 2 * q;
+      cm2[o][q] = mk2((colmul && c < cols) ? __ldg(colmul + o * cols + c) : 1.f,
+                      (colmul && c + 1 < cols) ? __ldg(colmul + o * cols + c + 1) : 1.f);
     }
+#pragma unroll
+    for (int k = 0; k < (W ? 4 : 1); ++k) cmaxw[o][k] = 0u;
+#pragma unroll
+    for (int j = 0; j < (W ? 1 : 8); ++j) cmax[o][j] = 0.f;
+  }
   const int nr = (int)min64(kDualARows, rows - r0);
 #pragma unroll 1
   for (int i0 = half; i0 < kDualARows; i0 += 2 * U) {
@@ -399,49 +484,80 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      float rm = 0.f;
-      float ev[NO][8];
-      src.eval8(v[u], ev);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-#pragma unroll
-        for (int o = 0; o < NO; ++o) {
-          const float e = ev[o][j];  // columns past the end were loaded as zeros: value 0
-          cmax[o][j] = fmaxf(cmax[o][j], fabsf(e));
-          rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(e, cm[o][j]) : e));
-        }
-      }
       const int i = i0 + 2 * u;
-      if (Src::kStore && store && i < nr) {  // the values as bf16 (they are bf16 already): panel o at column o*cols
+      float rm = 0.f;
+      if constexpr (W) {
+        uint32_t wv[NO][4];
+        src.eval_words(v[u], wv);  // columns past the end were loaded as zeros: value 0
+        uint32_t rmw = 0u;
 #pragma unroll
-        for (int o = 0; o < NO; ++o) {
-          __nv_bfloat16* dst = store + (r0 + i) * lds + o * cols + c0;
-          if (vec_store) {
-            uint4 w;
-            w.x = (__float_as_uint(ev[o][0]) >> 16) | (__float_as_uint(ev[o][1]) & 0xFFFF0000u);
-            w.y = (__float_as_uint(ev[o][2]) >> 16) | (__float_as_uint(ev[o][3]) & 0xFFFF0000u);
-            w.z = (__float_as_uint(ev[o][4]) >> 16) | (__float_as_uint(ev[o][5]) & 0xFFFF0000u);
-            w.w = (__float_as_uint(ev[o][6]) >> 16) | (__float_as_uint(ev[o][7]) & 0xFFFF0000u);
-            *reinterpret_cast<uint4*>(dst) = w;
-          } else {
+        for (int o = 0; o < NO; ++o)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              if (c0 + j < cols) dst[j] = __float2bfloat16_rn(ev[o][j]);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t aw = abs_bf16x2(wv[o][q]);
+            cmaxw[o][q] = max_bf16x2(cmaxw[o][q], aw);
+            if (colmul) {
+              float a0, a1;
+              un2(mul2(unpack_bf16x2(aw), cm2[o][q]), a0, a1);  // |v| * colmul (colmul >= 0)
+              rm = fmaxf(rm, fmaxf(a0, a1));
+            } else {
+              rmw = max_bf16x2(rmw, aw);
+            }
+          }
+        if (!colmul) rm = fmaxf(__uint_as_float(rmw << 16), __uint_as_float(rmw & 0xFFFF0000u));
+        if (Src::kStore && store && i < nr) {  // the values themselves: panel o at column o*cols
+#pragma unroll
+          for (int o = 0; o < NO; ++o) {
+            __nv_bfloat16* dst = store + (r0 + i) * lds + o * cols + c0;
+            if (vec_store) {
+              *reinterpret_cast<uint4*>(dst) = make_uint4(wv[o][0], wv[o][1], wv[o][2], wv[o][3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (c0 + j < cols)
+                  reinterpret_cast<uint16_t*>(dst)[j] = (uint16_t)(wv[o][j >> 1] >> (16 * (j & 1)));
+            }
           }
         }
+      } else {
+        float ev[NO][8];
+        src.eval8(v[u], ev);  // columns past the end were loaded as zeros: value 0
+#pragma unroll
+        for (int o = 0; o < NO; ++o)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float e = ev[o][j];
+            cmax[o][j] = fmaxf(cmax[o][j], fabsf(e));
+            float c2a, c2b;
+            un2(cm2[o][j >> 1], c2a, c2b);
+            rm = fmaxf(rm, fabsf(colmul ? __fmul_rn(e, (j & 1) ? c2b : c2a) : e));
+          }
       }
       if (want_rows) {
 #pragma unroll
         for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
-        if (lane == 0) red[i0 + 2 * u][warp & 3] = rm;
+        if (lane == 0) red[i][warp & 3] = rm;
       }
     }
   }
+  // column maxima of this thread as floats
+  float cfin[NO][8];
+#pragma unroll
+  for (int o = 0; o < NO; ++o)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if constexpr (W) {
+        const uint32_t w = cmaxw[o][j >> 1];
+        cfin[o][j] = __uint_as_float((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
+      } else {
+        cfin[o][j] = cmax[o][j];
+      }
+    }
   if (want_cols && half == 1) {
 #pragma unroll
     for (int o = 0; o < NO; ++o)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cred[o][ct * 8 + j] = cmax[o][j];
+      for (int j = 0; j < 8; ++j) cred[o][ct * 8 + j] = cfin[o][j];
   }
   __syncthreads();
   if (want_cols && half == 0) {
@@ -449,7 +565,7 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
     for (int o = 0; o < NO; ++o)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float m = fmaxf(cmax[o][j], cred[o][ct * 8 + j]);
+        const float m = fmaxf(cfin[o][j], cred[o][ct * 8 + j]);
         if (c0 + j < cols) atomicMax(col_amax + o * cols + c0 + j, __float_as_uint(m));
       }
   }
@@ -469,7 +585,7 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
 constexpr int kTile = 128;
 
 template <int DT>
-__global__ void __launch_bounds__(256) dual_quant_kernel(
+__global__ void __launch_bounds__(256, DT == FF_DTYPE_F32 ? 2 : 3) dual_quant_kernel(
     const typename Elem<DT>::T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
     const float* __restrict__ colmul, float eps, const uint32_t* __restrict__ row_amax,
     const uint32_t* __restrict__ col_amax, int8_t* __restrict__ q_rows, int64_t ldq,
@@ -504,12 +620,13 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
   const bool vec_ok = (c + 8 <= cols) && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
                       ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   const bool row_store = do_rows && c < ldq;
-  float cmv[8], scv[8], iscv[8];
+  // per column pair: colmul, -s_col, 1/s_col (the quantiser math runs on f32x2 pairs)
+  f2 cm2[4], nsc2[4], isc2[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    cmv[j] = cmul[cb + j];
-    scv[j] = scol[cb + j];
-    iscv[j] = iscol[cb + j];
+  for (int q = 0; q < 4; ++q) {
+    cm2[q] = mk2(cmul[cb + 2 * q], cmul[cb + 2 * q + 1]);
+    nsc2[q] = mk2(-scol[cb + 2 * q], -scol[cb + 2 * q + 1]);
+    isc2[q] = mk2(iscol[cb + 2 * q], iscol[cb + 2 * q + 1]);
   }
   // issue all eight row loads of this thread (two 4 x 8 micro-tiles) before any math
   Raw8<DT> raw[2][4];
@@ -526,33 +643,38 @@ __global__ void __launch_bounds__(256) dual_quant_kernel(
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int rb = (rg + half * 16) * 4;  // first row of this 4x8 micro-tile within the tile
-    uint32_t colw[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) colw[j] = 0u;
+    uint32_t colw[8];  // column j: the codes of rows rb..rb+3, one byte each
     int8_t* qr = q_rows + (R0 + rb) * ldq + c;
 #pragma unroll
     for (int i = 0; i < 4; ++i, qr += ldq) {
       const int64_t r = R0 + rb + i;
+      uint32_t tw[8];  // magic-number words: low byte = code
       if (do_rows) {
-        int code[8];
-        const float sr = srow[rb + i], isr = isrow[rb + i];
+        const f2 nsr = splat(-srow[rb + i]), isr = splat(isrow[rb + i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) code[j] = quant_code_nr(__fmul_rn(raw[half][i].get(j), cmv[j]), sr, isr);
+        for (int q = 0; q < 4; ++q)
+          words2(quant_words_nr2(mul2(raw[half][i].pair(q), cm2[q]), nsr, isr), tw[2 * q], tw[2 * q + 1]);
         if (row_store && r < rows) {
           if (c + 8 <= ldq) {
             *reinterpret_cast<uint2*>(qr) =
-                make_uint2(pack4(code[0], code[1], code[2], code[3]), pack4(code[4], code[5], code[6], code[7]));
+                make_uint2(pack_lo4(tw[0], tw[1], tw[2], tw[3]), pack_lo4(tw[4], tw[5], tw[6], tw[7]));
           } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              if (c + j < ldq) qr[j] = (int8_t)code[j];
+              if (c + j < ldq) qr[j] = (int8_t)(tw[j] & 0xFFu);
           }
         }
       }
-      if (do_cols) {
+      if (do_cols) {  // rows past the end hold zeros: code 0
 #pragma unroll
-        for (int j = 0; j < 8; ++j)  // rows past the end hold zeros: code 0
-          colw[j] |= (uint32_t)(quant_code_nr(raw[half][i].get(j), scv[j], iscv[j]) & 0xff) << (8 * i);
+        for (int q = 0; q < 4; ++q) words2(quant_words_nr2(raw[half][i].pair(q), nsc2[q], isc2[q]), tw[2 * q], tw[2 * q + 1]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (i == 0) colw[j] = tw[j];
+          else if (i == 1) colw[j] = put_byte<1>(colw[j], tw[j]);
+          else if (i == 2) colw[j] = put_byte<2>(colw[j], tw[j]);
+          else colw[j] = put_byte<3>(colw[j], tw[j]);
+        }
       }
     }
     if (do_cols) {
