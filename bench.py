@@ -107,9 +107,10 @@ def kernel_case(args):
         model = SwiGLUMLP(args.d_model, args.ffn).to(dev)
         model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
         opt = ZeroFireFlyOptim([model.gate_up, model.down], lr=1e-3, weight_decay=0.01, seed=7)
-        x = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+        xs = [torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+              for _ in range(2)]
         dy = torch.randn(args.tokens, args.d_model, device=dev, generator=g).to(torch.bfloat16)
-        for _ in range(2):
+        for x in xs:  # a new input each step, as in training
             y = model(x)
             y.backward(dy)
             x.grad = None
@@ -459,7 +460,10 @@ def main():
     opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     # the block input is an activation of the model: it needs a gradient (dX is part of the step)
-    x = torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(True)
+    # two resident input batches used alternately, so that every step quantises a new input
+    # (the op layer reuses the codes of an input tensor it has just quantised)
+    xs = [torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(True) for _ in range(2)]
+    x = xs[0]
     dy = torch.randn(T, d, device=dev, generator=gen).to(torch.bfloat16)
 
     def step(xi, dyi):
@@ -473,8 +477,8 @@ def main():
         if world > 1:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 3)):
-        step(x, dy)
+    for i in range(max(args.warmup, 3)):
+        step(xs[i % 2], dy)
     torch.cuda.synchronize()
     assert _capi.device_status() == 0
 
@@ -490,8 +494,8 @@ def main():
     clocks.mark()
     t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0e.record()
-    for _ in range(args.steps):
-        step(x, dy)
+    for i in range(args.steps):
+        step(xs[i % 2], dy)
     t1e.record()
     torch.cuda.synchronize()
     barrier()

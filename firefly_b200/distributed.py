@@ -275,3 +275,44 @@ class ZeroFireFlyOptim:
                 "r_absmax": full["r_absmax"][b0:b1].cpu().clone(),
             }
         return res
+
+    def load_bit_state(self, bit_state: dict) -> None:
+        """Load a full ``bit_state`` in the reference's checkpoint layout
+        (``{handle: {step, m_q, m_absmax, v_q, v_absmax, r_q, r_absmax}}``, fireflyoptim.py:213-233),
+        keeping only this rank's shard of it (the ZeRO-1 scatter).
+
+        Every rank passes the same dict (e.g. each loads the checkpoint file); the world size
+        may differ from the one that saved it.  Modules absent from the dict keep fresh states.
+        """
+        plan = self.plan
+        for i, m in enumerate(self.modules):
+            ent = bit_state.get(m._registered_handle, bit_state.get(str(m._registered_handle)))
+            if ent is None:
+                continue
+            self.steps[i] = int(ent["step"])
+            off, n = plan.offsets[i], plan.numels[i]
+            a, b = max(off, plan.lo), min(off + n, plan.hi)
+            if a >= b:
+                continue
+            for key in ("m_q", "v_q", "r_q"):
+                src = ent[key].reshape(-1)[a - off:b - off]
+                getattr(self, key)[a - plan.lo:b - plan.lo].copy_(src.to(getattr(self, key).device))
+            ga, gb = a // BLOCK, (b + BLOCK - 1) // BLOCK  # global 256-element blocks
+            for key in ("m_absmax", "v_absmax", "r_absmax"):
+                src = ent[key].reshape(-1)[ga - off // BLOCK:gb - off // BLOCK]
+                dst = getattr(self, key)
+                dst[ga - plan.lo // BLOCK:gb - plan.lo // BLOCK].copy_(src.to(dst.device))
+
+    def state_dict(self) -> dict:
+        """Collective (every rank calls it): ``bit_state`` in the reference layout on rank 0
+        (None on the other ranks), ``bit_rng_seed``, and the dense optimizer's state."""
+        return {"bit_state": self.gather_bit_state(), "bit_rng_seed": self.rng_seed,
+                "dense": self.dense_opt.state_dict() if self.dense_opt is not None else None}
+
+    def load_state_dict(self, state: dict) -> None:
+        """Inverse of ``state_dict``: every rank passes the full dict saved by rank 0."""
+        self.load_bit_state(state["bit_state"])
+        if state.get("bit_rng_seed") is not None:
+            self.rng_seed = int(state["bit_rng_seed"])
+        if self.dense_opt is not None and state.get("dense") is not None:
+            self.dense_opt.load_state_dict(state["dense"])

@@ -161,3 +161,83 @@ def test_zero1_matches_unsharded_oracle(tmp_path):
         np.testing.assert_array_equal(got["m_q"].numpy(), st["m_q"])
         np.testing.assert_array_equal(got["r_absmax"].numpy(), st["r_absmax"])
         assert got["step"] == st["step"]
+
+
+def _run_resume(rank, world, port, out_dir, save_world):
+    """Steps 0-1 at world size ``save_world`` are taken from a checkpoint written by a run
+    of that size; this run (``world`` ranks) loads it and takes step 2."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+    from firefly_b200.distributed import ZeroFireFlyOptim
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE
+
+    mods = _make_modules()
+    ckpt = torch.load(os.path.join(out_dir, f"mid_world{save_world}.pt"), weights_only=False)
+    with torch.no_grad():
+        for m, q in zip(mods, ckpt["q"]):
+            m.int_weight.copy_(q)
+    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=0, update_fn=None)
+    # the checkpoint's handles are the modules' handles of the saving run, in module order
+    state = ckpt["opt"]
+    handles = sorted(state["bit_state"])
+    state = dict(state, bit_state={m._registered_handle: state["bit_state"][h] for m, h in zip(mods, handles)})
+    opt.load_state_dict(state)
+    calls = []
+    opt.update_fn = _oracle_update(calls, opt.rng_seed)
+    for m, g in zip(mods, _grads(2)):
+        _BIT_GRAD_CACHE[m._registered_handle] = g.clone()
+    opt.step()
+    bits = opt.gather_bit_state()
+    if rank == 0:
+        torch.save({"q": [m.int_weight.clone() for m in mods], "bits": bits},
+                   os.path.join(out_dir, f"resumed_{save_world}_to_{world}.pt"))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _run_save_mid(rank, world, port, out_dir):
+    """Two steps, then the optimizer's state_dict (collective) saved by rank 0."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+    from firefly_b200.distributed import ZeroFireFlyOptim
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE
+
+    mods = _make_modules()
+    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update([], SEED))
+    for step in range(2):
+        for m, g in zip(mods, _grads(step)):
+            if step == 1 and m is mods[3]:
+                continue
+            _BIT_GRAD_CACHE[m._registered_handle] = g.clone()
+        opt.step()
+    state = opt.state_dict()
+    if rank == 0:
+        torch.save({"q": [m.int_weight.clone() for m in mods], "opt": state},
+                   os.path.join(out_dir, f"mid_world{world}.pt"))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_zero1_checkpoint_resume_across_world_sizes(tmp_path):
+    """A ZeRO-1 checkpoint (gathered into the reference bit_state layout) resumes at another
+    world size: save after two steps at world 1 and at world 2, resume each at the other size
+    for the third step, and compare with the uninterrupted three-step run."""
+    _run(0, 1, _free_port(), str(tmp_path))
+    _run_save_mid(0, 1, _free_port(), str(tmp_path))
+    mp.start_processes(_run_save_mid, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_run_resume, args=(2, _free_port(), str(tmp_path), 1), nprocs=2, start_method="spawn")
+    _run_resume(0, 1, _free_port(), str(tmp_path), 2)
+    full = torch.load(tmp_path / "world1.pt", weights_only=False)
+    for name in ("resumed_1_to_2.pt", "resumed_2_to_1.pt"):
+        res = torch.load(tmp_path / name, weights_only=False)
+        for a, b in zip(full["q"], res["q"]):
+            assert torch.equal(a, b), name
+        for hf, hr in zip(sorted(full["bits"]), sorted(res["bits"])):
+            for k, v in full["bits"][hf].items():
+                w = res["bits"][hr][k]
+                assert (torch.equal(v, w) if torch.is_tensor(v) else v == w), (name, k)
