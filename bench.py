@@ -477,7 +477,8 @@ def main():
         if world > 1:
             dist.barrier()
 
-    for i in range(max(args.warmup, 3)):
+    nwarm = max(args.warmup, 3)
+    for i in range(nwarm):
         step(xs[i % 2], dy)
     torch.cuda.synchronize()
     assert _capi.device_status() == 0
@@ -494,7 +495,7 @@ def main():
     clocks.mark()
     t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0e.record()
-    for i in range(args.steps):
+    for i in range(nwarm, nwarm + args.steps):
         step(xs[i % 2], dy)
     t1e.record()
     torch.cuda.synchronize()
