@@ -291,7 +291,7 @@ struct SwigluBwdSrc {
   static constexpr int NOUT = 2;
   static constexpr bool kPreloadBoth = false;
   static constexpr bool kStore = true;  // pass A writes [dg | du] (bf16) for pass B
-  static constexpr int kMinBlocks = 2;
+  static constexpr int kMinBlocks = 3;
   static constexpr int kRowsInFlight = 2;
   static constexpr bool kWords = true;
   const __nv_bfloat16* dh;  // [rows, ldh]
