@@ -58,7 +58,7 @@ def parse_args():
     ap.add_argument("--no-sub", action="store_true", help="skip the GEMM sweep and the AdamW sub-benchmarks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
-                                              "mlp"],
+                                              "swiglu_gemm", "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -99,6 +99,11 @@ def kernel_case(args):
         else:
             dh = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
             _capi.swiglu_bwd_quant(dh, gu, colmul=torch.rand(2 * 11008, device=dev) * 1e-3)
+    elif args.kernel_case == "swiglu_gemm":  # gate/up GEMM with h = silu(g) * u in its epilogue
+        a = torch.randint(-127, 128, (8192, 4096), dtype=torch.int8, device=dev, generator=g)
+        w = torch.randint(-127, 128, (2 * 11008, 4096), dtype=torch.int8, device=dev, generator=g)
+        sa, sb = torch.rand(8192, device=dev) * 1e-2, torch.rand(2 * 11008, device=dev) * 1e-3
+        _capi.swiglu_gemm(a, w, 4096, sa, sb)
     elif args.kernel_case == "mlp":
         # two training steps of the benchmark block; profile the second (skip the first's launches)
         from firefly_b200.distributed import ZeroFireFlyOptim

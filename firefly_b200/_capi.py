@@ -45,6 +45,8 @@ SIGNATURES = {
     "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_swiglu_selftest": (_I, [_P, _P, _P]),
+    "ff_swiglu_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _F, _P, _I64,
+                               _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_quant_i8": (_I, [_P, _P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_bwd_quant_i8": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _I64, _P, _P,
                                     _I64, _P, _P, _P]),
@@ -66,6 +68,7 @@ LAUNCHES = 0
 GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
+                     "ff_swiglu_gemm_i8": 2,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
 
@@ -276,6 +279,39 @@ def swiglu_quant(gu: torch.Tensor, eps: float = 1e-8, rows: bool = True, cols: b
         _call("ff_swiglu_quant_i8", _ptr(gu), _ptr(u), ld, T, F, float(eps), _ptr(h), ldh, _ptr(q_rows), ldq,
               _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols), _ptr(ws), _stream(dev))
     return q_rows, s_rows, q_cols, s_cols, h[:, :F]
+
+
+def swiglu_gemm(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                bias: torch.Tensor | None = None, eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """Gate/up GEMM of a SwiGLU block with h = silu(g) * u in its epilogue.
+
+    ``a``: int8 activation codes ``[T, lda]``, ``b``: int8 weight ``[2F, ldb]`` (gate rows, then
+    up rows), contraction over the first ``k`` columns.  Returns ``(gu, q_rows, s_rows,
+    q_cols_t, s_cols, h)``: gu = ``[g | u]`` bf16 ``[T, 2F]`` as ``gemm_i8`` gives it, and the
+    outputs of ``swiglu_quant(gu)``."""
+    dev = _require_cuda(a, b, scale_a, scale_b, bias)
+    _require_swiglu_math(dev)
+    a, lda = _rows_view(a)
+    b, ldb = _rows_view(b)
+    T, F2 = a.shape[0], b.shape[0]
+    F = F2 // 2
+    ldq, ldqt = round_up(F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((F,), dtype=torch.float32, device=dev)
+    gu = torch.empty((T, F2), dtype=torch.bfloat16, device=dev)
+    h = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + F,), dtype=torch.float32, device=dev)
+    f32 = [None if t is None else t.to(torch.float32).contiguous() for t in (scale_a, scale_b, bias)]
+    with torch.cuda.device(dev):
+        _call("ff_swiglu_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(f32[0]), _ptr(f32[1]), _ptr(f32[2]),
+              _ptr(gu), F2, _ptr(h), F, T, F, int(k), float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols),
+              ldqt, _ptr(s_cols), _ptr(ws), _stream(dev))
+    return gu, q_rows, s_rows, q_cols, s_cols, h
 
 
 def swiglu_bwd_quant(dh: torch.Tensor, gu: torch.Tensor, colmul: torch.Tensor | None = None,

@@ -184,7 +184,21 @@ struct EpiParams {
   int64_t ldd;
   int64_t M, N;
   int vec;  // 16-byte vector stores allowed
+  // SwiGLU forward epilogue only: h = silu(g) * u (bf16, leading dim ldh), F features,
+  // row / column absmax of h (float bits, atomicMax)
+  __nv_bfloat16* h;
+  int64_t ldh;
+  int64_t F;
+  uint32_t* row_amax;
+  uint32_t* col_amax;
 };
+
+// Epilogue kind of the gate/up GEMM of a SwiGLU block (not an FF_OUT_* value): the CTA
+// pair's 256 tile columns are 128 gate features and the same 128 up features; the
+// epilogue writes g and u (bf16, as FF_OUT_BF16 would) and h = silu(g) * u with the row
+// and column absmax of h, i.e. the first pass of the dual quantiser of h.
+constexpr int kOutSwigluFwd = 16;
+constexpr int kSwigluFeat = 128;  // features per tile
 
 template <int OUT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_t row, int64_t col0,
@@ -273,6 +287,104 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
 }
 
 // BMN: B is given MN-major (a K x N row-major matrix) instead of K-major (N x K)
+// 32 features of the SwiGLU forward epilogue for one row (one thread): accumulators of the
+// gate (ag) and up (au) columns -> g, u (bf16, stored at columns fb and F + fb of D), h (stored
+// at column fb of h); folds |h| into the row maximum rmax (bf16x2 word) and the column maxima
+// (a reduce-scatter over the warp's 32 rows, then one atomicMax per lane).
+// `cb` points at this chunk's entries of the warp's staged buffer: gate scales at [0, 32),
+// up scales at [64, 96), gate bias at [128, 160), up bias at [192, 224).
+__device__ __forceinline__ void swiglu_fwd_chunk(const uint32_t (&ag)[32], const uint32_t (&au)[32], int64_t row,
+                                                 int64_t fb, const EpiParams& p, float sa, int lane,
+                                                 const float* cb, uint32_t& rmax) {
+  const bool live = row < p.M;
+  float sg[32], su[32], bg[32], bu[32];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {  // shared-memory broadcasts: every lane reads the same values
+    const float4 a = *reinterpret_cast<const float4*>(cb + j);
+    const float4 b = *reinterpret_cast<const float4*>(cb + 64 + j);
+    sg[j] = a.x; sg[j + 1] = a.y; sg[j + 2] = a.z; sg[j + 3] = a.w;
+    su[j] = b.x; su[j + 1] = b.y; su[j + 2] = b.z; su[j + 3] = b.w;
+    if (p.bias) {
+      const float4 c = *reinterpret_cast<const float4*>(cb + 128 + j);
+      const float4 d = *reinterpret_cast<const float4*>(cb + 192 + j);
+      bg[j] = c.x; bg[j + 1] = c.y; bg[j + 2] = c.z; bg[j + 3] = c.w;
+      bu[j] = d.x; bu[j + 1] = d.y; bu[j + 2] = d.z; bu[j + 3] = d.w;
+    }
+  }
+  // g and u exactly as the FF_OUT_BF16 epilogue forms them: ((acc * sa) * sb) (+ bias) -> bf16
+  uint32_t wg[16], wu[16], wh[16];
+  const f2 sa2 = splat(sa);
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    f2 vg = mul2(mk2(__int2float_rn((int)ag[2 * q]), __int2float_rn((int)ag[2 * q + 1])), sa2);
+    f2 vu = mul2(mk2(__int2float_rn((int)au[2 * q]), __int2float_rn((int)au[2 * q + 1])), sa2);
+    vg = mul2(vg, mk2(sg[2 * q], sg[2 * q + 1]));
+    vu = mul2(vu, mk2(su[2 * q], su[2 * q + 1]));
+    if (p.bias) {
+      vg = add2(vg, mk2(bg[2 * q], bg[2 * q + 1]));
+      vu = add2(vu, mk2(bu[2 * q], bu[2 * q + 1]));
+    }
+    wg[q] = pack_bf16x2(vg);
+    wu[q] = pack_bf16x2(vu);
+  }
+  // h = bf16(bf16(silu(g)) * u), branch-free, with the IEEE operations for inputs outside the
+  // fast path's range
+  bool rare = false;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const SwigluMath2 m = swiglu_fast2(__uint_as_float(wg[q] << 16), __uint_as_float(wg[q] & 0xFFFF0000u), rare);
+    wh[q] = pack_bf16x2(mul2(unpack_bf16x2(pack_bf16x2(m.q)), unpack_bf16x2(wu[q])));
+  }
+  if (__builtin_expect(rare, 0)) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) wh[q] = swiglu_h_exact_word(wg[q], wu[q]);
+  }
+  if (live) {
+    __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + fb;
+    __nv_bfloat16* dh = p.h + row * p.ldh + fb;
+#pragma unroll
+    for (int q = 0; q < 16; q += 4) {
+      *reinterpret_cast<uint4*>(dg + 2 * q) = make_uint4(wg[q], wg[q + 1], wg[q + 2], wg[q + 3]);
+      *reinterpret_cast<uint4*>(dg + p.F + 2 * q) = make_uint4(wu[q], wu[q + 1], wu[q + 2], wu[q + 3]);
+      *reinterpret_cast<uint4*>(dh + 2 * q) = make_uint4(wh[q], wh[q + 1], wh[q + 2], wh[q + 3]);
+    }
+  }
+  // maxima of |h| (rows past M hold no data: excluded)
+  uint32_t a[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    a[q] = live ? abs_bf16x2(wh[q]) : 0u;
+    rmax = max_bf16x2(rmax, a[q]);
+  }
+  // reduce-scatter over the 32 lanes: after the rounds lane l holds the maximum of feature fb + l
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const bool up = lane & 16;
+    const uint32_t send = up ? a[q] : a[q + 8], keep = up ? a[q + 8] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const bool up = lane & 8;
+    const uint32_t send = up ? a[q] : a[q + 4], keep = up ? a[q + 4] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool up = lane & 4;
+    const uint32_t send = up ? a[q] : a[q + 2], keep = up ? a[q + 2] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  {
+    const bool up = lane & 2;
+    const uint32_t send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
+    a[0] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  }
+  a[0] = max_bf16x2(a[0], __shfl_xor_sync(0xffffffffu, a[0], 1));  // word (lane >> 1) & 15, all 32 rows
+  const uint32_t bits = (lane & 1) ? (a[0] & 0xFFFF0000u) : (a[0] << 16);
+  atomicMax(p.col_amax + fb + lane, bits);
+}
+
 template <int OUT, int BN_, int STAGES_, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
@@ -478,6 +590,20 @@ constexpr int C2_A_BYTES = C2_BM * BK;      // 16 KiB
 constexpr int C2_B_BYTES = C2_BN_CTA * BK;  // 16 KiB
 constexpr int C2_STAGE_BYTES = C2_A_BYTES + C2_B_BYTES;
 constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
+// SwiGLU epilogue: per epilogue warp, two buffers (by accumulator) of the column scales and
+// bias of its 64 features: gate scales, up scales, gate bias, up bias (4 x 64 floats)
+constexpr int C2_SW_BUF_FLOATS = 2 * kSwigluFeat;  // per warp and buffer: its 64 features x 4 arrays
+constexpr int C2_SMEM_BYTES_SW = C2_SMEM_BYTES + 8 * 2 * C2_SW_BUF_FLOATS * 4;
+template <int OUT>
+__host__ __device__ constexpr int c2_smem_bytes() {
+  return OUT == kOutSwigluFwd ? C2_SMEM_BYTES_SW : C2_SMEM_BYTES;
+}
+// threads of the 2-CTA kernel: TMA warp, MMA warp, then 4 epilogue warps (8 for the SwiGLU
+// epilogue: two per TMEM lane quarter, each on half of the tile's features)
+template <int OUT>
+__host__ __device__ constexpr int c2_threads() {
+  return OUT == kOutSwigluFwd ? 320 : NUM_THREADS;
+}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -528,7 +654,7 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 }
 
 template <int OUT, bool BMN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
                         int tiles_m, int tiles_n, EpiParams ep) {
   extern __shared__ uint8_t smem_raw[];
@@ -564,7 +690,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < ACC_STAGES; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 8);
+      mbar_init(tempty_bar(a), 2 * (c2_threads<OUT>() / 32 - 2));  // the pair's epilogue warps
     }
     mbar_init(drain, 1);
     mbar_init(done_bar, 1);
@@ -601,7 +727,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t lbar = mapa_shared(full_bar(stage), 0);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C2_STAGE_BYTES);
           tma_load_2d_pair(sA + stage * C2_A_BYTES, &tmA, kb * BK, tm * (2 * C2_BM) + (int)rank * C2_BM, lbar);
-          if constexpr (!BMN) {
+          if constexpr (OUT == kOutSwigluFwd) {  // gate rows of the tile's features, then the up rows
+            tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK,
+                             tn * kSwigluFeat + (rank ? (int)ep.F : 0), lbar);
+          } else if constexpr (!BMN) {
             tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK, tn * C2_BN + (int)rank * C2_BN_CTA, lbar);
           } else {  // this CTA's 128 columns of B: 128 k rows x 128 N bytes
             tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, tn * C2_BN + (int)rank * C2_BN_CTA, kb * BK, lbar);
@@ -659,28 +788,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
-    const int lg = warp & 3;
+    const int lg = warp & 3;           // TMEM lane quarter
+    const int eh = (warp - 2) >> 2;    // SwiGLU: which half of the tile's features (0 or 1)
     int acc = 0;
     uint32_t acc_phase = 0;
+    // SwiGLU: this warp's two staging buffers of its features' column scales and bias
+    float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
     for (int t = pair; t < total_tiles; t += num_pairs) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
+      float4 st_s, st_b;  // loaded before the accumulator wait, stored after it
+      if constexpr (OUT == kOutSwigluFwd) {
+        // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
+        const int64_t col = (int64_t)(lane >> 4) * ep.F + (int64_t)tn * kSwigluFeat + eh * 64 + (lane & 15) * 4;
+        st_s = ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        st_b = ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
+      if constexpr (OUT == kOutSwigluFwd) {
+        float* buf = sw_buf + acc * C2_SW_BUF_FLOATS;
+        reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
+        reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
+        __syncwarp();
+      }
       const int64_t row = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
       float sa = 1.f;
       if constexpr (OUT != FF_OUT_S32) {
         if (ep.scale_a && row < ep.M) sa = __ldg(ep.scale_a + row);
       }
       const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(acc * C2_BN);
-      const int64_t ncol_tile = min64(C2_BN, ep.N - (int64_t)tn * C2_BN);
+      if constexpr (OUT == kOutSwigluFwd) {
+        uint32_t rmax = 0u;
 #pragma unroll 1
-      for (int c = 0; c < C2_BN / 32; ++c) {
-        if ((int64_t)c * 32 >= ncol_tile) break;
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        tmem_wait_ld();
-        epilogue_chunk<OUT>(r, row, (int64_t)tn * C2_BN + c * 32, ep, sa, lane);
+        for (int c = 0; c < 2; ++c) {  // this warp's 64 features: two chunks of 32
+          const int fc = eh * 64 + c * 32;
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tbase + fc, rg);
+          tmem_ld32(tbase + kSwigluFeat + fc, ru);
+          tmem_wait_ld();
+          swiglu_fwd_chunk(rg, ru, row, (int64_t)tn * kSwigluFeat + fc, ep, sa, lane,
+                           sw_buf + acc * C2_SW_BUF_FLOATS + c * 32, rmax);
+        }
+        if (row < ep.M)
+          atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
+                                                               __uint_as_float(rmax & 0xFFFF0000u))));
+      } else {
+        const int64_t ncol_tile = min64(C2_BN, ep.N - (int64_t)tn * C2_BN);
+#pragma unroll 1
+        for (int c = 0; c < C2_BN / 32; ++c) {
+          if ((int64_t)c * 32 >= ncol_tile) break;
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_wait_ld();
+          epilogue_chunk<OUT>(r, row, (int64_t)tn * C2_BN + c * 32, ep, sa, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -778,15 +940,15 @@ inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     FF_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_2cta_kernel<OUT, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C2_SMEM_BYTES),
+                                     c2_smem_bytes<OUT>()),
                 "ff_gemm_i8 2-CTA smem attribute");
     attr_set[dev] = true;
   }
   const int pairs = min(tiles_m * tiles_n, max_pairs);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
-  cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = C2_SMEM_BYTES;
+  cfg.blockDim = dim3(c2_threads<OUT>());
+  cfg.dynamicSmemBytes = c2_smem_bytes<OUT>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -853,7 +1015,7 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
   int rc = make_map(&ma, A, M, K, lda, BM);
   if (rc) return rc;
   const int es = (out_kind == FF_OUT_BF16 || out_kind == FF_OUT_BF16_ACCUM) ? 2 : 4;
-  EpiParams ep;
+  EpiParams ep{};
   ep.scale_a = scale_a;
   ep.scale_b = scale_b;
   ep.bias = bias;
@@ -932,6 +1094,62 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
                           int64_t N, int64_t K, void* stream) {
   return ff::gemm::gemm_dispatch<false>("ff_gemm_i8", A, lda, B, ldb, scale_a, scale_b, bias, D, ldd, out_kind, M, N,
                                         K, stream);
+}
+
+extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                                 const float* scale_b, const float* bias, uint16_t* gu, int64_t ldgu, uint16_t* h,
+                                 int64_t ldh, int64_t M, int64_t F, int64_t K, float eps, int8_t* q_rows, int64_t ldq,
+                                 float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws,
+                                 void* stream) {
+  using namespace ff;
+  using namespace ff::gemm;
+  const char* name = "ff_swiglu_gemm_i8";
+  FF_REQUIRE(M >= 0 && F >= 1 && K >= 1, FF_ERR_INVALID_ARG, "%s: M=%lld F=%lld K=%lld", name, (long long)M,
+             (long long)F, (long long)K);
+  FF_REQUIRE(F % kSwigluFeat == 0, FF_ERR_UNSUPPORTED, "%s: F=%lld must be a multiple of %d", name, (long long)F,
+             kSwigluFeat);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "%s: nothing to do", name);
+  if (M == 0) return FF_OK;
+  FF_REQUIRE(A && B && gu && h, FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE(lda >= K && ldb >= K && ldgu >= 2 * F && ldh >= F, FF_ERR_INVALID_ARG, "%s: bad leading dims", name);
+  FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
+             "%s: A/B need 16-byte alignment and lda/ldb multiples of 16", name);
+  FF_REQUIRE(aligned(gu, 16) && aligned(h, 16) && ldgu % 8 == 0 && ldh % 8 == 0, FF_ERR_UNSUPPORTED,
+             "%s: gu/h need 16-byte alignment and leading dims multiples of 8", name);
+  FF_REQUIRE((!scale_b || aligned(scale_b, 16)) && (!bias || aligned(bias, 16)), FF_ERR_UNSUPPORTED,
+             "%s: scale_b/bias need 16-byte alignment", name);
+  FF_REQUIRE(M <= (int64_t)1 << 31 && 2 * F <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
+             "%s: dimension too large", name);
+  int rc = check_dual_outputs(name, M, F, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
+  const int max_pairs = max_pairs_current();
+  FF_REQUIRE(max_pairs > 0, FF_ERR_UNSUPPORTED, "%s: the 2-CTA GEMM cannot be resident on this device", name);
+  cudaStream_t st = as_stream(stream);
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(M + F), st), name);
+  CUtensorMap ma, mb;
+  rc = make_map(&ma, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, 2 * F, K, ldb, C2_BN_CTA);
+  if (rc) return rc;
+  EpiParams ep{};
+  ep.scale_a = scale_a;
+  ep.scale_b = scale_b;
+  ep.bias = bias;
+  ep.D = gu;
+  ep.ldd = ldgu;
+  ep.M = M;
+  ep.N = 2 * F;
+  ep.vec = 1;
+  ep.h = reinterpret_cast<__nv_bfloat16*>(h);
+  ep.ldh = ldh;
+  ep.F = F;
+  ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  ep.col_amax = ep.row_amax + M;
+  const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)(F / kSwigluFeat);
+  rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(h), M, F, ldh, nullptr, eps,
+                                      q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
 }
 
 extern "C" int ff_gemm_i8_kn(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,

@@ -6,8 +6,8 @@
 
 #include "ff_common.cuh"
 #include "ff_dqt_adamw8.cuh"
-#include "ff_gemm_i8.cuh"
 #include "ff_quant.cuh"
+#include "ff_gemm_i8.cuh"
 
 #ifndef FF_VERSION_STRING
 #define FF_VERSION_STRING "firefly_b200 0.1.0 sm_100a"

@@ -215,6 +215,27 @@ __device__ __forceinline__ float swiglu_dg(const SwigluMath& m, float x, float d
 }
 __device__ __forceinline__ float swiglu_du(const SwigluMath& m, float dh) { return bf16r(__fmul_rn(dh, bf16r(m.q))); }
 
+// The IEEE path for one bf16x2 word of inputs (called only when an input is outside the fast
+// path's range; kept out of line so that the callers' arrays stay in registers)
+__device__ __noinline__ uint32_t swiglu_h_exact_word(uint32_t gw, uint32_t uw) {
+  const float h0 = swiglu_h(swiglu_exact(__uint_as_float(gw << 16)), __uint_as_float(uw << 16));
+  const float h1 = swiglu_h(swiglu_exact(__uint_as_float(gw & 0xFFFF0000u)), __uint_as_float(uw & 0xFFFF0000u));
+  return pack_bf16x2(mk2(h0, h1));
+}
+__device__ __noinline__ uint2 swiglu_bwd_exact_word(uint32_t gw, uint32_t dw, uint32_t uw) {
+  float dg[2], du[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float x = __uint_as_float(k ? (gw & 0xFFFF0000u) : (gw << 16));
+    const float d = __uint_as_float(k ? (dw & 0xFFFF0000u) : (dw << 16));
+    const float u = __uint_as_float(k ? (uw & 0xFFFF0000u) : (uw << 16));
+    const SwigluMath m = swiglu_exact(x);
+    dg[k] = swiglu_dg(m, x, d, u);
+    du[k] = swiglu_du(m, d);
+  }
+  return make_uint2(pack_bf16x2(mk2(dg[0], dg[1])), pack_bf16x2(mk2(du[0], du[1])));
+}
+
 // every bf16 bit pattern x: fast path (where it applies) against the IEEE operations;
 // counts[0] = mismatches, counts[1] = inputs routed to the IEEE path, counts[2] = smallest
 // mismatching bf16 bit pattern (0xFFFFFFFF if none)
@@ -273,12 +294,8 @@ struct SwigluSrc {
       w[0][p] = pack_bf16x2(mul2(unpack_bf16x2(pack_bf16x2(m.q)), unpack_bf16x2(r.u.word(p))));
     }
     if (__builtin_expect(rare, 0)) {
-#pragma unroll 1
-      for (int p = 0; p < 4; ++p) {
-        const float h0 = swiglu_h(swiglu_exact(r.g.get(2 * p)), r.u.get(2 * p));
-        const float h1 = swiglu_h(swiglu_exact(r.g.get(2 * p + 1)), r.u.get(2 * p + 1));
-        w[0][p] = pack_bf16x2(mk2(h0, h1));
-      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) w[0][p] = swiglu_h_exact_word(r.g.word(p), r.u.word(p));
     }
   }
 };
@@ -328,18 +345,11 @@ struct SwigluBwdSrc {
       w[1][p] = pack_bf16x2(mul2(d, unpack_bf16x2(pack_bf16x2(m.q))));
     }
     if (__builtin_expect(rare, 0)) {
-#pragma unroll 1
+#pragma unroll
       for (int p = 0; p < 4; ++p) {
-        float dg[2], du[2];
-        for (int k = 0; k < 2; ++k) {
-          const int j = 2 * p + k;
-          const float x = r.g.get(j), d = r.dh.get(j);
-          const SwigluMath m = swiglu_exact(x);
-          dg[k] = swiglu_dg(m, x, d, r.u.get(j));
-          du[k] = swiglu_du(m, d);
-        }
-        w[0][p] = pack_bf16x2(mk2(dg[0], dg[1]));
-        w[1][p] = pack_bf16x2(mk2(du[0], du[1]));
+        const uint2 e = swiglu_bwd_exact_word(r.g.word(p), r.dh.word(p), r.u.word(p));
+        w[0][p] = e.x;
+        w[1][p] = e.y;
       }
     }
   }

@@ -10,8 +10,9 @@ harness for its SwiGLU-MLP configuration (d_model 4096, ffn 11008).
 composition ``down(F.silu(g) * u)`` of two BitLinear layers and torch's elementwise
 ops computes, with the elementwise work moved into the quantisers:
 
-* forward: ``ff_swiglu_quant_i8`` computes ``h = silu(g) * u`` from the gate/up GEMM
-  output in the quantiser's absmax pass (one read of g and u) and quantises it;
+* forward: ``ff_swiglu_gemm_i8`` computes ``h = silu(g) * u`` and its absmax in the gate/up
+  GEMM's epilogue and quantises h (f a multiple of 128; otherwise ``ff_swiglu_quant_i8``
+  computes h from the GEMM output in the quantiser's absmax pass);
 * backward: ``ff_swiglu_bwd_quant_i8`` forms ``[dg | du]`` from ``dh``, g and u in the
   absmax pass of the gate/up projection's operand quantiser, and ``dX`` is one GEMM
   over ``K = 2f``.
@@ -57,9 +58,12 @@ class SwiGLUMLPFn(torch.autograd.Function):
         saved = (None, None, None, None, None)
         if T > 0:
             q_x, s_x, q_xt, s_xc = _quantize_activation(x, with_cols=need_grad)
-            gu = _capi.gemm_i8(q_x, _weight_operand(gu_handle, gu_weight), K, scale_a=s_x,
-                               scale_b=gu_ws, out_kind=_capi.FF_OUT_BF16)
-            q_h, s_h, q_ht, s_hc, _ = _capi.swiglu_quant(gu, cols=need_grad)
+            w_gu = _weight_operand(gu_handle, gu_weight)
+            if Fh % 128 == 0:  # h and its absmax come out of the gate/up GEMM's epilogue
+                gu, q_h, s_h, q_ht, s_hc, _ = _capi.swiglu_gemm(q_x, w_gu, K, s_x, gu_ws, cols=need_grad)
+            else:
+                gu = _capi.gemm_i8(q_x, w_gu, K, scale_a=s_x, scale_b=gu_ws, out_kind=_capi.FF_OUT_BF16)
+                q_h, s_h, q_ht, s_hc, _ = _capi.swiglu_quant(gu, cols=need_grad)
             _capi.gemm_i8(q_h, _weight_operand(d_handle, d_weight), Fh, scale_a=s_h, scale_b=d_ws,
                           bias=b, out_kind=_capi.FF_OUT_BF16, out=y)
             if need_grad:

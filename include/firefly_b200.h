@@ -157,6 +157,25 @@ FF_API int ff_swiglu_quant_i8(const uint16_t* g, const uint16_t* u, int64_t ld, 
                               int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws, void* stream);
 
 /*
+ * The gate/up GEMM of a SwiGLU block with the activation and the first pass of its
+ * quantiser in the GEMM epilogue.  B: int8 [2F, K] (leading dim ldb): the F gate rows
+ * then the F up rows of one BitLinear d -> 2F; A: int8 activation codes [M, K].
+ * Writes gu = [g | u] (bf16 [M, 2F], leading dim ldgu), exactly as ff_gemm_i8 with
+ * FF_OUT_BF16 would (scale_a per row, scale_b per column of gu, optional bias), and
+ * h = bf16(bf16(silu(g)) * u) (bf16 [M, F], leading dim ldh) as ff_swiglu_quant_i8
+ * computes it, then quantises h exactly as ff_swiglu_quant_i8 does (outputs as
+ * ff_quant_dual_i8, no colmul; absmax_ws M + F floats).  Two kernels (the GEMM and the
+ * quantiser pass) instead of three.  F must be a multiple of 128; gu, h, scale_b and
+ * bias 16-byte aligned, ldgu and ldh multiples of 8.  Requires a passing
+ * ff_swiglu_selftest on the device.
+ */
+FF_API int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                             const float* scale_b, const float* bias, uint16_t* gu, int64_t ldgu, uint16_t* h,
+                             int64_t ldh, int64_t M, int64_t F, int64_t K, float eps, int8_t* q_rows, int64_t ldq,
+                             float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws,
+                             void* stream);
+
+/*
  * Backward of the SwiGLU activation fused with the dual quantiser of the gate/up
  * projection's output gradient.  With dh the gradient of h (bf16, leading dim ldh)
  * and g, u as in ff_swiglu_quant_i8, the gradient of the [rows, 2*cols] projection

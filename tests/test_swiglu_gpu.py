@@ -107,6 +107,53 @@ def test_swiglu_bwd_quant_matches_torch_autograd(T, Fh, colmul):
     assert _capi.device_status() == 0
 
 
+@pytest.mark.parametrize("T,F,K", [(256, 256, 512), (37, 128, 64), (300, 384, 1000), (1024, 1408, 4096),
+                                   (1, 128, 16)])
+def test_swiglu_gemm_epilogue_matches_gemm_then_quantiser(T, F, K):
+    """The gate/up GEMM with h in its epilogue equals ff_gemm_i8 (bf16 out) followed by
+    ff_swiglu_quant_i8, bit for bit: gu, h and all codes and scales."""
+    gen = torch.Generator(device=DEV).manual_seed(T + F + K)
+    ldk = _capi.round_up(K, 16)
+    a = torch.zeros(T, ldk, dtype=torch.int8, device=DEV)
+    a[:, :K] = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=DEV, generator=gen)
+    w = torch.zeros(2 * F, ldk, dtype=torch.int8, device=DEV)
+    w[:, :K] = torch.randint(-127, 128, (2 * F, K), dtype=torch.int8, device=DEV, generator=gen)
+    sa = torch.rand(T, device=DEV, generator=gen) * 2e-2 + 1e-3
+    sb = torch.rand(2 * F, device=DEV, generator=gen) * 2e-3 + 1e-4
+    gu_ref = _capi.gemm_i8(a, w, K, scale_a=sa, scale_b=sb, out_kind=_capi.FF_OUT_BF16)
+    want = _capi.swiglu_quant(gu_ref)
+    gu, *got = _capi.swiglu_gemm(a, w, K, sa, sb)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bf16_bits(gu), bf16_bits(gu_ref), err_msg="gu")
+    np.testing.assert_array_equal(bf16_bits(got[4]), bf16_bits(want[4]), err_msg="h")
+    _assert_same(got[:4], want[:4], f"T={T} F={F} K={K}")
+    # row codes only (the forward without gradient)
+    _, q, s_, qt, st, _ = _capi.swiglu_gemm(a, w, K, sa, sb, cols=False)
+    assert qt is None
+    np.testing.assert_array_equal(q.cpu().numpy(), want[0].cpu().numpy())
+    assert _capi.device_status() == 0
+
+
+def test_swiglu_gemm_with_bias_and_extreme_gates():
+    """Bias in the epilogue, and gate values beyond the fast path's range (IEEE fallback)."""
+    T, F, K = 128, 128, 64
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    a = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=DEV, generator=gen)
+    w = torch.randint(-127, 128, (2 * F, K), dtype=torch.int8, device=DEV, generator=gen)
+    sa = torch.rand(T, device=DEV, generator=gen) * 1e-1
+    sb = torch.rand(2 * F, device=DEV, generator=gen) * 1e-1
+    sb[:F:7] *= 100.0  # some gate columns reach |g| > 87
+    bias = torch.randn(2 * F, device=DEV, generator=gen)
+    gu_ref = _capi.gemm_i8(a, w, K, scale_a=sa, scale_b=sb, bias=bias, out_kind=_capi.FF_OUT_BF16)
+    assert (gu_ref[:, :F].float() < -87.4).any()
+    want = _capi.swiglu_quant(gu_ref)
+    gu, *got = _capi.swiglu_gemm(a, w, K, sa, sb, bias=bias)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bf16_bits(gu), bf16_bits(gu_ref), err_msg="gu")
+    np.testing.assert_array_equal(bf16_bits(got[4]), bf16_bits(want[4]), err_msg="h")
+    _assert_same(got[:4], want[:4], "bias")
+
+
 def test_oracle_swiglu_formulas_match_torch():
     """The oracle's restatement of torch's bf16 silu/mul and their autograd formulas."""
     T, Fh = 512, 512
@@ -150,7 +197,7 @@ def _pair(d, f, seed):
 
 @pytest.mark.parametrize("T,d,f,xdt", [(200, 256, 512, torch.bfloat16), (37, 96, 80, torch.float32),
                                        (1, 32, 16, torch.bfloat16), (50, 40, 24, torch.bfloat16),
-                                       (20, 48, 20, torch.bfloat16)])
+                                       (20, 48, 20, torch.bfloat16), (300, 64, 128, torch.float32)])
 def test_fused_mlp_matches_unfused_composition(T, d, f, xdt):
     fused, plain = _pair(d, f, seed=T + d)
     gen = torch.Generator(device=DEV).manual_seed(9)
