@@ -177,10 +177,10 @@ __device__ __forceinline__ float sqrt_nr(float x) {
 __device__ __forceinline__ float small_int_to_float(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), kMagic); }
 __device__ __forceinline__ int rne_int(float x) { return __float_as_int(__fadd_rn(x, kMagic)) - 0x4B400000; }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
+// maximum over the warp of non-negative floats: their bit patterns order like the values,
+// so one integer reduction does it
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
 
 // low bytes of four ints -> one word (byte permutes)
@@ -388,29 +388,34 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
         uj[0] = u[j0];
         uj[1] = u[j1];
       } else {
+        // u = (h + 0.5) / 65536 for the 16-bit halves h of the Philox word: 2^23 + h is built by a
+        // byte permute, and (2^23 + h) * 2^-16 + (2^-17 - 128) is exact in one FMA
         const uint32_t wd_ = rw4[pp];
-        uj[0] = __fmul_rn(__fadd_rn(__fsub_rn(__int_as_float(0x4B000000 | (wd_ & 0xFFFFu)), 8388608.f), 0.5f),
-                          1.0f / 65536.0f);
-        uj[1] = __fmul_rn(__fadd_rn(__fsub_rn(__int_as_float(0x4B000000 | (wd_ >> 16)), 8388608.f), 0.5f),
-                          1.0f / 65536.0f);
+        un2(fma2(mk2(__int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7610)),
+                     __int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7632))),
+                 splat(1.0f / 65536.0f), splat(1.0f / 131072.0f - 128.0f)),
+            uj[0], uj[1]);
       }
       const float rr[2] = {r0, r1}, aa[2] = {a0, a1}, fr[2] = {fr0, fr1}, bs[2] = {bs0, bs1};
       float dqf[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
+        // threshold frac(|r|) + tanh(a) * sr_bias * sign(r); tb * sign(r) is tb with its sign
+        // flipped for negative r (r = 0 is handled below: dq = sign(0) * ... = 0)
+        const uint32_t rsign = __float_as_uint(rr[e]) & 0x80000000u;
         float fb = fr[e];
         if (p.sr_bias != 0.f) {
-          // bias = tanh(a) * sr_bias * sign(r), sign(0) = 0
-          const float tb = rr[e] != 0.f ? __fmul_rn(tanh_approx(aa[e]), p.sr_bias) : 0.f;
-          fb = __fadd_rn(fr[e], copysignf(tb, tb * rr[e]));
+          const float tb = __fmul_rn(tanh_approx(aa[e]), p.sr_bias);
+          fb = __fadd_rn(fr[e], __uint_as_float(__float_as_uint(tb) ^ rsign));
           // tanh.approx is good to ~5e-4: near the decision use an accurate tanh
           if (fabsf(__fsub_rn(uj[e], fb)) < 2e-4f) {
-            const float tb2 = rr[e] != 0.f ? __fmul_rn(tanh_accurate(aa[e]), p.sr_bias) : 0.f;
-            fb = __fadd_rn(fr[e], copysignf(tb2, tb2 * rr[e]));
+            const float tb2 = __fmul_rn(tanh_accurate(aa[e]), p.sr_bias);
+            fb = __fadd_rn(fr[e], __uint_as_float(__float_as_uint(tb2) ^ rsign));
           }
         }
-        const float extra = (uj[e] < fb) ? 1.f : 0.f;   // u in (0,1): same as u < clamp(fb, 0, 1)
-        dqf[e] = copysignf(__fadd_rn(bs[e], extra), rr[e]);  // sign(r) * (floor|r| + extra)
+        // u in (0,1): u < fb is u < clamp(fb, 0, 1); dq = sign(r) * (floor|r| + [u < fb])
+        const bool up = (uj[e] < fb) && (rr[e] != 0.f);
+        dqf[e] = copysignf(up ? __fadd_rn(bs[e], 1.f) : bs[e], rr[e]);
       }
       qn[j0] = max(-127, min(127, q0 + rne_int(dqf[0])));
       qn[j1] = max(-127, min(127, q1 + rne_int(dqf[1])));
@@ -426,13 +431,13 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
       un2(mn[pp], a0, a1);
       xm = fmaxf(xm, fmaxf(fabsf(a0), fabsf(a1)));
       un2(vn[pp], a0, a1);
-      xv = fmaxf(xv, fmaxf(a0, a1));
+      xv = fmaxf(xv, fmaxf(fabsf(a0), fabsf(a1)));  // v >= 0; |.| turns -0 into +0
       un2(rn[pp], a0, a1);
       xr = fmaxf(xr, fmaxf(fabsf(a0), fabsf(a1)));
     }
-    xm = fmaxf(warp_max(xm), 1e-12f);
-    xv = fmaxf(warp_max(xv), 1e-12f);
-    xr = fmaxf(warp_max(xr), 1e-12f);
+    xm = fmaxf(warp_max_nonneg(xm), 1e-12f);
+    xv = fmaxf(warp_max_nonneg(xv), 1e-12f);
+    xr = fmaxf(warp_max_nonneg(xr), 1e-12f);
     const f2 ixm = splat(__frcp_rn(xm)), ixv = splat(__frcp_rn(xv)), ixr = splat(__frcp_rn(xr));
     const f2 k127 = splat(15.875f), k255 = splat(31.875f);
     int cm[8], cv[8], cr[8];
@@ -455,14 +460,15 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
           lv0, lv1);
       // rounding with +128 folded into the magic add
       float s0, s1;
+      // the magic-number words themselves: their low byte is the code (0x4B400000 + c, 0 <= c < 256)
       un2(add2(mk2(copysignf(lm0, x0), copysignf(lm1, x1)), splat(kMagic + 128.f)), s0, s1);
-      cm[2 * pp] = __float_as_int(s0) - 0x4B400000;
-      cm[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
+      cm[2 * pp] = __float_as_int(s0);
+      cm[2 * pp + 1] = __float_as_int(s1);
       un2(add2(mk2(copysignf(lr0, y0), copysignf(lr1, y1)), splat(kMagic + 128.f)), s0, s1);
-      cr[2 * pp] = __float_as_int(s0) - 0x4B400000;
-      cr[2 * pp + 1] = __float_as_int(s1) - 0x4B400000;
-      cv[2 * pp] = __float_as_int(lv0) - 0x4B400000;
-      cv[2 * pp + 1] = __float_as_int(lv1) - 0x4B400000;
+      cr[2 * pp] = __float_as_int(s0);
+      cr[2 * pp + 1] = __float_as_int(s1);
+      cv[2 * pp] = __float_as_int(lv0);
+      cv[2 * pp + 1] = __float_as_int(lv1);
     }
     if (nvalid == 8) {
       // generic-proxy stores; the bulk copies only ever read other blocks
