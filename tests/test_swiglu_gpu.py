@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 import torch
 from torch.nn import functional as F
+from torch.nn import functional as F_
 
 from firefly_b200 import _capi
 from firefly_b200.swiglu import SwiGLUMLP
@@ -245,3 +246,45 @@ def test_fused_mlp_three_d_input_and_no_grad():
     np.testing.assert_array_equal(bf16_bits(y), bf16_bits(y2))
     with pytest.raises(ValueError):
         fused(torch.randn(3, 65, device=DEV))
+
+
+def test_full_size_fused_kernels_equal_unfused():
+    """At the benchmark's shapes (T=8192, d=4096, f=11008): the gate/up GEMM with h in its
+    epilogue equals the GEMM followed by the quantiser, and the backward quantiser equals
+    torch's autograd followed by the plain dual quantiser, bit for bit."""
+    T, Fh, K = 8192, 11008, 4096
+    gen = torch.Generator(device=DEV).manual_seed(2024)
+    a = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=DEV, generator=gen)
+    w = torch.randint(-127, 128, (2 * Fh, K), dtype=torch.int8, device=DEV, generator=gen)
+    sa = torch.rand(T, device=DEV, generator=gen) * 2e-4 + 1e-5
+    sb = torch.rand(2 * Fh, device=DEV, generator=gen) * 2e-3 + 1e-4
+    gu_ref = _capi.gemm_i8(a, w, K, scale_a=sa, scale_b=sb, out_kind=_capi.FF_OUT_BF16)
+    want = _capi.swiglu_quant(gu_ref)
+    gu, *got = _capi.swiglu_gemm(a, w, K, sa, sb)
+    assert torch.equal(gu.view(torch.int16), gu_ref.view(torch.int16))
+    assert torch.equal(got[4].view(torch.int16), want[4].view(torch.int16))
+    for x, y in zip(got[:4], want[:4]):
+        assert torch.equal(x, y)
+    del a, w, gu, got, want
+    g = gu_ref.detach().requires_grad_(True)
+    dh = torch.randn(T, Fh, device=DEV, generator=gen).to(torch.bfloat16)
+    cm = torch.rand(2 * Fh, device=DEV, generator=gen) * 1e-3
+    gg, uu = g.chunk(2, dim=1)
+    (F.silu(gg) * uu).backward(dh)
+    want = _capi.quant_dual(g.grad, row_colmul=cm)
+    got = _capi.swiglu_bwd_quant(dh, gu_ref, colmul=cm)
+    assert torch.equal(got[4].view(torch.int16), g.grad.view(torch.int16))
+    for x, y in zip(got[:4], want[:4]):
+        assert torch.equal(x, y)
+    assert _capi.device_status() == 0
+
+
+def test_fused_mlp_empty_batch():
+    fused, _ = _pair(64, 128, seed=5)
+    x = torch.zeros(0, 64, device=DEV, dtype=torch.bfloat16).requires_grad_(True)
+    y = fused(x)
+    assert y.shape == (0, 64)
+    y.sum().backward()
+    assert x.grad.shape == (0, 64)
+    gw = fused.gate_up.consume_weight_grad()
+    assert gw.shape == (256, 64) and not gw.any()
