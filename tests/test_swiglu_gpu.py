@@ -11,7 +11,6 @@ import numpy as np
 import pytest
 import torch
 from torch.nn import functional as F
-from torch.nn import functional as F_
 
 from firefly_b200 import _capi
 from firefly_b200.swiglu import SwiGLUMLP
