@@ -66,6 +66,9 @@ _lib = None
 # and an optional list that collects (start_event, end_event, ops, algorithmic bytes) per GEMM launch.
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
+# the same for the gate/up GEMM with the SwiGLU epilogue (its window includes the quantiser pass
+# over h that the call launches after the GEMM)
+FUSED_GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
                      "ff_swiglu_gemm_i8": 2,
@@ -308,9 +311,16 @@ def swiglu_gemm(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor,
     ws = torch.empty((T + F,), dtype=torch.float32, device=dev)
     f32 = [None if t is None else t.to(torch.float32).contiguous() for t in (scale_a, scale_b, bias)]
     with torch.cuda.device(dev):
+        ev = None
+        if FUSED_GEMM_EVENTS is not None and T > 0:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         _call("ff_swiglu_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(f32[0]), _ptr(f32[1]), _ptr(f32[2]),
               _ptr(gu), F2, _ptr(h), F, T, F, int(k), float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols),
               ldqt, _ptr(s_cols), _ptr(ws), _stream(dev))
+        if ev is not None:
+            ev[1].record()
+            FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F2 * int(k)))
     return gu, q_rows, s_rows, q_cols, s_cols, h
 
 
