@@ -78,6 +78,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// TMA tile store shared -> global (bulk-group completion); the box is clipped at the tensor's bounds
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most one committed bulk group still reads shared memory
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// make this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -183,7 +197,8 @@ struct EpiParams {
   void* D;
   int64_t ldd;
   int64_t M, N;
-  int vec;  // 16-byte vector stores allowed
+  int vec;        // 16-byte vector stores allowed
+  int tma_store;  // bf16 output written by TMA tile stores from shared memory (2-CTA kernel)
   // SwiGLU forward epilogue only: h = silu(g) * u (bf16, leading dim ldh), F features,
   // row / column absmax of h (float bits, atomicMax)
   __nv_bfloat16* h;
@@ -287,6 +302,51 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
 }
 
 // BMN: B is given MN-major (a K x N row-major matrix) instead of K-major (N x K)
+// One 32 x 32 chunk of a bf16 output through shared memory and a TMA tile store: every lane
+// (one row of the warp's 32) converts its 32 values exactly as epilogue_chunk does, writes them
+// to a staging buffer, and lane 0 stores the box at (col0, row0).  Two staging buffers per warp
+// alternate; `n` counts the warp's stores so far.
+__device__ __forceinline__ void epilogue_chunk_tma(const uint32_t (&acc)[32], int64_t col0, int64_t row0,
+                                                   const EpiParams& p, const CUtensorMap* tmD, float sa, int lane,
+                                                   uint8_t* stage, uint32_t stage_addr, uint32_t& n) {
+  const int64_t mycol = col0 + lane;
+  float sbl = 1.f, bl = 0.f;
+  if (p.scale_b && mycol < p.N) sbl = __ldg(p.scale_b + mycol);
+  if (p.bias && mycol < p.N) bl = __ldg(p.bias + mycol);
+  uint32_t w[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    float t2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 2 * q + e;
+      float t = __int2float_rn((int)acc[j]);
+      if (p.scale_a) t = __fmul_rn(t, sa);
+      const float sb = __shfl_sync(0xffffffffu, sbl, j);
+      const float bj = __shfl_sync(0xffffffffu, bl, j);
+      if (p.scale_b) t = __fmul_rn(t, sb);
+      if (p.bias) t = __fadd_rn(t, bj);
+      t2[e] = t;
+    }
+    w[q] = pack_bf16x2(mk2(t2[0], t2[1]));
+  }
+  const uint32_t b = n & 1u;
+  if (n >= 2) {  // this buffer's previous store must have finished reading it
+    if (lane == 0) bulk_wait_read_1();
+    __syncwarp();
+  }
+  uint4* dst = reinterpret_cast<uint4*>(stage + b * 2048 + lane * 64);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmD, stage_addr + b * 2048, (int32_t)col0, (int32_t)row0);
+    bulk_commit_group();
+  }
+  ++n;
+}
+
 // 32 features of the SwiGLU forward epilogue for one row (one thread): accumulators of the
 // gate (ag) and up (au) columns -> g, u (bf16, stored at columns fb and F + fb of D), h (stored
 // at column fb of h); folds |h| into the row maximum rmax (bf16x2 word) and the column maxima
@@ -594,9 +654,11 @@ constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
 // bias of its 64 features: gate scales, up scales, gate bias, up bias (4 x 64 floats)
 constexpr int C2_SW_BUF_FLOATS = 2 * kSwigluFeat;  // per warp and buffer: its 64 features x 4 arrays
 constexpr int C2_SMEM_BYTES_SW = C2_SMEM_BYTES + 8 * 2 * C2_SW_BUF_FLOATS * 4;
+// bf16 output: per epilogue warp two 32 x 32 bf16 staging buffers for the TMA stores
+constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 4 * 2 * 2048;
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return OUT == kOutSwigluFwd ? C2_SMEM_BYTES_SW : C2_SMEM_BYTES;
+  return OUT == kOutSwigluFwd ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES);
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 4 epilogue warps (8 for the SwiGLU
 // epilogue: two per TMEM lane quarter, each on half of the tile's features)
@@ -655,8 +717,8 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 
 template <int OUT, bool BMN>
 __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
-    gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
-                        int tiles_m, int tiles_n, EpiParams ep) {
+    gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmD, int64_t K, int tiles_m, int tiles_n, EpiParams ep) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -794,6 +856,10 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     uint32_t acc_phase = 0;
     // SwiGLU: this warp's two staging buffers of its features' column scales and bias
     float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
+    // bf16 output: this warp's two TMA-store staging buffers (32 rows x 64 B each)
+    uint8_t* st_stage = ctrl + 256 + (warp - 2) * 2 * 2048;
+    const uint32_t st_stage_addr = cbase + 256 + (uint32_t)(warp - 2) * 2 * 2048;
+    uint32_t st_count = 0;
     for (int t = pair; t < total_tiles; t += num_pairs) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
@@ -841,6 +907,13 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tmem_wait_ld();
+          if constexpr (OUT == FF_OUT_BF16) {
+            if (ep.tma_store) {
+              epilogue_chunk_tma(r, (int64_t)tn * C2_BN + c * 32, row - lane, ep, &tmD, sa, lane, st_stage,
+                                 st_stage_addr, st_count);
+              continue;
+            }
+          }
           epilogue_chunk<OUT>(r, row, (int64_t)tn * C2_BN + c * 32, ep, sa, lane);
         }
       }
@@ -852,6 +925,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         acc_phase ^= 1u;
       }
     }
+    if (st_count && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -899,6 +974,20 @@ inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t col
   return FF_OK;
 }
 
+// bf16 output [rows, cols] (leading dim ld) for TMA tile stores of 32 x 32 boxes
+inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return FF_OK;
+}
+
 inline int num_sms_current() {
   static int cache[64] = {0};
   int dev = 0;
@@ -933,8 +1022,8 @@ constexpr int NARROW_BN = 64;
 constexpr int NARROW_STAGES = 8;
 
 template <int OUT, bool BMN>
-inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, int tiles_m, int tiles_n,
-                       const EpiParams& ep, int max_pairs, cudaStream_t st) {
+inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, int64_t K, int tiles_m,
+                       int tiles_n, const EpiParams& ep, int max_pairs, cudaStream_t st) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -957,7 +1046,7 @@ inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, int64_t K, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, K, tiles_m, tiles_n, ep),
+  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, md, K, tiles_m, tiles_n, ep),
               "ff_gemm_i8 2-CTA launch");
   return check_launch("ff_gemm_i8 (2-CTA)");
 }
@@ -969,11 +1058,11 @@ inline int max_pairs_current() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (!cache[dev]) {
     cudaFuncSetAttribute(gemm_i8_2cta_kernel<FF_OUT_BF16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         C2_SMEM_BYTES);
+                         c2_smem_bytes<FF_OUT_BF16>());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
     cfg.blockDim = dim3(NUM_THREADS);
-    cfg.dynamicSmemBytes = C2_SMEM_BYTES;
+    cfg.dynamicSmemBytes = c2_smem_bytes<FF_OUT_BF16>();
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -1045,11 +1134,18 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
     rc = map_b(C2_BN_CTA);
     if (rc) return rc;
     const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((N + C2_BN - 1) / C2_BN);
+    CUtensorMap md;
+    memset(&md, 0, sizeof(md));
+    if (out_kind == FF_OUT_BF16 && ep.vec) {  // 16-byte aligned output rows: TMA tile stores
+      rc = make_map_out_bf16(&md, D, M, N, ldd);
+      if (rc) return rc;
+      ep.tma_store = 1;
+    }
     switch (out_kind) {
-      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
-      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
+      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
     }
   }
   if (cost_wide <= cost_narrow) {  // 128 x 256 tiles, one CTA each
@@ -1146,7 +1242,9 @@ extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
   ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
   ep.col_amax = ep.row_amax + M;
   const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)(F / kSwigluFeat);
-  rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, K, t2m, t2n, ep, max_pairs, st);
+  CUtensorMap md;  // unused by this epilogue
+  memset(&md, 0, sizeof(md));
+  rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(h), M, F, ldh, nullptr, eps,
                                       q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
