@@ -302,6 +302,27 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
 }
 
 // BMN: B is given MN-major (a K x N row-major matrix) instead of K-major (N x K)
+// A warp's 32 x 32 bf16 box (lane = row, 16 bf16x2 words per lane) through one of its two
+// shared-memory staging buffers and a TMA tile store at (x, y); `n` counts the warp's stores.
+__device__ __forceinline__ void staged_store(const uint32_t (&w)[16], const CUtensorMap* map, int32_t x, int32_t y,
+                                             int lane, uint8_t* stage, uint32_t stage_addr, uint32_t& n) {
+  const uint32_t b = n & 1u;
+  if (n >= 2) {  // this buffer's previous store must have finished reading it
+    if (lane == 0) bulk_wait_read_1();
+    __syncwarp();
+  }
+  uint4* dst = reinterpret_cast<uint4*>(stage + b * 2048 + lane * 64);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, stage_addr + b * 2048, x, y);
+    bulk_commit_group();
+  }
+  ++n;
+}
+
 // One 32 x 32 chunk of a bf16 output through shared memory and a TMA tile store: every lane
 // (one row of the warp's 32) converts its 32 values exactly as epilogue_chunk does, writes them
 // to a staging buffer, and lane 0 stores the box at (col0, row0).  Two staging buffers per warp
@@ -330,21 +351,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const uint32_t (&acc)[32], in
     }
     w[q] = pack_bf16x2(mk2(t2[0], t2[1]));
   }
-  const uint32_t b = n & 1u;
-  if (n >= 2) {  // this buffer's previous store must have finished reading it
-    if (lane == 0) bulk_wait_read_1();
-    __syncwarp();
-  }
-  uint4* dst = reinterpret_cast<uint4*>(stage + b * 2048 + lane * 64);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    tma_store_2d(tmD, stage_addr + b * 2048, (int32_t)col0, (int32_t)row0);
-    bulk_commit_group();
-  }
-  ++n;
+  staged_store(w, tmD, (int32_t)col0, (int32_t)row0, lane, stage, stage_addr, n);
 }
 
 // 32 features of the SwiGLU forward epilogue for one row (one thread): accumulators of the
@@ -355,7 +362,9 @@ __device__ __forceinline__ void epilogue_chunk_tma(const uint32_t (&acc)[32], in
 // up scales at [64, 96), gate bias at [128, 160), up bias at [192, 224).
 __device__ __forceinline__ void swiglu_fwd_chunk(const uint32_t (&ag)[32], const uint32_t (&au)[32], int64_t row,
                                                  int64_t fb, const EpiParams& p, float sa, int lane,
-                                                 const float* cb, uint32_t& rmax) {
+                                                 const float* cb, uint32_t& rmax, const CUtensorMap* tmD,
+                                                 const CUtensorMap* tmH, uint8_t* stage, uint32_t stage_addr,
+                                                 uint32_t& nst) {
   const bool live = row < p.M;
   float sg[32], su[32], bg[32], bu[32];
 #pragma unroll
@@ -399,16 +408,11 @@ __device__ __forceinline__ void swiglu_fwd_chunk(const uint32_t (&ag)[32], const
 #pragma unroll
     for (int q = 0; q < 16; ++q) wh[q] = swiglu_h_exact_word(wg[q], wu[q]);
   }
-  if (live) {
-    __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + fb;
-    __nv_bfloat16* dh = p.h + row * p.ldh + fb;
-#pragma unroll
-    for (int q = 0; q < 16; q += 4) {
-      *reinterpret_cast<uint4*>(dg + 2 * q) = make_uint4(wg[q], wg[q + 1], wg[q + 2], wg[q + 3]);
-      *reinterpret_cast<uint4*>(dg + p.F + 2 * q) = make_uint4(wu[q], wu[q + 1], wu[q + 2], wu[q + 3]);
-      *reinterpret_cast<uint4*>(dh + 2 * q) = make_uint4(wh[q], wh[q + 1], wh[q + 2], wh[q + 3]);
-    }
-  }
+  // g, u (columns fb and F + fb of gu) and h: TMA tile stores of the warp's 32 rows (clipped at M)
+  const int32_t row0 = (int32_t)(row - lane);
+  staged_store(wg, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  staged_store(wu, tmD, (int32_t)(p.F + fb), row0, lane, stage, stage_addr, nst);
+  staged_store(wh, tmH, (int32_t)fb, row0, lane, stage, stage_addr, nst);
   // maxima of |h| (rows past M hold no data: excluded)
   uint32_t a[16];
 #pragma unroll
@@ -646,6 +650,7 @@ constexpr int C2_BM = 128;        // rows of A per CTA (256 per pair)
 constexpr int C2_BN = 256;        // columns of the pair's tile (128 rows of B per CTA)
 constexpr int C2_BN_CTA = 128;
 constexpr int C2_STAGES = 6;
+constexpr int C2_STAGES_SW = 5;  // the SwiGLU epilogue's staging buffers take one stage's space
 constexpr int C2_A_BYTES = C2_BM * BK;      // 16 KiB
 constexpr int C2_B_BYTES = C2_BN_CTA * BK;  // 16 KiB
 constexpr int C2_STAGE_BYTES = C2_A_BYTES + C2_B_BYTES;
@@ -653,9 +658,14 @@ constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
 // SwiGLU epilogue: per epilogue warp, two buffers (by accumulator) of the column scales and
 // bias of its 64 features: gate scales, up scales, gate bias, up bias (4 x 64 floats)
 constexpr int C2_SW_BUF_FLOATS = 2 * kSwigluFeat;  // per warp and buffer: its 64 features x 4 arrays
-constexpr int C2_SMEM_BYTES_SW = C2_SMEM_BYTES + 8 * 2 * C2_SW_BUF_FLOATS * 4;
+// SwiGLU: 5 stages, then 8 warps x (2 scale/bias buffers + 2 output staging buffers)
+constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 256 + 8 * 2 * C2_SW_BUF_FLOATS * 4 + 8 * 2 * 2048;
 // bf16 output: per epilogue warp two 32 x 32 bf16 staging buffers for the TMA stores
 constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 4 * 2 * 2048;
+template <int OUT>
+__host__ __device__ constexpr int c2_stages() {
+  return OUT == kOutSwigluFwd ? C2_STAGES_SW : C2_STAGES;
+}
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
   return OUT == kOutSwigluFwd ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES);
@@ -718,24 +728,26 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 template <int OUT, bool BMN>
 __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmD, int64_t K, int tiles_m, int tiles_n, EpiParams ep) {
+                        const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmH, int64_t K,
+                        int tiles_m, int tiles_n, EpiParams ep) {
+  constexpr int NST = c2_stages<OUT>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   const uint32_t sbase = raw_addr + pad;
-  const uint32_t sA = sbase;                       // C2_STAGES x C2_A_BYTES
-  const uint32_t sB = sbase + C2_STAGES * C2_A_BYTES;  // C2_STAGES x C2_B_BYTES
-  uint8_t* ctrl = smem + C2_STAGES * C2_STAGE_BYTES;
-  const uint32_t cbase = sbase + C2_STAGES * C2_STAGE_BYTES;
+  const uint32_t sA = sbase;                       // NST x C2_A_BYTES
+  const uint32_t sB = sbase + NST * C2_A_BYTES;  // NST x C2_B_BYTES
+  uint8_t* ctrl = smem + NST * C2_STAGE_BYTES;
+  const uint32_t cbase = sbase + NST * C2_STAGE_BYTES;
   auto full_bar = [&](int s) { return cbase + 8u * s; };
-  auto empty_bar = [&](int s) { return cbase + 8u * (C2_STAGES + s); };
-  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * C2_STAGES + a); };
-  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * C2_STAGES + ACC_STAGES + a); };
-  const uint32_t drain = cbase + 8u * (2 * C2_STAGES + 2 * ACC_STAGES);
+  auto empty_bar = [&](int s) { return cbase + 8u * (NST + s); };
+  auto tfull_bar = [&](int a) { return cbase + 8u * (2 * NST + a); };
+  auto tempty_bar = [&](int a) { return cbase + 8u * (2 * NST + ACC_STAGES + a); };
+  const uint32_t drain = cbase + 8u * (2 * NST + 2 * ACC_STAGES);
   const uint32_t done_bar = drain + 8u;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * C2_STAGES + 2 * ACC_STAGES + 2));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * C2_STAGES + 2 * ACC_STAGES + 2) + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8 * (2 * NST + 2 * ACC_STAGES + 2));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctrl + 8 * (2 * NST + 2 * ACC_STAGES + 2) + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -746,7 +758,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C2_STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -797,7 +809,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           } else {  // this CTA's 128 columns of B: 128 k rows x 128 N bytes
             tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, tn * C2_BN + (int)rank * C2_BN_CTA, kb * BK, lbar);
           }
-          if (++stage == C2_STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
@@ -832,7 +844,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
             tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), bdesc, idesc, (kb | k) != 0);
           }
           tc_commit_pair(empty_bar(stage));  // frees the stage in both CTAs
-          if (++stage == C2_STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
@@ -856,9 +868,11 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     uint32_t acc_phase = 0;
     // SwiGLU: this warp's two staging buffers of its features' column scales and bias
     float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
-    // bf16 output: this warp's two TMA-store staging buffers (32 rows x 64 B each)
-    uint8_t* st_stage = ctrl + 256 + (warp - 2) * 2 * 2048;
-    const uint32_t st_stage_addr = cbase + 256 + (uint32_t)(warp - 2) * 2 * 2048;
+    // this warp's two TMA-store staging buffers (32 rows x 64 B each); with the SwiGLU epilogue
+    // they follow the 8 warps' scale/bias buffers
+    constexpr uint32_t st_off = 256u + (OUT == kOutSwigluFwd ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
+    uint8_t* st_stage = ctrl + st_off + (warp - 2) * 2 * 2048;
+    const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
     for (int t = pair; t < total_tiles; t += num_pairs) {
       int tm, tn;
@@ -894,7 +908,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           tmem_ld32(tbase + kSwigluFeat + fc, ru);
           tmem_wait_ld();
           swiglu_fwd_chunk(rg, ru, row, (int64_t)tn * kSwigluFeat + fc, ep, sa, lane,
-                           sw_buf + acc * C2_SW_BUF_FLOATS + c * 32, rmax);
+                           sw_buf + acc * C2_SW_BUF_FLOATS + c * 32, rmax, &tmD, &tmH, st_stage, st_stage_addr,
+                           st_count);
         }
         if (row < ep.M)
           atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
@@ -1022,8 +1037,8 @@ constexpr int NARROW_BN = 64;
 constexpr int NARROW_STAGES = 8;
 
 template <int OUT, bool BMN>
-inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, int64_t K, int tiles_m,
-                       int tiles_n, const EpiParams& ep, int max_pairs, cudaStream_t st) {
+inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mh,
+                       int64_t K, int tiles_m, int tiles_n, const EpiParams& ep, int max_pairs, cudaStream_t st) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1046,7 +1061,7 @@ inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, md, K, tiles_m, tiles_n, ep),
+  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, md, mh, K, tiles_m, tiles_n, ep),
               "ff_gemm_i8 2-CTA launch");
   return check_launch("ff_gemm_i8 (2-CTA)");
 }
@@ -1142,10 +1157,10 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
       ep.tma_store = 1;
     }
     switch (out_kind) {
-      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
-      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
     }
   }
   if (cost_wide <= cost_narrow) {  // 128 x 256 tiles, one CTA each
@@ -1242,9 +1257,12 @@ extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
   ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
   ep.col_amax = ep.row_amax + M;
   const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)(F / kSwigluFeat);
-  CUtensorMap md;  // unused by this epilogue
-  memset(&md, 0, sizeof(md));
-  rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, md, K, t2m, t2n, ep, max_pairs, st);
+  CUtensorMap md, mh;  // gu and h, written by TMA tile stores
+  rc = make_map_out_bf16(&md, gu, M, 2 * F, ldgu);
+  if (rc) return rc;
+  rc = make_map_out_bf16(&mh, h, M, F, ldh);
+  if (rc) return rc;
+  rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, md, mh, K, t2m, t2n, ep, max_pairs, st);
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(h), M, F, ldh, nullptr, eps,
                                       q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
