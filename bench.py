@@ -633,9 +633,10 @@ def main():
                      f"being twice bf16; frac of nominal 4.5 POPS = {achieved / NOMINAL_INT8_TOPS:.3f}"
                      if achieved else ""),
             "gemm_launches": len(g_ms), "gemm_time_share": gemm_share,
-            # the gate/up GEMM runs separately, with the SwiGLU activation in its epilogue; its
-            # CUDA-event window also holds the quantiser pass over h launched by the same call
-            "fused_gate_up_gemm": ({
+            # the gate/up GEMM and the dh GEMM run separately, with the SwiGLU activation (its
+            # backward) in their epilogues; their CUDA-event windows also hold the quantiser pass
+            # over h ([dg | du]) launched by the same call
+            "swiglu_epilogue_gemms": ({
                 "launches": len(f_ms), "ms_mean": sum(f_ms) / len(f_ms),
                 "achieved_incl_quant_pass": sum(f_ops) / len(f_ops) / (sum(f_ms) / len(f_ms) / 1e3) / 1e12,
                 "unit": "TFLOP/s", "time_share": sum(f_ms) / 1e3 / sec,

@@ -45,6 +45,8 @@ SIGNATURES = {
     "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_swiglu_selftest": (_I, [_P, _P, _P]),
+    "ff_swiglu_bwd_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _F, _P,
+                                   _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _F, _P, _I64,
                                _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_quant_i8": (_I, [_P, _P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P]),
@@ -66,12 +68,12 @@ _lib = None
 # and an optional list that collects (start_event, end_event, ops, algorithmic bytes) per GEMM launch.
 LAUNCHES = 0
 GEMM_EVENTS: list | None = None
-# the same for the gate/up GEMM with the SwiGLU epilogue (its window includes the quantiser pass
-# over h that the call launches after the GEMM)
+# the same for the GEMMs with a SwiGLU epilogue (their windows include the quantiser pass that
+# the call launches after the GEMM)
 FUSED_GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
-                     "ff_swiglu_gemm_i8": 2,
+                     "ff_swiglu_gemm_i8": 2, "ff_swiglu_bwd_gemm_i8": 2,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
 
@@ -322,6 +324,44 @@ def swiglu_gemm(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor,
             ev[1].record()
             FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F2 * int(k)))
     return gu, q_rows, s_rows, q_cols, s_cols, h
+
+
+def swiglu_bwd_gemm(a: torch.Tensor, w: torch.Tensor, k: int, scale_a: torch.Tensor, gu: torch.Tensor,
+                    colmul: torch.Tensor | None = None, eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """``dh = a · w[:k]`` (w: int8 ``[k, F]`` row-major, the down projection's weight) with the
+    SwiGLU backward in the epilogue.  Returns ``swiglu_bwd_quant(dh, gu, colmul)``'s outputs
+    ``(q_rows, s_rows, q_cols_t, s_cols, dgu)`` without writing dh."""
+    dev = _require_cuda(a, w, scale_a, gu, colmul)
+    _require_swiglu_math(dev)
+    gu, ldgu, F = _swiglu_halves(gu)
+    a, lda = _rows_view(a)
+    w, ldw = _rows_view(w)
+    T = a.shape[0]
+    ldq, ldqt = round_up(2 * F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((2 * F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((2 * F,), dtype=torch.float32, device=dev)
+    dgu = torch.empty((T, 2 * F), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + 2 * F,), dtype=torch.float32, device=dev)
+    sa = scale_a.to(torch.float32).contiguous()
+    if colmul is not None:
+        colmul = colmul.to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        ev = None
+        if FUSED_GEMM_EVENTS is not None and T > 0:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        _call("ff_swiglu_bwd_gemm_i8", _ptr(a), lda, _ptr(w), ldw, _ptr(sa), _ptr(gu), ldgu, _ptr(colmul),
+              _ptr(dgu), 2 * F, T, F, int(k), float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt,
+              _ptr(s_cols), _ptr(ws), _stream(dev))
+        if ev is not None:
+            ev[1].record()
+            FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F * int(k)))
+    return q_rows, s_rows, q_cols, s_cols, dgu
 
 
 def swiglu_bwd_quant(dh: torch.Tensor, gu: torch.Tensor, colmul: torch.Tensor | None = None,

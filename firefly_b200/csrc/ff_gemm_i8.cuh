@@ -206,6 +206,11 @@ struct EpiParams {
   int64_t F;
   uint32_t* row_amax;
   uint32_t* col_amax;
+  // SwiGLU backward epilogue only: the saved gate/up output gu = [g | u] (bf16, leading dim
+  // ldg_in) and the column multipliers of the [dg | du] row quantiser (fp32 [2F], or null)
+  const __nv_bfloat16* g_in;
+  int64_t ldg_in;
+  const float* colmul;
 };
 
 // Epilogue kind of the gate/up GEMM of a SwiGLU block (not an FF_OUT_* value): the CTA
@@ -214,6 +219,12 @@ struct EpiParams {
 // and column absmax of h, i.e. the first pass of the dual quantiser of h.
 constexpr int kOutSwigluFwd = 16;
 constexpr int kSwigluFeat = 128;  // features per tile
+// Epilogue kind of the GEMM dh = dY * W_down of a SwiGLU block's backward: from the dh tile
+// and the saved g and u it forms the gradient [dg | du] of gu (bf16), writes it, and folds it
+// into the row maxima (with column multipliers) and column maxima: the first pass of the dual
+// quantiser of [dg | du].  dh itself is not written.
+constexpr int kOutSwigluBwd = 17;
+__host__ __device__ constexpr bool is_swiglu(int out) { return out == kOutSwigluFwd || out == kOutSwigluBwd; }
 
 template <int OUT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_t row, int64_t col0,
@@ -449,6 +460,116 @@ __device__ __forceinline__ void swiglu_fwd_chunk(const uint32_t (&ag)[32], const
   atomicMax(p.col_amax + fb + lane, bits);
 }
 
+// reduce-scatter of 16 bf16x2 words (32 features) over the warp's 32 rows: the maximum of
+// feature `lane` over all 32 lanes, as float bits
+__device__ __forceinline__ uint32_t warp_colmax_bits(uint32_t (&a)[16], int lane) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const bool up = lane & 16;
+    const uint32_t send = up ? a[q] : a[q + 8], keep = up ? a[q + 8] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const bool up = lane & 8;
+    const uint32_t send = up ? a[q] : a[q + 4], keep = up ? a[q + 4] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool up = lane & 4;
+    const uint32_t send = up ? a[q] : a[q + 2], keep = up ? a[q + 2] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  {
+    const bool up = lane & 2;
+    const uint32_t send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
+    a[0] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  }
+  a[0] = max_bf16x2(a[0], __shfl_xor_sync(0xffffffffu, a[0], 1));  // word (lane >> 1) & 15, all 32 rows
+  return (lane & 1) ? (a[0] & 0xFFFF0000u) : (a[0] << 16);
+}
+
+// g and u of one row's 32 features (64 B each), zeros for rows past M
+__device__ __forceinline__ void swiglu_bwd_load(const EpiParams& p, int64_t row, int64_t fb, uint4 (&gq)[4],
+                                                uint4 (&uq)[4]) {
+  if (row < p.M) {
+    const uint4* gp = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + fb);
+    const uint4* up = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + p.F + fb);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      gq[k] = __ldg(gp + k);
+      uq[k] = __ldg(up + k);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) gq[k] = uq[k] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// 32 features of the SwiGLU backward epilogue for one row (one thread): dh = bf16(acc * sa)
+// (as FF_OUT_BF16 forms it) with the row's g and u (gq, uq) gives dg = bf16(silu_backward(
+// bf16(dh * u), g)) and du = bf16(dh * bf16(silu(g))), stored by TMA at columns fb and F + fb of
+// D; folds |dg * colmul|, |du * colmul| into rmax and |dg|, |du| into the column maxima.  `cm`
+// points at this chunk's staged column multipliers: gate at [0, 32), up at [128, 160).
+__device__ __forceinline__ void swiglu_bwd_chunk(const uint32_t (&acc)[32], const uint4 (&gq)[4],
+                                                 const uint4 (&uq)[4], int64_t row, int64_t fb, const EpiParams& p,
+                                                 float sa, int lane, const float* cm, float& rmax,
+                                                 const CUtensorMap* tmD, uint8_t* stage, uint32_t stage_addr,
+                                                 uint32_t& nst) {
+  const bool live = row < p.M;
+  uint32_t gw[16], uw[16], dw[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    gw[4 * k] = gq[k].x; gw[4 * k + 1] = gq[k].y; gw[4 * k + 2] = gq[k].z; gw[4 * k + 3] = gq[k].w;
+    uw[4 * k] = uq[k].x; uw[4 * k + 1] = uq[k].y; uw[4 * k + 2] = uq[k].z; uw[4 * k + 3] = uq[k].w;
+  }
+  const f2 sa2 = splat(sa);
+#pragma unroll
+  for (int q = 0; q < 16; ++q)
+    dw[q] = pack_bf16x2(mul2(mk2(__int2float_rn((int)acc[2 * q]), __int2float_rn((int)acc[2 * q + 1])), sa2));
+  uint32_t wdg[16], wdu[16];
+  bool rare = false;
+  const f2 one = splat(1.f);
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const f2 x = unpack_bf16x2(gw[q]), d = unpack_bf16x2(dw[q]);
+    const SwigluMath2 m = swiglu_fast2(__uint_as_float(gw[q] << 16), __uint_as_float(gw[q] & 0xFFFF0000u), rare);
+    const f2 ds = unpack_bf16x2(pack_bf16x2(mul2(d, unpack_bf16x2(uw[q]))));
+    wdg[q] = pack_bf16x2(mul2(mul2(ds, m.s), fma2(x, sub2(one, m.s), one)));
+    wdu[q] = pack_bf16x2(mul2(d, unpack_bf16x2(pack_bf16x2(m.q))));
+  }
+  if (__builtin_expect(rare, 0)) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const uint2 e = swiglu_bwd_exact_word(gw[q], dw[q], uw[q]);
+      wdg[q] = e.x;
+      wdu[q] = e.y;
+    }
+  }
+  const int32_t row0 = (int32_t)(row - lane);
+  staged_store(wdg, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  staged_store(wdu, tmD, (int32_t)(p.F + fb), row0, lane, stage, stage_addr, nst);
+  uint32_t ag[16], au[16];
+  uint32_t rw = 0u;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    ag[q] = live ? abs_bf16x2(wdg[q]) : 0u;
+    au[q] = live ? abs_bf16x2(wdu[q]) : 0u;
+    if (p.colmul) {  // |v| * colmul (colmul >= 0) in fp32, as the row quantiser takes it
+      float a0, a1, b0, b1;
+      un2(mul2(unpack_bf16x2(ag[q]), mk2(cm[2 * q], cm[2 * q + 1])), a0, a1);
+      un2(mul2(unpack_bf16x2(au[q]), mk2(cm[kSwigluFeat + 2 * q], cm[kSwigluFeat + 2 * q + 1])), b0, b1);
+      rmax = fmaxf(rmax, fmaxf(fmaxf(a0, a1), fmaxf(b0, b1)));
+    } else {
+      rw = max_bf16x2(rw, max_bf16x2(ag[q], au[q]));
+    }
+  }
+  if (!p.colmul) rmax = fmaxf(rmax, fmaxf(__uint_as_float(rw << 16), __uint_as_float(rw & 0xFFFF0000u)));
+  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(ag, lane));
+  atomicMax(p.col_amax + p.F + fb + lane, warp_colmax_bits(au, lane));
+}
+
 template <int OUT, int BN_, int STAGES_, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
@@ -664,17 +785,17 @@ constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 256 + 8 
 constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 4 * 2 * 2048;
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
-  return OUT == kOutSwigluFwd ? C2_STAGES_SW : C2_STAGES;
+  return is_swiglu(OUT) ? C2_STAGES_SW : C2_STAGES;
 }
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return OUT == kOutSwigluFwd ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES);
+  return is_swiglu(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES);
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 4 epilogue warps (8 for the SwiGLU
 // epilogue: two per TMEM lane quarter, each on half of the tile's features)
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return OUT == kOutSwigluFwd ? 320 : NUM_THREADS;
+  return is_swiglu(OUT) ? 320 : NUM_THREADS;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -870,7 +991,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
     // this warp's two TMA-store staging buffers (32 rows x 64 B each); with the SwiGLU epilogue
     // they follow the 8 warps' scale/bias buffers
-    constexpr uint32_t st_off = 256u + (OUT == kOutSwigluFwd ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
+    constexpr uint32_t st_off = 256u + (is_swiglu(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
     uint8_t* st_stage = ctrl + st_off + (warp - 2) * 2 * 2048;
     const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
@@ -878,6 +999,17 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
       float4 st_s, st_b;  // loaded before the accumulator wait, stored after it
+      uint4 pg[4], pu[4];  // SwiGLU backward: g and u of the next chunk, loaded ahead
+      if constexpr (OUT == kOutSwigluBwd) {
+        // this warp's 128 features of the tile: lane l holds gate multipliers 4l..4l+3, up likewise
+        const int64_t col = (int64_t)tn * C2_BN + eh * 128 + lane * 4;
+        const bool in = ep.colmul && col < ep.F;
+        st_s = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        st_b = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + ep.F + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const int64_t fb0 = (int64_t)tn * C2_BN + eh * 128;
+        const int64_t prow = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
+        if (fb0 < ep.F) swiglu_bwd_load(ep, prow, fb0, pg, pu);
+      }
       if constexpr (OUT == kOutSwigluFwd) {
         // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
         const int64_t col = (int64_t)(lane >> 4) * ep.F + (int64_t)tn * kSwigluFeat + eh * 64 + (lane & 15) * 4;
@@ -886,7 +1018,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       }
       if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
-      if constexpr (OUT == kOutSwigluFwd) {
+      if constexpr (is_swiglu(OUT)) {
         float* buf = sw_buf + acc * C2_SW_BUF_FLOATS;
         reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
         reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
@@ -914,6 +1046,27 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         if (row < ep.M)
           atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
                                                                __uint_as_float(rmax & 0xFFFF0000u))));
+      } else if constexpr (OUT == kOutSwigluBwd) {
+        float rmax = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
+          const int fc = eh * 128 + c * 32;
+          const int64_t fb = (int64_t)tn * C2_BN + fc;
+          if (fb >= ep.F) break;
+          uint4 cg[4], cu[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            cg[k] = pg[k];
+            cu[k] = pu[k];
+          }
+          if (c + 1 < 4 && fb + 32 < ep.F) swiglu_bwd_load(ep, row, fb + 32, pg, pu);  // next chunk
+          uint32_t r[32];
+          tmem_ld32(tbase + fc, r);
+          tmem_wait_ld();
+          swiglu_bwd_chunk(r, cg, cu, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32, rmax, &tmD,
+                           st_stage, st_stage_addr, st_count);
+        }
+        if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
       } else {
         const int64_t ncol_tile = min64(C2_BN, ep.N - (int64_t)tn * C2_BN);
 #pragma unroll 1
@@ -1266,6 +1419,63 @@ extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(h), M, F, ldh, nullptr, eps,
                                       q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
+}
+
+extern "C" int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                                     const float* scale_a, const uint16_t* gu, int64_t ldgu, const float* colmul,
+                                     uint16_t* dgu, int64_t lddgu, int64_t M, int64_t F, int64_t K, float eps,
+                                     int8_t* q_rows, int64_t ldq, float* s_rows, int8_t* q_cols_t, int64_t ldqt,
+                                     float* s_cols, float* absmax_ws, void* stream) {
+  using namespace ff;
+  using namespace ff::gemm;
+  const char* name = "ff_swiglu_bwd_gemm_i8";
+  FF_REQUIRE(M >= 0 && F >= 1 && K >= 1, FF_ERR_INVALID_ARG, "%s: M=%lld F=%lld K=%lld", name, (long long)M,
+             (long long)F, (long long)K);
+  FF_REQUIRE(F % kSwigluFeat == 0, FF_ERR_UNSUPPORTED, "%s: F=%lld must be a multiple of %d", name, (long long)F,
+             kSwigluFeat);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "%s: nothing to do", name);
+  if (M == 0) return FF_OK;
+  FF_REQUIRE(A && B && gu && dgu, FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE(lda >= K && ldb >= F && ldgu >= 2 * F && lddgu >= 2 * F, FF_ERR_INVALID_ARG, "%s: bad leading dims",
+             name);
+  FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
+             "%s: A/B need 16-byte alignment and lda/ldb multiples of 16", name);
+  FF_REQUIRE(aligned(gu, 16) && aligned(dgu, 16) && ldgu % 8 == 0 && lddgu % 8 == 0, FF_ERR_UNSUPPORTED,
+             "%s: gu/dgu need 16-byte alignment and leading dims multiples of 8", name);
+  FF_REQUIRE(!colmul || aligned(colmul, 16), FF_ERR_UNSUPPORTED, "%s: colmul needs 16-byte alignment", name);
+  FF_REQUIRE(M <= (int64_t)1 << 31 && 2 * F <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
+             "%s: dimension too large", name);
+  int rc = check_dual_outputs(name, M, 2 * F, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
+  const int max_pairs = max_pairs_current();
+  FF_REQUIRE(max_pairs > 0, FF_ERR_UNSUPPORTED, "%s: the 2-CTA GEMM cannot be resident on this device", name);
+  cudaStream_t st = as_stream(stream);
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(M + 2 * F), st), name);
+  CUtensorMap ma, mb, md;
+  rc = make_map(&ma, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, K, F, ldb, BK);  // B is K x F row-major: read MN-major
+  if (rc) return rc;
+  rc = make_map_out_bf16(&md, dgu, M, 2 * F, lddgu);
+  if (rc) return rc;
+  EpiParams ep{};
+  ep.scale_a = scale_a;
+  ep.D = dgu;
+  ep.ldd = lddgu;
+  ep.M = M;
+  ep.N = F;
+  ep.vec = 1;
+  ep.F = F;
+  ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  ep.col_amax = ep.row_amax + M;
+  ep.g_in = reinterpret_cast<const __nv_bfloat16*>(gu);
+  ep.ldg_in = ldgu;
+  ep.colmul = colmul;
+  const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((F + C2_BN - 1) / C2_BN);
+  rc = launch_2cta<kOutSwigluBwd, true>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(dgu), M, 2 * F, lddgu, colmul,
+                                      eps, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
 }
 
 extern "C" int ff_gemm_i8_kn(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,

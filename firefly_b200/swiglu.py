@@ -13,9 +13,10 @@ ops computes, with the elementwise work moved into the quantisers:
 * forward: ``ff_swiglu_gemm_i8`` computes ``h = silu(g) * u`` and its absmax in the gate/up
   GEMM's epilogue and quantises h (f a multiple of 128; otherwise ``ff_swiglu_quant_i8``
   computes h from the GEMM output in the quantiser's absmax pass);
-* backward: ``ff_swiglu_bwd_quant_i8`` forms ``[dg | du]`` from ``dh``, g and u in the
-  absmax pass of the gate/up projection's operand quantiser, and ``dX`` is one GEMM
-  over ``K = 2f``.
+* backward: ``ff_swiglu_bwd_gemm_i8`` forms ``[dg | du]`` from the dh tile and the saved g
+  and u in the epilogue of the GEMM ``dh = dY·W_down`` (dh is never written) and quantises
+  it (otherwise ``ff_swiglu_bwd_quant_i8`` does that from dh); ``dX`` is one GEMM over
+  ``K = 2f``.
 
 The unfused composition (``fused=False``, or ffn not a multiple of 8) runs the same
 BitLinear kernels with torch's elementwise ops in between.
@@ -92,12 +93,14 @@ class SwiGLUMLPFn(torch.autograd.Function):
         dy = grad_out.to(torch.bfloat16).contiguous()
         # down projection: dH = dY·W_d, dW_d = dYᵀ·H, db = Σ dY
         q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=d_ws)
-        dh = _capi.gemm_i8(q_g, _weight_operand(d_handle, d_weight), O, scale_a=s_g,
-                           out_kind=_capi.FF_OUT_BF16, b_kn_cols=Fh)
+        w_d = _weight_operand(d_handle, d_weight)
+        if Fh % 128 == 0:  # dH, the SwiGLU backward and [dg | du]'s absmax in one GEMM epilogue
+            q_d, s_d, q_dt, s_dc, _ = _capi.swiglu_bwd_gemm(q_g, w_d, O, s_g, gu, colmul=gu_ws, rows=need_dx)
+        else:
+            dh = _capi.gemm_i8(q_g, w_d, O, scale_a=s_g, out_kind=_capi.FF_OUT_BF16, b_kn_cols=Fh)
+            q_d, s_d, q_dt, s_dc, _ = _capi.swiglu_bwd_quant(dh, gu, colmul=gu_ws, rows=need_dx)
         _weight_grad_gemm(d_handle, q_dyt, s_dy, q_ht, s_hc, O, Fh, T, dev)
         db = _capi.colsum_bf16(dy).to(grad_out.dtype) if ctx.has_bias else None
-        # SwiGLU backward fused into the quantiser of [dg | du]
-        q_d, s_d, q_dt, s_dc, _ = _capi.swiglu_bwd_quant(dh, gu, colmul=gu_ws, rows=need_dx)
         dx = None
         if need_dx:
             dx = _capi.gemm_i8(q_d, _weight_operand(gu_handle, gu_weight), F2, scale_a=s_d,

@@ -176,6 +176,25 @@ FF_API int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int6
                              void* stream);
 
 /*
+ * The GEMM dh = dY * W_down of a SwiGLU block's backward with the SwiGLU backward and the
+ * first pass of the [dg | du] quantiser in its epilogue.  A: int8 codes of dY * s_w
+ * [M, K] (K = the block's output width), B: W_down int8 [K, F] row-major (read as the
+ * K x N operand, as ff_gemm_i8_kn does), scale_a: fp32 [M] row scales.  With
+ * dh = bf16(acc * scale_a[m]) (what ff_gemm_i8_kn gives with FF_OUT_BF16) and gu = [g | u]
+ * (bf16 [M, 2F], leading dim ldgu: the saved gate/up output), writes
+ * dgu = [dg | du] (bf16 [M, 2F], leading dim lddgu) exactly as ff_swiglu_bwd_quant_i8
+ * forms it and quantises it exactly as ff_swiglu_bwd_quant_i8 does (colmul: NULL or fp32
+ * [2F]; outputs as there; absmax_ws M + 2F floats).  dh itself is not written.
+ * F must be a multiple of 128; gu, dgu and colmul 16-byte aligned, ldgu and lddgu
+ * multiples of 8.  Requires a passing ff_swiglu_selftest on the device.
+ */
+FF_API int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                                 const uint16_t* gu, int64_t ldgu, const float* colmul, uint16_t* dgu, int64_t lddgu,
+                                 int64_t M, int64_t F, int64_t K, float eps, int8_t* q_rows, int64_t ldq,
+                                 float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws,
+                                 void* stream);
+
+/*
  * Backward of the SwiGLU activation fused with the dual quantiser of the gate/up
  * projection's output gradient.  With dh the gradient of h (bf16, leading dim ldh)
  * and g, u as in ff_swiglu_quant_i8, the gradient of the [rows, 2*cols] projection

@@ -134,6 +134,31 @@ def test_swiglu_gemm_epilogue_matches_gemm_then_quantiser(T, F, K):
     assert _capi.device_status() == 0
 
 
+@pytest.mark.parametrize("T,F,O,colmul", [(256, 256, 512, True), (37, 128, 64, True), (300, 384, 1000, False),
+                                         (1024, 1408, 4096, True), (1, 128, 16, True)])
+def test_swiglu_bwd_gemm_epilogue_matches_gemm_then_quantiser(T, F, O, colmul):
+    """dH GEMM with the SwiGLU backward in its epilogue equals ff_gemm_i8_kn (bf16 dh)
+    followed by ff_swiglu_bwd_quant_i8, bit for bit."""
+    gen = torch.Generator(device=DEV).manual_seed(T + F + O)
+    ldo = _capi.round_up(O, 16)
+    a = torch.zeros(T, ldo, dtype=torch.int8, device=DEV)
+    a[:, :O] = torch.randint(-127, 128, (T, O), dtype=torch.int8, device=DEV, generator=gen)
+    w = torch.randint(-127, 128, (O, F), dtype=torch.int8, device=DEV, generator=gen)
+    sa = torch.rand(T, device=DEV, generator=gen) * 2e-3 + 1e-4
+    gu = _gu(T, F, seed=T + 3)
+    cm = torch.rand(2 * F, device=DEV, generator=gen) * 1e-2 + 1e-4 if colmul else None
+    dh = _capi.gemm_i8(a, w, O, scale_a=sa, out_kind=_capi.FF_OUT_BF16, b_kn_cols=F)
+    want = _capi.swiglu_bwd_quant(dh, gu, colmul=cm)
+    got = _capi.swiglu_bwd_gemm(a, w, O, sa, gu, colmul=cm)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bf16_bits(got[4]), bf16_bits(want[4]), err_msg="[dg | du]")
+    _assert_same(got[:4], want[:4], f"T={T} F={F} O={O}")
+    q, s_, qt, st, _ = _capi.swiglu_bwd_gemm(a, w, O, sa, gu, colmul=cm, rows=False)
+    assert q is None
+    np.testing.assert_array_equal(qt.cpu().numpy(), want[2].cpu().numpy())
+    assert _capi.device_status() == 0
+
+
 def test_swiglu_gemm_with_bias_and_extreme_gates():
     """Bias in the epilogue, and gate values beyond the fast path's range (IEEE fallback)."""
     T, F, K = 128, 128, 64
