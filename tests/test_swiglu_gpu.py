@@ -274,8 +274,9 @@ def test_fused_mlp_three_d_input_and_no_grad():
 
 def test_full_size_fused_kernels_equal_unfused():
     """At the benchmark's shapes (T=8192, d=4096, f=11008): the gate/up GEMM with h in its
-    epilogue equals the GEMM followed by the quantiser, and the backward quantiser equals
-    torch's autograd followed by the plain dual quantiser, bit for bit."""
+    epilogue equals the GEMM followed by the quantiser, the backward quantiser equals torch's
+    autograd followed by the plain dual quantiser, and the dh GEMM with the backward in its
+    epilogue equals the GEMM followed by the backward quantiser, bit for bit."""
     T, Fh, K = 8192, 11008, 4096
     gen = torch.Generator(device=DEV).manual_seed(2024)
     a = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=DEV, generator=gen)
@@ -298,6 +299,17 @@ def test_full_size_fused_kernels_equal_unfused():
     want = _capi.quant_dual(g.grad, row_colmul=cm)
     got = _capi.swiglu_bwd_quant(dh, gu_ref, colmul=cm)
     assert torch.equal(got[4].view(torch.int16), g.grad.view(torch.int16))
+    for x, y in zip(got[:4], want[:4]):
+        assert torch.equal(x, y)
+    del g, got, want
+    # the dh GEMM (K = 4096 -> F) with the backward in its epilogue
+    a = torch.randint(-127, 128, (T, K), dtype=torch.int8, device=DEV, generator=gen)
+    wd = torch.randint(-127, 128, (K, Fh), dtype=torch.int8, device=DEV, generator=gen)
+    sg = torch.rand(T, device=DEV, generator=gen) * 1e-4
+    dh = _capi.gemm_i8(a, wd, K, scale_a=sg, out_kind=_capi.FF_OUT_BF16, b_kn_cols=Fh)
+    want = _capi.swiglu_bwd_quant(dh, gu_ref, colmul=cm)
+    got = _capi.swiglu_bwd_gemm(a, wd, K, sg, gu_ref, colmul=cm)
+    assert torch.equal(got[4].view(torch.int16), want[4].view(torch.int16))
     for x, y in zip(got[:4], want[:4]):
         assert torch.equal(x, y)
     assert _capi.device_status() == 0
