@@ -18,8 +18,9 @@ the same metric through the public API with each step's data batch x copied from
 pinned host memory and the loss L = sum(y * R) read back, R a resident projection
 (so dL/dy = R is formed on the device, as in training).
 ``roofline`` is the int8 GEMM (the dominant kernel) timed per launch with CUDA
-events inside the timed region.  Extra keys carry the INT8 GEMM sweep (TOPS)
-and the 8-bit AdamW step over 6.7e9 parameters (HBM GB/s).  ``cpu_baseline``
+events inside the timed region.  Extra keys carry the INT8 GEMM sweep (TOPS),
+the 8-bit AdamW step over 6.7e9 parameters (HBM GB/s) and the dense-parameter
+8-bit AdamW over 268 M fp32 parameters (HBM GB/s).  ``cpu_baseline``
 is the CPU restatement of the same step timed on the host cores on a sample.
 
 ``--impl reference`` times the CPU implementation of the path (the oracle
@@ -60,7 +61,7 @@ def parse_args():
     ap.add_argument("--no-sub", action="store_true", help="skip the GEMM sweep and the AdamW sub-benchmarks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
-                                              "swiglu_gemm", "mlp"],
+                                              "swiglu_gemm", "dense_adamw", "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -101,6 +102,17 @@ def kernel_case(args):
         else:
             dh = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
             _capi.swiglu_bwd_quant(dh, gu, colmul=torch.rand(2 * 11008, device=dev) * 1e-3)
+    elif args.kernel_case == "dense_adamw":  # block-wise 8-bit AdamW of 67 M dense fp32 parameters
+        from firefly_b200.adamw8 import _qmaps_on
+
+        n = 1 << 26
+        p = torch.empty(n, device=dev).normal_(0, 0.02, generator=g)
+        grad = torch.empty(n, device=dev).normal_(0, 1e-3, generator=g)
+        codes = [torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g) for _ in range(2)]
+        am = [torch.empty(n // 2048, device=dev).uniform_(1e-8, 1e-2, generator=g) for _ in range(2)]
+        qs, qu = _qmaps_on(dev)
+        _capi.adamw8_blockwise(p, grad, codes[0], am[0], codes[1], am[1], lr=1e-3, beta1=0.9, beta2=0.999,
+                               eps=1e-8, wd=0.01, step=3, qmap_s=qs, qmap_u=qu)
     elif args.kernel_case == "swiglu_gemm":  # gate/up GEMM with h = silu(g) * u in its epilogue
         a = torch.randint(-127, 128, (8192, 4096), dtype=torch.int8, device=dev, generator=g)
         w = torch.randint(-127, 128, (2 * 11008, 4096), dtype=torch.int8, device=dev, generator=g)
@@ -407,6 +419,42 @@ def adamw_bench(dev, params: float, peak_gbs: float):
             "bytes_per_param": ADAMW_BYTES_PER_PARAM, "frac_of_measured_hbm": round(gbs / peak_gbs, 3)}
 
 
+# block-wise 8-bit AdamW of a dense fp32 parameter with an fp32 gradient: p r/w 8 + g 4 + m, v codes r/w 4
+# + two block absmax r/w (16 / 2048)
+DENSE_ADAMW_BYTES_PER_PARAM = 8 + 4 + 4 + 16 / 2048
+
+
+def dense_adamw_bench(dev, params: int, peak_gbs: float):
+    """The dense-parameter 8-bit AdamW kernel (ff_adamw8_blockwise) on ``params`` fp32 parameters."""
+    import torch
+
+    from firefly_b200 import _capi
+    from firefly_b200.adamw8 import _qmaps_on
+
+    n = int(params) // 2048 * 2048
+    g = torch.Generator(device=dev).manual_seed(0)
+    p = torch.empty(n, device=dev).normal_(0, 0.02, generator=g)
+    grad = torch.empty(n, device=dev).normal_(0, 1e-3, generator=g)
+    m_q = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g)
+    v_q = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g)
+    m_a = torch.empty(n // 2048, device=dev).uniform_(1e-4, 1e-2, generator=g)
+    v_a = torch.empty(n // 2048, device=dev).uniform_(1e-8, 1e-6, generator=g)
+    qs, qu = _qmaps_on(dev)
+    step = [0]
+
+    def run():
+        step[0] += 1
+        _capi.adamw8_blockwise(p, grad, m_q, m_a, v_q, v_a, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01,
+                               step=step[0] + 1, qmap_s=qs, qmap_u=qu)
+
+    t = _time_cuda(run, 5, warm=2)
+    gbs = n * DENSE_ADAMW_BYTES_PER_PARAM / t / 1e9
+    del p, grad, m_q, v_q, m_a, v_a
+    torch.cuda.empty_cache()
+    return {"params": n, "ms": round(t * 1e3, 3), "hbm_gbs": round(gbs, 1),
+            "bytes_per_param": DENSE_ADAMW_BYTES_PER_PARAM, "frac_of_measured_hbm": round(gbs / peak_gbs, 3)}
+
+
 def load_traffic():
     """DRAM bytes per launch of the dominant kernel, from the committed ncu capture."""
     p = ROOT / "profiles" / "traffic.json"
@@ -583,6 +631,7 @@ def main():
         torch.cuda.empty_cache()
         sub["int8_gemm_sweep"] = gemm_sweep(dev)
         sub["adamw8"] = adamw_bench(dev, args.adamw_params, peaks["hbm_gbs"])
+        sub["dense_adamw8"] = dense_adamw_bench(dev, 268435456, peaks["hbm_gbs"])
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         est, sample = cpu_mlp_step_estimate(d, f, T)

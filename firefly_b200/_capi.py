@@ -60,6 +60,7 @@ SIGNATURES = {
     "ff_dqt_adamw8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
                            _D, _D, _D, _D, _D, _D, _D, _D, _U64, _U64, _I64, _P, _P, _P, _P]),
     "ff_update_int8_weight": (_I, [_P, _P, _I64, _P]),
+    "ff_adamw8_blockwise": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I64, _D, _D, _D, _D, _D, _I64, _P, _P, _P]),
 }
 
 _lib = None
@@ -75,7 +76,8 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
                      "ff_swiglu_gemm_i8": 2, "ff_swiglu_bwd_gemm_i8": 2,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
-                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1}
+                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1,
+                     "ff_adamw8_blockwise": 1}
 
 
 def lib() -> ctypes.CDLL:
@@ -512,3 +514,23 @@ def update_int8_weight(w: torch.Tensor, dq: torch.Tensor) -> None:
         raise ValueError("update_int8_weight: shape mismatch")
     with torch.cuda.device(dev):
         _call("ff_update_int8_weight", _ptr(w), _ptr(dq), w.numel(), _stream(dev))
+
+
+def adamw8_blockwise(p: torch.Tensor, g: torch.Tensor, m_q: torch.Tensor, m_absmax: torch.Tensor,
+                     v_q: torch.Tensor, v_absmax: torch.Tensor, *, lr: float, beta1: float, beta2: float,
+                     eps: float, wd: float, step: int, qmap_s: torch.Tensor, qmap_u: torch.Tensor) -> None:
+    """In-place block-wise 8-bit AdamW step of a dense parameter (fp32 or bf16, contiguous)."""
+    dev = _require_cuda(p, g, m_q, m_absmax, v_q, v_absmax, qmap_s, qmap_u)
+    n = p.numel()
+    for name, t, want in (("g", g, n), ("m_q", m_q, n), ("v_q", v_q, n)):
+        if t.numel() != want or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous with {want} elements")
+    nb = (n + 2047) // 2048
+    if m_absmax.numel() != nb or v_absmax.numel() != nb or m_absmax.dtype != torch.float32:
+        raise ValueError(f"absmax arrays must be fp32 with {nb} elements")
+    if m_q.dtype != torch.uint8 or v_q.dtype != torch.uint8:
+        raise ValueError("state codes must be uint8")
+    with torch.cuda.device(dev):
+        _call("ff_adamw8_blockwise", _ptr(p), _dtype_code(p.dtype), _ptr(g), _dtype_code(g.dtype), _ptr(m_q),
+              _ptr(m_absmax), _ptr(v_q), _ptr(v_absmax), n, float(lr), float(beta1), float(beta2), float(eps),
+              float(wd), int(step), _ptr(qmap_s.contiguous()), _ptr(qmap_u.contiguous()), _stream(dev))

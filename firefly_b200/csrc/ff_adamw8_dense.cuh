@@ -1,0 +1,250 @@
+// ff_adamw8_dense.cuh — block-wise 8-bit AdamW for dense (non-BitLinear) parameters.
+//
+// The reference steps dense parameters with bitsandbytes' AdamW8bit (fireflyoptim.py:83,
+// :124): Adam moments kept as 8-bit codes of a "dynamic tree" quantisation map, scaled per
+// block by the block's absmax (Dettmers et al., "8-bit Optimizers via Block-wise
+// Quantization", ICLR 2022).  This kernel implements that algorithm; the two 256-entry maps
+// (signed for m, unsigned for v) are built on the host from the paper's description and
+// passed in, sorted ascending.
+//
+// Per element, in fp32 with every operation rounded once (no contractions):
+//   m0 = qs[cm] * am,  v0 = qu[cv] * av                 (decode, block absmax am / av)
+//   p  = p * (1 - lr*wd)                                (decoupled weight decay; skipped if wd = 0)
+//   m  = b1*m0 + (1-b1)*g,   v = b2*v0 + ((1-b2)*g)*g
+//   p  = p - a_t * (m / (sqrt(v) + e_t))               a_t = lr*sqrt(bc2)/bc1, e_t = eps*sqrt(bc2)
+// (Adam's bias corrections folded into the step size and epsilon, Kingma & Ba, section 2), then
+// per block of kBlock elements the new absmax of |m| and v, and each value's code is the nearest
+// map entry to value * (1 / absmax) (ties to the lower code).
+//
+// One CTA per block (256 threads x 8 consecutive elements, vector loads and stores), grid-stride
+// over blocks; the maps sit in shared memory in 16 replicas (bank-conflict-light lookups).
+#pragma once
+#include <cmath>
+
+#include "ff_common.cuh"
+
+namespace ff {
+namespace dense {
+
+constexpr int kBlock = 2048;
+constexpr int kThreads = 256;
+constexpr int kPer = kBlock / kThreads;  // 8 elements per thread
+
+struct Params {
+  void* p;
+  int p_dtype;  // FF_DTYPE_F32 or FF_DTYPE_BF16
+  const void* g;
+  int g_dtype;
+  uint8_t* m_q;
+  float* m_absmax;
+  uint8_t* v_q;
+  float* v_absmax;
+  int64_t n;
+  float lr, b1, b2, omb1, omb2, decay, step_size, eps_hat;
+  int use_decay;
+  const float* qs;
+  const float* qu;
+};
+
+constexpr int kRep = 16;  // map replicas: entry i of replica r at word i*kRep + r (lanes l, l+16 share one)
+
+__device__ __forceinline__ float load_elem(const void* base, int dtype, int64_t i) {
+  if (dtype == FF_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+  return reinterpret_cast<const float*>(base)[i];
+}
+
+// 8 consecutive elements (fp32 or bf16) starting at a multiple of 8
+__device__ __forceinline__ void load8(const void* base, int dtype, int64_t e0, float (&x)[8]) {
+  if (dtype == FF_DTYPE_BF16) {
+    const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + e0);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      x[2 * k] = __uint_as_float(ws[k] << 16);
+      x[2 * k + 1] = __uint_as_float(ws[k] & 0xFFFF0000u);
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e0);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e0 + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+}
+
+// largest index i with q[i] <= x (q sorted ascending, q[0] <= x), then the nearer of i, i+1;
+// q is read from this lane's replica (qr = table + slot, stride kRep)
+__device__ __forceinline__ int nearest_code(const float* qr, float x) {
+  int lo = 0;
+#pragma unroll
+  for (int step = 128; step > 0; step >>= 1)
+    if (qr[(lo + step) * kRep] <= x) lo += step;
+  if (lo < 255 && __fsub_rn(qr[(lo + 1) * kRep], x) < __fsub_rn(x, qr[lo * kRep])) ++lo;
+  return lo;
+}
+
+__global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
+  __shared__ float qs[256 * kRep], qu[256 * kRep];
+  __shared__ uint32_t red[2][kThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 256 * kRep; i += kThreads) {
+    qs[i] = p.qs[i / kRep];
+    qu[i] = p.qu[i / kRep];
+  }
+  __syncthreads();
+  const float* qsr = qs + (lane & (kRep - 1));
+  const float* qur = qu + (lane & (kRep - 1));
+  const int64_t nblocks = (p.n + kBlock - 1) / kBlock;
+  for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const int64_t e0 = blk * kBlock + (int64_t)tid * kPer;
+    const float am = p.m_absmax[blk], av = p.v_absmax[blk];
+    const bool full = e0 + kPer <= p.n;
+    float m[kPer], v[kPer], g[kPer], w[kPer];
+    uint32_t cm[2], cv[2];
+    if (full) {  // 16-byte (fp32: 2 x 16-byte) vectors and 8-byte code words
+      load8(p.g, p.g_dtype, e0, g);
+      load8(p.p, p.p_dtype, e0, w);
+      const uint2 a = *reinterpret_cast<const uint2*>(p.m_q + e0), b = *reinterpret_cast<const uint2*>(p.v_q + e0);
+      cm[0] = a.x; cm[1] = a.y;
+      cv[0] = b.x; cv[1] = b.y;
+    } else {
+      cm[0] = cm[1] = 0x80808080u;  // elements past n: the zero codes
+      cv[0] = cv[1] = 0u;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int64_t i = e0 + j;
+        const bool in = i < p.n;
+        g[j] = in ? load_elem(p.g, p.g_dtype, i) : 0.f;
+        w[j] = in ? load_elem(p.p, p.p_dtype, i) : 0.f;
+        if (in) {
+          const int sh = 8 * (j & 3);
+          cm[j >> 2] = (cm[j >> 2] & ~(0xFFu << sh)) | ((uint32_t)p.m_q[i] << sh);
+          cv[j >> 2] = (cv[j >> 2] & ~(0xFFu << sh)) | ((uint32_t)p.v_q[i] << sh);
+        }
+      }
+    }
+    float mx_m = 0.f, mx_v = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const uint32_t c_m = (cm[j >> 2] >> (8 * (j & 3))) & 0xFFu, c_v = (cv[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+      const float m0 = __fmul_rn(qsr[c_m * kRep], am), v0 = __fmul_rn(qur[c_v * kRep], av);
+      if (p.use_decay) w[j] = __fmul_rn(w[j], p.decay);
+      m[j] = __fadd_rn(__fmul_rn(p.b1, m0), __fmul_rn(p.omb1, g[j]));
+      v[j] = __fadd_rn(__fmul_rn(p.b2, v0), __fmul_rn(__fmul_rn(p.omb2, g[j]), g[j]));
+      const float den = __fadd_rn(__fsqrt_rn(v[j]), p.eps_hat);
+      w[j] = __fsub_rn(w[j], __fmul_rn(p.step_size, __fdiv_rn(m[j], den)));
+      mx_m = fmaxf(mx_m, fabsf(m[j]));  // elements past n have g = 0 and zero codes: m = v = 0
+      mx_v = fmaxf(mx_v, fabsf(v[j]));
+    }
+    // block maxima (non-negative floats order like their bit patterns)
+    const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(mx_m));
+    const uint32_t wv = __reduce_max_sync(0xffffffffu, __float_as_uint(mx_v));
+    if (lane == 0) {
+      red[0][warp] = wm;
+      red[1][warp] = wv;
+    }
+    __syncthreads();
+    uint32_t bm = 0u, bv = 0u;
+#pragma unroll
+    for (int k = 0; k < kThreads / 32; ++k) {
+      bm = max(bm, red[0][k]);
+      bv = max(bv, red[1][k]);
+    }
+    __syncthreads();  // red is rewritten by the next block
+    // an all-zero block keeps absmax 0 (its values all decode from the zero code)
+    const float nam = __uint_as_float(bm), nav = __uint_as_float(bv);
+    const float im = nam > 0.f ? __frcp_rn(nam) : 1.f, iv = nav > 0.f ? __frcp_rn(nav) : 1.f;
+    uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      // |m| * (1/absmax) can exceed 1 by an ulp: the search then returns the code of 1.0
+      om[j >> 2] |= (uint32_t)nearest_code(qsr, __fmul_rn(m[j], im)) << (8 * (j & 3));
+      ov[j >> 2] |= (uint32_t)nearest_code(qur, __fmul_rn(v[j], iv)) << (8 * (j & 3));
+    }
+    if (full) {
+      *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(om[0], om[1]);
+      *reinterpret_cast<uint2*>(p.v_q + e0) = make_uint2(ov[0], ov[1]);
+      if (p.p_dtype == FF_DTYPE_BF16) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(w[2 * k], w[2 * k + 1]);
+          o[k] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.p) + e0) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+        float* pw = reinterpret_cast<float*>(p.p) + e0;
+        *reinterpret_cast<float4*>(pw) = make_float4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<float4*>(pw + 4) = make_float4(w[4], w[5], w[6], w[7]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int64_t i = e0 + j;
+        if (i < p.n) {
+          p.m_q[i] = (uint8_t)(om[j >> 2] >> (8 * (j & 3)));
+          p.v_q[i] = (uint8_t)(ov[j >> 2] >> (8 * (j & 3)));
+          if (p.p_dtype == FF_DTYPE_BF16) reinterpret_cast<__nv_bfloat16*>(p.p)[i] = __float2bfloat16_rn(w[j]);
+          else reinterpret_cast<float*>(p.p)[i] = w[j];
+        }
+      }
+    }
+    if (tid == 0) {
+      p.m_absmax[blk] = nam;
+      p.v_absmax[blk] = nav;
+    }
+  }
+}
+
+}  // namespace dense
+}  // namespace ff
+
+extern "C" int ff_adamw8_blockwise(void* p, int p_dtype, const void* g, int g_dtype, uint8_t* m_q, float* m_absmax,
+                                   uint8_t* v_q, float* v_absmax, int64_t n, double lr, double beta1, double beta2,
+                                   double eps, double weight_decay, int64_t step, const float* qmap_s,
+                                   const float* qmap_u, void* stream) {
+  using namespace ff;
+  using namespace ff::dense;
+  FF_REQUIRE(n >= 0 && step >= 1, FF_ERR_INVALID_ARG, "ff_adamw8_blockwise: n=%lld step=%lld", (long long)n,
+             (long long)step);
+  FF_REQUIRE((p_dtype == FF_DTYPE_F32 || p_dtype == FF_DTYPE_BF16) &&
+                 (g_dtype == FF_DTYPE_F32 || g_dtype == FF_DTYPE_BF16),
+             FF_ERR_INVALID_ARG, "ff_adamw8_blockwise: parameters and gradients must be fp32 or bf16");
+  if (n == 0) return FF_OK;
+  FF_REQUIRE(p && g && m_q && m_absmax && v_q && v_absmax && qmap_s && qmap_u, FF_ERR_INVALID_ARG,
+             "ff_adamw8_blockwise: null pointer");
+  FF_REQUIRE(aligned(p, 16) && aligned(g, 16) && aligned(m_q, 8) && aligned(v_q, 8), FF_ERR_UNSUPPORTED,
+             "ff_adamw8_blockwise: p and g need 16-byte, the code arrays 8-byte alignment");
+  Params prm;
+  prm.p = p;
+  prm.p_dtype = p_dtype;
+  prm.g = g;
+  prm.g_dtype = g_dtype;
+  prm.m_q = m_q;
+  prm.m_absmax = m_absmax;
+  prm.v_q = v_q;
+  prm.v_absmax = v_absmax;
+  prm.n = n;
+  // scalars rounded to fp32 the way torch does for a python float operand
+  prm.lr = (float)lr;
+  prm.b1 = (float)beta1;
+  prm.b2 = (float)beta2;
+  prm.omb1 = (float)(1.0 - beta1);
+  prm.omb2 = (float)(1.0 - beta2);
+  prm.decay = (float)(1.0 - lr * weight_decay);
+  prm.use_decay = weight_decay != 0.0;
+  const double bc1 = 1.0 - std::pow(beta1, (double)step), bc2 = 1.0 - std::pow(beta2, (double)step);
+  FF_REQUIRE(bc1 > 0.0 && bc2 > 0.0, FF_ERR_INVALID_ARG, "ff_adamw8_blockwise: bias corrections must be > 0");
+  prm.step_size = (float)(lr * std::sqrt(bc2) / bc1);
+  prm.eps_hat = (float)(eps * std::sqrt(bc2));
+  prm.qs = qmap_s;
+  prm.qu = qmap_u;
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int64_t nblocks = (n + kBlock - 1) / kBlock;
+  const int grid = (int)min64(nblocks, (int64_t)sms * 8);
+  adamw8_dense_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(prm);
+  return check_launch("ff_adamw8_blockwise");
+}

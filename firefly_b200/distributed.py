@@ -30,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from . import _capi
+from .adamw8 import AdamW8bitDense
 from .bitLinear import BitLinear
 from .fireflykernels import _BIT_GRAD_CACHE, _invalidate_weight_cache, set_grad_slot
 from .fireflyoptim import BLOCK, _tables_on, bit_rng_offsets
@@ -177,7 +178,7 @@ class ZeroFireFlyOptim:
         self.rng_seed = seed
         self.update_fn = update_fn or self._kernel_update
         self.dense = [p for p in params if p.requires_grad]
-        self.dense_opt = (torch.optim.AdamW(self.dense, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        self.dense_opt = (AdamW8bitDense(self.dense, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
                           if self.dense else None)
         # every rank starts from rank 0's weights
         if self.world > 1:

@@ -23,9 +23,10 @@ on how the update is split across GPUs.  ``uniform_source`` may supply the
 uniforms instead (used to replay the reference's draws).
 
 Dense (non-BitLinear) parameters: the reference steps them with
-bitsandbytes ``AdamW8bit`` (fireflyoptim.py:83, :124), a third-party
-optimizer that is not part of this hot path; here they are stepped by
-``torch.optim.AdamW`` with the same hyperparameters.
+bitsandbytes ``AdamW8bit`` (fireflyoptim.py:83, :124), a third-party optimizer;
+here ``FireFlyOptim`` derives from ``AdamW8bitDense`` (``firefly_b200/adamw8.py``),
+the same block-wise 8-bit algorithm on the ``ff_adamw8_blockwise`` kernel, with fp32
+moments for parameters under 4096 elements.
 """
 from __future__ import annotations
 
@@ -34,6 +35,7 @@ from typing import Callable
 import torch
 
 from . import _capi
+from .adamw8 import AdamW8bitDense
 from .bitLinear import BitLinear
 from .fireflykernels import _invalidate_weight_cache
 
@@ -95,8 +97,8 @@ def bit_rng_offsets(modules) -> list[int]:
     return out
 
 
-class FireFlyOptim(torch.optim.AdamW):
-    """Dense params: AdamW.  BitLinear weights: fused 8-bit AdamW + DQT stochastic rounding."""
+class FireFlyOptim(AdamW8bitDense):
+    """Dense params: block-wise 8-bit AdamW.  BitLinear weights: fused 8-bit AdamW + DQT stochastic rounding."""
 
     def __init__(
         self,

@@ -261,6 +261,26 @@ FF_API int ff_colsum_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t
                    uint16_t* out, float* ws, void* stream);
 
 /*
+ * Block-wise 8-bit AdamW step of a dense (non-BitLinear) parameter, in place.
+ * Replaces bitsandbytes' AdamW8bit, which steps the reference's dense parameters
+ * (fireflyoptim.py:83, :124); the algorithm is the published one (Dettmers et al., ICLR
+ * 2022): m and v stored as uint8 codes of 256-entry maps (qmap_s signed for m, qmap_u
+ * unsigned for v, fp32, sorted ascending) scaled per block of 2048 elements by fp32
+ * absmax arrays [ceil(n/2048)].  Per element, fp32, each operation rounded once:
+ *   p *= 1 - lr*wd (if wd != 0);  m = b1*m + (1-b1)*g;  v = b2*v + ((1-b2)*g)*g;
+ *   p -= a_t * (m / (sqrt(v) + e_t)),  a_t = lr*sqrt(bc2)/bc1, e_t = eps*sqrt(bc2),
+ *   bc = 1 - beta^step (scalars in double, then fp32);
+ * then each block's absmax of |m| and v and the nearest map code of value * (1/absmax)
+ * (ties to the lower code; an all-zero block keeps absmax 0).  p: fp32 or bf16 (FF_DTYPE_*), g:
+ * fp32 or bf16; all arrays have n elements; p and g 16-byte aligned, m_q and v_q
+ * 8-byte aligned.
+ */
+FF_API int ff_adamw8_blockwise(void* p, int p_dtype, const void* g, int g_dtype, uint8_t* m_q, float* m_absmax,
+                               uint8_t* v_q, float* v_absmax, int64_t n, double lr, double beta1, double beta2,
+                               double eps, double weight_decay, int64_t step, const float* qmap_s,
+                               const float* qmap_u, void* stream);
+
+/*
  * Fused DQT-SR 8-bit AdamW update of one int8 weight tensor (one BitLinear).
  * Replaces FireFlyOptim.step's bit-module loop body fireflyoptim.py:137-209
  * together with update_int8_weight_ (fireflykernels.py:218-223) and the

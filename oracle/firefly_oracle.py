@@ -17,6 +17,11 @@ It restates the reference algorithm (fumitoshi0524/FireFly) in numpy:
 * ``encode_signed`` …         mu-law 8-bit blockwise codecs fireflyoptim.py:8-80
 * ``dqt_adamw8_step``         FireFlyOptim bit-module update fireflyoptim.py:136-209
 * ``philox_uniforms``         the counter-based uniforms the GPU optimizer draws
+* ``dynamic_qmap`` / ``dense_adamw8_step``
+                              block-wise 8-bit AdamW of dense parameters (the published
+                              algorithm of the bitsandbytes optimizer the reference uses,
+                              fireflyoptim.py:83, :124; bitsandbytes itself is absent, so
+                              this follows the B200 build's own map and rounding)
 * ``swiglu_forward`` / ``swiglu_backward`` / ``swiglu_mlp_step``
                               the SwiGLU MLP block of BitLinear layers (the benchmark
                               workload; the reference has no model code): torch's
@@ -415,3 +420,71 @@ def philox_uniforms(numel: int, seed: int, step: int, elem_offset: int = 0) -> n
     idx = (e // np.uint64(8) - call[0]).astype(np.int64)
     h = halves[idx, (e % np.uint64(8)).astype(np.int64)].astype(np.float32)
     return (h + F32(0.5)) * F32(1.0 / 65536.0)
+
+
+# --------------------------------------------------------------------------
+# Block-wise 8-bit AdamW of dense parameters
+# --------------------------------------------------------------------------
+DENSE_BLOCK = 2048
+
+
+def dynamic_qmap(signed: bool) -> np.ndarray:
+    """The dynamic tree map: sign (signed only), a zero run selecting the decade 10^-e, an
+    indicator bit, and the remaining bits as a linear fraction in (0.1, 1].  Signed: e = 0..6
+    with 6-e fraction bits, both signs, zero twice; unsigned: e = 0..7 with 7-e fraction bits
+    and zero.  256 fp32 values, ascending."""
+    fb = 6 if signed else 7
+    mags = [10.0 ** (-e) * (0.1 + 0.9 * k / 2 ** (fb - e)) for e in range(fb + 1) for k in range(1, 2 ** (fb - e) + 1)]
+    vals = ([0.0, 0.0] + mags + [-m for m in mags]) if signed else ([0.0] + mags)
+    return np.array(sorted(vals), dtype=np.float64).astype(np.float32)
+
+
+def _nearest_codes(x, q):
+    """Nearest map entry of each value (ties to the lower code); x within [q[0], q[-1]]."""
+    x = np.asarray(x, np.float32)
+    lo = np.clip(np.searchsorted(q, x, side="right") - 1, 0, 255)
+    hi = np.minimum(lo + 1, 255)
+    d_lo = (x - q[lo]).astype(np.float32)
+    d_hi = (q[hi] - x).astype(np.float32)
+    return np.where((hi > lo) & (d_hi < d_lo), hi, lo).astype(np.uint8)
+
+
+def init_dense_state(n: int) -> dict:
+    nb = -(-n // DENSE_BLOCK)
+    return {"step": 0, "m_q": np.full(n, 128, np.uint8), "m_absmax": np.zeros(nb, np.float32),
+            "v_q": np.zeros(n, np.uint8), "v_absmax": np.zeros(nb, np.float32)}
+
+
+def dense_adamw8_step(p, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01):
+    """One block-wise 8-bit AdamW step (fp32, every operation rounded once):
+    m = b1*m + (1-b1)*g, v = b2*v + ((1-b2)*g)*g, p = p*(1-lr*wd) - a_t*(m/(sqrt(v)+e_t)) with
+    a_t = lr*sqrt(bc2)/bc1, e_t = eps*sqrt(bc2) (Kingma & Ba, section 2), then per block of 2048
+    the absmax of |m| and v and the nearest codes of value*(1/absmax).  Returns (p, state)."""
+    p = np.asarray(p, np.float32).ravel().copy()
+    g = np.asarray(g, np.float32).ravel()
+    n = p.size
+    qs, qu = dynamic_qmap(True), dynamic_qmap(False)
+    t = state["step"] + 1
+    blk = np.arange(n) // DENSE_BLOCK
+    m0 = (qs[state["m_q"]] * state["m_absmax"][blk]).astype(np.float32)
+    v0 = (qu[state["v_q"]] * state["v_absmax"][blk]).astype(np.float32)
+    F = np.float32
+    b1, b2 = F(beta1), F(beta2)
+    if wd != 0.0:
+        p = (p * F(1.0 - lr * wd)).astype(np.float32)
+    m = (b1 * m0 + (F(1.0 - beta1) * g).astype(np.float32)).astype(np.float32)
+    v = (b2 * v0 + ((F(1.0 - beta2) * g).astype(np.float32) * g).astype(np.float32)).astype(np.float32)
+    bc1, bc2 = 1.0 - beta1 ** t, 1.0 - beta2 ** t
+    step_size, eps_hat = F(lr * np.sqrt(bc2) / bc1), F(eps * np.sqrt(bc2))
+    den = (np.sqrt(v) + eps_hat).astype(np.float32)
+    p = (p - (step_size * (m / den).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    nb = -(-n // DENSE_BLOCK)
+    pad = nb * DENSE_BLOCK - n
+    am = np.abs(np.pad(m, (0, pad))).reshape(nb, DENSE_BLOCK).max(axis=1).astype(np.float32)
+    av = np.abs(np.pad(v, (0, pad))).reshape(nb, DENSE_BLOCK).max(axis=1).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        im = np.where(am > 0, F(1.0) / am, F(1.0)).astype(np.float32)
+        iv = np.where(av > 0, F(1.0) / av, F(1.0)).astype(np.float32)
+    st = {"step": t, "m_q": _nearest_codes((m * im[blk]).astype(np.float32), qs), "m_absmax": am,
+          "v_q": _nearest_codes((v * iv[blk]).astype(np.float32), qu), "v_absmax": av}
+    return p, st

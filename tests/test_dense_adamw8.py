@@ -1,0 +1,85 @@
+"""Block-wise 8-bit AdamW of dense parameters (the reference's bitsandbytes AdamW8bit path).
+
+bitsandbytes is absent, so parity is against the oracle's restatement of the published
+algorithm with this build's map and rounding (``oracle.dense_adamw8_step``), not against
+bitsandbytes itself: parity unpinned for this path.
+"""
+import numpy as np
+import pytest
+import torch
+
+from firefly_b200.adamw8 import AdamW8bitDense, dynamic_qmap
+from oracle import firefly_oracle as O
+
+DEV = torch.device("cuda")
+
+
+def test_dynamic_maps():
+    for signed in (True, False):
+        q = O.dynamic_qmap(signed)
+        assert q.shape == (256,) and q.dtype == np.float32
+        assert np.all(np.diff(q) >= 0)
+        assert q[-1] == 1.0
+        np.testing.assert_array_equal(q, dynamic_qmap(signed).numpy())
+    qs, qu = O.dynamic_qmap(True), O.dynamic_qmap(False)
+    np.testing.assert_array_equal(qs, -qs[::-1])  # symmetric
+    assert qs[127] == qs[128] == 0.0 and qu[0] == 0.0 and qu[1] == np.float32(1e-7)
+    # nearest-code encoding of the map's own values returns a code of the same value
+    for q in (qs, qu):
+        np.testing.assert_array_equal(q[O._nearest_codes(q, q)], q)
+
+
+def test_oracle_zero_gradient_keeps_zero_state():
+    st = O.init_dense_state(3000)
+    p = np.ones(3000, np.float32)
+    p2, st2 = O.dense_adamw8_step(p, np.zeros(3000, np.float32), st, lr=1e-3, wd=0.0)
+    np.testing.assert_array_equal(p2, p)
+    assert (st2["m_q"] == 128).all() and (st2["v_q"] == 0).all() and not st2["m_absmax"].any()
+
+
+def _run_kernel_steps(n, pdt, steps=3, wd=0.01, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    p0 = (torch.randn(n, generator=gen) * 0.1).to(pdt)
+    grads = [(torch.randn(n, generator=gen) * 1e-2) for _ in range(steps)]
+    p = torch.nn.Parameter(p0.clone().to(DEV))
+    opt = AdamW8bitDense([p], lr=1e-3, weight_decay=wd)
+    pn = p0.float().numpy()
+    st = O.init_dense_state(n)
+    for g in grads:
+        p.grad = g.to(DEV).to(pdt)
+        opt.step()
+        pn, st = O.dense_adamw8_step(pn, p.grad.float().cpu().numpy(), st, lr=1e-3, wd=wd)
+        if pdt == torch.bfloat16:
+            pn = O.round_bf16(pn)
+    return p, opt.state[p], pn, st
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,pdt", [(10000, torch.float32), (2048 * 3, torch.float32), (4097, torch.bfloat16),
+                                   (50000, torch.bfloat16)])
+def test_kernel_matches_oracle(n, pdt):
+    p, st, pn, sto = _run_kernel_steps(n, pdt)
+    np.testing.assert_array_equal(p.detach().float().cpu().numpy(), pn)
+    for k in ("m_q", "v_q", "m_absmax", "v_absmax"):
+        np.testing.assert_array_equal(st[k].cpu().numpy(), sto[k], err_msg=k)
+    assert st["step"] == sto["step"] == 3
+
+
+@pytest.mark.gpu
+def test_small_params_keep_fp32_moments_and_checkpoint_roundtrip():
+    big = torch.nn.Parameter(torch.randn(8192, device=DEV, dtype=torch.bfloat16))
+    small = torch.nn.Parameter(torch.randn(100, device=DEV))
+    opt = AdamW8bitDense([big, small], lr=1e-2, weight_decay=0.1)
+    for _ in range(2):
+        big.grad = torch.randn_like(big)
+        small.grad = torch.randn_like(small)
+        opt.step()
+    assert set(opt.state[big]) == {"step", "m_q", "m_absmax", "v_q", "v_absmax"}
+    assert opt.state[big]["m_absmax"].dtype == torch.float32
+    assert set(opt.state[small]) == {"step", "exp_avg", "exp_avg_sq"}
+    sd = opt.state_dict()
+    opt2 = AdamW8bitDense([big, small], lr=1e-2, weight_decay=0.1)
+    opt2.load_state_dict(sd)
+    for k in ("m_q", "m_absmax", "v_q", "v_absmax"):
+        assert torch.equal(opt2.state[big][k], opt.state[big][k]), k
+    assert opt2.state[big]["m_absmax"].dtype == torch.float32  # not cast to the bf16 parameter's dtype
