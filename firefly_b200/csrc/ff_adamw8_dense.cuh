@@ -17,7 +17,9 @@
 // map entry to value * (1 / absmax) (ties to the lower code).
 //
 // One CTA per block (256 threads x 8 consecutive elements, vector loads and stores), grid-stride
-// over blocks; the maps sit in shared memory in 16 replicas (bank-conflict-light lookups).
+// over blocks; the maps sit in shared memory in 8 replicas (bank-conflict-light decode), and the
+// nearest code is one read of a table of decision thresholds indexed by the value's exponent
+// and top fraction bits (see the threshold buckets below).
 #pragma once
 #include <cmath>
 
@@ -46,7 +48,7 @@ struct Params {
   const float* qu;
 };
 
-constexpr int kRep = 16;  // map replicas: entry i of replica r at word i*kRep + r (lanes l, l+16 share one)
+constexpr int kRep = 8;  // map replicas: entry i of replica r at word i*kRep + r (lanes l, l+8, ... share one)
 
 __device__ __forceinline__ float load_elem(const void* base, int dtype, int64_t i) {
   if (dtype == FF_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
@@ -72,7 +74,8 @@ __device__ __forceinline__ void load8(const void* base, int dtype, int64_t e0, f
 }
 
 // largest index i with q[i] <= x (q sorted ascending, q[0] <= x), then the nearer of i, i+1;
-// q is read from this lane's replica (qr = table + slot, stride kRep)
+// q is read from this lane's replica (qr = table + slot, stride kRep).  The general path, for
+// maps the bucket tables below cannot serve.
 __device__ __forceinline__ int nearest_code(const float* qr, float x) {
   int lo = 0;
 #pragma unroll
@@ -82,32 +85,117 @@ __device__ __forceinline__ int nearest_code(const float* qr, float x) {
   return lo;
 }
 
+// ---- threshold buckets
+// Over ascending magnitudes M[0..len) the nearest index of a >= 0 (the comparison of the two
+// rounded distances fsub(M[k+1], a) < fsub(a, M[k]), or <= when ties go to the larger
+// magnitude) is monotone in a, so it equals the number of thresholds t_k <= a, t_k being the
+// smallest float at which the choice between M[k] and M[k+1] flips to M[k+1].  A magnitude
+// falls in bucket
+//   b = clamp((bits(a) >> 16) - kBucketBias, 0, kBuckets - 1)
+// (bucket 0: [0, 2^-25); bucket b >= 1: the floats whose top 16 bits, exponent and 7 fraction
+// bits, are b + kBucketBias; the last: 1.0 and up).  When no bucket holds two thresholds, the
+// bucket's word is  count | (low 16 bits of the threshold inside it, or 0x10000 for none) << 8
+// and the nearest index is  count + [low16(a) >= word >> 8]:  one shared-memory read.  The
+// tables are built per CTA from the maps and checked; maps they cannot serve (unsorted,
+// asymmetric, more than one threshold in a bucket, values above 1) use the search above.
+constexpr int kBuckets = 25 * 128 + 2;
+constexpr int kBucketBias = (102 << 7) - 1;
+constexpr uint32_t kNoThreshold = 0x10000u;
+constexpr int kTables = 3;  // signed map's magnitudes (ties to smaller | larger), unsigned map
+constexpr int kSmemBytes = 2 * 256 * kRep * 4 + kTables * kBuckets * 4 + 2 * (kThreads / 32) * 4;
+
+__device__ __forceinline__ float bucket_start(int b) {
+  return b == 0 ? 0.f : __uint_as_float((uint32_t)(b + kBucketBias) << 16);
+}
+
+// whether a is past the threshold between M[k] = lo and M[k+1] = hi
+__device__ __forceinline__ bool takes_upper(float lo, float hi, float a, bool ties_up) {
+  const float du = __fsub_rn(hi, a), dl = __fsub_rn(a, lo);
+  return ties_up ? du <= dl : du < dl;
+}
+
+// nearest index by search over magnitudes read at stride kRep (replica 0)
+__device__ int nearest_index_search(const float* m0, int len, float a, bool ties_up) {
+  int lo = 0;
+  for (int step = 128; step > 0; step >>= 1)
+    if (lo + step < len && m0[(lo + step) * kRep] <= a) lo += step;
+  if (lo + 1 < len && takes_upper(m0[lo * kRep], m0[(lo + 1) * kRep], a, ties_up)) ++lo;
+  return lo;
+}
+
+// bucket word of bucket b; *bad set when the bucket cannot be described by one word
+__device__ uint32_t bucket_word(const float* m0, int len, bool ties_up, int b, int* bad) {
+  const int k = nearest_index_search(m0, len, bucket_start(b), ties_up);
+  const int kn = b + 1 < kBuckets ? nearest_index_search(m0, len, bucket_start(b + 1), ties_up) : k;
+  uint32_t thr = kNoThreshold;
+  if (kn - k > 1 || (kn > k && b == 0)) {
+    *bad = 1;
+  } else if (kn > k) {  // smallest low16 past the threshold, by bisection
+    const float lo = m0[k * kRep], hi = m0[(k + 1) * kRep];
+    const uint32_t top = (uint32_t)(b + kBucketBias) << 16;
+    int l = -1, h = (int)kNoThreshold;  // takes_upper false at l, true at h
+    while (h - l > 1) {
+      const int mid = (l + h) >> 1;
+      if (takes_upper(lo, hi, __uint_as_float(top | (uint32_t)mid), ties_up)) h = mid;
+      else l = mid;
+    }
+    thr = (uint32_t)h;
+  }
+  return (uint32_t)k | (thr << 8);
+}
+
+__device__ __forceinline__ uint32_t bucket_index(const uint32_t* bt, float a) {
+  const uint32_t bits = __float_as_uint(a);
+  const uint32_t w = bt[min(max((int)(bits >> 16) - kBucketBias, 0), kBuckets - 1)];
+  return (w & 0xFFu) + ((bits & 0xFFFFu) >= (w >> 8) ? 1u : 0u);
+}
+
 __global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
-  __shared__ float qs[256 * kRep], qu[256 * kRep];
-  __shared__ uint32_t red[2][kThreads / 32];
+  extern __shared__ __align__(16) uint32_t smem[];
+  float* qs = reinterpret_cast<float*>(smem);  // [256][kRep]
+  float* qu = qs + 256 * kRep;                 // [256][kRep]
+  uint32_t* bt = smem + 2 * 256 * kRep;        // [kTables][kBuckets]
+  uint32_t(*red)[kThreads / 32] = reinterpret_cast<uint32_t(*)[kThreads / 32]>(bt + kTables * kBuckets);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < 256 * kRep; i += kThreads) {
     qs[i] = p.qs[i / kRep];
     qu[i] = p.qu[i / kRep];
   }
   __syncthreads();
+  // tables over the signed map's non-negative half qs[128..255] (ties to the smaller magnitude
+  // for x >= 0, to the larger for x < 0: both are ties to the lower code) and the unsigned map
+  int bad = 0;
+  for (int i = tid; i < kTables * kBuckets; i += kThreads) {
+    const int t = i / kBuckets, b = i - t * kBuckets;
+    bt[i] = t < 2 ? bucket_word(qs + 128 * kRep, 128, t == 1, b, &bad) : bucket_word(qu, 256, false, b, &bad);
+  }
+  for (int k = tid; k < 256; k += kThreads) {
+    if (k < 128) bad |= qs[(127 - k) * kRep] != -qs[(128 + k) * kRep];
+    if (k > 0) bad |= !(qs[(k - 1) * kRep] < qs[k * kRep] || k == 128) || !(qu[(k - 1) * kRep] < qu[k * kRep]);
+  }
+  if (tid == 0) bad |= (qs[128 * kRep] != 0.f) | (qu[0] != 0.f) | !(qs[255 * kRep] <= 1.f) | !(qu[255 * kRep] <= 1.f);
+  const bool fast = !__syncthreads_or(bad);
+  const uint32_t* bt_dn = bt;
+  const uint32_t* bt_up = bt + kBuckets;
+  const uint32_t* bt_u = bt + 2 * kBuckets;
   const float* qsr = qs + (lane & (kRep - 1));
   const float* qur = qu + (lane & (kRep - 1));
   const int64_t nblocks = (p.n + kBlock - 1) / kBlock;
-  for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+  // one block's inputs for this thread: 8 elements of g and p, their m and v codes, and the
+  // block's absmax pair (elements past n get g = p = 0 and the zero codes)
+  auto load_block = [&](int64_t blk, float (&g)[kPer], float (&w)[kPer], uint32_t (&cm)[2], uint32_t (&cv)[2],
+                        float& am, float& av) {
     const int64_t e0 = blk * kBlock + (int64_t)tid * kPer;
-    const float am = p.m_absmax[blk], av = p.v_absmax[blk];
-    const bool full = e0 + kPer <= p.n;
-    float m[kPer], v[kPer], g[kPer], w[kPer];
-    uint32_t cm[2], cv[2];
-    if (full) {  // 16-byte (fp32: 2 x 16-byte) vectors and 8-byte code words
+    am = p.m_absmax[blk];
+    av = p.v_absmax[blk];
+    if (e0 + kPer <= p.n) {  // 16-byte (fp32: 2 x 16-byte) vectors and 8-byte code words
       load8(p.g, p.g_dtype, e0, g);
       load8(p.p, p.p_dtype, e0, w);
       const uint2 a = *reinterpret_cast<const uint2*>(p.m_q + e0), b = *reinterpret_cast<const uint2*>(p.v_q + e0);
       cm[0] = a.x; cm[1] = a.y;
       cv[0] = b.x; cv[1] = b.y;
     } else {
-      cm[0] = cm[1] = 0x80808080u;  // elements past n: the zero codes
+      cm[0] = cm[1] = 0x80808080u;
       cv[0] = cv[1] = 0u;
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
@@ -122,6 +210,18 @@ __global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
         }
       }
     }
+  };
+  // software pipeline: the next block's loads are in flight while this one is computed
+  float g[kPer], w[kPer], am = 0.f, av = 0.f;
+  uint32_t cm[2] = {0u, 0u}, cv[2] = {0u, 0u};
+  if ((int64_t)blockIdx.x < nblocks) load_block(blockIdx.x, g, w, cm, cv, am, av);
+  for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const int64_t e0 = blk * kBlock + (int64_t)tid * kPer;
+    const bool full = e0 + kPer <= p.n;
+    float gn[kPer], wn[kPer], amn = 0.f, avn = 0.f;
+    uint32_t cmn[2] = {0u, 0u}, cvn[2] = {0u, 0u};
+    if (blk + gridDim.x < nblocks) load_block(blk + gridDim.x, gn, wn, cmn, cvn, amn, avn);
+    float m[kPer], v[kPer];
     float mx_m = 0.f, mx_v = 0.f;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
@@ -154,11 +254,24 @@ __global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
     const float nam = __uint_as_float(bm), nav = __uint_as_float(bv);
     const float im = nam > 0.f ? __frcp_rn(nam) : 1.f, iv = nav > 0.f ? __frcp_rn(nav) : 1.f;
     uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
+    // |m| * (1/absmax) can exceed 1 by an ulp: both searches then return the code of 1.0
+    if (fast) {
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      // |m| * (1/absmax) can exceed 1 by an ulp: the search then returns the code of 1.0
-      om[j >> 2] |= (uint32_t)nearest_code(qsr, __fmul_rn(m[j], im)) << (8 * (j & 3));
-      ov[j >> 2] |= (uint32_t)nearest_code(qur, __fmul_rn(v[j], iv)) << (8 * (j & 3));
+      for (int j = 0; j < kPer; ++j) {
+        // signed: index k of |x| among the magnitudes -> code 128 + k, or 127 - k for x < 0;
+        // unsigned: code k
+        const float x = __fmul_rn(m[j], im);
+        const bool neg = x < 0.f;
+        const uint32_t k = bucket_index(neg ? bt_up : bt_dn, fabsf(x));
+        om[j >> 2] |= (neg ? 127u - k : 128u + k) << (8 * (j & 3));
+        ov[j >> 2] |= bucket_index(bt_u, __fmul_rn(v[j], iv)) << (8 * (j & 3));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        om[j >> 2] |= (uint32_t)nearest_code(qsr, __fmul_rn(m[j], im)) << (8 * (j & 3));
+        ov[j >> 2] |= (uint32_t)nearest_code(qur, __fmul_rn(v[j], iv)) << (8 * (j & 3));
+      }
     }
     if (full) {
       *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(om[0], om[1]);
@@ -192,6 +305,15 @@ __global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
       p.m_absmax[blk] = nam;
       p.v_absmax[blk] = nav;
     }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      g[j] = gn[j];
+      w[j] = wn[j];
+    }
+    cm[0] = cmn[0]; cm[1] = cmn[1];
+    cv[0] = cvn[0]; cv[1] = cvn[1];
+    am = amn;
+    av = avn;
   }
 }
 
@@ -238,13 +360,22 @@ extern "C" int ff_adamw8_blockwise(void* p, int p_dtype, const void* g, int g_dt
   prm.eps_hat = (float)(eps * std::sqrt(bc2));
   prm.qs = qmap_s;
   prm.qu = qmap_u;
-  int sms = 148;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // as many CTAs as are resident at once: each builds its tables once and strides over blocks
+  static int resident[64] = {0};
+  int dev = 0;
+  FF_CUDA_TRY(cudaGetDevice(&dev), "ff_adamw8_blockwise device");
+  if (dev < 0 || dev >= 64) return set_error(FF_ERR_UNSUPPORTED, "ff_adamw8_blockwise: device %d", dev);
+  if (resident[dev] == 0) {
+    FF_CUDA_TRY(cudaFuncSetAttribute(adamw8_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                "ff_adamw8_blockwise smem attribute");
+    int per_sm = 0, sms = 0;
+    FF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw8_dense_kernel, kThreads, kSmemBytes),
+                "ff_adamw8_blockwise occupancy");
+    FF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "ff_adamw8_blockwise SMs");
+    resident[dev] = max(1, per_sm) * sms;
   }
   const int64_t nblocks = (n + kBlock - 1) / kBlock;
-  const int grid = (int)min64(nblocks, (int64_t)sms * 8);
-  adamw8_dense_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(prm);
+  const int grid = (int)min64(nblocks, (int64_t)resident[dev]);
+  adamw8_dense_kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(prm);
   return check_launch("ff_adamw8_blockwise");
 }

@@ -455,15 +455,19 @@ def init_dense_state(n: int) -> dict:
             "v_q": np.zeros(n, np.uint8), "v_absmax": np.zeros(nb, np.float32)}
 
 
-def dense_adamw8_step(p, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01):
+def dense_adamw8_step(p, g, state, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01, qmaps=None):
     """One block-wise 8-bit AdamW step (fp32, every operation rounded once):
     m = b1*m + (1-b1)*g, v = b2*v + ((1-b2)*g)*g, p = p*(1-lr*wd) - a_t*(m/(sqrt(v)+e_t)) with
     a_t = lr*sqrt(bc2)/bc1, e_t = eps*sqrt(bc2) (Kingma & Ba, section 2), then per block of 2048
-    the absmax of |m| and v and the nearest codes of value*(1/absmax).  Returns (p, state)."""
+    the absmax of |m| and v and the nearest codes of value*(1/absmax).  ``qmaps`` = (signed,
+    unsigned) 256-entry ascending maps, the dynamic tree maps by default.  Returns (p, state)."""
     p = np.asarray(p, np.float32).ravel().copy()
     g = np.asarray(g, np.float32).ravel()
     n = p.size
-    qs, qu = dynamic_qmap(True), dynamic_qmap(False)
+    if qmaps is None:
+        qs, qu = dynamic_qmap(True), dynamic_qmap(False)
+    else:
+        qs, qu = (np.asarray(q, np.float32) for q in qmaps)
     t = state["step"] + 1
     blk = np.arange(n) // DENSE_BLOCK
     m0 = (qs[state["m_q"]] * state["m_absmax"][blk]).astype(np.float32)

@@ -83,3 +83,70 @@ def test_small_params_keep_fp32_moments_and_checkpoint_roundtrip():
     for k in ("m_q", "m_absmax", "v_q", "v_absmax"):
         assert torch.equal(opt2.state[big][k], opt.state[big][k]), k
     assert opt2.state[big]["m_absmax"].dtype == torch.float32  # not cast to the bf16 parameter's dtype
+
+
+def _encode_probe_grads(n, seed=0):
+    """Gradients whose values hit every map entry, every midpoint between neighbours and the
+    floats just either side of both, with 1.0 first in each block (so the block absmax of m is
+    1 and m * (1/absmax) = g when beta1 = 0)."""
+    qs = O.dynamic_qmap(True)
+    mids = ((qs[:-1].astype(np.float64) + qs[1:]) / 2).astype(np.float32)
+    pts = np.concatenate([qs, mids])
+    pts = np.concatenate([pts, np.nextafter(pts, np.float32(2)), np.nextafter(pts, np.float32(-2))])
+    pts = pts[np.abs(pts) <= 1].astype(np.float32)
+    rng = np.random.default_rng(seed)
+    rest = n - pts.size
+    extra = (rng.choice([-1, 1], rest) * 10.0 ** rng.uniform(-9, 0, rest)).astype(np.float32)
+    g = np.concatenate([pts, extra]).astype(np.float32)
+    rng.shuffle(g)
+    g[::2048] = 1.0
+    return g
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("betas", [(0.0, 0.0), (0.9, 0.999)])
+def test_codes_at_map_points_and_midpoints(betas):
+    n = 2048 * 8
+    g = _encode_probe_grads(n)
+    p = torch.nn.Parameter(torch.zeros(n, device=DEV))
+    opt = AdamW8bitDense([p], lr=1e-3, betas=betas, weight_decay=0.0)
+    p.grad = torch.from_numpy(g).to(DEV)
+    opt.step()
+    pn, sto = O.dense_adamw8_step(np.zeros(n, np.float32), g, O.init_dense_state(n), lr=1e-3, beta1=betas[0],
+                                  beta2=betas[1], wd=0.0)
+    st = opt.state[p]
+    for k in ("m_q", "v_q", "m_absmax", "v_absmax"):
+        np.testing.assert_array_equal(st[k].cpu().numpy(), sto[k], err_msg=k)
+    np.testing.assert_array_equal(p.detach().cpu().numpy(), pn)
+    if betas[0] == 0.0:  # m = g: its codes are the nearest entries of g itself
+        np.testing.assert_array_equal(st["m_q"].cpu().numpy(), O._nearest_codes(g, O.dynamic_qmap(True)))
+
+
+@pytest.mark.gpu
+def test_maps_without_bucket_property_take_the_search_path():
+    # a linear signed map has no zero entry and a dense unsigned one puts two entries in one
+    # bucket: the kernel must fall back to the binary search and still match the oracle
+    from firefly_b200 import _capi
+
+    qs = np.linspace(-1, 1, 256).astype(np.float32)
+    qu = np.concatenate([[0.0], np.sort(np.random.default_rng(1).uniform(0.999, 1.0, 254)), [1.0]]).astype(np.float32)
+    n = 2048 * 3 + 100
+    rng = np.random.default_rng(2)
+    g = (rng.standard_normal(n) * 1e-2).astype(np.float32)
+    p0 = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    st = O.init_dense_state(n)
+    st["m_q"][:] = 100
+    st["m_absmax"][:] = 1e-2
+    st["v_q"][:] = 7
+    st["v_absmax"][:] = 1e-5
+    pn, sto = O.dense_adamw8_step(p0, g, st, lr=1e-3, wd=0.01, qmaps=(qs, qu))
+    p = torch.from_numpy(p0).to(DEV)
+    m_q, v_q = torch.from_numpy(st["m_q"]).to(DEV), torch.from_numpy(st["v_q"]).to(DEV)
+    m_a, v_a = torch.from_numpy(st["m_absmax"]).to(DEV), torch.from_numpy(st["v_absmax"]).to(DEV)
+    _capi.adamw8_blockwise(p, torch.from_numpy(g).to(DEV), m_q, m_a, v_q, v_a, lr=1e-3, beta1=0.9, beta2=0.999,
+                           eps=1e-8, wd=0.01, step=1, qmap_s=torch.from_numpy(qs).to(DEV),
+                           qmap_u=torch.from_numpy(qu).to(DEV))
+    np.testing.assert_array_equal(p.cpu().numpy(), pn)
+    np.testing.assert_array_equal(m_q.cpu().numpy(), sto["m_q"])
+    np.testing.assert_array_equal(v_q.cpu().numpy(), sto["v_q"])
+    np.testing.assert_array_equal(m_a.cpu().numpy(), sto["m_absmax"])
