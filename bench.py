@@ -60,6 +60,9 @@ def parse_args():
     ap.add_argument("--adamw-params", type=float, default=6.7e9)
     ap.add_argument("--no-sub", action="store_true", help="skip the GEMM sweep and the AdamW sub-benchmarks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the 1.3B decoder data-parallel step")
+    ap.add_argument("--decoder-steps", type=int, default=3)
+    ap.add_argument("--decoder-warmup", type=int, default=2)
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
                                               "swiglu_gemm", "dense_adamw", "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
@@ -419,6 +422,60 @@ def adamw_bench(dev, params: float, peak_gbs: float):
             "bytes_per_param": ADAMW_BYTES_PER_PARAM, "frac_of_measured_hbm": round(gbs / peak_gbs, 3)}
 
 
+def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: int = 64, seq: int = 2048,
+                     micro: int = 8):
+    """Data-parallel training step of the 1.3B BitLinear decoder (24 layers, d 2048, 16 heads,
+    ffn 8192 GELU, vocab 32000) on a global batch of ``seqs`` sequences of ``seq`` tokens split
+    over the ranks (strong scaling), micro-batches of ``micro`` sequences, ZeRO-1 8-bit optimizer.
+    Every rank runs it; the time is the max over ranks of CUDA-event time."""
+    import torch
+    import torch.distributed as dist
+
+    from firefly_b200.decoder import DECODER_1P3B, attention_flops_per_sequence, build_decoder, synthetic_batches
+    from firefly_b200.decoder import train_step
+    from firefly_b200.distributed import ZeroFireFlyOptim
+
+    cfg = DECODER_1P3B
+    if seqs % world:
+        raise ValueError(f"global batch {seqs} is not divisible by {world} ranks")
+    per_rank = seqs // world
+    model = build_decoder(cfg, dev, seed=0)
+    opt = ZeroFireFlyOptim(model.bit_modules(), params=model.dense_parameters(), lr=1e-4, betas=(0.9, 0.999),
+                           eps=1e-8, weight_decay=0.01, seed=11)
+    batches = synthetic_batches(cfg, per_rank, seq, min(micro, per_rank), dev, seed=1000 + rank)
+    for _ in range(max(warmup, 1)):
+        train_step(model, opt, batches)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = train_step(model, opt, batches)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+    sec = float(sec.item())
+    tokens = seqs * seq * steps
+    out = {
+        "workload": (f"decoder_1p3b_dp_train_step: {cfg.layers} layers, d {cfg.d_model}, {cfg.heads} heads, ffn "
+                     f"{cfg.ffn} GELU, vocab {cfg.vocab}, all Linears BitLinear ({cfg.bit_params / 1e9:.3f}e9 int8 "
+                     f"params); global batch {seqs} x {seq} tokens over {world} GPU(s), micro-batches of "
+                     f"{min(micro, per_rank)}, ZeRO-1 8-bit DQT AdamW + 8-bit dense AdamW"),
+        "tokens_per_s": tokens / sec, "unit": "tokens/s", "scaling": "strong", "n_gpus": world,
+        "steps": steps, "warmup": max(warmup, 1), "ms_per_step": sec / steps * 1e3,
+        "int8_gemm_tops_effective": cfg.int8_ops_per_token() * tokens / sec / 1e12,
+        "attention_tflops_effective": attention_flops_per_sequence(cfg, seq) * seqs * steps / sec / 1e12,
+        "final_loss": float(loss), "data": "synthetic token ids uniform over the vocabulary; weights N(0,0.02)",
+    }
+    del model, opt, batches
+    torch.cuda.empty_cache()
+    return out
+
+
 # block-wise 8-bit AdamW of a dense fp32 parameter with an fp32 gradient: p r/w 8 + g 4 + m, v codes r/w 4
 # + two block absmax r/w (16 / 2048)
 DENSE_ADAMW_BYTES_PER_PARAM = 8 + 4 + 4 + 16 / 2048
@@ -626,9 +683,11 @@ def main():
 
     peaks = load_peaks()
     sub = {}
+    del model, opt
+    torch.cuda.empty_cache()
+    if not args.no_decoder:  # every rank: the data-parallel step
+        sub["decoder_1p3b_dp"] = decoder_dp_bench(dev, world, rank, args.decoder_steps, args.decoder_warmup)
     if rank == 0 and world == 1 and not args.no_sub:
-        del model, opt
-        torch.cuda.empty_cache()
         sub["int8_gemm_sweep"] = gemm_sweep(dev)
         sub["adamw8"] = adamw_bench(dev, args.adamw_params, peaks["hbm_gbs"])
         sub["dense_adamw8"] = dense_adamw_bench(dev, 268435456, peaks["hbm_gbs"])

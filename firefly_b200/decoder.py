@@ -1,0 +1,183 @@
+"""Decoder-only transformer with every Linear a BitLinear — the data-parallel training workload.
+
+The reference ships no model code; this is the harness for its 1.3B data-parallel
+configuration (24 layers, d_model 2048, 16 heads, ffn 8192 with GELU, vocab 32000,
+sequence 2048).  Per layer (pre-LayerNorm):
+
+    x = x + proj(attention(qkv(ln1(x))))        qkv: BitLinear d -> 3d, proj: BitLinear d -> d
+    x = x + down(gelu(up(ln2(x))))              up:  BitLinear d -> ffn, down: BitLinear ffn -> d
+
+then ``logits = lm_head(ln_f(x))`` (BitLinear d -> vocab) and the mean token cross-entropy.
+The residual stream is bf16; LayerNorm, GELU (tanh form), causal attention (torch's
+``scaled_dot_product_attention``) and the loss are torch ops around the BitLinear path.
+Dense parameters — token and position embeddings, LayerNorm weights and biases — are
+stepped by ``AdamW8bitDense`` (block-wise 8-bit for the embeddings, fp32 moments for the
+norms), the BitLinear weights by the fused DQT 8-bit AdamW, as ``FireFlyOptim`` splits
+them (fireflyoptim.py:83-211).
+
+``train_step`` runs one optimizer step over a list of micro-batches: the BitLinear weight
+gradients accumulate in the grad cache (fireflykernels.py:200-210), the dense gradients in
+``.grad``, and the optimizer steps once.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from .bitLinear import BitLinear, collect_bitlinear_modules
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    vocab: int = 32000
+    d_model: int = 2048
+    heads: int = 16
+    ffn: int = 8192
+    layers: int = 24
+    max_seq: int = 2048
+
+    @property
+    def bit_params(self) -> int:
+        d = self.d_model
+        return self.layers * (3 * d * d + d * d + 2 * d * self.ffn) + d * self.vocab
+
+    def int8_ops_per_token(self) -> float:
+        """Int8 GEMM operations per token of one training step (forward, dX and dW GEMMs)."""
+        return 6.0 * self.bit_params
+
+
+DECODER_1P3B = DecoderConfig()
+
+
+class LayerNormBF16(nn.Module):
+    """LayerNorm with fp32 parameters over a bf16 input (the parameters are cast per call)."""
+
+    def __init__(self, d: int, eps: float = 1e-5):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.bias = nn.Parameter(torch.zeros(d))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.layer_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.bias.to(x.dtype), self.eps)
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: DecoderConfig):
+        super().__init__()
+        d = cfg.d_model
+        if d % cfg.heads:
+            raise ValueError(f"d_model {d} is not a multiple of heads {cfg.heads}")
+        self.heads = cfg.heads
+        self.ln1 = LayerNormBF16(d)
+        self.qkv = BitLinear(d, 3 * d)
+        self.proj = BitLinear(d, d)
+        self.ln2 = LayerNormBF16(d)
+        self.up = BitLinear(d, cfg.ffn)
+        self.down = BitLinear(cfg.ffn, d)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, S, d = x.shape
+        hd = d // self.heads
+        # q, k, v as [B, H, S, hd] views of the packed [B, S, 3, H, hd] output (no copies; the
+        # backward of unbind writes their gradients into one packed buffer), and the attention
+        # output comes back in [B, S, H, hd] memory order, so the reshape below is a view
+        q, k, v = self.qkv(self.ln1(x)).view(B, S, 3, self.heads, hd).unbind(2)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+        x = x + self.proj(a.transpose(1, 2).reshape(B, S, d))
+        return x + self.down(F.gelu(self.up(self.ln2(x)), approximate="tanh"))
+
+
+class BitDecoder(nn.Module):
+    def __init__(self, cfg: DecoderConfig = DECODER_1P3B):
+        super().__init__()
+        self.cfg = cfg
+        self.tok = nn.Embedding(cfg.vocab, cfg.d_model)
+        self.pos = nn.Parameter(torch.zeros(cfg.max_seq, cfg.d_model))
+        self.layers = nn.ModuleList(DecoderLayer(cfg) for _ in range(cfg.layers))
+        self.ln_f = LayerNormBF16(cfg.d_model)
+        self.lm_head = BitLinear(cfg.d_model, cfg.vocab)
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        """Logits (bf16 [B, S, vocab]) of token ids [B, S]."""
+        S = ids.shape[1]
+        if S > self.cfg.max_seq:
+            raise ValueError(f"sequence {S} longer than max_seq {self.cfg.max_seq}")
+        x = (self.tok(ids) + self.pos[:S]).to(torch.bfloat16)
+        for layer in self.layers:
+            x = layer(x)
+        return self.lm_head(self.ln_f(x))
+
+    def loss(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        logits = self(ids)
+        return F.cross_entropy(logits.view(-1, logits.shape[-1]), targets.reshape(-1))
+
+    def bit_modules(self) -> list[BitLinear]:
+        return collect_bitlinear_modules(self)
+
+    def dense_parameters(self) -> list[nn.Parameter]:
+        return [p for p in self.parameters() if p.requires_grad]
+
+    @torch.no_grad()
+    def init_normal_(self, std: float = 0.02, generator: torch.Generator | None = None) -> None:
+        """Every weight ~ N(0, std) (BitLinear weights quantised per row), LayerNorms at (1, 0)."""
+        from .fireflykernels import quantize_fp_to_int8
+
+        for lin in self.bit_modules():
+            w = torch.empty(lin.out_features, lin.in_features, device=lin.int_weight.device)
+            w.normal_(0.0, std, generator=generator)
+            q, s = quantize_fp_to_int8(w)
+            lin.int_weight.copy_(q)
+            lin.weight_scale.copy_(s)
+        self.tok.weight.normal_(0.0, std, generator=generator)
+        self.pos.normal_(0.0, std, generator=generator)
+
+
+def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0) -> BitDecoder:
+    """The decoder on ``device`` with N(0, 0.02) weights drawn from a seeded generator."""
+    with torch.device(device):
+        model = BitDecoder(cfg)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    model.init_normal_(0.02, generator=gen)
+    return model
+
+
+def train_step(model: BitDecoder, opt, micro_batches: Sequence[tuple[torch.Tensor, torch.Tensor]]) -> torch.Tensor:
+    """One optimizer step over ``micro_batches`` of (ids, targets); returns the mean loss
+    (a device scalar, no host sync)."""
+    total = None
+    n = len(micro_batches)
+    for ids, targets in micro_batches:
+        loss = model.loss(ids, targets)
+        (loss / n).backward()
+        total = loss.detach() if total is None else total + loss.detach()
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    return total / n
+
+
+def synthetic_batches(cfg: DecoderConfig, sequences: int, seq: int, micro: int, device: torch.device,
+                      seed: int = 0) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Token ids uniform over the vocabulary, split into micro-batches of ``micro`` sequences;
+    the targets are the ids shifted by one."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    ids = torch.randint(0, cfg.vocab, (sequences, seq + 1), device=device, generator=gen)
+    out = []
+    for i in range(0, sequences, micro):
+        chunk = ids[i:i + micro]
+        out.append((chunk[:, :-1].contiguous(), chunk[:, 1:].contiguous()))
+    return out
+
+
+def attention_flops_per_sequence(cfg: DecoderConfig, seq: int) -> float:
+    """Causal attention matmul FLOPs of one training step per sequence (forward 2 matmuls,
+    backward 5, each 2·S·S/2·d per layer)."""
+    return cfg.layers * 7 * 2 * seq * (seq / 2) * cfg.d_model
+
+
+__all__ = ["DecoderConfig", "DECODER_1P3B", "BitDecoder", "DecoderLayer", "LayerNormBF16", "build_decoder",
+           "train_step", "synthetic_batches", "attention_flops_per_sequence"]
