@@ -63,6 +63,10 @@ def parse_args():
     ap.add_argument("--no-decoder", action="store_true", help="skip the 1.3B decoder data-parallel step")
     ap.add_argument("--decoder-steps", type=int, default=3)
     ap.add_argument("--decoder-warmup", type=int, default=2)
+    ap.add_argument("--zero-bucket-mb", type=float, default=256.0,
+                    help="ZeRO-1 gradient bucket size (MB of bf16); 0 = one bucket")
+    ap.add_argument("--zero-overlap", type=int, choices=[0, 1], default=1,
+                    help="start each bucket's reduce-scatter from the backward pass")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
                                               "swiglu_gemm", "dense_adamw", "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
@@ -423,7 +427,7 @@ def adamw_bench(dev, params: float, peak_gbs: float):
 
 
 def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: int = 64, seq: int = 2048,
-                     micro: int = 8):
+                     micro: int = 8, bucket_mb: float = 256.0, overlap: bool = True):
     """Data-parallel training step of the 1.3B BitLinear decoder (24 layers, d 2048, 16 heads,
     ffn 8192 GELU, vocab 32000) on a global batch of ``seqs`` sequences of ``seq`` tokens split
     over the ranks (strong scaling), micro-batches of ``micro`` sequences, ZeRO-1 8-bit optimizer.
@@ -441,7 +445,7 @@ def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: 
     per_rank = seqs // world
     model = build_decoder(cfg, dev, seed=0)
     opt = ZeroFireFlyOptim(model.bit_modules(), params=model.dense_parameters(), lr=1e-4, betas=(0.9, 0.999),
-                           eps=1e-8, weight_decay=0.01, seed=11)
+                           eps=1e-8, weight_decay=0.01, seed=11, bucket_mb=bucket_mb, overlap=overlap)
     batches = synthetic_batches(cfg, per_rank, seq, min(micro, per_rank), dev, seed=1000 + rank)
     for _ in range(max(warmup, 1)):
         train_step(model, opt, batches)
@@ -533,6 +537,32 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def bind_to_gpu_cpus(dev):
+    """Restrict this process to the CPU cores NVML reports as nearest to its GPU, so that the
+    pinned host buffers of the end-to-end run sit on the GPU's NUMA node.  Returns the core
+    count, or None when NVML cannot tell."""
+    try:
+        import pynvml
+        import torch
+
+        prop = torch.cuda.get_device_properties(dev)
+        bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, mask in enumerate(words) for b in range(64) if (int(mask) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:  # no NVML, or a device it does not list: keep the inherited affinity
+        return None
+    return None
+
+
 # ---------------------------------------------------------------------------
 # main arm
 # ---------------------------------------------------------------------------
@@ -559,6 +589,7 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    bound_cpus = bind_to_gpu_cpus(dev) if world > 1 else None
     if world > 1:
         # keep stdout to the one JSON line (NCCL's version banner would precede it)
         if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
@@ -569,7 +600,8 @@ def main():
     model = SwiGLUMLP(d, f).to(dev)
     model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
     mods = [model.gate_up, model.down]
-    opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7)
+    opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7,
+                           bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap))
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     # the block input is an activation of the model: it needs a gradient (dX is part of the step)
     # two resident input batches used alternately, so that every step quantises a new input
@@ -686,7 +718,8 @@ def main():
     del model, opt
     torch.cuda.empty_cache()
     if not args.no_decoder:  # every rank: the data-parallel step
-        sub["decoder_1p3b_dp"] = decoder_dp_bench(dev, world, rank, args.decoder_steps, args.decoder_warmup)
+        sub["decoder_1p3b_dp"] = decoder_dp_bench(dev, world, rank, args.decoder_steps, args.decoder_warmup,
+                                                  bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap))
     if rank == 0 and world == 1 and not args.no_sub:
         sub["int8_gemm_sweep"] = gemm_sweep(dev)
         sub["adamw8"] = adamw_bench(dev, args.adamw_params, peaks["hbm_gbs"])
@@ -726,10 +759,12 @@ def main():
             "workload": f"swiglu_mlp_train_step T={T}/GPU d={d} f={f} (BitLinear fwd+bwd + 8-bit DQT AdamW)",
             "tokens_per_gpu": T, "global_batch_tokens": T * world,
             "parallelism": f"dp{world}" + ("+zero1" if world > 1 else ""),
+            "zero1": {"bucket_mb": args.zero_bucket_mb, "overlap": bool(args.zero_overlap)},
             "l2": "inputs larger than L2 (step working set > 126 MB)",
         },
         "e2e": {"value": T * world * e2e_steps / e2e_sec, "unit": "tokens/s",
-                "h2d_bytes_per_step": int(xh.numel() * xh.element_size()), "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": int(xh.numel() * xh.element_size()), "d2h_bytes_per_step": 4,
+                "host_cpus_per_rank": bound_cpus},
         "gpu_launches": launches,
         "roofline": {
             "kernel": "ff_gemm_i8 (tcgen05 kind::i8)", "bound": "tensor",

@@ -21,6 +21,7 @@ gradients accumulate in the grad cache (fireflykernels.py:200-210), the dense gr
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -148,12 +149,17 @@ def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0) -> Bi
 
 def train_step(model: BitDecoder, opt, micro_batches: Sequence[tuple[torch.Tensor, torch.Tensor]]) -> torch.Tensor:
     """One optimizer step over ``micro_batches`` of (ids, targets); returns the mean loss
-    (a device scalar, no host sync)."""
+    (a device scalar, no host sync).  With a data-parallel optimizer that has ``no_sync``
+    (``ZeroFireFlyOptim``), every backward but the last only accumulates, and the last one
+    starts the gradient reduction bucket by bucket."""
     total = None
     n = len(micro_batches)
-    for ids, targets in micro_batches:
-        loss = model.loss(ids, targets)
-        (loss / n).backward()
+    for k, (ids, targets) in enumerate(micro_batches):
+        last = k == n - 1
+        ctx = opt.no_sync() if (not last and hasattr(opt, "no_sync")) else contextlib.nullcontext()
+        with ctx:
+            loss = model.loss(ids, targets)
+            (loss / n).backward()
         total = loss.detach() if total is None else total + loss.detach()
     opt.step()
     opt.zero_grad(set_to_none=True)

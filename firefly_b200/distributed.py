@@ -13,16 +13,21 @@ stays on one GPU), then
    ``int_weight`` is a view of) are all-gathered back to every rank.
 
 Per step and rank that moves (p-1)/p x (2 + 1) bytes per parameter over NVLink.
+The arena is split into buckets of whole modules: a bucket's reduce-scatter starts from
+the backward pass once its last weight gradient is issued (overlapping the rest of the
+backward), and its all-gather right after its update (overlapping the next bucket's).
 
-Arena layout: module i occupies elements ``[off_i, off_i + numel_i)`` with
-``off_i`` a multiple of 256, in ``bit_modules`` order, so its 256-element
-optimizer blocks are exactly the reference's per-module blocks
-(fireflyoptim.py:13-19, :142-161), and the global element index that keys the
-stochastic-rounding uniforms is the same on 1 GPU (``FireFlyOptim``) and on
-any number of GPUs: the sharded update equals the single-GPU update.
+Arena layout: buckets of consecutive modules in ``bit_modules`` order; inside a bucket
+module i occupies ``[off_i, off_i + numel_i)`` with ``off_i`` a multiple of 256, so its
+256-element optimizer blocks are exactly the reference's per-module blocks
+(fireflyoptim.py:13-19, :142-161).  The global element index that keys the
+stochastic-rounding uniforms (module starts rounded up to 256, no bucket padding) is the
+same on 1 GPU (``FireFlyOptim``) and on any number of GPUs: the sharded update equals the
+single-GPU update.
 """
 from __future__ import annotations
 
+from contextlib import contextmanager
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
@@ -32,7 +37,7 @@ import torch.distributed as dist
 from . import _capi
 from .adamw8 import AdamW8bitDense
 from .bitLinear import BitLinear
-from .fireflykernels import _BIT_GRAD_CACHE, _invalidate_weight_cache, set_grad_slot
+from .fireflykernels import _BIT_GRAD_CACHE, _invalidate_weight_cache, set_grad_ready_hook, set_grad_slot
 from .fireflyoptim import BLOCK, _tables_on, bit_rng_offsets
 
 
@@ -44,35 +49,104 @@ class Segment:
     lo: int  # arena element range [lo, hi)
     hi: int
     elem_base: int  # element index of ``lo`` within the module's weight
+    rng: int  # global element index of ``lo`` (keys the stochastic rounding; world-size independent)
+    local: int  # index of ``lo`` in this rank's state arrays
+    bucket: int
+
+
+@dataclass(frozen=True)
+class Bucket:
+    """Consecutive modules whose gradients are reduced (and weights gathered) by one collective."""
+
+    modules: tuple[int, ...]
+    lo: int  # arena range [lo, lo + size)
+    size: int  # a multiple of block * world_size; rank r owns [lo + r*size/world, lo + (r+1)*size/world)
+    local: int  # start of this rank's slice in the state arrays
 
 
 class ShardPlan:
-    """Which arena elements (and module pieces) each rank updates.  Pure host logic."""
+    """Which arena elements (and module pieces) each rank updates.  Pure host logic.
 
-    def __init__(self, numels: Sequence[int], world_size: int, rank: int, block: int = BLOCK):
+    Modules are grouped, in order, into buckets of at least ``bucket_elems`` elements (0: one
+    bucket).  Inside a bucket every module starts at a multiple of ``block``; a bucket is padded
+    to a multiple of ``block * world_size`` and each rank owns the same 1/world slice of every
+    bucket, so a bucket's gradients are one reduce-scatter and its weights one all-gather.
+    The global element index of a weight element (``rng_offsets[i]`` + its index in module i,
+    module starts rounded up to ``block``) does not depend on the world size or the buckets.
+    """
+
+    def __init__(self, numels: Sequence[int], world_size: int, rank: int, block: int = BLOCK,
+                 bucket_elems: int = 0):
         if world_size < 1 or not 0 <= rank < world_size:
             raise ValueError(f"bad rank {rank} of {world_size}")
         self.block = block
         self.numels = [int(n) for n in numels]
-        self.offsets = []
+        self.world_size, self.rank = world_size, rank
+        self.rng_offsets = []
         off = 0
         for n in self.numels:
-            self.offsets.append(off)
+            self.rng_offsets.append(off)
             off += _capi.round_up(n, block)
         self.used = off
-        self.total = _capi.round_up(max(off, 1), block * world_size)
-        self.world_size, self.rank = world_size, rank
-        self.shard = self.total // world_size
-        self.lo, self.hi = rank * self.shard, (rank + 1) * self.shard
+        groups, cur, cur_elems = [], [], 0
+        for i, n in enumerate(self.numels):
+            cur.append(i)
+            cur_elems += _capi.round_up(n, block)
+            if bucket_elems > 0 and cur_elems >= bucket_elems:
+                groups.append(cur)
+                cur, cur_elems = [], 0
+        if cur or not groups:
+            groups.append(cur)
+        self.offsets = [0] * len(self.numels)
+        self.buckets: list[Bucket] = []
+        arena = local = 0
+        for mods in groups:
+            start = self.rng_offsets[mods[0]] if mods else 0
+            inner = sum(_capi.round_up(self.numels[i], block) for i in mods)
+            size = _capi.round_up(max(inner, 1), block * world_size)
+            for i in mods:
+                self.offsets[i] = arena + self.rng_offsets[i] - start
+            self.buckets.append(Bucket(tuple(mods), arena, size, local))
+            arena += size
+            local += size // world_size
+        self.total = arena
+        self.shard = local  # state elements on each rank
+        self.bucket_of = [0] * len(self.numels)
         self.segments: list[Segment] = []
-        for i, (o, n) in enumerate(zip(self.offsets, self.numels)):
-            a, b = max(o, self.lo), min(o + n, self.hi)
-            if a < b:
-                self.segments.append(Segment(i, a, b, a - o))
+        for bi, bk in enumerate(self.buckets):
+            lo, hi = self.rank_slice(bi)
+            for i in bk.modules:
+                self.bucket_of[i] = bi
+                o, n = self.offsets[i], self.numels[i]
+                a, e = max(o, lo), min(o + n, hi)
+                if a < e:
+                    self.segments.append(Segment(i, a, e, a - o, self.rng_offsets[i] + a - o, bk.local + a - lo, bi))
+
+    def rank_slice(self, bucket: int, rank: int | None = None) -> tuple[int, int]:
+        """Arena range of ``rank``'s slice of a bucket (this rank by default)."""
+        bk = self.buckets[bucket]
+        r = self.rank if rank is None else rank
+        s = bk.size // self.world_size
+        return bk.lo + r * s, bk.lo + (r + 1) * s
 
     def local_blocks(self, seg: Segment) -> tuple[int, int]:
         """Block range of ``seg`` within this rank's absmax arrays."""
-        return (seg.lo - self.lo) // self.block, (seg.hi - self.lo + self.block - 1) // self.block
+        return seg.local // self.block, (seg.local + seg.hi - seg.lo + self.block - 1) // self.block
+
+    def to_arena(self, gathered: torch.Tensor, unit: int = 1) -> torch.Tensor:
+        """Reorder the rank-major concatenation of every rank's state array (``world * shard / unit``
+        entries, ``unit`` arena elements per entry) into arena order (``total / unit`` entries)."""
+        if self.world_size == 1:
+            return gathered
+        out = torch.empty((self.total // unit,), dtype=gathered.dtype, device=gathered.device)
+        per = self.shard // unit
+        for bk in self.buckets:
+            s = bk.size // self.world_size // unit
+            for r in range(self.world_size):
+                src = r * per + bk.local // unit
+                dst = bk.lo // unit + r * s
+                out[dst:dst + s] = gathered[src:src + s]
+        return out
 
 
 class BitArena:
@@ -83,13 +157,14 @@ class BitArena:
     """
 
     def __init__(self, modules: Sequence[BitLinear], world_size: int = 1, rank: int = 0,
-                 device: torch.device | None = None):
+                 device: torch.device | None = None, bucket_elems: int = 0):
         self.modules = list(modules)
         if not self.modules:
             raise ValueError("BitArena needs at least one BitLinear")
         device = device or self.modules[0].int_weight.device
-        self.plan = ShardPlan([m.int_weight.numel() for m in self.modules], world_size, rank)
-        assert self.plan.offsets == bit_rng_offsets(self.modules)
+        self.plan = ShardPlan([m.int_weight.numel() for m in self.modules], world_size, rank,
+                              bucket_elems=bucket_elems)
+        assert self.plan.rng_offsets == bit_rng_offsets(self.modules)
         self.q = torch.zeros(self.plan.total, dtype=torch.int8, device=device)
         self.g = torch.zeros(self.plan.total, dtype=torch.bfloat16, device=device)
         self.g_views = []
@@ -102,6 +177,18 @@ class BitArena:
             set_grad_slot(m._registered_handle, gv)
             self.g_views.append(gv)
 
+    def take_grad(self, i: int) -> bool:
+        """Make module i's slot hold its gradient of this step (copying one that was set by hand
+        elsewhere); False when it has none."""
+        m, gv = self.modules[i], self.g_views[i]
+        g = _BIT_GRAD_CACHE.get(m._registered_handle)
+        if g is None:
+            return False
+        if g.data_ptr() != gv.data_ptr():
+            gv.copy_(g.reshape(gv.shape))
+            _BIT_GRAD_CACHE[m._registered_handle] = gv
+        return True
+
     def collect_grads(self) -> list[bool]:
         """Hand the gradients of this step over from the grad cache to the arena.
 
@@ -111,23 +198,13 @@ class BitArena:
         set by hand) is copied in.
         """
         has = []
-        for m, gv in zip(self.modules, self.g_views):
-            g = _BIT_GRAD_CACHE.pop(m._registered_handle, None)
-            if g is None:
+        for i, (m, gv) in enumerate(zip(self.modules, self.g_views)):
+            h = self.take_grad(i)
+            _BIT_GRAD_CACHE.pop(m._registered_handle, None)
+            if not h:
                 gv.zero_()
-            elif g.data_ptr() != gv.data_ptr():
-                gv.copy_(g.reshape(gv.shape))
-            has.append(g is not None)
+            has.append(h)
         return has
-
-
-def _reduce_scatter_avg(out: torch.Tensor, inp: torch.Tensor, group) -> None:
-    ws = dist.get_world_size(group)
-    if dist.get_backend(group) == "nccl":
-        dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.AVG, group=group)
-    else:  # gloo: no AVG
-        dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM, group=group)
-        out.div_(ws)
 
 
 class ZeroFireFlyOptim:
@@ -135,7 +212,16 @@ class ZeroFireFlyOptim:
 
     Same hyperparameters and update as ``FireFlyOptim`` (fireflyoptim.py:86-211).
     Call ``step()`` after the backward pass of every rank.  Dense parameters
-    (``params``) are all-reduced (average) and stepped by AdamW on every rank.
+    (``params``) are all-reduced (average) and stepped by ``AdamW8bitDense`` on every rank.
+
+    The arena is split into buckets of whole modules (``bucket_mb`` of bf16 gradient each).
+    With ``overlap`` (and more than one rank) a bucket's reduce-scatter is issued from the
+    backward pass as soon as the weight-gradient GEMM of its last module has been issued,
+    so it runs under the rest of the backward; ``step()`` then updates the buckets in that
+    order, each as soon as its reduction is done, and issues each bucket's weight all-gather
+    right after its update.  With gradient accumulation, run every backward but the last of
+    a step under ``no_sync()`` (each BitLinear must produce one weight gradient per synced
+    backward).
 
     ``update_fn`` (default: the ``ff_dqt_adamw8`` kernel) receives keyword
     arguments for one segment; it exists so the sharding and collectives can be
@@ -144,7 +230,8 @@ class ZeroFireFlyOptim:
 
     def __init__(self, bit_modules: Sequence[BitLinear], params=(), lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
                  weight_decay=0.1, block_size=256, sr_bias_scale=0.15, process_group=None,
-                 update_fn: Callable | None = None, seed: int | None = None):
+                 update_fn: Callable | None = None, seed: int | None = None, bucket_mb: float = 256.0,
+                 overlap: bool = True):
         if int(block_size) != BLOCK:
             raise ValueError(f"block_size must be {BLOCK} on this build")
         self.group = process_group
@@ -156,7 +243,8 @@ class ZeroFireFlyOptim:
                 raise TypeError(f"expected BitLinear, got {type(m).__name__}")
         self.lr, self.betas, self.eps, self.wd = float(lr), tuple(betas), float(eps), float(weight_decay)
         self.sr_bias_scale = float(sr_bias_scale)
-        self.arena = BitArena(self.modules, self.world, self.rank)
+        bucket_elems = int(bucket_mb * 2**20) // 2 if bucket_mb and bucket_mb > 0 else 0
+        self.arena = BitArena(self.modules, self.world, self.rank, bucket_elems=bucket_elems)
         self.plan = self.arena.plan
         dev = self.arena.q.device
         n = self.plan.shard
@@ -187,6 +275,82 @@ class ZeroFireFlyOptim:
                 dist.broadcast(p.data, src=0, group=self.group)
         for m in self.modules:
             _invalidate_weight_cache(m._registered_handle)
+        # overlapped gradient reduction
+        self._nccl = self.world > 1 and dist.get_backend(self.group) == "nccl"
+        self._sync = True
+        self._module_of = {m._registered_handle: i for i, m in enumerate(self.modules)}
+        self._reset_pending()
+        self.overlap = bool(overlap) and self.world > 1
+        if self.overlap:
+            for m in self.modules:
+                set_grad_ready_hook(m._registered_handle, self._on_grad_ready)
+
+    # -- overlapped reduction ----------------------------------------------------
+    def _reset_pending(self) -> None:
+        self._ready: set[int] = set()
+        self._remaining = [len(b.modules) for b in self.plan.buckets]
+        self._rs_work: dict[int, object] = {}
+        self._rs_order: list[int] = []
+
+    @contextmanager
+    def no_sync(self):
+        """Backward passes inside only accumulate gradients (no reduction is issued)."""
+        prev, self._sync = self._sync, False
+        try:
+            yield
+        finally:
+            self._sync = prev
+
+    def _on_grad_ready(self, handle: int) -> None:
+        if not self._sync:
+            return
+        i = self._module_of[handle]
+        if i in self._ready:
+            raise RuntimeError(
+                f"BitLinear handle {handle} produced a second weight gradient in one synced backward; run the "
+                "accumulating backward passes under no_sync(), or construct ZeroFireFlyOptim with overlap=False")
+        self.arena.take_grad(i)
+        self._ready.add(i)
+        b = self.plan.bucket_of[i]
+        self._remaining[b] -= 1
+        if self._remaining[b] == 0:
+            self._launch_reduce(b)
+
+    def _launch_reduce(self, b: int) -> None:
+        bk = self.plan.buckets[b]
+        s = bk.size // self.world
+        out, inp = self.g_shard[bk.local:bk.local + s], self.arena.g[bk.lo:bk.lo + bk.size]
+        op = dist.ReduceOp.AVG if self._nccl else dist.ReduceOp.SUM  # gloo has no AVG
+        self._rs_work[b] = dist.reduce_scatter_tensor(out, inp, op=op, group=self.group, async_op=True)
+        self._rs_order.append(b)
+
+    def _finish_reduce(self, b: int) -> None:
+        self._rs_work.pop(b).wait()  # the current stream waits for the reduction
+        if not self._nccl:
+            bk = self.plan.buckets[b]
+            s = bk.size // self.world
+            self.g_shard[bk.local:bk.local + s].div_(self.world)
+
+    def _launch_dense_reduce(self):
+        """One all-reduce (average) per dtype over the flattened dense gradients."""
+        groups: dict[torch.dtype, list[torch.Tensor]] = {}
+        for p in self.dense:
+            if p.grad is not None:
+                groups.setdefault(p.grad.dtype, []).append(p.grad)
+        pending = []
+        for grads in groups.values():
+            flat = torch._utils._flatten_dense_tensors(grads)
+            op = dist.ReduceOp.AVG if self._nccl else dist.ReduceOp.SUM
+            pending.append((grads, flat, dist.all_reduce(flat, op=op, group=self.group, async_op=True)))
+        return pending
+
+    def _finish_dense_reduce(self, pending) -> None:
+        for grads, flat, work in pending:
+            work.wait()
+            if not self._nccl:
+                flat.div_(self.world)
+            for g, f in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+                g.copy_(f)
 
     # -- the per-segment update ------------------------------------------------
     def _kernel_update(self, *, q, wscale, row_len, elem_base, g, m_q, m_absmax, v_q, v_absmax, r_q, r_absmax,
@@ -197,38 +361,59 @@ class ZeroFireFlyOptim:
                          step=step, sr_bias=self.sr_bias_scale, seed=self.rng_seed, rng_offset=rng_offset,
                          elem_base=elem_base, dec_s=dec_s, dec_u=dec_u)
 
+    def _update_bucket(self, b: int, g_local: torch.Tensor, has_grad: list[bool]) -> None:
+        plan = self.plan
+        for seg in self._segments_of[b]:
+            if not has_grad[seg.module]:
+                continue
+            m = self.modules[seg.module]
+            a, e = seg.local, seg.local + seg.hi - seg.lo
+            ba, bb = plan.local_blocks(seg)
+            self.update_fn(
+                q=self.arena.q[seg.lo:seg.hi], wscale=m.weight_scale, row_len=m.in_features,
+                elem_base=seg.elem_base, g=g_local[a:e], m_q=self.m_q[a:e], m_absmax=self.m_absmax[ba:bb],
+                v_q=self.v_q[a:e], v_absmax=self.v_absmax[ba:bb], r_q=self.r_q[a:e],
+                r_absmax=self.r_absmax[ba:bb], step=self.steps[seg.module], rng_offset=seg.rng,
+            )
+
+    @property
+    def _segments_of(self) -> list[list[Segment]]:
+        segs = getattr(self, "_segs_cache", None)
+        if segs is None:
+            segs = [[] for _ in self.plan.buckets]
+            for seg in self.plan.segments:
+                segs[seg.bucket].append(seg)
+            self._segs_cache = segs
+        return segs
+
     @torch.no_grad()
     def step(self) -> None:
         plan = self.plan
         has_grad = self.arena.collect_grads()
-        if self.world > 1:
-            _reduce_scatter_avg(self.g_shard, self.arena.g, self.group)
-            g_local = self.g_shard
-        else:
-            g_local = self.arena.g[plan.lo:plan.hi]
         for i, h in enumerate(has_grad):
             self.steps[i] += int(h)
-        for seg in plan.segments:
-            if not has_grad[seg.module]:
-                continue
-            m = self.modules[seg.module]
-            a, b = seg.lo - plan.lo, seg.hi - plan.lo
-            ba, bb = plan.local_blocks(seg)
-            self.update_fn(
-                q=self.arena.q[seg.lo:seg.hi], wscale=m.weight_scale, row_len=m.in_features,
-                elem_base=seg.elem_base, g=g_local[a:b], m_q=self.m_q[a:b], m_absmax=self.m_absmax[ba:bb],
-                v_q=self.v_q[a:b], v_absmax=self.v_absmax[ba:bb], r_q=self.r_q[a:b],
-                r_absmax=self.r_absmax[ba:bb], step=self.steps[seg.module], rng_offset=seg.lo,
-            )
         if self.world > 1:
-            dist.all_gather_into_tensor(self.arena.q, self.arena.q[plan.lo:plan.hi], group=self.group)
-            for p in self.dense:
-                if p.grad is not None:
-                    if dist.get_backend(self.group) == "nccl":
-                        dist.all_reduce(p.grad, op=dist.ReduceOp.AVG, group=self.group)
-                    else:
-                        dist.all_reduce(p.grad, group=self.group)
-                        p.grad.div_(self.world)
+            # buckets not reduced during the backward (no overlap, or a module without a
+            # gradient, whose slot now holds zeros) are reduced now, last bucket first
+            for b in reversed(range(len(plan.buckets))):
+                if b not in self._rs_order:
+                    self._launch_reduce(b)
+            dense = self._launch_dense_reduce()
+            gathers = []
+            for b in list(self._rs_order):
+                self._finish_reduce(b)
+                self._update_bucket(b, self.g_shard, has_grad)
+                bk = plan.buckets[b]
+                lo, hi = plan.rank_slice(b)
+                gathers.append(dist.all_gather_into_tensor(self.arena.q[bk.lo:bk.lo + bk.size], self.arena.q[lo:hi],
+                                                           group=self.group, async_op=True))
+            self._finish_dense_reduce(dense)
+            for w in gathers:
+                w.wait()  # the next forward reads the gathered weights
+        else:
+            for b in range(len(plan.buckets)):
+                self._update_bucket(b, self.arena.g, has_grad)
+        self._reset_pending()
         if self.dense_opt is not None:
             self.dense_opt.step()
         for m in self.modules:
@@ -239,7 +424,7 @@ class ZeroFireFlyOptim:
             self.dense_opt.zero_grad(set_to_none=set_to_none)
 
     def shard_state(self) -> dict:
-        """This rank's 8-bit states (flat, shard-local)."""
+        """This rank's 8-bit states (flat, shard-local: the rank's slice of every bucket)."""
         return {"m_q": self.m_q, "m_absmax": self.m_absmax, "v_q": self.v_q, "v_absmax": self.v_absmax,
                 "r_q": self.r_q, "r_absmax": self.r_absmax, "steps": list(self.steps)}
 
@@ -251,15 +436,15 @@ class ZeroFireFlyOptim:
         """
         plan = self.plan
         full = {}
-        for key, is_abs in (("m_q", False), ("v_q", False), ("r_q", False),
-                            ("m_absmax", True), ("v_absmax", True), ("r_absmax", True)):
+        for key, unit in (("m_q", 1), ("v_q", 1), ("r_q", 1), ("m_absmax", BLOCK), ("v_absmax", BLOCK),
+                          ("r_absmax", BLOCK)):
             local = getattr(self, key)
             if self.world > 1:
                 out = torch.empty((local.numel() * self.world,), dtype=local.dtype, device=local.device)
                 dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
             else:
                 out = local
-            full[key] = out
+            full[key] = plan.to_arena(out, unit)
         if self.rank != 0:
             return None
         res = {}
@@ -285,24 +470,27 @@ class ZeroFireFlyOptim:
         Every rank passes the same dict (e.g. each loads the checkpoint file); the world size
         may differ from the one that saved it.  Modules absent from the dict keep fresh states.
         """
-        plan = self.plan
+        def entry(m):
+            return bit_state.get(m._registered_handle, bit_state.get(str(m._registered_handle)))
+
         for i, m in enumerate(self.modules):
-            ent = bit_state.get(m._registered_handle, bit_state.get(str(m._registered_handle)))
+            ent = entry(m)
+            if ent is not None:
+                self.steps[i] = int(ent["step"])
+        for seg in self.plan.segments:
+            ent = entry(self.modules[seg.module])
             if ent is None:
                 continue
-            self.steps[i] = int(ent["step"])
-            off, n = plan.offsets[i], plan.numels[i]
-            a, b = max(off, plan.lo), min(off + n, plan.hi)
-            if a >= b:
-                continue
+            n = seg.hi - seg.lo
             for key in ("m_q", "v_q", "r_q"):
-                src = ent[key].reshape(-1)[a - off:b - off]
-                getattr(self, key)[a - plan.lo:b - plan.lo].copy_(src.to(getattr(self, key).device))
-            ga, gb = a // BLOCK, (b + BLOCK - 1) // BLOCK  # global 256-element blocks
+                src = ent[key].reshape(-1)[seg.elem_base:seg.elem_base + n]
+                getattr(self, key)[seg.local:seg.local + n].copy_(src.to(getattr(self, key).device))
+            ba, bb = self.plan.local_blocks(seg)
+            g0 = seg.elem_base // BLOCK
             for key in ("m_absmax", "v_absmax", "r_absmax"):
-                src = ent[key].reshape(-1)[ga - off // BLOCK:gb - off // BLOCK]
+                src = ent[key].reshape(-1)[g0:g0 + bb - ba]
                 dst = getattr(self, key)
-                dst[ga - plan.lo // BLOCK:gb - plan.lo // BLOCK].copy_(src.to(dst.device))
+                dst[ba:bb].copy_(src.to(dst.device))
 
     def state_dict(self) -> dict:
         """Collective (every rank calls it): ``bit_state`` in the reference layout on rank 0

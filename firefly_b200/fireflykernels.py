@@ -28,6 +28,8 @@ is no CPU path.
 """
 from __future__ import annotations
 
+from typing import Callable
+
 import torch
 
 from . import _capi
@@ -42,6 +44,24 @@ _BIT_GRAD_CACHE: dict[int, torch.Tensor] = {}
 # data-parallel path).  When a handle has a slot and the cache is empty, the dW
 # GEMM writes straight into the slot instead of allocating.
 _GRAD_SLOTS: dict[int, torch.Tensor] = {}
+# Called with the handle once that handle's weight gradient of the current backward has been
+# issued (the data-parallel optimizer starts reducing a bucket of gradients from them).
+_GRAD_READY_HOOKS: dict[int, Callable[[int], None]] = {}
+
+
+def set_grad_ready_hook(handle: int, fn) -> None:
+    """Register ``fn(handle)`` to run after each weight-gradient GEMM of ``handle`` is issued
+    (``None`` removes it)."""
+    if fn is None:
+        _GRAD_READY_HOOKS.pop(int(handle), None)
+    else:
+        _GRAD_READY_HOOKS[int(handle)] = fn
+
+
+def _grad_ready(handle: int) -> None:
+    fn = _GRAD_READY_HOOKS.get(handle)
+    if fn is not None:
+        fn(handle)
 
 
 def next_bit_handle() -> int:
@@ -71,6 +91,7 @@ def release_bit_handle(handle: int) -> None:
     _REGISTERED_HANDLES.discard(handle)
     _BIT_GRAD_CACHE.pop(handle, None)
     _GRAD_SLOTS.pop(handle, None)
+    _GRAD_READY_HOOKS.pop(handle, None)
     _W_CACHE.pop(handle, None)
 
 
@@ -272,6 +293,7 @@ def _weight_grad_gemm(handle, q_dyt, s_dy, q_xt, s_xc, O, K, T, device):
         gw = _capi.gemm_i8(q_dyt, q_xt, T, scale_a=s_dy, scale_b=s_xc,
                            out_kind=_capi.FF_OUT_BF16)
         cached.add_(gw.to(device=cached.device, dtype=cached.dtype))
+    _grad_ready(handle)
 
 
 def _accumulate_weight_grad(handle: int, gw: torch.Tensor) -> None:
@@ -280,6 +302,7 @@ def _accumulate_weight_grad(handle: int, gw: torch.Tensor) -> None:
         _BIT_GRAD_CACHE[handle] = gw
     else:
         cached.add_(gw.to(dtype=cached.dtype))
+    _grad_ready(handle)
 
 
 # ---------------------------------------------------------------------------

@@ -18,28 +18,52 @@ WD, LR, SEED = 0.01, 1e-3, 1234
 SHAPES = [(48, 80), (33, 70), (16, 256), (7, 40)]
 
 
-def test_shard_plan_covers_every_element_once():
+@pytest.mark.parametrize("bucket_elems", [0, 1, 5000])
+def test_shard_plan_covers_every_element_once(bucket_elems):
     numels = [o * k for o, k in SHAPES]
+    rng_starts = np.cumsum([0] + [-(-n // 256) * 256 for n in numels[:-1]])
     for world in (1, 2, 3, 4, 8):
         seen = np.zeros(sum(numels), np.int64)
         flat_starts = np.cumsum([0] + numels[:-1])
         total = None
         for rank in range(world):
-            plan = ShardPlan(numels, world, rank)
+            plan = ShardPlan(numels, world, rank, bucket_elems=bucket_elems)
             total = plan.total
             assert plan.total % (256 * world) == 0 and plan.shard * world == plan.total
             assert all(o % 256 == 0 for o in plan.offsets)
+            assert plan.rng_offsets == list(rng_starts)
+            if bucket_elems == 1:
+                assert len(plan.buckets) == len(numels)
+            for bi, bk in enumerate(plan.buckets):
+                assert bk.size % (256 * world) == 0
+                assert all(plan.bucket_of[i] == bi for i in bk.modules)
+            local_seen = np.zeros(plan.shard, np.int64)
             for seg in plan.segments:
-                assert plan.lo <= seg.lo < seg.hi <= plan.hi
-                assert seg.lo % 256 == 0
+                lo, hi = plan.rank_slice(seg.bucket)
+                assert lo <= seg.lo < seg.hi <= hi
+                assert seg.lo % 256 == 0 and seg.local % 256 == 0
                 off = plan.offsets[seg.module]
                 assert seg.elem_base == seg.lo - off and seg.hi <= off + numels[seg.module]
+                assert seg.rng == rng_starts[seg.module] + seg.elem_base
+                assert seg.local == plan.buckets[seg.bucket].local + seg.lo - lo
+                local_seen[seg.local:seg.local + seg.hi - seg.lo] += 1
                 start = flat_starts[seg.module] + seg.elem_base
                 seen[start:start + seg.hi - seg.lo] += 1
                 b0, b1 = plan.local_blocks(seg)
                 assert 0 <= b0 < b1 <= plan.shard // 256
+            assert local_seen.max(initial=0) <= 1
         assert (seen == 1).all(), world
         assert total >= sum(-(-n // 256) * 256 for n in numels)
+
+
+def test_shard_plan_to_arena_inverts_the_rank_major_gather():
+    numels = [o * k for o, k in SHAPES]
+    for world in (2, 3):
+        plans = [ShardPlan(numels, world, r, bucket_elems=5000) for r in range(world)]
+        arena = torch.arange(plans[0].total)
+        gathered = torch.cat([torch.cat([arena[slice(*p.rank_slice(b))] for b in range(len(p.buckets))])
+                              for p in plans])
+        assert torch.equal(plans[0].to_arena(gathered), arena)
 
 
 def _free_port():
@@ -85,26 +109,37 @@ def _grads(step):
     return [(torch.randn(o, k, generator=g) * 1e-2).to(torch.bfloat16) for o, k in SHAPES]
 
 
-def _run(rank, world, port, out_dir):
+def _run(rank, world, port, out_dir, buckets=False):
+    """Three steps; with ``buckets`` the arena is split into two buckets and the gradients are
+    announced module by module, last module first, as a backward pass does (the overlapped
+    reduce-scatters start from those announcements)."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
     from firefly_b200.distributed import ZeroFireFlyOptim
-    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE, _grad_ready
 
     mods = _make_modules()
     calls = []
-    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update(calls, SEED))
+    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update(calls, SEED),
+                           bucket_mb=0.01 if buckets else 64.0)
+    if buckets:
+        assert [b.modules for b in opt.plan.buckets] == [(0, 1), (2, 3)]
     for step in range(3):
-        for m, g in zip(mods, _grads(step)):
+        for m, g in reversed(list(zip(mods, _grads(step)))):
             if step == 1 and m is mods[3]:
                 continue  # a module without gradient this step is skipped
             _BIT_GRAD_CACHE[m._registered_handle] = g.clone()
+            if buckets:
+                _grad_ready(m._registered_handle)
+        if buckets and world > 1:
+            # bucket (2, 3) is complete only when module 3 has a gradient
+            assert opt._rs_order == ([0] if step == 1 else [1, 0])
         opt.step()
     bits = opt.gather_bit_state()
     if rank == 0:
         torch.save({"q": [m.int_weight.clone() for m in mods], "bits": bits, "steps": list(opt.steps)},
-                   os.path.join(out_dir, f"world{world}.pt"))
+                   os.path.join(out_dir, f"world{world}{'_buckets' if buckets else ''}.pt"))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -132,6 +167,23 @@ def test_zero1_two_ranks_equal_single_rank(tmp_path):
     assert set(ent) == {"step", "m_q", "m_absmax", "v_q", "v_absmax", "r_q", "r_absmax"}
     assert ent["m_q"].shape == SHAPES[0] and ent["m_q"].dtype == torch.uint8
     assert ent["m_absmax"].shape == (-(-SHAPES[0][0] * SHAPES[0][1] // 256),)
+
+
+@pytest.mark.timeout(300)
+def test_zero1_overlapped_buckets_equal_single_rank(tmp_path):
+    """Two buckets whose reduce-scatters start from the backward's gradient announcements:
+    same weights and gathered states as the single-rank run."""
+    _run(0, 1, _free_port(), str(tmp_path))
+    mp.start_processes(_run, args=(2, _free_port(), str(tmp_path), True), nprocs=2, start_method="spawn")
+    one = torch.load(tmp_path / "world1.pt", weights_only=False)
+    two = torch.load(tmp_path / "world2_buckets.pt", weights_only=False)
+    assert one["steps"] == two["steps"]
+    for a, b in zip(one["q"], two["q"]):
+        assert torch.equal(a, b)
+    for h1, h2 in zip(sorted(one["bits"]), sorted(two["bits"])):
+        for k, v in one["bits"][h1].items():
+            w = two["bits"][h2][k]
+            assert (torch.equal(v, w) if torch.is_tensor(v) else v == w), k
 
 
 @pytest.mark.timeout(300)
