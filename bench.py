@@ -68,7 +68,7 @@ def parse_args():
     ap.add_argument("--zero-overlap", type=int, choices=[0, 1], default=1,
                     help="start each bucket's reduce-scatter from the backward pass")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
-                                              "swiglu_gemm", "dense_adamw", "mlp"],
+                                              "swiglu_gemm", "gelu_gemm", "dense_adamw", "mlp"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -120,6 +120,11 @@ def kernel_case(args):
         qs, qu = _qmaps_on(dev)
         _capi.adamw8_blockwise(p, grad, codes[0], am[0], codes[1], am[1], lr=1e-3, beta1=0.9, beta2=0.999,
                                eps=1e-8, wd=0.01, step=3, qmap_s=qs, qmap_u=qu)
+    elif args.kernel_case == "gelu_gemm":  # the 1.3B decoder's up GEMM (16384 x 8192 x 2048) with GELU in its epilogue
+        a = torch.randint(-127, 128, (16384, 2048), dtype=torch.int8, device=dev, generator=g)
+        w = torch.randint(-127, 128, (8192, 2048), dtype=torch.int8, device=dev, generator=g)
+        sa, sb = torch.rand(16384, device=dev) * 1e-2, torch.rand(8192, device=dev) * 1e-3
+        _capi.gelu_gemm(a, w, 2048, sa, sb)
     elif args.kernel_case == "swiglu_gemm":  # gate/up GEMM with h = silu(g) * u in its epilogue
         a = torch.randint(-127, 128, (8192, 4096), dtype=torch.int8, device=dev, generator=g)
         w = torch.randint(-127, 128, (2 * 11008, 4096), dtype=torch.int8, device=dev, generator=g)

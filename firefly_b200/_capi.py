@@ -45,6 +45,11 @@ SIGNATURES = {
     "ff_quant_dual_i8": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_swiglu_selftest": (_I, [_P, _P, _P]),
+    "ff_gelu_eval": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "ff_gelu_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _F, _I, _P,
+                             _I64, _P, _P, _I64, _P, _P, _P]),
+    "ff_gelu_bwd_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _F, _I, _P,
+                                 _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_bwd_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _F, _P,
                                    _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_swiglu_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _F, _P, _I64,
@@ -75,6 +80,7 @@ FUSED_GEMM_EVENTS: list | None = None
 _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dual_i8_noalloc": 2,
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
                      "ff_swiglu_gemm_i8": 2, "ff_swiglu_bwd_gemm_i8": 2,
+                     "ff_gelu_eval": 1, "ff_gelu_gemm_i8": 2, "ff_gelu_bwd_gemm_i8": 2,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1,
                      "ff_adamw8_blockwise": 1}
@@ -364,6 +370,152 @@ def swiglu_bwd_gemm(a: torch.Tensor, w: torch.Tensor, k: int, scale_a: torch.Ten
             ev[1].record()
             FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F * int(k)))
     return q_rows, s_rows, q_cols, s_cols, dgu
+
+
+# ---------------------------------------------------------------------------
+# GELU (tanh form) in the GEMM epilogues of a BitLinear GELU MLP block
+# ---------------------------------------------------------------------------
+_GELU_VARIANT: dict[int, int] = {}
+
+
+def gelu_eval(x: torch.Tensor, fwd_variant: int = 0, bwd_variant: int = 0):
+    """``(gelu(x), gelu'(x))`` in fp32, as the GELU epilogues compute them, for a bf16 tensor x
+    (``ff_gelu_eval``); the variant bits choose where multiplies and adds are fused."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"gelu_eval takes bf16 inputs, got {x.dtype}")
+    x = x.contiguous().view(-1)
+    h = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    d = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _call("ff_gelu_eval", _ptr(x), x.numel(), int(fwd_variant), int(bwd_variant), _ptr(h), _ptr(d), _stream(dev))
+    return h, d
+
+
+def _same_bits(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Bitwise equal, NaNs equal to any NaN."""
+    nan = torch.isnan(a.float())
+    if not torch.equal(nan, torch.isnan(b.float())):
+        return False
+    ib = torch.int16 if a.element_size() == 2 else torch.int32
+    return bool(torch.equal(a.view(ib)[~nan], b.view(ib)[~nan]))
+
+
+def gelu_variant(device: torch.device | None = None) -> int:
+    """Variant bits under which the GELU epilogues equal torch's tanh-form GELU kernels on
+    ``device``: ``gelu(x, approximate="tanh")`` for every bf16 x, and ``gelu_backward`` (fp32,
+    unit gradient, i.e. gelu'(x) itself) for every bf16-valued x.  Found once per device
+    (synchronises); raises if no variant matches."""
+    from torch.nn import functional as F
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx in _GELU_VARIANT:
+        return _GELU_VARIANT[idx]
+    dev = torch.device("cuda", idx)
+    x = torch.arange(-32768, 32768, dtype=torch.int32, device=dev).to(torch.int16).view(torch.bfloat16)
+    ref_h = F.gelu(x, approximate="tanh")
+    ref_d = torch.ops.aten.gelu_backward(torch.ones(x.shape, dtype=torch.float32, device=dev), x.float(),
+                                         approximate="tanh")
+    fwd = next((v for v in (0, 1) if _same_bits(gelu_eval(x, v, 0)[0].to(torch.bfloat16), ref_h)), None)
+    bwd = next((v for v in range(0, 64, 2) if _same_bits(gelu_eval(x, 0, v)[1], ref_d)), None)
+    if fwd is None or bwd is None:
+        def misses(a, b):
+            ok = (a.view(torch.int32) == b.view(torch.int32)) | (torch.isnan(a) & torch.isnan(b))
+            return int((~ok).sum())
+        best = min((misses(gelu_eval(x, 0, v)[1], ref_d), v) for v in range(0, 64, 2))
+        raise RuntimeError(f"no GELU epilogue variant reproduces torch's GELU kernels on cuda:{idx} "
+                           f"(forward {'ok' if fwd is not None else 'unmatched'}, backward "
+                           f"{'ok' if bwd is not None else f'unmatched: closest variant {best[1]} differs on {best[0]} inputs'}"
+                           "); the fused GELU path cannot be used")
+    # the bf16 backward is one more rounding of dy * gelu'(x): check it on sampled gradients
+    g = torch.Generator(device=dev).manual_seed(0)
+    dy = (torch.randn(x.shape, device=dev, generator=g) * 4).to(torch.bfloat16)
+    got = (dy.float() * gelu_eval(x, 0, bwd)[1]).to(torch.bfloat16)
+    if not _same_bits(got, torch.ops.aten.gelu_backward(dy, x, approximate="tanh")):
+        raise RuntimeError(f"the GELU epilogues' bf16 backward differs from torch's on cuda:{idx}")
+    _GELU_VARIANT[idx] = fwd | bwd
+    return fwd | bwd
+
+
+def gelu_gemm(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor, scale_b: torch.Tensor,
+              bias: torch.Tensor | None = None, eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """Up GEMM of a GELU MLP block with h = gelu(u) (tanh form) in its epilogue.
+
+    ``a``: int8 activation codes ``[T, lda]``, ``b``: int8 weight ``[F, ldb]``, contraction over
+    the first ``k`` columns.  Returns ``(u, q_rows, s_rows, q_cols_t, s_cols, h)``: u bf16
+    ``[T, F]`` as ``gemm_i8`` gives it, h = bf16(gelu(u)) as torch forms it, and h's dual codes
+    (``quant_dual(h)``)."""
+    dev = _require_cuda(a, b, scale_a, scale_b, bias)
+    variant = gelu_variant(dev)
+    a, lda = _rows_view(a)
+    b, ldb = _rows_view(b)
+    T, F = a.shape[0], b.shape[0]
+    ldq, ldqt = round_up(F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((F,), dtype=torch.float32, device=dev)
+    u = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
+    h = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + F,), dtype=torch.float32, device=dev)
+    f32 = [None if t is None else t.to(torch.float32).contiguous() for t in (scale_a, scale_b, bias)]
+    with torch.cuda.device(dev):
+        ev = None
+        if FUSED_GEMM_EVENTS is not None and T > 0:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        _call("ff_gelu_gemm_i8", _ptr(a), lda, _ptr(b), ldb, _ptr(f32[0]), _ptr(f32[1]), _ptr(f32[2]), _ptr(u), F,
+              _ptr(h), F, T, F, int(k), float(eps), variant, _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt,
+              _ptr(s_cols), _ptr(ws), _stream(dev))
+        if ev is not None:
+            ev[1].record()
+            FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F * int(k)))
+    return u, q_rows, s_rows, q_cols, s_cols, h
+
+
+def gelu_bwd_gemm(a: torch.Tensor, w: torch.Tensor, k: int, scale_a: torch.Tensor, u: torch.Tensor,
+                  colmul: torch.Tensor | None = None, eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """``dh = a · w[:k]`` (w: int8 ``[k, F]`` row-major, the down projection's weight) with the
+    GELU backward ``du = dh * gelu'(u)`` in the epilogue.  Returns ``(q_rows, s_rows, q_cols_t,
+    s_cols, du)``: du bf16 ``[T, F]`` as torch's ``gelu_backward`` forms it from the bf16 dh, and
+    ``quant_dual(du, row_colmul=colmul)``; dh is not written."""
+    dev = _require_cuda(a, w, scale_a, u, colmul)
+    variant = gelu_variant(dev)
+    if u.dtype != torch.bfloat16 or u.dim() != 2:
+        raise ValueError(f"expected a bf16 [T, F] up output, got {u.dtype} {tuple(u.shape)}")
+    u, ldu = _rows_view(u)
+    a, lda = _rows_view(a)
+    w, ldw = _rows_view(w)
+    T, F = a.shape[0], u.shape[1]
+    ldq, ldqt = round_up(F, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((F, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((F,), dtype=torch.float32, device=dev)
+    du = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((T + F,), dtype=torch.float32, device=dev)
+    sa = scale_a.to(torch.float32).contiguous()
+    if colmul is not None:
+        colmul = colmul.to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        ev = None
+        if FUSED_GEMM_EVENTS is not None and T > 0:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        _call("ff_gelu_bwd_gemm_i8", _ptr(a), lda, _ptr(w), ldw, _ptr(sa), _ptr(u), ldu, _ptr(colmul), _ptr(du), F,
+              T, F, int(k), float(eps), variant, _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols),
+              _ptr(ws), _stream(dev))
+        if ev is not None:
+            ev[1].record()
+            FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F * int(k)))
+    return q_rows, s_rows, q_cols, s_cols, du
 
 
 def swiglu_bwd_quant(dh: torch.Tensor, gu: torch.Tensor, colmul: torch.Tensor | None = None,

@@ -211,6 +211,8 @@ struct EpiParams {
   const __nv_bfloat16* g_in;
   int64_t ldg_in;
   const float* colmul;
+  // GELU epilogues: the contraction variant of the GELU arithmetic (ff_gelu.cuh)
+  int act_variant;
 };
 
 // Epilogue kind of the gate/up GEMM of a SwiGLU block (not an FF_OUT_* value): the CTA
@@ -225,6 +227,46 @@ constexpr int kSwigluFeat = 128;  // features per tile
 // quantiser of [dg | du].  dh itself is not written.
 constexpr int kOutSwigluBwd = 17;
 __host__ __device__ constexpr bool is_swiglu(int out) { return out == kOutSwigluFwd || out == kOutSwigluBwd; }
+// Epilogue kind of the up GEMM of a GELU MLP block: u (bf16, as FF_OUT_BF16 forms it) and
+// h = gelu(u) (tanh form) written by TMA, |h| folded into the row and column maxima: the first
+// pass of the dual quantiser of h.
+constexpr int kOutGeluFwd = 18;
+// Epilogue kind of the GEMM dh = dY * W_down of a GELU MLP block's backward: du = dh * gelu'(u)
+// from the dh tile and the saved u, written by TMA and folded into the row maxima (with column
+// multipliers) and column maxima; dh itself is not written.
+constexpr int kOutGeluBwd = 19;
+// the activation epilogues run on 8 warps (two per TMEM lane quarter) with staged column operands
+__host__ __device__ constexpr bool is_fused_act(int out) { return out >= kOutSwigluFwd && out <= kOutGeluBwd; }
+__host__ __device__ constexpr bool is_gelu(int out) { return out == kOutGeluFwd || out == kOutGeluBwd; }
+// The GELU epilogues read gelu(u) (bf16 bits) or gelu'(u) (fp32) from a shared-memory table that
+// each CTA fills once (with the same arithmetic) for the bf16 inputs with |u| in [2^-16, 16):
+// entry i < kGeluTabSpan is +u with bits (kGeluTabExpLo << 7) + i, entry kGeluTabSpan + i is -u.
+// Other inputs (rare for activations) take the arithmetic itself.
+constexpr int kGeluTabExpLo = 127 - 16;
+constexpr int kGeluTabSpan = 20 * 128;
+constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
+__device__ __forceinline__ uint32_t gelu_tab_bits(int i) {
+  return (i >= kGeluTabSpan ? 0x8000u : 0u) | (uint32_t)((i % kGeluTabSpan) + (kGeluTabExpLo << 7));
+}
+// table entry of a bf16 bit pattern, or -1 outside the table
+__device__ __forceinline__ int gelu_tab_index(uint32_t b16) {
+  const int t = (int)(b16 & 0x7FFFu) - (kGeluTabExpLo << 7);
+  return (unsigned)t < (unsigned)kGeluTabSpan ? t + ((b16 & 0x8000u) ? kGeluTabSpan : 0) : -1;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint16_t v;
+  asm("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __noinline__ uint32_t gelu_fwd_bits_slow(uint32_t b16, int v) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(gelu::fwd(__uint_as_float(b16 << 16), v)));
+}
+__device__ __noinline__ float gelu_grad_slow(uint32_t b16, int v) { return gelu::grad(__uint_as_float(b16 << 16), v); }
 
 template <int OUT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_t row, int64_t col0,
@@ -315,6 +357,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int64_
 // BMN: B is given MN-major (a K x N row-major matrix) instead of K-major (N x K)
 // A warp's 32 x 32 bf16 box (lane = row, 16 bf16x2 words per lane) through one of its two
 // shared-memory staging buffers and a TMA tile store at (x, y); `n` counts the warp's stores.
+// With SWZ the buffers (512-byte aligned) hold the box in the tensor map's 64-byte swizzle:
+// 16-byte chunk k of row r sits at chunk k ^ ((r >> 1) & 3), so the 32 lanes' 16-byte stores
+// spread over all banks instead of 8 lanes per bank group.
+template <bool SWZ = false>
 __device__ __forceinline__ void staged_store(const uint32_t (&w)[16], const CUtensorMap* map, int32_t x, int32_t y,
                                              int lane, uint8_t* stage, uint32_t stage_addr, uint32_t& n) {
   const uint32_t b = n & 1u;
@@ -323,8 +369,9 @@ __device__ __forceinline__ void staged_store(const uint32_t (&w)[16], const CUte
     __syncwarp();
   }
   uint4* dst = reinterpret_cast<uint4*>(stage + b * 2048 + lane * 64);
+  const int sw = SWZ ? (lane >> 1) & 3 : 0;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  for (int k = 0; k < 4; ++k) dst[k ^ sw] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
@@ -570,6 +617,131 @@ __device__ __forceinline__ void swiglu_bwd_chunk(const uint32_t (&acc)[32], cons
   atomicMax(p.col_amax + p.F + fb + lane, warp_colmax_bits(au, lane));
 }
 
+// 32 features of the GELU forward epilogue for one row (one thread): u exactly as the
+// FF_OUT_BF16 epilogue forms it (((acc * sa) * sb) (+ bias) -> bf16, stored at column fb of D)
+// and h = bf16(gelu(u)) (column fb of H); |h| is folded into the row maximum rmax (bf16x2 word)
+// and the column maxima.  `cb`: this chunk's column scales at [0, 32), bias at [128, 160).
+__device__ __forceinline__ void gelu_fwd_chunk(const uint32_t (&acc)[32], int64_t row, int64_t fb,
+                                               const EpiParams& p, float sa, int lane, const float* cb,
+                                               uint32_t tab, uint32_t& rmax, const CUtensorMap* tmD,
+                                               const CUtensorMap* tmH, uint8_t* stage, uint32_t stage_addr,
+                                               uint32_t& nst) {
+  const bool live = row < p.M;
+  float sb[32], bb[32];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {  // shared-memory broadcasts: every lane reads the same values
+    const float4 a = *reinterpret_cast<const float4*>(cb + j);
+    sb[j] = a.x; sb[j + 1] = a.y; sb[j + 2] = a.z; sb[j + 3] = a.w;
+    const float4 c = *reinterpret_cast<const float4*>(cb + 128 + j);
+    bb[j] = c.x; bb[j + 1] = c.y; bb[j + 2] = c.z; bb[j + 3] = c.w;
+  }
+  uint32_t wu[16], wh[16];
+  bool rare = false;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    float t2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 2 * q + e;
+      float t = __int2float_rn((int)acc[j]);
+      if (p.scale_a) t = __fmul_rn(t, sa);
+      if (p.scale_b) t = __fmul_rn(t, sb[j]);
+      if (p.bias) t = __fadd_rn(t, bb[j]);
+      t2[e] = t;
+    }
+    wu[q] = pack_bf16x2(mk2(t2[0], t2[1]));
+    const int i0 = gelu_tab_index(wu[q] & 0xFFFFu), i1 = gelu_tab_index(wu[q] >> 16);
+    rare |= (i0 | i1) < 0;
+    wh[q] = lds_u16(tab + 2u * (uint32_t)max(i0, 0)) | (lds_u16(tab + 2u * (uint32_t)max(i1, 0)) << 16);
+  }
+  if (__builtin_expect(rare, 0)) {  // inputs outside the table: the arithmetic itself
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const uint32_t b0 = wu[q] & 0xFFFFu, b1 = wu[q] >> 16;
+      if (gelu_tab_index(b0) < 0) wh[q] = (wh[q] & 0xFFFF0000u) | gelu_fwd_bits_slow(b0, p.act_variant);
+      if (gelu_tab_index(b1) < 0) wh[q] = (wh[q] & 0xFFFFu) | (gelu_fwd_bits_slow(b1, p.act_variant) << 16);
+    }
+  }
+  const int32_t row0 = (int32_t)(row - lane);
+  staged_store<true>(wu, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  staged_store<true>(wh, tmH, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  uint32_t a[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    a[q] = live ? abs_bf16x2(wh[q]) : 0u;  // rows past M hold no data
+    rmax = max_bf16x2(rmax, a[q]);
+  }
+  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(a, lane));
+}
+
+// u of one row's 32 features (64 B), zeros for rows past M
+__device__ __forceinline__ void gelu_bwd_load(const EpiParams& p, int64_t row, int64_t fb, uint4 (&uq)[4]) {
+  if (row < p.M) {
+    const uint4* up = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + fb);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) uq[k] = __ldg(up + k);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) uq[k] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// 32 features of the GELU backward epilogue for one row (one thread): dh = bf16(acc * sa) (as
+// FF_OUT_BF16 forms it) and the row's u (uq) give du = bf16(dh * gelu'(u)), stored by TMA at
+// column fb of D; |du * colmul| is folded into rmax and |du| into the column maxima.  `cm`:
+// this chunk's column multipliers at [0, 32).
+__device__ __forceinline__ void gelu_bwd_chunk(const uint32_t (&acc)[32], const uint4 (&uq)[4], int64_t row,
+                                               int64_t fb, const EpiParams& p, float sa, int lane, const float* cm,
+                                               uint32_t tab, float& rmax, const CUtensorMap* tmD,
+                                               uint8_t* stage, uint32_t stage_addr, uint32_t& nst) {
+  const bool live = row < p.M;
+  uint32_t uw[16], wdu[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uw[4 * k] = uq[k].x; uw[4 * k + 1] = uq[k].y; uw[4 * k + 2] = uq[k].z; uw[4 * k + 3] = uq[k].w;
+  }
+  const f2 sa2 = splat(sa);
+  uint32_t dwv[16];
+  bool rare = false;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    dwv[q] = pack_bf16x2(mul2(mk2(__int2float_rn((int)acc[2 * q]), __int2float_rn((int)acc[2 * q + 1])), sa2));
+    const int i0 = gelu_tab_index(uw[q] & 0xFFFFu), i1 = gelu_tab_index(uw[q] >> 16);
+    rare |= (i0 | i1) < 0;
+    wdu[q] = pack_bf16x2(mul2(unpack_bf16x2(dwv[q]), mk2(lds_f32(tab + 4u * (uint32_t)max(i0, 0)),
+                                                         lds_f32(tab + 4u * (uint32_t)max(i1, 0)))));
+  }
+  if (__builtin_expect(rare, 0)) {  // inputs outside the table: the arithmetic itself
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const uint32_t b0 = uw[q] & 0xFFFFu, b1 = uw[q] >> 16;
+      if ((gelu_tab_index(b0) | gelu_tab_index(b1)) < 0) {
+        const int i0 = gelu_tab_index(b0), i1 = gelu_tab_index(b1);
+        const float g0 = i0 >= 0 ? lds_f32(tab + 4u * (uint32_t)i0) : gelu_grad_slow(b0, p.act_variant);
+        const float g1 = i1 >= 0 ? lds_f32(tab + 4u * (uint32_t)i1) : gelu_grad_slow(b1, p.act_variant);
+        wdu[q] = pack_bf16x2(mul2(unpack_bf16x2(dwv[q]), mk2(g0, g1)));
+      }
+    }
+  }
+  const int32_t row0 = (int32_t)(row - lane);
+  staged_store<true>(wdu, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  uint32_t a[16];
+  uint32_t rw = 0u;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    a[q] = live ? abs_bf16x2(wdu[q]) : 0u;
+    if (p.colmul) {  // |v| * colmul (colmul >= 0) in fp32, as the row quantiser takes it
+      float a0, a1;
+      un2(mul2(unpack_bf16x2(a[q]), mk2(cm[2 * q], cm[2 * q + 1])), a0, a1);
+      rmax = fmaxf(rmax, fmaxf(a0, a1));
+    } else {
+      rw = max_bf16x2(rw, a[q]);
+    }
+  }
+  if (!p.colmul) rmax = fmaxf(rmax, fmaxf(__uint_as_float(rw << 16), __uint_as_float(rw & 0xFFFF0000u)));
+  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(a, lane));
+}
+
 template <int OUT, int BN_, int STAGES_, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t K,
@@ -772,6 +944,7 @@ constexpr int C2_BN = 256;        // columns of the pair's tile (128 rows of B p
 constexpr int C2_BN_CTA = 128;
 constexpr int C2_STAGES = 6;
 constexpr int C2_STAGES_SW = 5;  // the SwiGLU epilogue's staging buffers take one stage's space
+constexpr int C2_STAGES_GELU = 4;  // the GELU epilogues also hold their value table
 constexpr int C2_A_BYTES = C2_BM * BK;      // 16 KiB
 constexpr int C2_B_BYTES = C2_BN_CTA * BK;  // 16 KiB
 constexpr int C2_STAGE_BYTES = C2_A_BYTES + C2_B_BYTES;
@@ -781,21 +954,25 @@ constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
 constexpr int C2_SW_BUF_FLOATS = 2 * kSwigluFeat;  // per warp and buffer: its 64 features x 4 arrays
 // SwiGLU: 5 stages, then 8 warps x (2 scale/bias buffers + 2 output staging buffers)
 constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 256 + 8 * 2 * C2_SW_BUF_FLOATS * 4 + 8 * 2 * 2048;
+// GELU: 4 stages, the SwiGLU layout's buffers, then the table of gelu (bf16) or gelu' (fp32)
+constexpr int C2_SMEM_BYTES_GELU = C2_STAGES_GELU * C2_STAGE_BYTES + 1024 + 512 + 8 * 2 * C2_SW_BUF_FLOATS * 4 +
+                                   8 * 2 * 2048 + kGeluTabEntries * 4;
 // bf16 output: per epilogue warp two 32 x 32 bf16 staging buffers for the TMA stores
 constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 4 * 2 * 2048;
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
-  return is_swiglu(OUT) ? C2_STAGES_SW : C2_STAGES;
+  return is_gelu(OUT) ? C2_STAGES_GELU : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
 }
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return is_swiglu(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES);
+  return is_gelu(OUT) ? C2_SMEM_BYTES_GELU
+                      : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 4 epilogue warps (8 for the SwiGLU
 // epilogue: two per TMEM lane quarter, each on half of the tile's features)
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return is_swiglu(OUT) ? 320 : NUM_THREADS;
+  return is_fused_act(OUT) ? 320 : NUM_THREADS;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -900,8 +1077,18 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
+  constexpr uint32_t gelu_tab_off = 512u + 8u * 2u * C2_SW_BUF_FLOATS * 4u + 8u * 2u * 2048u;
+  if constexpr (is_gelu(OUT)) {  // the CTA's GELU table, by all threads
+    for (int i = threadIdx.x; i < kGeluTabEntries; i += c2_threads<OUT>()) {
+      const uint32_t b16 = gelu_tab_bits(i);
+      if constexpr (OUT == kOutGeluFwd)
+        reinterpret_cast<uint16_t*>(ctrl + gelu_tab_off)[i] = (uint16_t)gelu_fwd_bits_slow(b16, ep.act_variant);
+      else
+        reinterpret_cast<float*>(ctrl + gelu_tab_off)[i] = gelu_grad_slow(b16, ep.act_variant);
+    }
+  }
   tc_fence_before();
-  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated (and GELU tables filled)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -991,7 +1178,9 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
     // this warp's two TMA-store staging buffers (32 rows x 64 B each); with the SwiGLU epilogue
     // they follow the 8 warps' scale/bias buffers
-    constexpr uint32_t st_off = 256u + (is_swiglu(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
+    // (the GELU epilogues' buffers start 512-byte aligned, for the 64-byte swizzle)
+    constexpr uint32_t st_off = 256u + (is_fused_act(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u) +
+                                (is_gelu(OUT) ? 256u : 0u);
     uint8_t* st_stage = ctrl + st_off + (warp - 2) * 2 * 2048;
     const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
@@ -1010,6 +1199,20 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         const int64_t prow = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
         if (fb0 < ep.F) swiglu_bwd_load(ep, prow, fb0, pg, pu);
       }
+      if constexpr (OUT == kOutGeluFwd || OUT == kOutGeluBwd) {
+        // this warp's 128 features of the tile: lane l holds features 4l..4l+3 (forward: column
+        // scales and bias; backward: the row quantiser's column multipliers)
+        const int64_t col = (int64_t)tn * C2_BN + eh * 128 + lane * 4;
+        const bool in = col < ep.F;
+        const float* s4 = OUT == kOutGeluFwd ? ep.scale_b : ep.colmul;
+        st_s = in && s4 ? __ldg(reinterpret_cast<const float4*>(s4 + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        st_b = in && OUT == kOutGeluFwd && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col))
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (OUT == kOutGeluBwd) {
+          const int64_t prow = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
+          if (col - lane * 4 < ep.F) gelu_bwd_load(ep, prow, col - lane * 4, pu);
+        }
+      }
       if constexpr (OUT == kOutSwigluFwd) {
         // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
         const int64_t col = (int64_t)(lane >> 4) * ep.F + (int64_t)tn * kSwigluFeat + eh * 64 + (lane & 15) * 4;
@@ -1018,7 +1221,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       }
       if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
-      if constexpr (is_swiglu(OUT)) {
+      if constexpr (is_fused_act(OUT)) {
         float* buf = sw_buf + acc * C2_SW_BUF_FLOATS;
         reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
         reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
@@ -1046,6 +1249,40 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         if (row < ep.M)
           atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
                                                                __uint_as_float(rmax & 0xFFFF0000u))));
+      } else if constexpr (OUT == kOutGeluFwd) {
+        uint32_t rmax = 0u;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
+          const int fc = eh * 128 + c * 32;
+          const int64_t fb = (int64_t)tn * C2_BN + fc;
+          if (fb >= ep.F) break;
+          uint32_t r[32];
+          tmem_ld32(tbase + fc, r);
+          tmem_wait_ld();
+          gelu_fwd_chunk(r, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32,
+                         cbase + gelu_tab_off, rmax, &tmD, &tmH, st_stage, st_stage_addr, st_count);
+        }
+        if (row < ep.M)
+          atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
+                                                               __uint_as_float(rmax & 0xFFFF0000u))));
+      } else if constexpr (OUT == kOutGeluBwd) {
+        float rmax = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
+          const int fc = eh * 128 + c * 32;
+          const int64_t fb = (int64_t)tn * C2_BN + fc;
+          if (fb >= ep.F) break;
+          uint4 cu[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cu[k] = pu[k];
+          if (c + 1 < 4 && fb + 32 < ep.F) gelu_bwd_load(ep, row, fb + 32, pu);  // next chunk
+          uint32_t r[32];
+          tmem_ld32(tbase + fc, r);
+          tmem_wait_ld();
+          gelu_bwd_chunk(r, cu, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32,
+                         cbase + gelu_tab_off, rmax, &tmD, st_stage, st_stage_addr, st_count);
+        }
+        if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
       } else if constexpr (OUT == kOutSwigluBwd) {
         float rmax = 0.f;
 #pragma unroll 1
@@ -1143,7 +1380,7 @@ inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t col
 }
 
 // bf16 output [rows, cols] (leading dim ld) for TMA tile stores of 32 x 32 boxes
-inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, bool swz64 = false) {
   auto fn = encode_fn();
   if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -1151,7 +1388,8 @@ inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t co
   cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swz64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
   return FF_OK;
 }
@@ -1476,6 +1714,122 @@ extern "C" int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t*
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(dgu), M, 2 * F, lddgu, colmul,
                                       eps, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
+}
+
+extern "C" int ff_gelu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                               const float* scale_b, const float* bias, uint16_t* u, int64_t ldu, uint16_t* h,
+                               int64_t ldh, int64_t M, int64_t F, int64_t K, float eps, int variant, int8_t* q_rows,
+                               int64_t ldq, float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                               float* absmax_ws, void* stream) {
+  using namespace ff;
+  using namespace ff::gemm;
+  const char* name = "ff_gelu_gemm_i8";
+  FF_REQUIRE(M >= 0 && F >= 1 && K >= 1 && variant >= 0 && variant < 64, FF_ERR_INVALID_ARG,
+             "%s: M=%lld F=%lld K=%lld variant=%d", name, (long long)M, (long long)F, (long long)K, variant);
+  FF_REQUIRE(F % 32 == 0, FF_ERR_UNSUPPORTED, "%s: F=%lld must be a multiple of 32", name, (long long)F);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "%s: nothing to do", name);
+  if (M == 0) return FF_OK;
+  FF_REQUIRE(A && B && u && h, FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE(lda >= K && ldb >= K && ldu >= F && ldh >= F, FF_ERR_INVALID_ARG, "%s: bad leading dims", name);
+  FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
+             "%s: A/B need 16-byte alignment and lda/ldb multiples of 16", name);
+  FF_REQUIRE(aligned(u, 16) && aligned(h, 16) && ldu % 8 == 0 && ldh % 8 == 0, FF_ERR_UNSUPPORTED,
+             "%s: u/h need 16-byte alignment and leading dims multiples of 8", name);
+  FF_REQUIRE((!scale_b || aligned(scale_b, 16)) && (!bias || aligned(bias, 16)), FF_ERR_UNSUPPORTED,
+             "%s: scale_b/bias need 16-byte alignment", name);
+  FF_REQUIRE(M <= (int64_t)1 << 31 && F <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
+             "%s: dimension too large", name);
+  int rc = check_dual_outputs(name, M, F, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
+  const int max_pairs = max_pairs_current();
+  FF_REQUIRE(max_pairs > 0, FF_ERR_UNSUPPORTED, "%s: the 2-CTA GEMM cannot be resident on this device", name);
+  cudaStream_t st = as_stream(stream);
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(M + F), st), name);
+  CUtensorMap ma, mb, md, mh;
+  rc = make_map(&ma, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, F, K, ldb, C2_BN_CTA);
+  if (rc) return rc;
+  rc = make_map_out_bf16(&md, u, M, F, ldu, true);
+  if (rc) return rc;
+  rc = make_map_out_bf16(&mh, h, M, F, ldh, true);
+  if (rc) return rc;
+  EpiParams ep{};
+  ep.scale_a = scale_a;
+  ep.scale_b = scale_b;
+  ep.bias = bias;
+  ep.D = u;
+  ep.ldd = ldu;
+  ep.M = M;
+  ep.N = F;
+  ep.vec = 1;
+  ep.h = reinterpret_cast<__nv_bfloat16*>(h);
+  ep.ldh = ldh;
+  ep.F = F;
+  ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  ep.col_amax = ep.row_amax + M;
+  ep.act_variant = variant;
+  const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((F + C2_BN - 1) / C2_BN);
+  rc = launch_2cta<kOutGeluFwd, false>(ma, mb, md, mh, K, t2m, t2n, ep, max_pairs, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(h), M, F, ldh, nullptr, eps,
+                                      q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
+}
+
+extern "C" int ff_gelu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                                   const float* scale_a, const uint16_t* u, int64_t ldu, const float* colmul,
+                                   uint16_t* du, int64_t lddu, int64_t M, int64_t F, int64_t K, float eps,
+                                   int variant, int8_t* q_rows, int64_t ldq, float* s_rows, int8_t* q_cols_t,
+                                   int64_t ldqt, float* s_cols, float* absmax_ws, void* stream) {
+  using namespace ff;
+  using namespace ff::gemm;
+  const char* name = "ff_gelu_bwd_gemm_i8";
+  FF_REQUIRE(M >= 0 && F >= 1 && K >= 1 && variant >= 0 && variant < 64, FF_ERR_INVALID_ARG,
+             "%s: M=%lld F=%lld K=%lld variant=%d", name, (long long)M, (long long)F, (long long)K, variant);
+  FF_REQUIRE(F % 32 == 0, FF_ERR_UNSUPPORTED, "%s: F=%lld must be a multiple of 32", name, (long long)F);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "%s: nothing to do", name);
+  if (M == 0) return FF_OK;
+  FF_REQUIRE(A && B && u && du, FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE(lda >= K && ldb >= F && ldu >= F && lddu >= F, FF_ERR_INVALID_ARG, "%s: bad leading dims", name);
+  FF_REQUIRE(aligned(A, 16) && aligned(B, 16) && lda % 16 == 0 && ldb % 16 == 0, FF_ERR_UNSUPPORTED,
+             "%s: A/B need 16-byte alignment and lda/ldb multiples of 16", name);
+  FF_REQUIRE(aligned(u, 16) && aligned(du, 16) && ldu % 8 == 0 && lddu % 8 == 0, FF_ERR_UNSUPPORTED,
+             "%s: u/du need 16-byte alignment and leading dims multiples of 8", name);
+  FF_REQUIRE(!colmul || aligned(colmul, 16), FF_ERR_UNSUPPORTED, "%s: colmul needs 16-byte alignment", name);
+  FF_REQUIRE(M <= (int64_t)1 << 31 && F <= (int64_t)1 << 31 && K <= (int64_t)1 << 31, FF_ERR_UNSUPPORTED,
+             "%s: dimension too large", name);
+  int rc = check_dual_outputs(name, M, F, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws);
+  if (rc != FF_OK) return rc;
+  const int max_pairs = max_pairs_current();
+  FF_REQUIRE(max_pairs > 0, FF_ERR_UNSUPPORTED, "%s: the 2-CTA GEMM cannot be resident on this device", name);
+  cudaStream_t st = as_stream(stream);
+  FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(M + F), st), name);
+  CUtensorMap ma, mb, md;
+  rc = make_map(&ma, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, K, F, ldb, BK);  // B is K x F row-major: read MN-major
+  if (rc) return rc;
+  rc = make_map_out_bf16(&md, du, M, F, lddu, true);
+  if (rc) return rc;
+  EpiParams ep{};
+  ep.scale_a = scale_a;
+  ep.D = du;
+  ep.ldd = lddu;
+  ep.M = M;
+  ep.N = F;
+  ep.vec = 1;
+  ep.F = F;
+  ep.row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
+  ep.col_amax = ep.row_amax + M;
+  ep.g_in = reinterpret_cast<const __nv_bfloat16*>(u);
+  ep.ldg_in = ldu;
+  ep.colmul = colmul;
+  ep.act_variant = variant;
+  const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((F + C2_BN - 1) / C2_BN);
+  rc = launch_2cta<kOutGeluBwd, true>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(du), M, F, lddu, colmul, eps,
+                                      q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
 }
 
 extern "C" int ff_gemm_i8_kn(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,

@@ -7,6 +7,7 @@
 #include "ff_common.cuh"
 #include "ff_adamw8_dense.cuh"
 #include "ff_dqt_adamw8.cuh"
+#include "ff_gelu.cuh"
 #include "ff_quant.cuh"
 #include "ff_gemm_i8.cuh"
 

@@ -8,8 +8,9 @@ sequence 2048).  Per layer (pre-LayerNorm):
     x = x + down(gelu(up(ln2(x))))              up:  BitLinear d -> ffn, down: BitLinear ffn -> d
 
 then ``logits = lm_head(ln_f(x))`` (BitLinear d -> vocab) and the mean token cross-entropy.
-The residual stream is bf16; LayerNorm, GELU (tanh form), causal attention (torch's
-``scaled_dot_product_attention``) and the loss are torch ops around the BitLinear path.
+The residual stream is bf16; LayerNorm, causal attention (torch's
+``scaled_dot_product_attention``) and the loss are torch ops around the BitLinear path; the
+GELU (tanh form) and its backward run in the epilogues of the MLP's GEMMs (``GeluMLPFn``).
 Dense parameters — token and position embeddings, LayerNorm weights and biases — are
 stepped by ``AdamW8bitDense`` (block-wise 8-bit for the embeddings, fp32 moments for the
 norms), the BitLinear weights by the fused DQT 8-bit AdamW, as ``FireFlyOptim`` splits
@@ -29,7 +30,15 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from . import _capi
 from .bitLinear import BitLinear, collect_bitlinear_modules
+from .fireflykernels import (
+    _accumulate_weight_grad,
+    _as_float_input,
+    _quantize_activation,
+    _weight_grad_gemm,
+    _weight_operand,
+)
 
 
 @dataclass(frozen=True)
@@ -67,8 +76,78 @@ class LayerNormBF16(nn.Module):
         return F.layer_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.bias.to(x.dtype), self.eps)
 
 
+class GeluMLPFn(torch.autograd.Function):
+    """Fused forward/backward of ``down(gelu(up(x)))`` (tanh GELU), up and down BitLinear.
+
+    It computes exactly what the composition of the two BitLinear layers and torch's
+    ``F.gelu(·, approximate="tanh")`` computes, with the elementwise work moved into the GEMMs:
+    the up GEMM's epilogue writes u and h = gelu(u) and takes h's absmax (``ff_gelu_gemm_i8``),
+    and the epilogue of the backward GEMM dh = dY·W_down forms du = dh·gelu'(u) and takes its
+    absmax (``ff_gelu_bwd_gemm_i8``; dh is never written).
+    """
+
+    @staticmethod
+    def forward(ctx, x2d, up_weight, up_scale, up_handle, d_weight, d_scale, d_bias, d_handle):
+        _capi._require_cuda(x2d, up_weight, up_scale, d_weight, d_scale, d_bias)
+        Fu, K = up_weight.shape
+        O, Fh = d_weight.shape
+        if Fu != Fh or x2d.dim() != 2 or x2d.shape[1] != K:
+            raise ValueError(f"GELU MLP shapes: x {tuple(x2d.shape)}, up {tuple(up_weight.shape)}, "
+                             f"down {tuple(d_weight.shape)}")
+        x = _as_float_input(x2d)
+        T = x.shape[0]
+        up_ws = up_scale.to(torch.float32).contiguous()
+        d_ws = d_scale.to(torch.float32).contiguous()
+        b = None if d_bias is None else d_bias.detach().to(torch.float32).contiguous()
+        need_grad = any(ctx.needs_input_grad)
+        y = torch.empty((T, O), dtype=torch.bfloat16, device=x.device)
+        saved = (None, None, None, None, None)
+        if T > 0:
+            q_x, s_x, q_xt, s_xc = _quantize_activation(x, with_cols=need_grad)
+            u, q_h, s_h, q_ht, s_hc, _ = _capi.gelu_gemm(q_x, _weight_operand(up_handle, up_weight), K, s_x, up_ws,
+                                                         cols=need_grad)
+            _capi.gemm_i8(q_h, _weight_operand(d_handle, d_weight), Fh, scale_a=s_h, scale_b=d_ws, bias=b,
+                          out_kind=_capi.FF_OUT_BF16, out=y)
+            if need_grad:
+                saved = (q_xt, s_xc, u, q_ht, s_hc)
+        ctx.save_for_backward(*saved, up_weight, up_ws, d_weight, d_ws)
+        ctx.handles = (int(up_handle), int(d_handle))
+        ctx.has_bias = d_bias is not None
+        ctx.T = T
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q_xt, s_xc, u, q_ht, s_hc, up_weight, up_ws, d_weight, d_ws = ctx.saved_tensors
+        up_handle, d_handle = ctx.handles
+        Fu, K = up_weight.shape
+        O, Fh = d_weight.shape
+        T = ctx.T
+        dev = grad_out.device
+        need_dx = ctx.needs_input_grad[0]
+        if T == 0:
+            for h, (o, k) in ((up_handle, (Fu, K)), (d_handle, (O, Fh))):
+                _accumulate_weight_grad(h, torch.zeros((o, k), dtype=torch.bfloat16, device=dev))
+            dx = torch.zeros((0, K), dtype=grad_out.dtype, device=dev) if need_dx else None
+            db = torch.zeros((O,), dtype=grad_out.dtype, device=dev) if ctx.has_bias else None
+            return dx, None, None, None, None, None, db, None
+        dy = grad_out.to(torch.bfloat16).contiguous()
+        # down projection: dH = dY·W_d (GELU backward and du's absmax in its epilogue), dW_d = dYᵀ·H
+        q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=d_ws)
+        q_d, s_d, q_dt, s_dc, _ = _capi.gelu_bwd_gemm(q_g, _weight_operand(d_handle, d_weight), O, s_g, u,
+                                                      colmul=up_ws, rows=need_dx)
+        _weight_grad_gemm(d_handle, q_dyt, s_dy, q_ht, s_hc, O, Fh, T, dev)
+        db = _capi.colsum_bf16(dy).to(grad_out.dtype) if ctx.has_bias else None
+        dx = None
+        if need_dx:
+            dx = _capi.gemm_i8(q_d, _weight_operand(up_handle, up_weight), Fu, scale_a=s_d,
+                               out_kind=_capi.FF_OUT_BF16, b_kn_cols=K).to(grad_out.dtype)
+        _weight_grad_gemm(up_handle, q_dt, s_dc, q_xt, s_xc, Fu, K, T, dev)
+        return dx, None, None, None, None, None, db, None
+
+
 class DecoderLayer(nn.Module):
-    def __init__(self, cfg: DecoderConfig):
+    def __init__(self, cfg: DecoderConfig, fused: bool = True):
         super().__init__()
         d = cfg.d_model
         if d % cfg.heads:
@@ -80,6 +159,17 @@ class DecoderLayer(nn.Module):
         self.ln2 = LayerNormBF16(d)
         self.up = BitLinear(d, cfg.ffn)
         self.down = BitLinear(cfg.ffn, d)
+        self.fused = fused
+
+    def mlp(self, x: torch.Tensor) -> torch.Tensor:
+        """down(gelu(up(x))): the fused GELU MLP op, or the composition of the two BitLinear
+        layers and torch's GELU (``fused=False``, an up bias, or ffn not a multiple of 32)."""
+        if self.fused and self.up.bias is None and self.up.out_features % 32 == 0:
+            y = GeluMLPFn.apply(x.reshape(-1, x.shape[-1]), self.up.int_weight, self.up.weight_scale,
+                                self.up._registered_handle, self.down.int_weight, self.down.weight_scale,
+                                self.down.bias, self.down._registered_handle)
+            return y.view(*x.shape[:-1], y.shape[-1])
+        return self.down(F.gelu(self.up(x), approximate="tanh"))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, S, d = x.shape
@@ -90,16 +180,16 @@ class DecoderLayer(nn.Module):
         q, k, v = self.qkv(self.ln1(x)).view(B, S, 3, self.heads, hd).unbind(2)
         a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
         x = x + self.proj(a.transpose(1, 2).reshape(B, S, d))
-        return x + self.down(F.gelu(self.up(self.ln2(x)), approximate="tanh"))
+        return x + self.mlp(self.ln2(x))
 
 
 class BitDecoder(nn.Module):
-    def __init__(self, cfg: DecoderConfig = DECODER_1P3B):
+    def __init__(self, cfg: DecoderConfig = DECODER_1P3B, fused: bool = True):
         super().__init__()
         self.cfg = cfg
         self.tok = nn.Embedding(cfg.vocab, cfg.d_model)
         self.pos = nn.Parameter(torch.zeros(cfg.max_seq, cfg.d_model))
-        self.layers = nn.ModuleList(DecoderLayer(cfg) for _ in range(cfg.layers))
+        self.layers = nn.ModuleList(DecoderLayer(cfg, fused=fused) for _ in range(cfg.layers))
         self.ln_f = LayerNormBF16(cfg.d_model)
         self.lm_head = BitLinear(cfg.d_model, cfg.vocab)
 
@@ -138,10 +228,10 @@ class BitDecoder(nn.Module):
         self.pos.normal_(0.0, std, generator=generator)
 
 
-def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0) -> BitDecoder:
+def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0, fused: bool = True) -> BitDecoder:
     """The decoder on ``device`` with N(0, 0.02) weights drawn from a seeded generator."""
     with torch.device(device):
-        model = BitDecoder(cfg)
+        model = BitDecoder(cfg, fused=fused)
     gen = torch.Generator(device=device).manual_seed(seed)
     model.init_normal_(0.02, generator=gen)
     return model
@@ -185,5 +275,5 @@ def attention_flops_per_sequence(cfg: DecoderConfig, seq: int) -> float:
     return cfg.layers * 7 * 2 * seq * (seq / 2) * cfg.d_model
 
 
-__all__ = ["DecoderConfig", "DECODER_1P3B", "BitDecoder", "DecoderLayer", "LayerNormBF16", "build_decoder",
+__all__ = ["DecoderConfig", "DECODER_1P3B", "BitDecoder", "DecoderLayer", "GeluMLPFn", "LayerNormBF16", "build_decoder",
            "train_step", "synthetic_batches", "attention_flops_per_sequence"]

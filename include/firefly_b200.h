@@ -195,6 +195,58 @@ FF_API int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
                                  void* stream);
 
 /*
+ * GELU, tanh form, as the GELU GEMM epilogues evaluate it: for n bf16 inputs x writes
+ *   h[i] = 0.5*x*(1 + tanhf(b*(x + k*x^3)))                            (fp32, before rounding)
+ *   d[i] = 0.5*(1 + t) + 0.5*x*(1 - t*t)*b*(1 + 3k*x^2),  t = tanhf(b*(x + k*x^3))
+ * with b = sqrt(2/pi), k = 0.044715, every operation rounded once; the variant bits (0-63)
+ * choose which multiply-add pairs are fused (1: x + k*x^3 in h; 16: the same in d; 2: 1 - t*t;
+ * 4: 1 + 3k*x^2; 8: the final sum of d) and, with 32, the product order of d's second term
+ * ((0.5x*(1 - t*t)) * (b*(1 + 3k*x^2)) instead of ((0.5x*(1 - t*t))*b) * (1 + 3k*x^2)).
+ * h or d may be NULL.  The host compares the results
+ * with its framework's GELU kernels over all 65536 bf16 inputs and passes the matching
+ * variant to ff_gelu_gemm_i8 / ff_gelu_bwd_gemm_i8.
+ */
+FF_API int ff_gelu_eval(const uint16_t* x, int64_t n, int fwd_variant, int bwd_variant, float* h, float* d,
+                        void* stream);
+
+/*
+ * The up GEMM of a GELU MLP block (BitLinear d -> F, GELU, BitLinear F -> d) with the
+ * activation and the first pass of its quantiser in the epilogue.  A: int8 activation codes
+ * [M, K], B: int8 weight [F, K].  Writes u (bf16 [M, F], leading dim ldu) exactly as
+ * ff_gemm_i8 with FF_OUT_BF16 would (scale_a per row, scale_b per column, optional bias) and
+ * h = bf16(gelu(u)) (ff_gelu_eval's h under `variant`, rounded to bf16; leading dim ldh),
+ * then quantises h exactly as ff_quant_dual_i8 quantises a bf16 matrix (no colmul; outputs as
+ * there; absmax_ws M + F floats).  Two kernels.  F a multiple of 32; u, h, scale_b and bias
+ * 16-byte aligned, ldu and ldh multiples of 8.
+ * Replaces the up projection's matmul (fireflykernels.py:167), the elementwise GELU and the
+ * down projection's input quantisation.
+ */
+FF_API int ff_gelu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                           const float* scale_b, const float* bias, uint16_t* u, int64_t ldu, uint16_t* h,
+                           int64_t ldh, int64_t M, int64_t F, int64_t K, float eps, int variant, int8_t* q_rows,
+                           int64_t ldq, float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                           float* absmax_ws, void* stream);
+
+/*
+ * The GEMM dh = dY * W_down of a GELU MLP block's backward with the GELU backward and the
+ * first pass of the du quantiser in its epilogue.  A: int8 codes of dY * s_w [M, K], B: W_down
+ * int8 [K, F] row-major (the K x N operand, as ff_gemm_i8_kn reads it), scale_a: fp32 [M].
+ * With dh = bf16(acc * scale_a[m]) and u the saved up output (bf16 [M, F], leading dim ldu),
+ * writes du = bf16(dh * gelu'(u)) (ff_gelu_eval's d under `variant`; leading dim lddu) and
+ * quantises it exactly as ff_quant_dual_i8 quantises the bf16 matrix du with row_colmul =
+ * colmul (NULL or fp32 [F], the up projection's weight scales); absmax_ws M + F floats.  dh is
+ * not written.  F a multiple of 32; u, du and colmul 16-byte aligned, ldu and lddu multiples
+ * of 8.
+ * Replaces the down projection's dX matmul (fireflykernels.py:191), torch's GELU backward and
+ * the up projection's backward operand preparation (fireflykernels.py:184-193).
+ */
+FF_API int ff_gelu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                               const uint16_t* u, int64_t ldu, const float* colmul, uint16_t* du, int64_t lddu,
+                               int64_t M, int64_t F, int64_t K, float eps, int variant, int8_t* q_rows, int64_t ldq,
+                               float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols, float* absmax_ws,
+                               void* stream);
+
+/*
  * Backward of the SwiGLU activation fused with the dual quantiser of the gate/up
  * projection's output gradient.  With dh the gradient of h (bf16, leading dim ldh)
  * and g, u as in ff_swiglu_quant_i8, the gradient of the [rows, 2*cols] projection
