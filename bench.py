@@ -68,7 +68,7 @@ def parse_args():
     ap.add_argument("--zero-overlap", type=int, choices=[0, 1], default=1,
                     help="start each bucket's reduce-scatter from the backward pass")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "adamw", "quant", "swiglu", "swiglu_bwd",
-                                              "swiglu_gemm", "gelu_gemm", "dense_adamw", "mlp"],
+                                              "swiglu_gemm", "gelu_gemm", "dense_adamw", "mlp", "decoder4"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -120,6 +120,21 @@ def kernel_case(args):
         qs, qu = _qmaps_on(dev)
         _capi.adamw8_blockwise(p, grad, codes[0], am[0], codes[1], am[1], lr=1e-3, beta1=0.9, beta2=0.999,
                                eps=1e-8, wd=0.01, step=3, qmap_s=qs, qmap_u=qu)
+    elif args.kernel_case == "decoder4":
+        # two training steps of a 4-layer slice of the 1.3B decoder (d 2048, ffn 8192, vocab 32000)
+        # on one micro-batch of 8 x 2048 tokens; profile the second
+        from dataclasses import replace
+
+        from firefly_b200.decoder import DECODER_1P3B, build_decoder, synthetic_batches, train_step
+        from firefly_b200.distributed import ZeroFireFlyOptim
+
+        cfg = replace(DECODER_1P3B, layers=4)
+        model = build_decoder(cfg, dev)
+        opt = ZeroFireFlyOptim(model.bit_modules(), params=model.dense_parameters(), lr=1e-4, weight_decay=0.01,
+                               seed=1)
+        batches = synthetic_batches(cfg, 8, 2048, 8, dev)
+        for _ in range(2):
+            train_step(model, opt, batches)
     elif args.kernel_case == "gelu_gemm":  # the 1.3B decoder's up GEMM (16384 x 8192 x 2048) with GELU in its epilogue
         a = torch.randint(-127, 128, (16384, 2048), dtype=torch.int8, device=dev, generator=g)
         w = torch.randint(-127, 128, (8192, 2048), dtype=torch.int8, device=dev, generator=g)
