@@ -46,6 +46,10 @@ SIGNATURES = {
     "ff_quant_dual_i8_noalloc": (_I, [_P, _I, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P]),
     "ff_swiglu_selftest": (_I, [_P, _P, _P]),
     "ff_gelu_eval": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "ff_layernorm_i8": (_I, [_P, _I64, _I64, _I64, _P, _P, _F, _P, _I64, _P, _P, _F, _P, _I64, _P, _P, _I64, _P,
+                             _P, _P]),
+    "ff_layernorm_bwd_ws_elems": (_I64, [_I64, _I64]),
+    "ff_layernorm_bwd": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _P, _P]),
     "ff_gelu_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _F, _I, _P,
                              _I64, _P, _P, _I64, _P, _P, _P]),
     "ff_gelu_bwd_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _F, _I, _P,
@@ -81,6 +85,7 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_swiglu_quant_i8": 2, "ff_swiglu_bwd_quant_i8": 2, "ff_swiglu_selftest": 1,
                      "ff_swiglu_gemm_i8": 2, "ff_swiglu_bwd_gemm_i8": 2,
                      "ff_gelu_eval": 1, "ff_gelu_gemm_i8": 2, "ff_gelu_bwd_gemm_i8": 2,
+                     "ff_layernorm_i8": 2, "ff_layernorm_bwd": 3,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1,
                      "ff_adamw8_blockwise": 1}
@@ -370,6 +375,62 @@ def swiglu_bwd_gemm(a: torch.Tensor, w: torch.Tensor, k: int, scale_a: torch.Ten
             ev[1].record()
             FUSED_GEMM_EVENTS.append((ev[0], ev[1], 2 * T * F * int(k)))
     return q_rows, s_rows, q_cols, s_cols, dgu
+
+
+# ---------------------------------------------------------------------------
+# LayerNorm with the first pass of the dual quantiser of its output
+# ---------------------------------------------------------------------------
+def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+                    q_eps: float = 1e-8, rows: bool = True, cols: bool = True):
+    """LayerNorm of the rows of a bf16 ``[T, C]`` matrix (fp32 gamma, beta) and, unless both
+    ``rows`` and ``cols`` are False, ``quant_dual`` of the bf16 output in the same call.
+    Returns ``(y, mean, rstd, (q_rows, s_rows, q_cols_t, s_cols))``."""
+    dev = _require_cuda(x, gamma, beta)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise ValueError(f"layernorm_quant takes a bf16 [T, C] matrix, got {x.dtype} {tuple(x.shape)}")
+    x, ldx = _rows_view(x)
+    T, C = x.shape
+    ldq, ldqt = round_up(C, 16), round_up(max(T, 1), 16)
+    q_rows = s_rows = q_cols = s_cols = ws = None
+    if rows:
+        q_rows = torch.empty((T, ldq), dtype=torch.int8, device=dev)
+        s_rows = torch.empty((T,), dtype=torch.float32, device=dev)
+    if cols:
+        q_cols = torch.empty((C, ldqt), dtype=torch.int8, device=dev)
+        s_cols = torch.empty((C,), dtype=torch.float32, device=dev)
+    if rows or cols:
+        ws = torch.empty((T + C,), dtype=torch.float32, device=dev)
+    y = torch.empty((T, C), dtype=torch.bfloat16, device=dev)
+    mean = torch.empty((T,), dtype=torch.float32, device=dev)
+    rstd = torch.empty((T,), dtype=torch.float32, device=dev)
+    g = gamma.detach().to(torch.float32).contiguous()
+    b = beta.detach().to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        _call("ff_layernorm_i8", _ptr(x), ldx, T, C, _ptr(g), _ptr(b), float(eps), _ptr(y), C, _ptr(mean), _ptr(rstd),
+              float(q_eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols), _ptr(ws), _stream(dev))
+    return y, mean, rstd, (q_rows, s_rows, q_cols, s_cols)
+
+
+def layernorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor, gamma: torch.Tensor,
+                  dx: bool = True, wgrad: bool = True):
+    """``(dx, dgamma, dbeta)`` of ``layernorm_quant``'s LayerNorm from its output gradient dy and
+    input x (bf16 ``[T, C]``), the forward's mean and rstd and fp32 gamma (dx bf16, the others
+    fp32; None where not asked for).  Deterministic."""
+    dev = _require_cuda(dy, x, mean, rstd, gamma)
+    dy, lddy = _rows_view(dy.to(torch.bfloat16))
+    x, ldx = _rows_view(x)
+    T, C = x.shape
+    g = gamma.detach().to(torch.float32).contiguous()
+    out_dx = torch.empty((T, C), dtype=torch.bfloat16, device=dev) if dx else None
+    dgamma = dbeta = ws = None
+    if wgrad:
+        ws = torch.empty((max(int(lib().ff_layernorm_bwd_ws_elems(T, C)), 4),), dtype=torch.float32, device=dev)
+        dgamma = torch.empty((C,), dtype=torch.float32, device=dev)
+        dbeta = torch.empty((C,), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _call("ff_layernorm_bwd", _ptr(dy), lddy, _ptr(x), ldx, T, C, _ptr(mean.contiguous()), _ptr(rstd.contiguous()),
+              _ptr(g), _ptr(out_dx), C, _ptr(dgamma), _ptr(dbeta), _ptr(ws), _stream(dev))
+    return out_dx, dgamma, dbeta
 
 
 # ---------------------------------------------------------------------------

@@ -9,6 +9,7 @@
 #include "ff_dqt_adamw8.cuh"
 #include "ff_gelu.cuh"
 #include "ff_quant.cuh"
+#include "ff_norm.cuh"
 #include "ff_gemm_i8.cuh"
 
 #ifndef FF_VERSION_STRING

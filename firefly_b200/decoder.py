@@ -8,9 +8,10 @@ sequence 2048).  Per layer (pre-LayerNorm):
     x = x + down(gelu(up(ln2(x))))              up:  BitLinear d -> ffn, down: BitLinear ffn -> d
 
 then ``logits = lm_head(ln_f(x))`` (BitLinear d -> vocab) and the mean token cross-entropy.
-The residual stream is bf16; LayerNorm, causal attention (torch's
-``scaled_dot_product_attention``) and the loss are torch ops around the BitLinear path; the
-GELU (tanh form) and its backward run in the epilogues of the MLP's GEMMs (``GeluMLPFn``).
+The residual stream is bf16; causal attention (torch's ``scaled_dot_product_attention``) and the
+loss are torch ops around the BitLinear path; the GELU (tanh form) and its backward run in the
+epilogues of the MLP's GEMMs (``GeluMLPFn``), and each LayerNorm quantises its output for the
+BitLinear that reads it (``LayerNormQuantFn``).
 Dense parameters — token and position embeddings, LayerNorm weights and biases — are
 stepped by ``AdamW8bitDense`` (block-wise 8-bit for the embeddings, fp32 moments for the
 norms), the BitLinear weights by the fused DQT 8-bit AdamW, as ``FireFlyOptim`` splits
@@ -33,7 +34,9 @@ from torch.nn import functional as F
 from . import _capi
 from .bitLinear import BitLinear, collect_bitlinear_modules
 from .fireflykernels import (
+    _ACT_CACHE,
     _accumulate_weight_grad,
+    _act_key,
     _as_float_input,
     _quantize_activation,
     _weight_grad_gemm,
@@ -63,17 +66,55 @@ class DecoderConfig:
 DECODER_1P3B = DecoderConfig()
 
 
-class LayerNormBF16(nn.Module):
-    """LayerNorm with fp32 parameters over a bf16 input (the parameters are cast per call)."""
+class LayerNormQuantFn(torch.autograd.Function):
+    """LayerNorm of a bf16 input with fp32 weight and bias (``ff_layernorm_i8``) that also
+    quantises its output for the BitLinear that reads it next: the dual codes go into the op
+    layer's activation cache under the output's key, so that layer's forward finds them instead
+    of running the quantiser.  Backward: ``ff_layernorm_bwd`` (dx, dgamma, dbeta)."""
 
-    def __init__(self, d: int, eps: float = 1e-5):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps, with_cols):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        y, mean, rstd, codes = _capi.layernorm_quant(x2, weight, bias, eps, rows=True, cols=with_cols)
+        if not with_cols:
+            codes = (codes[0], codes[1], None, None)
+        _ACT_CACHE["entry"] = (_act_key(y, with_cols), y, codes)
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape, ctx.in_dtype = shape, x.dtype
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        dy2 = dy.reshape(x2.shape).to(torch.bfloat16).contiguous()
+        want_dx = ctx.needs_input_grad[0]
+        want_w = ctx.needs_input_grad[1] or ctx.needs_input_grad[2]
+        dx, dg, db = _capi.layernorm_bwd(dy2, x2, mean, rstd, weight, dx=want_dx, wgrad=want_w)
+        if dx is not None:
+            dx = dx.view(ctx.shape).to(ctx.in_dtype)
+        return dx, dg, db, None, None
+
+
+class LayerNormBF16(nn.Module):
+    """LayerNorm with fp32 parameters over a bf16 input.  ``fused``: ``LayerNormQuantFn`` (the
+    output's int8 codes for the next BitLinear come out of the same call); otherwise torch's
+    LayerNorm with the parameters cast to the input's dtype per call."""
+
+    def __init__(self, d: int, eps: float = 1e-5, fused: bool = False):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(d))
         self.bias = nn.Parameter(torch.zeros(d))
         self.eps = eps
+        self.fused = fused
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return F.layer_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.bias.to(x.dtype), self.eps)
+        d = x.shape[-1]
+        if self.fused and x.is_cuda and d % 8 == 0 and d <= 4096:
+            with_cols = torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad
+                                                     or self.bias.requires_grad)
+            return LayerNormQuantFn.apply(x, self.weight, self.bias, self.eps, with_cols)
+        return F.layer_norm(x, (d,), self.weight.to(x.dtype), self.bias.to(x.dtype), self.eps)
 
 
 class GeluMLPFn(torch.autograd.Function):
@@ -147,16 +188,17 @@ class GeluMLPFn(torch.autograd.Function):
 
 
 class DecoderLayer(nn.Module):
-    def __init__(self, cfg: DecoderConfig, fused: bool = True):
+    def __init__(self, cfg: DecoderConfig, fused: bool = True, fused_norm: bool | None = None):
         super().__init__()
         d = cfg.d_model
         if d % cfg.heads:
             raise ValueError(f"d_model {d} is not a multiple of heads {cfg.heads}")
+        fused_norm = fused if fused_norm is None else fused_norm
         self.heads = cfg.heads
-        self.ln1 = LayerNormBF16(d)
+        self.ln1 = LayerNormBF16(d, fused=fused_norm)
         self.qkv = BitLinear(d, 3 * d)
         self.proj = BitLinear(d, d)
-        self.ln2 = LayerNormBF16(d)
+        self.ln2 = LayerNormBF16(d, fused=fused_norm)
         self.up = BitLinear(d, cfg.ffn)
         self.down = BitLinear(cfg.ffn, d)
         self.fused = fused
@@ -184,13 +226,17 @@ class DecoderLayer(nn.Module):
 
 
 class BitDecoder(nn.Module):
-    def __init__(self, cfg: DecoderConfig = DECODER_1P3B, fused: bool = True):
+    """``fused``: the GELU MLP op; ``fused_norm`` (default: ``fused``): the LayerNorms that
+    quantise their outputs for the next BitLinear."""
+
+    def __init__(self, cfg: DecoderConfig = DECODER_1P3B, fused: bool = True, fused_norm: bool | None = None):
         super().__init__()
+        fused_norm = fused if fused_norm is None else fused_norm
         self.cfg = cfg
         self.tok = nn.Embedding(cfg.vocab, cfg.d_model)
         self.pos = nn.Parameter(torch.zeros(cfg.max_seq, cfg.d_model))
-        self.layers = nn.ModuleList(DecoderLayer(cfg, fused=fused) for _ in range(cfg.layers))
-        self.ln_f = LayerNormBF16(cfg.d_model)
+        self.layers = nn.ModuleList(DecoderLayer(cfg, fused=fused, fused_norm=fused_norm) for _ in range(cfg.layers))
+        self.ln_f = LayerNormBF16(cfg.d_model, fused=fused_norm)
         self.lm_head = BitLinear(cfg.d_model, cfg.vocab)
 
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
@@ -228,10 +274,11 @@ class BitDecoder(nn.Module):
         self.pos.normal_(0.0, std, generator=generator)
 
 
-def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0, fused: bool = True) -> BitDecoder:
+def build_decoder(cfg: DecoderConfig, device: torch.device, seed: int = 0, fused: bool = True,
+                  fused_norm: bool | None = None) -> BitDecoder:
     """The decoder on ``device`` with N(0, 0.02) weights drawn from a seeded generator."""
     with torch.device(device):
-        model = BitDecoder(cfg, fused=fused)
+        model = BitDecoder(cfg, fused=fused, fused_norm=fused_norm)
     gen = torch.Generator(device=device).manual_seed(seed)
     model.init_normal_(0.02, generator=gen)
     return model
@@ -275,5 +322,6 @@ def attention_flops_per_sequence(cfg: DecoderConfig, seq: int) -> float:
     return cfg.layers * 7 * 2 * seq * (seq / 2) * cfg.d_model
 
 
-__all__ = ["DecoderConfig", "DECODER_1P3B", "BitDecoder", "DecoderLayer", "GeluMLPFn", "LayerNormBF16", "build_decoder",
+__all__ = ["DecoderConfig", "DECODER_1P3B", "BitDecoder", "DecoderLayer", "GeluMLPFn", "LayerNormBF16",
+           "LayerNormQuantFn", "build_decoder",
            "train_step", "synthetic_batches", "attention_flops_per_sequence"]

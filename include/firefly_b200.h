@@ -195,6 +195,40 @@ FF_API int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
                                  void* stream);
 
 /*
+ * LayerNorm of the rows of a bf16 matrix x [rows, cols] (leading dim ldx) with fp32 gamma, beta:
+ *   mean = sum(x)/cols, var = sum((x - mean)^2)/cols, rstd = 1/sqrt(var + eps)   (fp32)
+ *   y = bf16((x - mean)*rstd*gamma + beta)        (bf16 [rows, cols], leading dim ldy)
+ * writing mean and rstd (fp32 [rows]).  Unless q_rows and q_cols_t are both NULL it also
+ * quantises y exactly as ff_quant_dual_i8 quantises a bf16 matrix (no colmul; outputs and
+ * absmax_ws (rows + cols floats) as there; q_eps its eps), taking the absmax pass inside the
+ * LayerNorm kernel.  cols a multiple of 8 up to 4096; x, y, gamma, beta 16-byte aligned,
+ * ldx and ldy multiples of 8.  One kernel, or two with the quantiser.
+ * No reference counterpart (the reference has no model code): the LayerNorm before a BitLinear
+ * of the decoder plus that BitLinear's input quantisation (fireflykernels.py:164-167).
+ */
+FF_API int ff_layernorm_i8(const uint16_t* x, int64_t ldx, int64_t rows, int64_t cols, const float* gamma,
+                           const float* beta, float eps, uint16_t* y, int64_t ldy, float* mean, float* rstd,
+                           float q_eps, int8_t* q_rows, int64_t ldq, float* s_rows, int8_t* q_cols_t, int64_t ldqt,
+                           float* s_cols, float* absmax_ws, void* stream);
+
+/* fp32 workspace elements ff_layernorm_bwd needs for dgamma / dbeta of a [rows, cols] input. */
+FF_API int64_t ff_layernorm_bwd_ws_elems(int64_t rows, int64_t cols);
+
+/*
+ * Backward of ff_layernorm_i8's LayerNorm from its output gradient dy and input x (both bf16
+ * [rows, cols], leading dims lddy, ldx) and the forward's mean and rstd:
+ *   dx = bf16(rstd*(g - mean_c(g) - xhat*mean_c(g*xhat))),  g = dy*gamma, xhat = (x - mean)*rstd
+ * (bf16, leading dim lddx; cols up to 4096), dgamma[c] = sum_r dy*xhat and dbeta[c] = sum_r dy
+ * (fp32 [cols]), each output NULL when not wanted.  The column sums go per block of 64 rows and
+ * then over the blocks in order (deterministic); ws: ff_layernorm_bwd_ws_elems(rows, cols)
+ * floats when dgamma or dbeta is wanted.  cols and leading dims multiples of 8; dy, x, dx,
+ * gamma, ws 16-byte aligned.
+ */
+FF_API int ff_layernorm_bwd(const uint16_t* dy, int64_t lddy, const uint16_t* x, int64_t ldx, int64_t rows,
+                            int64_t cols, const float* mean, const float* rstd, const float* gamma, uint16_t* dx,
+                            int64_t lddx, float* dgamma, float* dbeta, float* ws, void* stream);
+
+/*
  * GELU, tanh form, as the GELU GEMM epilogues evaluate it: for n bf16 inputs x writes
  *   h[i] = 0.5*x*(1 + tanhf(b*(x + k*x^3)))                            (fp32, before rounding)
  *   d[i] = 0.5*(1 + t) + 0.5*x*(1 - t*t)*b*(1 + 3k*x^2),  t = tanhf(b*(x + k*x^3))
