@@ -27,6 +27,7 @@ single-GPU update.
 """
 from __future__ import annotations
 
+import weakref
 from contextlib import contextmanager
 from dataclasses import dataclass
 from typing import Callable, Sequence
@@ -282,8 +283,24 @@ class ZeroFireFlyOptim:
         self._reset_pending()
         self.overlap = bool(overlap) and self.world > 1
         if self.overlap:
+            # the hooks hold the optimizer weakly: a discarded optimizer stops reducing
+            ref = weakref.ref(self)
+
+            def hook(handle, ref=ref):
+                opt = ref()
+                if opt is not None:
+                    opt._on_grad_ready(handle)
+
             for m in self.modules:
-                set_grad_ready_hook(m._registered_handle, self._on_grad_ready)
+                set_grad_ready_hook(m._registered_handle, hook)
+
+    def close(self) -> None:
+        """Remove this optimizer's gradient hooks from its modules (later backward passes no
+        longer start reductions for it)."""
+        if self.overlap:
+            for m in self.modules:
+                set_grad_ready_hook(m._registered_handle, None)
+            self.overlap = False
 
     # -- overlapped reduction ----------------------------------------------------
     def _reset_pending(self) -> None:

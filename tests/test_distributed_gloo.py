@@ -293,3 +293,37 @@ def test_zero1_checkpoint_resume_across_world_sizes(tmp_path):
             for k, v in full["bits"][hf].items():
                 w = res["bits"][hr][k]
                 assert (torch.equal(v, w) if torch.is_tensor(v) else v == w), (name, k)
+
+
+def _run_hook_lifetime(rank, world, port, out_dir):
+    """A discarded or closed optimizer's gradient hooks do nothing."""
+    import gc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from firefly_b200.distributed import ZeroFireFlyOptim
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE, _grad_ready
+
+    mods = _make_modules()
+    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update([], SEED),
+                           bucket_mb=0.01)
+    assert opt.overlap
+    opt.close()
+    for m, g in zip(mods, _grads(0)):
+        _BIT_GRAD_CACHE[m._registered_handle] = g.clone()
+        _grad_ready(m._registered_handle)
+    assert opt._rs_order == []  # closed: no reduction started
+    opt2 = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update([], SEED),
+                            bucket_mb=0.01)
+    del opt2
+    gc.collect()
+    for m in mods:
+        _grad_ready(m._registered_handle)  # the discarded optimizer's hooks are no-ops
+    _BIT_GRAD_CACHE.clear()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_zero1_hooks_do_not_outlive_the_optimizer(tmp_path):
+    mp.start_processes(_run_hook_lifetime, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
