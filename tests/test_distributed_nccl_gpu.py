@@ -43,7 +43,8 @@ def _train(rank, world, port, out_path):
     opt = ZeroFireFlyOptim(mods, lr=1e-3, weight_decay=0.01, seed=5, bucket_mb=0.05, overlap=True)
     g = torch.Generator(device=dev).manual_seed(123)  # the same tokens on every rank
     for step in range(3):
-        x = torch.randn(64, SHAPES[0][1], device=dev, generator=g)
+        # the BitLinear weights are buffers: the input carries the autograd graph
+        x = torch.randn(64, SHAPES[0][1], device=dev, generator=g).requires_grad_(True)
         y = mods[2](mods[1](mods[0](x)))
         y.float().pow(2).mean().backward()
         opt.step()
