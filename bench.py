@@ -20,8 +20,12 @@ pinned host memory and the loss L = sum(y * R) read back, R a resident projectio
 ``roofline`` is the int8 GEMM (the dominant kernel) timed per launch with CUDA
 events inside the timed region.  Extra keys carry the INT8 GEMM sweep (TOPS),
 the 8-bit AdamW step over 6.7e9 parameters (HBM GB/s) and the dense-parameter
-8-bit AdamW over 268 M fp32 parameters (HBM GB/s).  ``cpu_baseline``
-is the CPU restatement of the same step timed on the host cores on a sample.
+8-bit AdamW over 268 M fp32 parameters (HBM GB/s) (one GPU only), and, on every
+rank count, ``decoder_1p3b_dp``: the data-parallel training step of the 1.3B
+BitLinear decoder (24 layers, d_model 2048, ffn 8192 GELU, vocab 32000) on a
+global batch of 64 x 2048 tokens split over the ranks (strong scaling).
+``cpu_baseline`` is the CPU restatement of the same step timed on the host cores on
+a sample.
 
 ``--impl reference`` times the CPU implementation of the path (the oracle
 restatement of the reference's algorithm; the reference itself is pure Python
