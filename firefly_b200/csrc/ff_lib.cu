@@ -2,8 +2,6 @@
 //
 // One TU keeps the device status word (ff::g_status) a plain __device__
 // variable of this module without relocatable device code.
-#include <mutex>
-
 #include "ff_common.cuh"
 #include "ff_adamw8_dense.cuh"
 #include "ff_dqt_adamw8.cuh"
@@ -45,19 +43,15 @@ extern "C" int ff_device_status(uint32_t* out, int clear) {
 //
 // The array (FF_NOALLOC_DUAL_MAX_ELEMS floats, 1 MiB) exists on every GPU that
 // loads the library, for the life of the process.  Host code cannot use the
-// symbol itself as a device address, so the first call on each device asks the
-// runtime for the array's device address (cudaGetSymbolAddress, with that
-// device current) and keeps it; later calls on that device reuse it.  Every
-// call shares the array: ff_quant_dual_i8 clears the part it uses (the absmax
-// accumulators must start at zero) with cudaMemsetAsync on the call's stream,
-// so calls that overlap on the GPU would race on it.
+// symbol itself as a device address, so every call asks the runtime for the
+// array's device address on the current device (cudaGetSymbolAddress: a query,
+// no allocation).  Asking each time keeps the address right after a context
+// reset, which reloads the module and can move the array.  Every call shares the
+// array: ff_quant_dual_i8 clears the part it uses (the absmax accumulators must
+// start at zero) with cudaMemsetAsync on the call's stream, so calls that overlap
+// on the GPU would race on it.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) float g_noalloc_absmax[FF_NOALLOC_DUAL_MAX_ELEMS];
-
-namespace {
-std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {nullptr};
-}  // namespace
 
 extern "C" int ff_quant_dual_i8_noalloc(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
                                         const float* row_colmul, float eps, int8_t* q_rows, int64_t ldq,
@@ -65,26 +59,15 @@ extern "C" int ff_quant_dual_i8_noalloc(const void* x, int dtype, int64_t rows, 
                                         void* stream) {
   FF_REQUIRE(rows >= 0 && cols >= 0, FF_ERR_INVALID_ARG, "ff_quant_dual_i8_noalloc: rows=%lld cols=%lld",
              (long long)rows, (long long)cols);
-  FF_REQUIRE(rows + cols <= (int64_t)FF_NOALLOC_DUAL_MAX_ELEMS, FF_ERR_UNSUPPORTED,
-             "ff_quant_dual_i8_noalloc: rows + cols = %lld exceeds the built-in scratch of %d elements; "
+  constexpr int64_t kMax = FF_NOALLOC_DUAL_MAX_ELEMS;
+  FF_REQUIRE(rows <= kMax && cols <= kMax - rows, FF_ERR_UNSUPPORTED,
+             "ff_quant_dual_i8_noalloc: rows=%lld + cols=%lld exceeds the built-in scratch of %lld elements; "
              "use ff_quant_dual_i8 with a workspace",
-             (long long)(rows + cols), (int)FF_NOALLOC_DUAL_MAX_ELEMS);
-  int dev = 0;
-  FF_CUDA_TRY(cudaGetDevice(&dev), "ff_quant_dual_i8_noalloc: cudaGetDevice");
-  FF_REQUIRE(dev >= 0 && dev < 64, FF_ERR_UNSUPPORTED, "ff_quant_dual_i8_noalloc: device %d out of range", dev);
-  float* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      void* addr = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_absmax);
-      if (e != cudaSuccess || addr == nullptr)
-        return ff::set_error(FF_ERR_CUDA, "ff_quant_dual_i8_noalloc: cudaGetSymbolAddress: %s",
-                             cudaGetErrorString(e));
-      g_noalloc_ptr[dev] = static_cast<float*>(addr);
-    }
-    scratch = g_noalloc_ptr[dev];
-  }
+             (long long)rows, (long long)cols, (long long)kMax);
+  void* addr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_absmax);
+  if (e != cudaSuccess || addr == nullptr)
+    return ff::set_error(FF_ERR_CUDA, "ff_quant_dual_i8_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
   return ff_quant_dual_i8(x, dtype, rows, cols, ldx, row_colmul, eps, q_rows, ldq, s_rows, q_cols_t, ldqt,
-                          s_cols, scratch, stream);
+                          s_cols, static_cast<float*>(addr), stream);
 }

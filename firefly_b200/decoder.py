@@ -39,6 +39,7 @@ from .fireflykernels import (
     _act_key,
     _as_float_input,
     _quantize_activation,
+    clear_activation_cache,
     _weight_grad_gemm,
     _weight_operand,
 )
@@ -159,6 +160,7 @@ class GeluMLPFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
+        clear_activation_cache()
         q_xt, s_xc, u, q_ht, s_hc, up_weight, up_ws, d_weight, d_ws = ctx.saved_tensors
         up_handle, d_handle = ctx.handles
         Fu, K = up_weight.shape

@@ -38,7 +38,13 @@ import torch.distributed as dist
 from . import _capi
 from .adamw8 import AdamW8bitDense
 from .bitLinear import BitLinear
-from .fireflykernels import _BIT_GRAD_CACHE, _invalidate_weight_cache, set_grad_ready_hook, set_grad_slot
+from .fireflykernels import (
+    _BIT_GRAD_CACHE,
+    _invalidate_weight_cache,
+    clear_activation_cache,
+    set_grad_ready_hook,
+    set_grad_slot,
+)
 from .fireflyoptim import BLOCK, _tables_on, bit_rng_offsets
 
 
@@ -217,12 +223,20 @@ class ZeroFireFlyOptim:
 
     The arena is split into buckets of whole modules (``bucket_mb`` of bf16 gradient each).
     With ``overlap`` (and more than one rank) a bucket's reduce-scatter is issued from the
-    backward pass as soon as the weight-gradient GEMM of its last module has been issued,
-    so it runs under the rest of the backward; ``step()`` then updates the buckets in that
-    order, each as soon as its reduction is done, and issues each bucket's weight all-gather
-    right after its update.  With gradient accumulation, run every backward but the last of
-    a step under ``no_sync()`` (each BitLinear must produce one weight gradient per synced
-    backward).
+    backward pass once the weight-gradient GEMMs of all its modules have been issued, so it
+    runs under the rest of the backward; buckets are always reduced in the same order on
+    every rank (last bucket first; a complete bucket waits for the ones after it), which keeps
+    the ranks' collectives matched when the backward produces gradients in another order or
+    a module has no gradient on some ranks.  ``step()`` updates the buckets in that order,
+    each as soon as its reduction is done, and issues each bucket's weight all-gather right
+    after its update.  With gradient accumulation, run every backward but the last of a step
+    under ``no_sync()`` (each BitLinear must produce one weight gradient per synced backward).
+
+    A module that produced a weight gradient on some ranks only (e.g. it was not used in the
+    forward of the others) is updated on every rank with the average in which the other ranks
+    count zero, and its step count advances everywhere: the ranks agree on which modules have
+    gradients through a small host-side all-reduce (gloo; a side group when the main group is
+    NCCL), which never waits for the GPU.
 
     ``update_fn`` (default: the ``ff_dqt_adamw8`` kernel) receives keyword
     arguments for one segment; it exists so the sharding and collectives can be
@@ -278,6 +292,14 @@ class ZeroFireFlyOptim:
             _invalidate_weight_cache(m._registered_handle)
         # overlapped gradient reduction
         self._nccl = self.world > 1 and dist.get_backend(self.group) == "nccl"
+        # host-side agreement on which modules have gradients (no GPU synchronisation)
+        self._host_group = None
+        if self.world > 1:
+            if dist.get_backend(self.group) == "gloo":
+                self._host_group = self.group
+            else:
+                ranks = None if self.group is None else dist.get_process_group_ranks(self.group)
+                self._host_group = dist.new_group(ranks=ranks, backend="gloo")
         self._sync = True
         self._module_of = {m._registered_handle: i for i, m in enumerate(self.modules)}
         self._reset_pending()
@@ -308,6 +330,13 @@ class ZeroFireFlyOptim:
         self._remaining = [len(b.modules) for b in self.plan.buckets]
         self._rs_work: dict[int, object] = {}
         self._rs_order: list[int] = []
+        self._next_reduce = len(self.plan.buckets) - 1  # buckets are reduced from the last one down
+
+    def _launch_ready_reductions(self) -> None:
+        """Issue the reduce-scatters of complete buckets, in the fixed order (last bucket first)."""
+        while self._next_reduce >= 0 and self._remaining[self._next_reduce] == 0:
+            self._launch_reduce(self._next_reduce)
+            self._next_reduce -= 1
 
     @contextmanager
     def no_sync(self):
@@ -328,10 +357,8 @@ class ZeroFireFlyOptim:
                 "accumulating backward passes under no_sync(), or construct ZeroFireFlyOptim with overlap=False")
         self.arena.take_grad(i)
         self._ready.add(i)
-        b = self.plan.bucket_of[i]
-        self._remaining[b] -= 1
-        if self._remaining[b] == 0:
-            self._launch_reduce(b)
+        self._remaining[self.plan.bucket_of[i]] -= 1
+        self._launch_ready_reductions()
 
     def _launch_reduce(self, b: int) -> None:
         bk = self.plan.buckets[b]
@@ -406,15 +433,21 @@ class ZeroFireFlyOptim:
     @torch.no_grad()
     def step(self) -> None:
         plan = self.plan
+        clear_activation_cache()  # the next step's inputs are quantised afresh
         has_grad = self.arena.collect_grads()
+        if self.world > 1:
+            # buckets not reduced during the backward (no overlap, or a module without a
+            # gradient, whose slot now holds zeros) are reduced now, in the same fixed order
+            for b in range(self._next_reduce, -1, -1):
+                self._launch_reduce(b)
+            self._next_reduce = -1
+            # a module with a gradient on any rank is updated on every rank
+            flags = torch.tensor(has_grad, dtype=torch.int32)
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self._host_group)
+            has_grad = [bool(v) for v in flags.tolist()]
         for i, h in enumerate(has_grad):
             self.steps[i] += int(h)
         if self.world > 1:
-            # buckets not reduced during the backward (no overlap, or a module without a
-            # gradient, whose slot now holds zeros) are reduced now, last bucket first
-            for b in reversed(range(len(plan.buckets))):
-                if b not in self._rs_order:
-                    self._launch_reduce(b)
             dense = self._launch_dense_reduce()
             gathers = []
             for b in list(self._rs_order):

@@ -181,7 +181,13 @@ def _as_float_input(x: torch.Tensor) -> torch.Tensor:
 # The activation codes of the last quantised input.  Two BitLinear layers that read the
 # same tensor (the gate and up projections of a SwiGLU block) quantise it once.  The entry
 # holds a reference to the tensor, so its storage cannot be reused while cached, and is
-# keyed by storage, offset, shape, strides, dtype and the in-place version counter.
+# keyed by storage, offset, shape, strides, dtype and the in-place version counter (the
+# same counter autograd relies on).  A write that does not bump that counter (through
+# ``.data``, ctypes, or a collective writing into the storage) is not seen by the key, so
+# the entry is also dropped at the start of every backward pass and by every optimizer
+# step: codes are then reused only within one forward pass.  Code that writes such an
+# input out of band between two forward passes with neither in between calls
+# ``clear_activation_cache()``.
 _ACT_CACHE: dict = {}
 
 
@@ -242,6 +248,7 @@ class Int8LinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
+        _ACT_CACHE.clear()
         q_xt, s_xc, int_weight, ws = ctx.saved_tensors
         O, K = int_weight.shape
         T = ctx.T

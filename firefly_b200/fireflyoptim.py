@@ -37,7 +37,7 @@ import torch
 from . import _capi
 from .adamw8 import AdamW8bitDense
 from .bitLinear import BitLinear
-from .fireflykernels import _invalidate_weight_cache
+from .fireflykernels import _invalidate_weight_cache, clear_activation_cache
 
 _MU = 255.0
 _1_OVER_LN1P_MU = 1.0 / 5.545177444479562  # 1 / ln(1 + 255), fireflyoptim.py:10
@@ -155,6 +155,7 @@ class FireFlyOptim(AdamW8bitDense):
     @torch.no_grad()
     def step(self, closure=None):
         loss = super().step(closure)
+        clear_activation_cache()  # the next step's inputs are quantised afresh
         if not self.bit_modules:
             return loss
         lr, beta1, beta2, eps, wd = self._hyper()

@@ -33,6 +33,7 @@ from .fireflykernels import (
     _accumulate_weight_grad,
     _as_float_input,
     _quantize_activation,
+    clear_activation_cache,
     _weight_grad_gemm,
     _weight_operand,
 )
@@ -77,6 +78,7 @@ class SwiGLUMLPFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
+        clear_activation_cache()
         q_xt, s_xc, gu, q_ht, s_hc, gu_weight, gu_ws, d_weight, d_ws = ctx.saved_tensors
         gu_handle, d_handle = ctx.handles
         F2, K = gu_weight.shape

@@ -113,9 +113,11 @@ FF_API int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols
  * step that cannot afford cudaMalloc's implicit device-wide synchronisation.
  * The absmax scratch is a static array inside this library (FF_NOALLOC_DUAL_MAX_ELEMS
  * floats, held on every GPU that loads the library until the process exits);
- * rows + cols above that limit return FF_ERR_UNSUPPORTED.  The first call on a
- * device looks up the array's device address (a runtime call, no allocation),
- * so make that first call before any stream capture.  All calls share the
+ * rows + cols above that limit return FF_ERR_UNSUPPORTED.  Each call looks up the
+ * array's device address on the current device (cudaGetSymbolAddress: a runtime
+ * query, no allocation, correct again after a context reset); the first call on a
+ * device may also load this library's kernels there, so make that first call
+ * before any stream capture.  All calls share the
  * array: calls whose kernels overlap on the GPU (different streams, no ordering)
  * race on it and must be serialised by the caller.  The call allocates nothing
  * (no cudaMalloc, cudaFree or allocating library routine).

@@ -2,10 +2,11 @@
 
 The reference is the pure-PyTorch package fumitoshi0524/FireFly (files
 ``fireflykernels.py``, ``bitLinear.py``, ``fireflyoptim.py``).  This script
-imports it from a local checkout (default ``/root/reference``, override with
-``FIREFLY_REFERENCE``), runs its CPU path on small seeded inputs and stores
-inputs and outputs as ``.npz`` files next to this script.  Nothing else in the
-repository reads the reference; the parity tests only read the fixtures.
+imports it from a local checkout whose folder is given as the first argument
+(or by the ``FIREFLY_REFERENCE`` environment variable), runs its CPU path on
+small seeded inputs and stores inputs and outputs as ``.npz`` files next to this
+script.  Nothing else in the repository reads the reference; the parity tests
+only read the fixtures.
 
 ``fireflyoptim.py:2`` imports ``bitsandbytes.optim.AdamW8bit`` at module import
 time.  bitsandbytes is not installed here, so a stand-in module whose
@@ -16,7 +17,7 @@ parameter, and the BitLinear branch (``fireflyoptim.py:126-209``) is pure torch.
 ``torch.rand_like`` draws of the optimizer step (``fireflyoptim.py:192``) are
 recorded so that a replay can feed the same uniforms.
 
-Run:  python tests/golden/make_golden.py
+Run:  python tests/golden/make_golden.py <reference checkout>
 """
 from __future__ import annotations
 
@@ -31,8 +32,11 @@ import torch
 HERE = Path(__file__).resolve().parent
 
 
-def _import_reference():
-    ref_dir = Path(os.environ.get("FIREFLY_REFERENCE", "/root/reference")).resolve()
+def _import_reference(path: str | None):
+    path = path or os.environ.get("FIREFLY_REFERENCE")
+    if not path:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set FIREFLY_REFERENCE)")
+    ref_dir = Path(path).resolve()
     if not (ref_dir / "fireflyoptim.py").exists():
         raise SystemExit(f"reference checkout not found at {ref_dir}")
     bnb = types.ModuleType("bitsandbytes")
@@ -253,9 +257,26 @@ def gen_linear(pkg, fk) -> None:
     np.savez_compressed(HERE / "linear_bf16.npz", **out)
 
 
+def gen_init(pkg) -> None:
+    """``BitLinear(K, O)`` construction under ``torch.manual_seed`` (bitLinear.py:15-27, :40-66):
+    the Kaiming-uniform draw from torch's default CPU generator, quantised per row."""
+    out = {}
+    cases = [("sq", 64, 64, 0), ("wide", 300, 70, 1), ("tall", 33, 257, 2), ("one", 1, 5, 3), ("cfg1rows", 1024, 48, 4)]
+    for name, K, O, seed in cases:
+        torch.manual_seed(seed)
+        layer = pkg.BitLinear(K, O)
+        out[f"{name}_meta"] = np.array([K, O, seed], dtype=np.int64)
+        out[f"{name}_q"] = layer.int_weight.numpy().copy()
+        out[f"{name}_s"] = layer.weight_scale.numpy().copy()
+        # the next draw of the default generator: the construction consumed exactly the Kaiming draw
+        out[f"{name}_next"] = torch.rand(4).numpy()
+    np.savez_compressed(HERE / "bitlinear_init.npz", **out)
+
+
 def main() -> None:
     torch.set_num_threads(1)
-    pkg, fk, fo, _ = _import_reference()
+    pkg, fk, fo, _ = _import_reference(sys.argv[1] if len(sys.argv) > 1 else None)
+    gen_init(pkg)
     gen_quant(fk)
     gen_mulaw(fo)
     gen_optim(pkg, fk, fo)

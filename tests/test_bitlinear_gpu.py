@@ -6,7 +6,7 @@ import torch
 import firefly_b200 as ff
 from firefly_b200 import fireflykernels as fk
 from oracle import firefly_oracle as O
-from tests._util import assert_close_rel, bf16_bits, bf16_ulp_diff, from_bf16_bits, load_golden
+from tests._util import assert_close_rel, bf16_bits, bf16_ulp_diff, check_optim_step, from_bf16_bits, load_golden
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
@@ -138,3 +138,100 @@ def test_weight_cache_invalidated_by_optimizer():
         q = layer.int_weight.cpu().numpy()
         wk = fk._weight_operand(layer._registered_handle, layer.int_weight)
         np.testing.assert_array_equal(wk.cpu().numpy()[:, :70], q)
+
+
+# --------------------------------------------------------------------------
+# Construction and module discovery (bitLinear.py:15-27, :40-66, :107-108; fireflyoptim.py:114-120)
+# --------------------------------------------------------------------------
+def test_init_matches_reference_construction():
+    """``BitLinear(K, O)`` under ``torch.manual_seed(s)`` holds the reference's ``int_weight`` and
+    ``weight_scale`` bit for bit (recorded by running the reference's constructor), and draws
+    exactly as many numbers from the default generator."""
+    z = load_golden("bitlinear_init.npz")
+    cases = sorted(k[:-5] for k in z.files if k.endswith("_meta"))
+    assert len(cases) >= 4
+    for c in cases:
+        K, O_, seed = (int(v) for v in z[c + "_meta"])
+        torch.manual_seed(seed)
+        layer = ff.BitLinear(K, O_)
+        nxt = torch.rand(4).numpy()
+        assert layer.int_weight.dtype == torch.int8 and layer.int_weight.shape == (O_, K)
+        assert layer.weight_scale.dtype == torch.float32 and layer.weight_scale.shape == (O_,)
+        np.testing.assert_array_equal(layer.int_weight.numpy(), z[c + "_q"], err_msg=c)
+        np.testing.assert_array_equal(layer.weight_scale.numpy().view(np.uint32), z[c + "_s"].view(np.uint32),
+                                      err_msg=c)
+        np.testing.assert_array_equal(nxt, z[c + "_next"], err_msg=c)
+        # reset_int8_ redraws from the generator like the constructor
+        torch.manual_seed(seed)
+        layer.reset_int8_()
+        np.testing.assert_array_equal(layer.int_weight.numpy(), z[c + "_q"], err_msg=c)
+
+
+def test_collect_and_add_bit_modules():
+    a, b = ff.BitLinear(32, 16), ff.BitLinear(16, 8, bias=True)
+    net = torch.nn.Sequential(a, torch.nn.GELU(), torch.nn.Sequential(torch.nn.Identity(), b))
+    assert ff.collect_bitlinear_modules(net) == [a, b]
+    assert ff.collect_bitlinear_modules(torch.nn.Linear(3, 3)) == []
+    opt = ff.FireFlyOptim([torch.nn.Parameter(torch.zeros(1))], bit_modules=[a])
+    opt.add_bit_modules(ff.collect_bitlinear_modules(net))  # a is already there
+    assert opt.bit_modules == [a, b]
+    assert opt._bit_handles == [a._registered_handle, b._registered_handle]
+    with pytest.raises(TypeError, match="expected BitLinear, got Linear"):
+        opt.add_bit_modules([torch.nn.Linear(2, 2)])
+    assert opt.bit_modules == [a, b]
+
+
+def test_fireflyoptim_sr_is_unbiased_rounding():
+    """``FireFlyOptimSR`` (fireflyoptim.py:236-258) is ``FireFlyOptim`` with ``sr_bias_scale`` 0: with
+    the same uniforms its steps equal the oracle's unbiased update and differ from the biased one."""
+    layer = _layer(256, 64, False, seed=8)
+    opt = ff.FireFlyOptimSR([torch.nn.Parameter(torch.zeros(1, device=DEV))], lr=5e-3, weight_decay=0.01,
+                            bit_modules=[layer])
+    assert opt.sr_bias_scale == 0.0 and isinstance(opt, ff.FireFlyOptim)
+    rng = np.random.default_rng(8)
+    q, ws = layer.int_weight.cpu().numpy(), layer.weight_scale.cpu().numpy()
+    st = O.init_state(q.shape)
+    us = {}
+    opt.uniform_source = lambda m, h, t: torch.from_numpy(us[t])
+    h = layer._registered_handle
+    biased_differs = False
+    for t in range(1, 4):
+        g_bits = O.f32_to_bf16_bits(rng.standard_normal(q.shape).astype(np.float32))
+        us[t] = rng.random(q.shape, dtype=np.float32)
+        fk._BIT_GRAD_CACHE[h] = from_bf16_bits(g_bits, DEV)
+        opt.step()
+        q_o, st_o = O.dqt_adamw8_step(q, ws, O.bf16_bits_to_f32(g_bits), st, lr=5e-3, wd=0.01, sr_bias=0.0,
+                                      u=us[t])
+        q_b, _ = O.dqt_adamw8_step(q, ws, O.bf16_bits_to_f32(g_bits), st, lr=5e-3, wd=0.01, sr_bias=0.15,
+                                   u=us[t])
+        got = {k: v.cpu().numpy() for k, v in opt._bit_state[h].items() if torch.is_tensor(v)}
+        check_optim_step(layer.int_weight.cpu().numpy(), got, q_o, st_o, f"SR step {t}")
+        biased_differs |= not np.array_equal(q_b, q_o)
+        q, st = layer.int_weight.cpu().numpy(), {"step": t, **got}
+    assert biased_differs  # the bias term matters on these inputs, so the test can tell them apart
+
+
+# --------------------------------------------------------------------------
+# The activation-code cache
+# --------------------------------------------------------------------------
+def test_activation_codes_not_reused_across_steps_after_untracked_write():
+    """An input buffer rewritten through ``.data`` (which does not bump the version counter that keys
+    the activation-code cache) between training steps is quantised afresh: the cache is dropped by
+    the backward pass and by the optimizer step."""
+    layer = _layer(128, 64, False, seed=9)
+    opt = ff.FireFlyOptim([torch.nn.Parameter(torch.zeros(1, device=DEV))], lr=0.0, weight_decay=0.0,
+                          bit_modules=[layer])
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(32, 128, device=DEV, generator=g).requires_grad_(True)
+    x2 = torch.randn(32, 128, device=DEV, generator=g)
+    want = layer(x2.clone().requires_grad_(True)).detach()
+    y = layer(x)
+    y.backward(torch.ones_like(y))
+    x.data.copy_(x2)  # untracked write: x._version does not change
+    assert torch.equal(layer(x).detach(), want)  # dropped by the backward pass
+    with torch.no_grad():
+        layer(x)
+    opt.step()
+    x.data.copy_(x2 * 2)
+    with torch.no_grad():
+        assert torch.equal(layer(x), layer((x2 * 2).clone()))  # dropped by the optimizer step

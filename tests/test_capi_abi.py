@@ -59,3 +59,15 @@ def test_no_cpu_fallback():
         _capi.quant_rows(torch.zeros(2, 8))
     with pytest.raises(RuntimeError):
         _capi.gemm_i8(torch.zeros(2, 16, dtype=torch.int8), torch.zeros(2, 16, dtype=torch.int8), 16)
+
+
+def test_noalloc_size_limit_checked_on_the_host_without_overflow():
+    """The no-allocation dual quantiser refuses rows + cols above its built-in scratch before any
+    CUDA call, also for sizes whose sum would overflow a signed 64-bit integer."""
+    lib = _capi.lib()
+    big = 2 ** 62
+    for rows, cols in ((big, big), (2 ** 63 - 1, 1), (1, 2 ** 63 - 1), (262144, 1)):
+        rc = lib.ff_quant_dual_i8_noalloc(None, _capi.FF_DTYPE_BF16, rows, cols, cols, None, 1e-8,
+                                          None, 16, None, None, 16, None, None)
+        assert rc == _capi.FF_ERR_UNSUPPORTED, (rows, cols)
+        assert b"exceeds the built-in scratch" in lib.ff_last_error()

@@ -134,7 +134,9 @@ def _run(rank, world, port, out_dir, buckets=False):
                 _grad_ready(m._registered_handle)
         if buckets and world > 1:
             # bucket (2, 3) is complete only when module 3 has a gradient
-            assert opt._rs_order == ([0] if step == 1 else [1, 0])
+            # buckets are reduced last first: bucket (0, 1) waits for (2, 3), which is complete
+            # only when module 3 has a gradient (at step 1 both are reduced from step())
+            assert opt._rs_order == ([] if step == 1 else [1, 0])
         opt.step()
     bits = opt.gather_bit_state()
     if rank == 0:
@@ -327,3 +329,53 @@ def _run_hook_lifetime(rank, world, port, out_dir):
 @pytest.mark.timeout(300)
 def test_zero1_hooks_do_not_outlive_the_optimizer(tmp_path):
     mp.start_processes(_run_hook_lifetime, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+
+
+def _run_uneven(rank, world, port, out_dir):
+    """Three steps in which module 3 has no gradient on rank 1 at step 1 (as if it were not used
+    in that rank's forward) while rank 0 has one.  On one rank the same steps see the average
+    of the two ranks' gradients: module 3's gradient halved at step 1."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+    from firefly_b200.distributed import ZeroFireFlyOptim
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE, _grad_ready
+
+    mods = _make_modules()
+    opt = ZeroFireFlyOptim(mods, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update([], SEED),
+                           bucket_mb=0.01)
+    for step in range(3):
+        for i, (m, g) in reversed(list(enumerate(zip(mods, _grads(step))))):
+            if step == 1 and i == 3:
+                if world > 1 and rank == 1:
+                    continue
+                if world == 1:
+                    g = g / 2  # exact in bf16
+            _BIT_GRAD_CACHE[m._registered_handle] = g.clone()
+            _grad_ready(m._registered_handle)
+        opt.step()
+    bits = opt.gather_bit_state()
+    if rank == 0:
+        torch.save({"q": [m.int_weight.clone() for m in mods], "bits": bits, "steps": list(opt.steps)},
+                   os.path.join(out_dir, f"uneven{world}.pt"))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_zero1_module_without_gradient_on_one_rank(tmp_path):
+    """A module with a gradient on rank 0 only is still updated on every rank with the averaged
+    gradient, and its step count advances on all of them: the result equals one rank fed the
+    averaged gradients (the reductions stay matched although rank 1 issues them from step())."""
+    _run_uneven(0, 1, _free_port(), str(tmp_path))
+    mp.start_processes(_run_uneven, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    one = torch.load(tmp_path / "uneven1.pt", weights_only=False)
+    two = torch.load(tmp_path / "uneven2.pt", weights_only=False)
+    assert one["steps"] == two["steps"] == [3, 3, 3, 3]
+    for a, b in zip(one["q"], two["q"]):
+        assert torch.equal(a, b)
+    for h1, h2 in zip(sorted(one["bits"]), sorted(two["bits"])):
+        for k, v in one["bits"][h1].items():
+            w = two["bits"][h2][k]
+            assert (torch.equal(v, w) if torch.is_tensor(v) else v == w), k

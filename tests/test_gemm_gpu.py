@@ -42,6 +42,8 @@ SHAPES = [
     (513, 200, 4096),
     (130, 18944, 512),    # 128 x 256 tiles, one CTA each
     (2600, 2600, 1000),   # 256 x 256 tiles on CTA pairs, ragged M, N and K
+    (16, 8192, 8192),     # the skinny sizes of the GEMM sweep (HBM-bound: B streamed once)
+    (128, 8192, 8192),
 ]
 
 

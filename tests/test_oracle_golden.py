@@ -129,3 +129,82 @@ def test_philox_uniforms_layout():
     u2 = O.philox_uniforms(32, seed=7, step=3, elem_offset=48)
     np.testing.assert_array_equal(u[32:], u2)
     assert not np.array_equal(O.philox_uniforms(8, 7, 4), O.philox_uniforms(8, 7, 3))
+
+
+# --------------------------------------------------------------------------
+# BitLinear construction (bitLinear.py:15-27, :40-66)
+# --------------------------------------------------------------------------
+def test_kaiming_draw_quantised_by_oracle_matches_reference_init():
+    """The reference's ``BitLinear(K, O)`` under ``torch.manual_seed(s)``: a Kaiming-uniform draw of
+    torch's default CPU generator, quantised per row.  The oracle's quantiser on the same draw gives
+    the reference's buffers bit for bit, and the construction consumed exactly that draw."""
+    import math
+
+    import torch
+
+    z = load_golden("bitlinear_init.npz")
+    cases = _golden_cases(z, "_meta")
+    assert len(cases) >= 4
+    for c in cases:
+        K, O_, seed = (int(v) for v in z[c + "_meta"])
+        torch.manual_seed(seed)
+        w = torch.empty((O_, K), dtype=torch.float32)
+        torch.nn.init.kaiming_uniform_(w, a=math.sqrt(5))
+        nxt = torch.rand(4).numpy()
+        q, s = O.quantize_rows(w.numpy())
+        np.testing.assert_array_equal(q, z[c + "_q"], err_msg=c)
+        np.testing.assert_array_equal(s.view(np.uint32), z[c + "_s"].view(np.uint32), err_msg=c)
+        np.testing.assert_array_equal(nxt, z[c + "_next"], err_msg=c)
+
+
+# --------------------------------------------------------------------------
+# The torch restatement of the reference's live path (the CPU baseline)
+# --------------------------------------------------------------------------
+def test_ref_torch_linear_equals_reference():
+    """``oracle.ref_torch`` forward/backward (fireflykernels.py:164-210) on the recorded inputs, run
+    twice like the fixture (the grad cache accumulates): y, dX, dW and db equal the reference's bits."""
+    import torch
+
+    from oracle import ref_torch as R
+    from tests._util import from_bf16_bits
+
+    z = load_golden("linear_bf16.npz")
+    for c in ("fp32", "bias_bf16"):
+        xdt = torch.bfloat16 if bool(z[c + "_xisbf16"]) else torch.float32
+        x = torch.from_numpy(z[c + "_x"]).to(xdt).requires_grad_(True)
+        q, s = torch.from_numpy(z[c + "_q"]), torch.from_numpy(z[c + "_s"])
+        bias = torch.from_numpy(z[c + "_bias"]).requires_grad_(True) if z[c + "_bias"].size else None
+        dy = from_bf16_bits(z[c + "_dy"])
+        cache = {}
+        for _ in range(2):
+            y = R._LinearFn.apply(x, q, s, bias, cache, 1)
+            y.backward(dy)
+        np.testing.assert_array_equal(y.detach().view(torch.int16).numpy().view(np.uint16), z[c + "_y"], err_msg=c)
+        np.testing.assert_array_equal(x.grad.float().numpy(), z[c + "_dx"], err_msg=c)
+        np.testing.assert_array_equal(cache[1].view(torch.int16).numpy().view(np.uint16), z[c + "_gw2"], err_msg=c)
+        if bias is not None:
+            np.testing.assert_array_equal(bias.grad.numpy(), z[c + "_db2"], err_msg=c)
+
+
+@pytest.mark.parametrize("case", ["cfg1like", "ragged", "defaultwd", "unbiased", "bigstep"])
+def test_ref_torch_optimizer_step_equals_reference(case):
+    """``oracle.ref_torch.dqt_step`` (fireflyoptim.py:136-209) from the reference's zero state, fed the
+    recorded gradients and uniforms, reproduces every recorded weight, code and absmax exactly."""
+    import torch
+
+    from oracle import ref_torch as R
+    from tests._util import from_bf16_bits
+
+    z = load_golden("optim_step.npz")
+    O_, K, bs = (int(v) for v in z[case + "_meta"])
+    lr, b1, b2, eps, wd, sr = (float(v) for v in z[case + "_hyper"])
+    q = torch.from_numpy(z[case + "_q0"].copy())
+    ws = torch.from_numpy(z[case + "_ws"])
+    st = R.init_state((O_, K), bs=bs)
+    for s in range(3):
+        R.dqt_step(q, ws, from_bf16_bits(z[f"{case}_s{s}_g"]), st, lr=lr, beta1=b1, beta2=b2, eps=eps, wd=wd,
+                   sr_bias=sr, bs=bs, u=torch.from_numpy(z[f"{case}_s{s}_u"]))
+        np.testing.assert_array_equal(q.numpy(), z[f"{case}_s{s}_q"], err_msg=f"{case} step {s}")
+        for k in ("m_q", "m_absmax", "v_q", "v_absmax", "r_q", "r_absmax"):
+            np.testing.assert_array_equal(st[k].numpy(), z[f"{case}_s{s}_{k}"], err_msg=f"{case} step {s} {k}")
+        assert st["step"] == s + 1
