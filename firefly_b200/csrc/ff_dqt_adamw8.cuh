@@ -6,39 +6,59 @@
 // writes q, the codes and the new absmax.
 //
 // Work split: one warp per 256-element block, 8 consecutive elements per lane
-// (16 B of g, 8 B of each code array per lane: fully coalesced).  The block
-// absmax of the re-encoded r, m, v is a warp max-reduction.
+// (16 B of g, 8 B of each code array per lane: fully coalesced), staged into
+// shared memory by per-warp double-buffered 1-D bulk copies.  The block absmax of
+// the re-encoded r, m, v is a warp max-reduction.
 //
-// Decode uses the exact per-code tables x_norm(code) of fireflyoptim.py:47-48
-// and :77-78 (computed once on the host), replicated 16 times in shared memory
-// (entry e of replica k at word e*16+k; lanes l and l+16 share a replica).
-// Encode evaluates the mu-law curve as 127/8*log2(1+255|x|) (signed) and
-// 255/8*log2(1+255 x) (unsigned): ln(1+255x)/ln(256) = log2(1+255x)/8.
+// The kernel is bound by instruction issue (about 10 B of HBM traffic per element
+// against some 60 instructions), so every step is written for the fewest issue slots:
 //
-// The kernel is bound by instruction issue as much as by HBM, so the fp32 math
-// uses the special-function unit's approximations (rsqrt, lg2, tanh) and the
-// 1.5*2^23 magic add for rounding and int<->float, each checked against the exact
-// formulation where a result could land on a decision boundary: the eps term of
-// the Adam denominator, and the stochastic-rounding comparison (an accurate tanh
-// is recomputed when |u - threshold| < 2e-4).
+// * Decode.  The decode tables x_norm(code) of fireflyoptim.py:47-48 and :77-78
+//   (computed on the host by the reference formula) sit in shared memory as 256
+//   rows of 256 bytes: row c holds 32 copies of the signed entry (one per lane)
+//   and 32 of the unsigned one.  The byte offset of lane l's copy of code c is
+//   c*256 + 4*l, which one byte permute builds from the code word and the lane's
+//   4*l: a decode is one permute and one conflict-free shared load.
+// * Packed pairs.  Two elements go through each f32x2 add/mul/fma; int8 and
+//   uint8 values become floats through the 1.5*2^23 magic word built by a byte
+//   permute, and codes are packed back from magic words by byte permutes.
+// * Adam.  m' = dec(m)*(am*b1) + (1-b1)*g, v' = dec(v)*(av*b2) + (1-b2)*g*g, and
+//   a = m' / (bc1*sqrt(v'/bc2) + bc1*eps) with the special-function unit's sqrt
+//   and reciprocal.  The residual r' = dec(r)*ar + a*(-lr/ws) + q*(-lr*wd).  These
+//   regroup the reference's roundings: every value is within a few ulps of the
+//   reference chain, so a code moves by one step only when its value sits within a
+//   few ulps of a code boundary (the parity bar allows one LSB on 0.1% of elements).
+// * Stochastic rounding (fireflyoptim.py:186-198) in the signed domain:
+//   with t = trunc(r'), phi = (r' - t) + sr_bias*tanh(a) and d = phi - copysign(u, r'),
+//   dq = t + sign(r') * [d*r' > 0], which is sign(r')*(floor|r'| + [u < clamp(frac|r'|
+//   + tanh(a)*sr_bias*sign(r'), 0, 1)]) for |r'| < 2^22 (trunc is the magic add with
+//   round-toward-zero).  tanh.approx is good to about 5e-4 relative: where |d| < 2e-4
+//   the decision is redone with an accurate tanh.
+// * Encode (fireflyoptim.py:22-67): 127/8*log2(1 + 255|x|/absmax) (signed) and
+//   255/8*log2(1 + 255 x/absmax) (unsigned) with lg2.approx, rounded by the magic add
+//   with the +128 offset folded in (ln(1+y)/ln 256 = log2(1+y)/8).
 #pragma once
 #include "ff_common.cuh"
 
 namespace ff {
 namespace optim {
 
-constexpr int kThreads = 256;
+#ifndef FF_DQT_THREADS
+#define FF_DQT_THREADS 384
+#endif
+constexpr int kThreads = FF_DQT_THREADS;
+constexpr int kCtasPerSm = 2;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBlock = 256;
-constexpr int kRep = 16;                  // table replicas: lanes l and l+16 share one
-constexpr int kTabWords = 256 * kRep;     // one replicated table
-constexpr int kTabBytes = 2 * kTabWords * 4;
+constexpr int kTabBytes = 256 * 256;  // 256 codes x (32 signed + 32 unsigned copies)
 // per warp, two stages of one block's inputs, filled by 1-D bulk (TMA) copies:
-// g (512 B) | q (256) | m (256) | v (256) | r (256) | u (1024, parity mode only)
-constexpr int kStageBytes = 512 + 4 * 256 + 1024;
+// g (512 B) | q (256) | m (256) | v (256) | r (256) | u (1024, supplied-uniform mode only)
 constexpr int kStageOffQ = 512, kStageOffM = 768, kStageOffV = 1024, kStageOffR = 1280, kStageOffU = 1536;
-constexpr int kSmemBytes = kTabBytes + kWarps * 2 * kStageBytes + kWarps * 2 * 8;
+__host__ __device__ constexpr int stage_bytes(bool has_u) { return has_u ? 2560 : 1536; }
+__host__ __device__ constexpr int smem_bytes(bool has_u) { return kTabBytes + kWarps * 2 * stage_bytes(has_u) + kWarps * 2 * 8; }
 constexpr float kMagic = 12582912.0f;     // 1.5 * 2^23
+// rows with lr / max(ws, eps) above this take the step-by-step chain (see exact_pair)
+constexpr float kFastRatio = 16.f;
 
 struct Params {
   int8_t* q;
@@ -59,6 +79,10 @@ struct Params {
   int64_t rng_offset;
   int64_t row_step, in_row_step;  // grid-stride advance in (rows, elements within a row)
   int bulk;                       // all arrays 16-byte aligned: stage inputs with bulk copies
+  // Philox4x32-10 with the counter (call_lo, call_hi, step_lo, step_hi): the round keys, and the
+  // first round's products of the constant counter word step_lo
+  uint32_t key0[10], key1[10];
+  uint32_t r1_hi, r1_lo, r1_c3k;  // mulhi(M1, step_lo), M1 * step_lo, step_hi ^ key1[0]
   const float* u;
   const float* dec_s;
   const float* dec_u;
@@ -154,77 +178,169 @@ __device__ __forceinline__ float tanh_accurate(float x) {
   return __fsub_rn(1.f, __fmul_rn(2.f, rcp_approx(__fadd_rn(1.f, e))));
 }
 
-// x / d from inv_d ~ 1/d with one residual correction: q0 = x*inv_d, r = x - q0*d (exact by
-// FMA), q = q0 + r*inv_d.  This is the correctly rounded quotient except when it lies
-// extremely close to a rounding midpoint.
-__device__ __forceinline__ float div_nr(float x, float d, float inv_d) {
-  const float q0 = __fmul_rn(x, inv_d);
-  const float r = __fmaf_rn(-q0, d, x);
-  return __fmaf_rn(r, inv_d, q0);
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
-
-// sqrt(x) from rsqrt.approx with one residual correction, x >= 0.  Arguments below
-// 1e-37 (whose square roots are far below any eps added to them) use rsqrt(1e-37), so
-// x == 0 gives exactly 0 without a select.
-__device__ __forceinline__ float sqrt_nr(float x) {
-  const float rs = rsqrt_approx(fmaxf(x, 1e-37f));
-  const float s0 = __fmul_rn(x, rs);
-  const float e = __fmaf_rn(-s0, s0, x);
-  return __fmaf_rn(e, __fmul_rn(0.5f, rs), s0);
+__device__ __forceinline__ f2 add2_rz(f2 a, f2 b) {
+  f2 r;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
 }
-
-// exact int <-> float for small integers on the FMA/ALU pipes
-__device__ __forceinline__ float small_int_to_float(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), kMagic); }
-__device__ __forceinline__ int rne_int(float x) { return __float_as_int(__fadd_rn(x, kMagic)) - 0x4B400000; }
-
+// max(a, |x|, |y|) for a >= 0 (three-input max)
+__device__ __forceinline__ float max3_abs(float a, float x, float y) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(fabsf(x)), "f"(fabsf(y)));
+  return r;
+}
 // maximum over the warp of non-negative floats: their bit patterns order like the values,
 // so one integer reduction does it
 __device__ __forceinline__ float warp_max_nonneg(float v) {
   return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
-
-// low bytes of four ints -> one word (byte permutes)
-__device__ __forceinline__ uint32_t pack_codes(const int (&c)[8], int base) {
-  const uint32_t lo = __byte_perm((uint32_t)c[base], (uint32_t)c[base + 1], 0x0040);
-  const uint32_t hi = __byte_perm((uint32_t)c[base + 2], (uint32_t)c[base + 3], 0x0040);
-  return __byte_perm(lo, hi, 0x5410);
+// byte offset c*256 + lane4 of lane l's copy of code c = byte k of w (lane4 = 4*l < 256)
+template <int K>
+__device__ __forceinline__ uint32_t tab_off(uint32_t w, uint32_t lane4) {
+  return __byte_perm(w, lane4, 0x5504u | (K << 4));
 }
+// the magic word 0x4B4000xx of byte k of w (xx = the byte): its float is 1.5*2^23 + xx
+template <int K>
+__device__ __forceinline__ float magic_of_byte(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4B400000u, 0x7650u | K));
+}
+// the low bytes of the magic words of four floats, packed into one word
+__device__ __forceinline__ uint32_t pack_magic4(float a, float b, float c, float d) {
+  return pack_lo4(__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d));
+}
+__device__ __forceinline__ uint32_t sign_of(float x) { return __float_as_uint(x) & 0x80000000u; }
+__device__ __forceinline__ float with_sign(float mag, uint32_t sign) { return __uint_as_float(__float_as_uint(mag) | sign); }
 
-// x / d with nd = -d and id ~ 1/d: q0 = x*id, r = x - q0*d (exact), q = q0 + r*id
+// x / d with nd = -d and id ~ 1/d: q0 = x*id, r = x - q0*d (exact by FMA), q = q0 + r*id, the
+// correctly rounded quotient except extremely close to a rounding midpoint
 __device__ __forceinline__ f2 div2(f2 x, f2 nd, f2 id) {
   const f2 q0 = mul2(x, id);
   return fma2(fma2(q0, nd, x), id, q0);
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xFFu; }
+// Hyperparameters of the update as fp32 scalars (the roundings of the reference's torch ops).
+struct Hyper {
+  float neg_lr, beta1, beta2, eps, wd, sr_bias, omb1, omb2, bc1, bc2, ibc1, ibc2;
+};
 
-// ROWS: 0 = row_len a multiple of 8 (a lane's 8 elements share one weight row),
-//       1 = row_len >= 8 (they span at most two rows), 2 = row_len < 8
-template <bool HAS_U, int ROWS>
-__global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
-  extern __shared__ __align__(128) float tab[];  // [2][256 codes][kRep], then staging, then barriers
-  float* tabS = tab;
-  float* tabU = tab + kTabWords;
-  uint8_t* stage_base = reinterpret_cast<uint8_t*>(tab) + kTabBytes;
-  const int warp = threadIdx.x >> 5;
-  uint8_t* my_stage = stage_base + warp * 2 * kStageBytes;
-  const uint32_t bar0 = smem_addr(stage_base + kWarps * 2 * kStageBytes) + warp * 16;
-  for (int i = threadIdx.x; i < kTabWords; i += kThreads) {
-    tabS[i] = __ldg(p.dec_s + i / kRep);
-    tabU[i] = __ldg(p.dec_u + i / kRep);
+// The reference's chain for one pair of elements, rounding step by step like its torch ops
+// (fireflyoptim.py:163-198): used for weight rows whose lr / max(ws, eps) is large, where
+// the residual r is large and loses its leading digits when dq is subtracted, so that a
+// few ulps of r would move its code.  Inputs: g, the decoded m, v, r (code value times
+// block absmax), q (ints), the rows' max(ws, eps) and 1/that, the uniforms.  Outputs the
+// new m, v, r and the magic words (1.5*2^23 + q') of the new weights.
+__device__ __forceinline__ void exact_pair(const Hyper& h, f2 g, f2 m, f2 v, f2 r, int q0, int q1, float ws0,
+                                           float ws1, float iws0, float iws1, float u0, float u1, f2& m_out,
+                                           f2& v_out, f2& r_out, f2& q_out) {
+  const f2 mone2 = splat(-1.f);
+  m = fma2(g, splat(h.omb1), mul2(m, splat(h.beta1)));
+  v = fma2(mul2(splat(h.omb2), g), g, mul2(v, splat(h.beta2)));
+  const f2 mh = div2(m, splat(-h.bc1), splat(h.ibc1));
+  const f2 vh = div2(v, splat(-h.bc2), splat(h.ibc2));
+  float vh0, vh1;
+  un2(vh, vh0, vh1);
+  // sqrt from rsqrt.approx with one residual correction; arguments below 1e-37 (square roots
+  // far below eps) use rsqrt(1e-37), so that sqrt(0) = 0 exactly
+  const f2 rs = mk2(rsqrt_approx(fmaxf(vh0, 1e-37f)), rsqrt_approx(fmaxf(vh1, 1e-37f)));
+  const f2 s0 = mul2(vh, rs);
+  const f2 sq = fma2(fma2(s0, mul2(s0, mone2), vh), mul2(rs, splat(0.5f)), s0);
+  const f2 den = add2(sq, splat(h.eps));
+  float dn0, dn1;
+  un2(den, dn0, dn1);
+  const f2 a = div2(mh, mul2(den, mone2), mk2(rcp_approx(dn0), rcp_approx(dn1)));
+  const f2 qf = mk2((float)q0, (float)q1);
+  const f2 ws = mk2(ws0, ws1);
+  const f2 dwe = mul2(splat(h.neg_lr), add2(a, mul2(mul2(splat(h.wd), qf), ws)));
+  r = add2(r, div2(dwe, mk2(-ws0, -ws1), mk2(iws0, iws1)));
+  float r0, r1, a0, a1;
+  un2(r, r0, r1);
+  un2(a, a0, a1);
+  const float rr[2] = {r0, r1}, aa[2] = {a0, a1}, uu[2] = {u0, u1};
+  float dqf[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    // floor and frac of |r| (|r| clamped to 2^21, far above any value the update reaches,
+    // so that the floor is exact by the magic add with round-down)
+    const float absr = fminf(fabsf(rr[e]), 2097152.f);
+    const float base = __fsub_rn(__fadd_rd(absr, kMagic), kMagic);
+    const float fr = __fsub_rn(absr, base);
+    const uint32_t rsign = sign_of(rr[e]);
+    float fb = fr;
+    if (h.sr_bias != 0.f) {
+      const float tb = __fmul_rn(tanh_approx(aa[e]), h.sr_bias);
+      fb = __fadd_rn(fr, __uint_as_float(__float_as_uint(tb) ^ rsign));
+      if (fabsf(__fsub_rn(uu[e], fb)) < 2e-4f) {
+        const float tb2 = __fmul_rn(tanh_accurate(aa[e]), h.sr_bias);
+        fb = __fadd_rn(fr, __uint_as_float(__float_as_uint(tb2) ^ rsign));
+      }
+    }
+    const bool up = (uu[e] < fb) && (rr[e] != 0.f);
+    dqf[e] = copysignf(up ? __fadd_rn(base, 1.f) : base, rr[e]);
   }
-  if ((threadIdx.x & 31) == 0) {
-    bar_init(bar0);
-    bar_init(bar0 + 8);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const int qa = max(-127, min(127, q0 + (__float_as_int(__fadd_rn(dqf[0], kMagic)) - 0x4B400000)));
+  const int qb = max(-127, min(127, q1 + (__float_as_int(__fadd_rn(dqf[1], kMagic)) - 0x4B400000)));
+  q_out = mk2(__int_as_float(0x4B400000 + qa), __int_as_float(0x4B400000 + qb));
+  r_out = sub2(r, mk2(dqf[0], dqf[1]));
+  m_out = m;
+  v_out = v;
+}
+
+// Philox4x32-10 of the counter (c0, c1, step_lo, step_hi) with the launch's round keys; the
+// first round's product of the constant counter word comes precomputed
+__device__ __forceinline__ void philox_call(uint32_t c0, uint32_t c1, const Params& p, uint32_t (&out)[4]) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  uint32_t x0 = p.r1_hi ^ c1 ^ p.key0[0];
+  uint32_t x1 = p.r1_lo;
+  const uint64_t p0 = (uint64_t)M0 * c0;
+  uint32_t x2 = (uint32_t)(p0 >> 32) ^ p.r1_c3k;
+  uint32_t x3 = (uint32_t)p0;
+#pragma unroll
+  for (int r = 1; r < 10; ++r) {
+    const uint64_t a = (uint64_t)M0 * x0, b = (uint64_t)M1 * x2;
+    x0 = (uint32_t)(b >> 32) ^ x1 ^ p.key0[r];
+    x1 = (uint32_t)b;
+    x2 = (uint32_t)(a >> 32) ^ x3 ^ p.key1[r];
+    x3 = (uint32_t)a;
   }
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int slot = lane & (kRep - 1);
+  out[0] = x0;
+  out[1] = x1;
+  out[2] = x2;
+  out[3] = x3;
+}
+
+// decode-table load of the entry at byte offset `off` + IMM of the rows, which start at shared
+// address BASE (>= 0: known when compiled, folded into the load's immediate) or `base` (BASE < 0)
+template <int BASE, int IMM>
+__device__ __forceinline__ float ld_tab(uint32_t base, uint32_t off) {
+  float v;
+  if constexpr (BASE >= 0)
+    asm("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(off), "n"(BASE + IMM));
+  else
+    asm("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(base + off), "n"(IMM));
+  return v;
+}
+
+// The per-block work of one warp (8 elements per lane).  ROWS: 0 = row_len a multiple of 8 (a
+// lane's 8 elements share one weight row), 1 = row_len >= 8 (they span at most two rows),
+// 2 = row_len < 8.  TAB: the shared address of the decode rows when known at compile time (the
+// kernel dispatches on the usual values), else -1.
+template <bool HAS_U, int ROWS, int TAB>
+__device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
+  constexpr int kStage = stage_bytes(HAS_U);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* my_stage = smem + kTabBytes + warp * 2 * kStage;
+  const uint32_t bar0 = smem_addr(smem + kTabBytes + kWarps * 2 * kStage) + warp * 16;
+  const uint32_t tab_base = smem_addr(smem);
+  const uint32_t lane4 = 4u * lane;
   const uint32_t stage_bytes_tx = 512 + 4 * 256 + (HAS_U ? 1024 : 0);
   // lane 0 stages block b (a full block) into stage s
   auto prefetch = [&](int64_t b, int s) {
-    const uint32_t dst = smem_addr(my_stage + s * kStageBytes), bar = bar0 + 8 * s;
+    const uint32_t dst = smem_addr(my_stage + s * kStage), bar = bar0 + 8 * s;
     const int64_t e = b * kBlock;
     bar_expect(bar, stage_bytes_tx);
     bulk_g2s(dst, p.g + e, 512, bar);
@@ -236,15 +352,198 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
   };
   const int64_t full_blocks = p.numel / kBlock;  // blocks [0, full_blocks) have 256 elements
   const int64_t nblocks = (p.numel + kBlock - 1) / kBlock;
+  const int64_t staged_blocks = p.bulk ? full_blocks : 0;
   const int64_t wstride = (int64_t)gridDim.x * kWarps;
   const float eps = p.eps;
   const int64_t last_row = (p.elem_base + p.numel - 1) / p.row_len;
-  // loop-invariant pairs
-  const f2 b1 = splat(p.beta1), b2 = splat(p.beta2), omb1 = splat(p.omb1), omb2 = splat(p.omb2);
-  const f2 nbc1 = splat(-p.bc1), nbc2 = splat(-p.bc2), ibc1 = splat(p.ibc1), ibc2 = splat(p.ibc2);
-  const f2 eps2 = splat(eps), nlr = splat(p.neg_lr), wd2 = splat(p.wd), magic2 = splat(kMagic);
-  const f2 half2 = splat(0.5f), mone2 = splat(-1.f);
+  const Hyper hy{p.neg_lr, p.beta1, p.beta2, eps, p.wd, p.sr_bias, p.omb1, p.omb2, p.bc1, p.bc2, p.ibc1, p.ibc2};
+
+  // One block: inputs as packed words (g bf16 pairs; q, m, v, r bytes), uniforms, the weight rows'
+  // max(ws, eps) and where the second row starts (jsw), the block absmax; writes nvalid elements.
+  auto process = [&](int64_t blk, const uint32_t (&gw)[4], const uint32_t (&qw)[2], const uint32_t (&mw)[2],
+                     const uint32_t (&vw)[2], const uint32_t (&rw)[2], const float* u, float wsa, float wsb,
+                     int jsw, float am, float av, float ar, int nvalid) {
+    const int64_t e0 = blk * kBlock + lane * 8;
+    uint32_t rw4[4];  // Philox output: 16 bits per element
+    if constexpr (!HAS_U) {
+      const uint64_t call = (uint64_t)(p.rng_offset + e0) >> 3;
+      philox_call((uint32_t)call, (uint32_t)(call >> 32), p, rw4);
+    }
+    const float caa = __fmul_rn(p.neg_lr, rcp_approx(wsa)), cab = __fmul_rn(p.neg_lr, rcp_approx(wsb));
+    // rows with a large lr/ws carry large residuals: they take the step-by-step chain
+    const bool exact = ROWS == 2 || fabsf(caa) > kFastRatio || fabsf(cab) > kFastRatio;
+    const uint32_t qb[2] = {qw[0] ^ 0x80808080u, qw[1] ^ 0x80808080u};  // bytes biased by 128
+    // decode of pair pp (fireflyoptim.py:39-80): one permute + one shared load per code
+    auto decode = [&](int pp, f2& tm, f2& tv, f2& tr, f2& qm) {
+      const int w = pp >> 1;
+      uint32_t om0, om1, ov0, ov1, or0, or1;
+      float qm0, qm1;
+      if (pp & 1) {
+        om0 = tab_off<2>(mw[w], lane4); om1 = tab_off<3>(mw[w], lane4);
+        ov0 = tab_off<2>(vw[w], lane4); ov1 = tab_off<3>(vw[w], lane4);
+        or0 = tab_off<2>(rw[w], lane4); or1 = tab_off<3>(rw[w], lane4);
+        qm0 = magic_of_byte<2>(qb[w]); qm1 = magic_of_byte<3>(qb[w]);
+      } else {
+        om0 = tab_off<0>(mw[w], lane4); om1 = tab_off<1>(mw[w], lane4);
+        ov0 = tab_off<0>(vw[w], lane4); ov1 = tab_off<1>(vw[w], lane4);
+        or0 = tab_off<0>(rw[w], lane4); or1 = tab_off<1>(rw[w], lane4);
+        qm0 = magic_of_byte<0>(qb[w]); qm1 = magic_of_byte<1>(qb[w]);
+      }
+      tm = mk2(ld_tab<TAB, 0>(tab_base, om0), ld_tab<TAB, 0>(tab_base, om1));
+      tv = mk2(ld_tab<TAB, 128>(tab_base, ov0), ld_tab<TAB, 128>(tab_base, ov1));
+      tr = mk2(ld_tab<TAB, 0>(tab_base, or0), ld_tab<TAB, 0>(tab_base, or1));
+      qm = mk2(qm0, qm1);
+    };
+    auto uniforms = [&](int pp, float& u0, float& u1) {
+      if constexpr (HAS_U) {
+        u0 = u[2 * pp];
+        u1 = u[2 * pp + 1];
+      } else {
+        // u = (h + 0.5) / 65536 for the 16-bit halves h of the Philox word: 2^23 + h is built by a
+        // byte permute, and (2^23 + h) * 2^-16 + (2^-17 - 128) is exact in one FMA
+        const uint32_t wd_ = rw4[pp];
+        u0 = __fmaf_rn(__int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7610)), 1.0f / 65536.0f, 1.0f / 131072.0f - 128.0f);
+        u1 = __fmaf_rn(__int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7632)), 1.0f / 65536.0f, 1.0f / 131072.0f - 128.0f);
+      }
+    };
+    f2 mn[4], vn[4], rn[4], qn[4];
+    if (!exact) {
+      const f2 am2 = splat(am * p.beta1), av2 = splat(av * p.beta2), ar2 = splat(ar);
+      const f2 den_k = splat(p.bc1 * sqrtf(p.ibc2)), den_c = splat(p.bc1 * eps);  // bc1*sqrt(v/bc2) + bc1*eps
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) {
+        const int j0 = 2 * pp, j1 = 2 * pp + 1;
+        const float ca0 = j0 < jsw ? caa : cab, ca1 = j1 < jsw ? caa : cab;
+        f2 tm, tv, tr, qm;
+        decode(pp, tm, tv, tr, qm);
+        const f2 g = mk2(__uint_as_float(gw[pp] << 16), __uint_as_float(gw[pp] & 0xFFFF0000u));
+        // Adam moments (fireflyoptim.py:175-182)
+        const f2 m = fma2(tm, am2, mul2(g, splat(p.omb1)));
+        const f2 v = fma2(tv, av2, mul2(mul2(g, g), splat(p.omb2)));
+        float v0, v1;
+        un2(v, v0, v1);
+        float d0, d1;
+        un2(fma2(mk2(sqrt_approx(v0), sqrt_approx(v1)), den_k, den_c), d0, d1);
+        const f2 a = mul2(m, mk2(rcp_approx(d0), rcp_approx(d1)));
+        // DQT residual (fireflyoptim.py:180-184)
+        const f2 qf = sub2(qm, splat(kMagic + 128.f));
+        const f2 r = fma2(tr, ar2, fma2(a, mk2(ca0, ca1), mul2(qf, splat(p.neg_lr * p.wd))));
+        // momentum-biased stochastic rounding (fireflyoptim.py:186-198)
+        float r0, r1, a0, a1;
+        un2(r, r0, r1);
+        un2(a, a0, a1);
+        const uint32_t s0 = sign_of(r0), s1 = sign_of(r1);
+        const f2 ms = mk2(with_sign(kMagic, s0), with_sign(kMagic, s1));
+        const f2 rt = sub2(add2_rz(r, ms), ms);  // trunc(r) for |r| < 2^22
+        float uj0, uj1;
+        uniforms(pp, uj0, uj1);
+        // sr_bias * tanh(a) = sr_bias - 2 sr_bias / (1 + e^{2a}) (absolute error about 1e-7)
+        float e0_, e1_;
+        un2(mul2(a, splat(2.8853900817779268f)), e0_, e1_);  // 2a / ln 2
+        float w0, w1;
+        un2(add2(mk2(ex2_approx(e0_), ex2_approx(e1_)), splat(1.f)), w0, w1);
+        const f2 phi = fma2(mk2(rcp_approx(w0), rcp_approx(w1)), splat(-2.f * p.sr_bias),
+                            add2(sub2(r, rt), splat(p.sr_bias)));
+        const f2 us = mk2(with_sign(uj0, s0), with_sign(uj1, s1));
+        float p0, p1;
+        un2(mul2(sub2(phi, us), r), p0, p1);
+        // dq = trunc(r) + sign(r) * [u < threshold]  (d*r > 0: u on the rounding-up side, r != 0)
+        const f2 inc = mk2(p0 > 0.f ? with_sign(1.f, s0) : 0.f, p1 > 0.f ? with_sign(1.f, s1) : 0.f);
+        const f2 dq = add2(rt, inc);
+        float qs0, qs1;
+        un2(add2(qf, dq), qs0, qs1);
+        qn[pp] = add2(mk2(fminf(fmaxf(qs0, -127.f), 127.f), fminf(fmaxf(qs1, -127.f), 127.f)), splat(kMagic));
+        rn[pp] = sub2(r, dq);
+        mn[pp] = m;
+        vn[pp] = v;
+      }
+    } else {
+      const f2 am2 = splat(am), av2 = splat(av), ar2 = splat(ar);
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) {
+        const int j0 = 2 * pp, j1 = 2 * pp + 1;
+        float ws0 = j0 < jsw ? wsa : wsb, ws1 = j1 < jsw ? wsa : wsb;
+        if constexpr (ROWS == 2) {  // rows shorter than 8 elements: one lookup per element
+          ws0 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j0, p.numel - 1)) / p.row_len, last_row)), eps);
+          ws1 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j1, p.numel - 1)) / p.row_len, last_row)), eps);
+        }
+        f2 tm, tv, tr, qm;
+        decode(pp, tm, tv, tr, qm);
+        float qm0, qm1;
+        un2(qm, qm0, qm1);
+        const int q0 = (int)(__float_as_uint(qm0) & 0xFFu) - 128, q1 = (int)(__float_as_uint(qm1) & 0xFFu) - 128;
+        const f2 g = mk2(__uint_as_float(gw[pp] << 16), __uint_as_float(gw[pp] & 0xFFFF0000u));
+        float uj0, uj1;
+        uniforms(pp, uj0, uj1);
+        exact_pair(hy, g, mul2(tm, am2), mul2(tv, av2), mul2(tr, ar2), q0, q1, ws0, ws1, __frcp_rn(ws0),
+                   __frcp_rn(ws1), uj0, uj1, mn[pp], vn[pp], rn[pp], qn[pp]);
+      }
+    }
+    // ---------------- block absmax and re-encode (mu-law, fireflyoptim.py:22-67)
+    float xm = 0.f, xv = 0.f, xr = 0.f;
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      float a0, a1;
+      un2(mn[pp], a0, a1);
+      xm = max3_abs(xm, a0, a1);
+      un2(vn[pp], a0, a1);
+      xv = max3_abs(xv, a0, a1);  // v >= 0; |.| turns -0 into +0
+      un2(rn[pp], a0, a1);
+      xr = max3_abs(xr, a0, a1);
+    }
+    xm = fmaxf(warp_max_nonneg(xm), 1e-12f);
+    xv = fmaxf(warp_max_nonneg(xv), 1e-12f);
+    xr = fmaxf(warp_max_nonneg(xr), 1e-12f);
+    // 255 / absmax: |x| * this is 255 * |x| / absmax (within an ulp or two)
+    const float km = __fmul_rn(255.f, rcp_approx(xm)), kr = __fmul_rn(255.f, rcp_approx(xr));
+    const f2 kv = splat(__fmul_rn(255.f, rcp_approx(xv)));
+    float cm[8], cv[8], cr[8], cq[8];
+    // |x| / absmax can exceed 1 by an ulp (absmax is the largest |x|); log2(256 + tiny) * 127/8
+    // still rounds to 127 (255 for v), so no clamps are needed.  v is never negative.
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      float x0, x1, y0, y1, z0, z1;
+      un2(mn[pp], x0, x1);
+      un2(rn[pp], y0, y1);
+      // signed m and r: code = 128 + sign(x) * rint(127/8 * log2(1 + 255 |x| / absmax))
+      float lm0, lm1, lr0, lr1;
+      un2(add2(mk2(__fmul_rn(fabsf(x0), km), __fmul_rn(fabsf(x1), km)), splat(1.f)), lm0, lm1);
+      un2(add2(mk2(__fmul_rn(fabsf(y0), kr), __fmul_rn(fabsf(y1), kr)), splat(1.f)), lr0, lr1);
+      un2(fma2(mk2(with_sign(lg2_approx(lm0), sign_of(x0)), with_sign(lg2_approx(lm1), sign_of(x1))),
+               splat(15.875f), splat(kMagic + 128.f)),
+          cm[2 * pp], cm[2 * pp + 1]);
+      un2(fma2(mk2(with_sign(lg2_approx(lr0), sign_of(y0)), with_sign(lg2_approx(lr1), sign_of(y1))),
+               splat(15.875f), splat(kMagic + 128.f)),
+          cr[2 * pp], cr[2 * pp + 1]);
+      // unsigned v: code = rint(255/8 * log2(1 + 255 v / absmax))
+      un2(fma2(vn[pp], kv, splat(1.f)), z0, z1);
+      un2(fma2(mk2(lg2_approx(z0), lg2_approx(z1)), splat(31.875f), splat(kMagic)), cv[2 * pp], cv[2 * pp + 1]);
+      un2(qn[pp], cq[2 * pp], cq[2 * pp + 1]);
+    }
+    if (nvalid == 8) {
+      // generic-proxy stores; the bulk copies only ever read other blocks
+      *reinterpret_cast<uint2*>(p.q + e0) = make_uint2(pack_magic4(cq[0], cq[1], cq[2], cq[3]), pack_magic4(cq[4], cq[5], cq[6], cq[7]));
+      *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(pack_magic4(cm[0], cm[1], cm[2], cm[3]), pack_magic4(cm[4], cm[5], cm[6], cm[7]));
+      *reinterpret_cast<uint2*>(p.v_q + e0) = make_uint2(pack_magic4(cv[0], cv[1], cv[2], cv[3]), pack_magic4(cv[4], cv[5], cv[6], cv[7]));
+      *reinterpret_cast<uint2*>(p.r_q + e0) = make_uint2(pack_magic4(cr[0], cr[1], cr[2], cr[3]), pack_magic4(cr[4], cr[5], cr[6], cr[7]));
+    } else {
+      for (int j = 0; j < nvalid; ++j) {
+        p.q[e0 + j] = (int8_t)__float_as_uint(cq[j]);
+        p.m_q[e0 + j] = (uint8_t)__float_as_uint(cm[j]);
+        p.v_q[e0 + j] = (uint8_t)__float_as_uint(cv[j]);
+        p.r_q[e0 + j] = (uint8_t)__float_as_uint(cr[j]);
+      }
+    }
+    if (lane == 0) {
+      p.m_absmax[blk] = xm;
+      p.v_absmax[blk] = xv;
+      p.r_absmax[blk] = xr;
+    }
+  };
+
+  // ---- staged loop: full blocks whose inputs arrive by bulk copies into the warp's two stages
   int64_t blk = (int64_t)blockIdx.x * kWarps + warp;
+  if (lane == 0 && blk < staged_blocks) prefetch(blk, 0);
   // weight row of this lane's first element, advanced incrementally (no division per block)
   int64_t row, in_row;
   {
@@ -252,37 +551,59 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
     row = ge / p.row_len;
     in_row = ge - row * p.row_len;
   }
-  if (p.bulk && lane == 0 && blk < full_blocks) prefetch(blk, 0);
-  for (int it = 0; blk < nblocks; blk += wstride, ++it) {
+  float am = 0.f, av = 0.f, ar = 0.f;
+  if (blk < staged_blocks) {
+    am = __ldg(p.m_absmax + blk);
+    av = __ldg(p.v_absmax + blk);
+    ar = __ldg(p.r_absmax + blk);
+  }
+  for (int it = 0; blk < staged_blocks; blk += wstride, ++it) {
+    const int stg = it & 1;
+    const int64_t nxt = blk + wstride;
+    // stage the next block while this one is computed (its stage was consumed last iteration)
+    if (lane == 0 && nxt < staged_blocks) prefetch(nxt, stg ^ 1);
+    const float am_c = am, av_c = av, ar_c = ar;
+    if (nxt < staged_blocks) {  // the next block's absmax, one iteration ahead
+      am = __ldg(p.m_absmax + nxt);
+      av = __ldg(p.v_absmax + nxt);
+      ar = __ldg(p.r_absmax + nxt);
+    }
+    const int64_t ra = min64(row, last_row), rb = min64(row + 1, last_row);
+    const int jsw = ROWS != 1 ? 8 : (int)min64(8, p.row_len - in_row);  // j >= jsw: next row
+    const float wsa = fmaxf(__ldg(p.wscale + ra), eps);
+    const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
+    if (!bar_wait(bar0 + 8 * stg, (it >> 1) & 1)) return;  // copies lost: status raised
+    const uint8_t* sb = my_stage + stg * kStage;
+    const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
+    const uint2 q2 = *reinterpret_cast<const uint2*>(sb + kStageOffQ + lane * 8);
+    const uint2 m2 = *reinterpret_cast<const uint2*>(sb + kStageOffM + lane * 8);
+    const uint2 v2 = *reinterpret_cast<const uint2*>(sb + kStageOffV + lane * 8);
+    const uint2 r2 = *reinterpret_cast<const uint2*>(sb + kStageOffR + lane * 8);
+    const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+    const uint32_t qw[2] = {q2.x, q2.y}, mw[2] = {m2.x, m2.y}, vw[2] = {v2.x, v2.y}, rw[2] = {r2.x, r2.y};
+    float u[HAS_U ? 8 : 1];
+    if constexpr (HAS_U) {
+      const float4 u0 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32);
+      const float4 u1 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32 + 16);
+      u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w;
+      u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
+    }
+    __syncwarp();  // every lane has its inputs: the stage may be refilled next iteration
+    process(blk, gw, qw, mw, vw, rw, u, wsa, wsb, jsw, am_c, av_c, ar_c, 8);
+    row += p.row_step;
+    in_row += p.in_row_step;
+    if (in_row >= p.row_len) {
+      in_row -= p.row_len;
+      ++row;
+    }
+  }
+  // ---- the rest: the ragged last block, or every block when the arrays are not 16-byte aligned
+  for (; blk < nblocks; blk += wstride) {
     const int64_t e0 = blk * kBlock + lane * 8;
     const int nvalid = (int)max64(0, min64(8, p.numel - e0));
-    const int stg = it & 1;
-    const bool staged = p.bulk && blk < full_blocks;
-    // stage the next block while this one is computed (its stage was consumed last iteration)
-    if (p.bulk && lane == 0 && blk + wstride < full_blocks) prefetch(blk + wstride, stg ^ 1);
-    const float am = __ldg(p.m_absmax + blk), av = __ldg(p.v_absmax + blk), ar = __ldg(p.r_absmax + blk);
-    // ---------------- inputs as packed words: g (bf16 pairs), q/m/v/r (bytes)
     uint32_t gw[4], qw[2], mw[2], vw[2], rw[2];
     float u[HAS_U ? 8 : 1];
-    if (staged) {
-      if (!bar_wait(bar0 + 8 * stg, (it >> 1) & 1)) return;  // copies lost: status raised
-      const uint8_t* sb = my_stage + stg * kStageBytes;
-      const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
-      const uint2 q2 = *reinterpret_cast<const uint2*>(sb + kStageOffQ + lane * 8);
-      const uint2 m2 = *reinterpret_cast<const uint2*>(sb + kStageOffM + lane * 8);
-      const uint2 v2 = *reinterpret_cast<const uint2*>(sb + kStageOffV + lane * 8);
-      const uint2 r2 = *reinterpret_cast<const uint2*>(sb + kStageOffR + lane * 8);
-      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
-      qw[0] = q2.x; qw[1] = q2.y; mw[0] = m2.x; mw[1] = m2.y;
-      vw[0] = v2.x; vw[1] = v2.y; rw[0] = r2.x; rw[1] = r2.y;
-      if constexpr (HAS_U) {
-        const float4 u0 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32);
-        const float4 u1 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32 + 16);
-        u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w;
-        u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
-      }
-      __syncwarp();  // every lane has its inputs: the stage may be refilled next iteration
-    } else if (nvalid == 8) {
+    if (nvalid == 8) {
       const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(p.g + e0));
       const uint2 q2 = *reinterpret_cast<const uint2*>(p.q + e0);
       const uint2 m2 = *reinterpret_cast<const uint2*>(p.m_q + e0);
@@ -315,187 +636,44 @@ __global__ void __launch_bounds__(kThreads, 3) dqt_adamw8_kernel(Params p) {
         if constexpr (HAS_U) u[j] = j < nvalid ? __ldg(p.u + e0 + j) : 2.f;
       }
     }
-    uint32_t rw4[4];  // Philox output: 16 bits per element
-    if constexpr (!HAS_U) {
-      const uint64_t call = (uint64_t)(p.rng_offset + e0) >> 3;
-      philox4x32_10((uint32_t)call, (uint32_t)(call >> 32), p.step_lo, p.step_hi, p.seed_lo, p.seed_hi, rw4);
-    }
-    // weight-row scales: with row_len >= 8 the 8 elements span at most two rows
-    const int64_t ra = min64(row, last_row), rb = min64(row + 1, last_row);
-    const int jsw = ROWS != 1 ? 8 : (int)min64(8, p.row_len - in_row);  // j >= jsw: next row
+    const int64_t ge = p.elem_base + min64(e0, p.numel - 1);
+    const int64_t r0 = ge / p.row_len, in0 = ge - r0 * p.row_len;
+    const int64_t ra = min64(r0, last_row), rb = min64(r0 + 1, last_row);
+    const int jsw = ROWS != 1 ? 8 : (int)min64(8, p.row_len - in0);
     const float wsa = fmaxf(__ldg(p.wscale + ra), eps);
     const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
-    const float iwsa = __frcp_rn(wsa), iwsb = __frcp_rn(wsb);
-    const f2 am2 = splat(am), av2 = splat(av), ar2 = splat(ar);
-    f2 mn[4], vn[4], rn[4];
-    int qn[8];
-#pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      const int j0 = 2 * pp, j1 = 2 * pp + 1;
-      const int w = pp >> 1, k0 = j0 & 3, k1 = j1 & 3;
-      // weight-row scale of both elements
-      float ws0 = j0 < jsw ? wsa : wsb, ws1 = j1 < jsw ? wsa : wsb;
-      float iws0 = j0 < jsw ? iwsa : iwsb, iws1 = j1 < jsw ? iwsa : iwsb;
-      if constexpr (ROWS == 2) {  // rows shorter than 8 elements: one division per element
-        ws0 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j0, p.numel - 1)) / p.row_len, last_row)), eps);
-        ws1 = fmaxf(__ldg(p.wscale + min64((p.elem_base + min64(e0 + j1, p.numel - 1)) / p.row_len, last_row)), eps);
-        iws0 = __frcp_rn(ws0);
-        iws1 = __frcp_rn(ws1);
-      }
-      const f2 ws = mk2(ws0, ws1), nws = mk2(-ws0, -ws1), iws = mk2(iws0, iws1);
-      // decode (fireflyoptim.py:39-80): table value * block absmax
-      const f2 g = mk2(__uint_as_float(gw[pp] << 16), __uint_as_float(gw[pp] & 0xFFFF0000u));
-      f2 m = mul2(mk2(tabS[byte_of(mw[w], k0) * kRep + slot], tabS[byte_of(mw[w], k1) * kRep + slot]), am2);
-      f2 v = mul2(mk2(tabU[byte_of(vw[w], k0) * kRep + slot], tabU[byte_of(vw[w], k1) * kRep + slot]), av2);
-      f2 r = mul2(mk2(tabS[byte_of(rw[w], k0) * kRep + slot], tabS[byte_of(rw[w], k1) * kRep + slot]), ar2);
-      // Adam moments (fireflyoptim.py:175-178); the chain below follows the reference's
-      // rounding step by step because the residual loses its leading digits when dq is
-      // subtracted (fireflyoptim.py:177-184)
-      m = fma2(g, omb1, mul2(m, b1));
-      v = fma2(mul2(omb2, g), g, mul2(v, b2));
-      const f2 mh = div2(m, nbc1, ibc1);
-      const f2 vh = div2(v, nbc2, ibc2);
-      float vh0, vh1;
-      un2(vh, vh0, vh1);
-      // sqrt from rsqrt.approx with one residual correction; arguments below 1e-37 (square
-      // roots far below eps) use rsqrt(1e-37) so that sqrt(0) = 0 exactly
-      const f2 rs = mk2(rsqrt_approx(fmaxf(vh0, 1e-37f)), rsqrt_approx(fmaxf(vh1, 1e-37f)));
-      const f2 s0 = mul2(vh, rs);
-      const f2 sq = fma2(fma2(s0, mul2(s0, mone2), vh), mul2(rs, half2), s0);
-      const f2 den = add2(sq, eps2);
-      float d0, d1;
-      un2(den, d0, d1);
-      const f2 a = div2(mh, mul2(den, mone2), mk2(rcp_approx(d0), rcp_approx(d1)));
-      // DQT residual (fireflyoptim.py:180-184)
-      const int q0 = (int)(int8_t)byte_of(qw[w], k0), q1 = (int)(int8_t)byte_of(qw[w], k1);
-      const f2 qf = sub2(mk2(__int_as_float(0x4B400000 + q0), __int_as_float(0x4B400000 + q1)), magic2);
-      const f2 dwe = mul2(nlr, add2(a, mul2(mul2(wd2, qf), ws)));
-      r = add2(r, div2(dwe, nws, iws));
-      // momentum-biased stochastic rounding (fireflyoptim.py:186-198)
-      float r0, r1, a0, a1;
-      un2(r, r0, r1);
-      un2(a, a0, a1);
-      // |r| is clamped to 2^21 (far above any reachable residual) so that the floor and the
-      // integer conversion below are exact magic-number adds
-      const f2 absr = mk2(fminf(fabsf(r0), 2097152.f), fminf(fabsf(r1), 2097152.f));
-      const f2 base = sub2(add2_rm(absr, magic2), magic2);  // floor(|r|)
-      const f2 frac = sub2(absr, base);
-      float fr0, fr1, bs0, bs1;
-      un2(frac, fr0, fr1);
-      un2(base, bs0, bs1);
-      float uj[2];
-      if constexpr (HAS_U) {
-        uj[0] = u[j0];
-        uj[1] = u[j1];
-      } else {
-        // u = (h + 0.5) / 65536 for the 16-bit halves h of the Philox word: 2^23 + h is built by a
-        // byte permute, and (2^23 + h) * 2^-16 + (2^-17 - 128) is exact in one FMA
-        const uint32_t wd_ = rw4[pp];
-        un2(fma2(mk2(__int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7610)),
-                     __int_as_float(__byte_perm(wd_, 0x4B000000u, 0x7632))),
-                 splat(1.0f / 65536.0f), splat(1.0f / 131072.0f - 128.0f)),
-            uj[0], uj[1]);
-      }
-      const float rr[2] = {r0, r1}, aa[2] = {a0, a1}, fr[2] = {fr0, fr1}, bs[2] = {bs0, bs1};
-      float dqf[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        // threshold frac(|r|) + tanh(a) * sr_bias * sign(r); tb * sign(r) is tb with its sign
-        // flipped for negative r (r = 0 is handled below: dq = sign(0) * ... = 0)
-        const uint32_t rsign = __float_as_uint(rr[e]) & 0x80000000u;
-        float fb = fr[e];
-        if (p.sr_bias != 0.f) {
-          const float tb = __fmul_rn(tanh_approx(aa[e]), p.sr_bias);
-          fb = __fadd_rn(fr[e], __uint_as_float(__float_as_uint(tb) ^ rsign));
-          // tanh.approx is good to ~5e-4: near the decision use an accurate tanh
-          if (fabsf(__fsub_rn(uj[e], fb)) < 2e-4f) {
-            const float tb2 = __fmul_rn(tanh_accurate(aa[e]), p.sr_bias);
-            fb = __fadd_rn(fr[e], __uint_as_float(__float_as_uint(tb2) ^ rsign));
-          }
-        }
-        // u in (0,1): u < fb is u < clamp(fb, 0, 1); dq = sign(r) * (floor|r| + [u < fb])
-        const bool up = (uj[e] < fb) && (rr[e] != 0.f);
-        dqf[e] = copysignf(up ? __fadd_rn(bs[e], 1.f) : bs[e], rr[e]);
-      }
-      qn[j0] = max(-127, min(127, q0 + rne_int(dqf[0])));
-      qn[j1] = max(-127, min(127, q1 + rne_int(dqf[1])));
-      rn[pp] = sub2(r, mk2(dqf[0], dqf[1]));
-      mn[pp] = m;
-      vn[pp] = v;
-    }
-    // ---------------- block absmax and re-encode (mu-law, fireflyoptim.py:22-67)
-    float xm = 0.f, xv = 0.f, xr = 0.f;
-#pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      float a0, a1;
-      un2(mn[pp], a0, a1);
-      xm = fmaxf(xm, fmaxf(fabsf(a0), fabsf(a1)));
-      un2(vn[pp], a0, a1);
-      xv = fmaxf(xv, fmaxf(fabsf(a0), fabsf(a1)));  // v >= 0; |.| turns -0 into +0
-      un2(rn[pp], a0, a1);
-      xr = fmaxf(xr, fmaxf(fabsf(a0), fabsf(a1)));
-    }
-    xm = fmaxf(warp_max_nonneg(xm), 1e-12f);
-    xv = fmaxf(warp_max_nonneg(xv), 1e-12f);
-    xr = fmaxf(warp_max_nonneg(xr), 1e-12f);
-    const f2 ixm = splat(__frcp_rn(xm)), ixv = splat(__frcp_rn(xv)), ixr = splat(__frcp_rn(xr));
-    const f2 k127 = splat(15.875f), k255 = splat(31.875f);
-    int cm[8], cv[8], cr[8];
-    // |x| / absmax can exceed 1 by an ulp (absmax is the largest |x|); log2(256 + tiny) * 127/8
-    // still rounds to 127 (255 for v), so no clamps are needed.  v is never negative.
-#pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      float x0, x1, y0, y1, z0, z1;
-      un2(mul2(mn[pp], ixm), x0, x1);
-      un2(mul2(rn[pp], ixr), y0, y1);
-      un2(mul2(vn[pp], ixv), z0, z1);
-      // signed m and r: code = 128 + sign(x) * rint(127/8 * log2(1 + 255 |x|/absmax))
-      float lm0, lm1, lr0, lr1, lv0, lv1;
-      un2(mul2(mk2(lg2_approx(__fmaf_rn(255.f, fabsf(x0), 1.f)), lg2_approx(__fmaf_rn(255.f, fabsf(x1), 1.f))), k127),
-          lm0, lm1);
-      un2(mul2(mk2(lg2_approx(__fmaf_rn(255.f, fabsf(y0), 1.f)), lg2_approx(__fmaf_rn(255.f, fabsf(y1), 1.f))), k127),
-          lr0, lr1);
-      // unsigned v: code = rint(255/8 * log2(1 + 255 v/absmax)), +magic folded in
-      un2(fma2(mk2(lg2_approx(__fmaf_rn(255.f, z0, 1.f)), lg2_approx(__fmaf_rn(255.f, z1, 1.f))), k255, magic2),
-          lv0, lv1);
-      // rounding with +128 folded into the magic add
-      float s0, s1;
-      // the magic-number words themselves: their low byte is the code (0x4B400000 + c, 0 <= c < 256)
-      un2(add2(mk2(copysignf(lm0, x0), copysignf(lm1, x1)), splat(kMagic + 128.f)), s0, s1);
-      cm[2 * pp] = __float_as_int(s0);
-      cm[2 * pp + 1] = __float_as_int(s1);
-      un2(add2(mk2(copysignf(lr0, y0), copysignf(lr1, y1)), splat(kMagic + 128.f)), s0, s1);
-      cr[2 * pp] = __float_as_int(s0);
-      cr[2 * pp + 1] = __float_as_int(s1);
-      cv[2 * pp] = __float_as_int(lv0);
-      cv[2 * pp + 1] = __float_as_int(lv1);
-    }
-    if (nvalid == 8) {
-      // generic-proxy stores; the bulk copies only ever read other blocks
-      *reinterpret_cast<uint2*>(p.q + e0) = make_uint2(pack_codes(qn, 0), pack_codes(qn, 4));
-      *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(pack_codes(cm, 0), pack_codes(cm, 4));
-      *reinterpret_cast<uint2*>(p.v_q + e0) = make_uint2(pack_codes(cv, 0), pack_codes(cv, 4));
-      *reinterpret_cast<uint2*>(p.r_q + e0) = make_uint2(pack_codes(cr, 0), pack_codes(cr, 4));
-    } else {
-      for (int j = 0; j < nvalid; ++j) {
-        p.q[e0 + j] = (int8_t)qn[j];
-        p.m_q[e0 + j] = (uint8_t)cm[j];
-        p.v_q[e0 + j] = (uint8_t)cv[j];
-        p.r_q[e0 + j] = (uint8_t)cr[j];
-      }
-    }
-    if (lane == 0) {
-      p.m_absmax[blk] = xm;
-      p.v_absmax[blk] = xv;
-      p.r_absmax[blk] = xr;
-    }
-    row += p.row_step;
-    in_row += p.in_row_step;
-    if (in_row >= p.row_len) {
-      in_row -= p.row_len;
-      ++row;
+    process(blk, gw, qw, mw, vw, rw, u, wsa, wsb, jsw, __ldg(p.m_absmax + blk), __ldg(p.v_absmax + blk),
+            __ldg(p.r_absmax + blk), nvalid);
+  }
+}
+
+template <bool HAS_U, int ROWS>
+__global__ void __launch_bounds__(kThreads, HAS_U ? 1 : kCtasPerSm) dqt_adamw8_kernel(Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];  // decode rows, then staging, then barriers
+  constexpr int kStage = stage_bytes(HAS_U);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // decode rows: word 64*c + l = signed entry of code c, word 64*c + 32 + l = unsigned entry
+  {
+    float* tw = reinterpret_cast<float*>(smem);
+    for (int i = threadIdx.x; i < kTabBytes / 4; i += kThreads) {
+      const int c = i >> 6;
+      tw[i] = (i & 32) ? __ldg(p.dec_u + c) : __ldg(p.dec_s + c);
     }
   }
+  if (lane == 0) {
+    const uint32_t bar0 = smem_addr(smem + kTabBytes + kWarps * 2 * kStage) + warp * 16;
+    bar_init(bar0);
+    bar_init(bar0 + 8);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint32_t base = smem_addr(smem);
+  if (base == 0)
+    dqt_run<HAS_U, ROWS, 0>(p, smem);
+  else if (base == 1024)
+    dqt_run<HAS_U, ROWS, 1024>(p, smem);
+  else
+    dqt_run<HAS_U, ROWS, -1>(p, smem);
 }
 
 }  // namespace optim
@@ -551,6 +729,16 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   p.seed_hi = (uint32_t)(seed >> 32);
   p.step_lo = (uint32_t)step;
   p.step_hi = (uint32_t)(step >> 32);
+  for (int r = 0; r < 10; ++r) {  // Philox4x32-10 key schedule (Weyl increments)
+    p.key0[r] = p.seed_lo + (uint32_t)r * 0x9E3779B9u;
+    p.key1[r] = p.seed_hi + (uint32_t)r * 0xBB67AE85u;
+  }
+  {
+    const uint64_t prod = (uint64_t)0xCD9E8D57u * (uint64_t)p.step_lo;
+    p.r1_hi = (uint32_t)(prod >> 32);
+    p.r1_lo = (uint32_t)prod;
+    p.r1_c3k = p.step_hi ^ p.key1[0];
+  }
   p.rng_offset = rng_offset;
   p.u = u;
   p.dec_s = dec_s;
@@ -560,11 +748,15 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   cudaGetDevice(&dev);
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    const void* fns[] = {(const void*)dqt_adamw8_kernel<true, 0>, (const void*)dqt_adamw8_kernel<true, 1>,
-                         (const void*)dqt_adamw8_kernel<true, 2>, (const void*)dqt_adamw8_kernel<false, 0>,
-                         (const void*)dqt_adamw8_kernel<false, 1>, (const void*)dqt_adamw8_kernel<false, 2>};
+    const void* fns_u[] = {(const void*)dqt_adamw8_kernel<true, 0>, (const void*)dqt_adamw8_kernel<true, 1>,
+                           (const void*)dqt_adamw8_kernel<true, 2>};
+    const void* fns[] = {(const void*)dqt_adamw8_kernel<false, 0>, (const void*)dqt_adamw8_kernel<false, 1>,
+                         (const void*)dqt_adamw8_kernel<false, 2>};
+    for (const void* fn : fns_u)
+      FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(true)),
+                  "ff_dqt_adamw8 smem attribute");
     for (const void* fn : fns)
-      FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+      FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(false)),
                   "ff_dqt_adamw8 smem attribute");
     attr_set[dev] = true;
   }
@@ -572,14 +764,14 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   int nsm = 148;
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (nblocks + kWarps - 1) / kWarps;
-  const int grid = (int)min64(want, (int64_t)nsm * 3);
+  const int grid = (int)min64(want, (int64_t)nsm * (u ? 1 : kCtasPerSm));
   const int64_t stride_elems = (int64_t)grid * kWarps * kBlock;
   p.row_step = stride_elems / row_len;
   p.in_row_step = stride_elems % row_len;
   cudaStream_t st = as_stream(stream);
   // a lane's 8 elements start at a multiple of 8 of the weight when elem_base is one
   const int rows_mode = (row_len % 8 == 0 && elem_base % 8 == 0) ? 0 : (row_len >= 8 ? 1 : 2);
-#define FF_DQT_LAUNCH(HU, RM) dqt_adamw8_kernel<HU, RM><<<grid, kThreads, kSmemBytes, st>>>(p)
+#define FF_DQT_LAUNCH(HU, RM) dqt_adamw8_kernel<HU, RM><<<grid, kThreads, smem_bytes(HU), st>>>(p)
   if (u) {
     if (rows_mode == 0) FF_DQT_LAUNCH(true, 0);
     else if (rows_mode == 1) FF_DQT_LAUNCH(true, 1);
