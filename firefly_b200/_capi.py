@@ -63,6 +63,9 @@ SIGNATURES = {
                                     _I64, _P, _P, _P]),
     "ff_transpose_i8": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P]),
     "ff_gemm_i8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
+    "ff_gemm_i8_ws_bytes": (_I64, [_I64, _I64, _I64]),
+    "ff_set_wait_limit_ns": (_I, [_U64]),
+    "ff_gemm_i8_ws": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P, _I64, _P]),
     "ff_gemm_i8_kn": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "ff_colsum_ws_elems": (_I64, [_I64, _I64]),
     "ff_colsum_bf16": (_I, [_P, _I64, _I64, _I64, _P, _P, _P]),
@@ -86,7 +89,7 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_swiglu_gemm_i8": 2, "ff_swiglu_bwd_gemm_i8": 2,
                      "ff_gelu_eval": 1, "ff_gelu_gemm_i8": 2, "ff_gelu_bwd_gemm_i8": 2,
                      "ff_layernorm_i8": 2, "ff_layernorm_bwd": 3,
-                     "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1,
+                     "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1, "ff_gemm_i8_ws": 1,
                      "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1,
                      "ff_adamw8_blockwise": 1}
 
@@ -187,11 +190,28 @@ def num_sms(device: torch.device | None = None) -> int:
 
 
 def device_status(device: torch.device | int | None = None, clear: bool = True) -> int:
-    """Read (and by default clear) the device status word; synchronises the device."""
+    """Read (and by default clear) the device status word; synchronises the device.  A nonzero
+    status also drops the split-K workspaces (an aborted GEMM may have left partial sums)."""
     out = ctypes.c_uint32(0)
     with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
         _call("ff_device_status", ctypes.byref(out), int(clear))
+    if out.value:
+        _SPLITK_WS.clear()
     return out.value
+
+
+# Split-K workspaces of the skinny GEMMs, per (device, stream): zero-filled once, and left
+# all zeros by every ff_gemm_i8_ws call, so calls on one stream can share one.
+_SPLITK_WS: dict = {}
+
+
+def _splitk_ws(dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _SPLITK_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros((max(nbytes, 1 << 20) + 15) // 16 * 16, dtype=torch.uint8, device=dev)
+        _SPLITK_WS[key] = ws
+    return ws
 
 
 def quant_rows(x: torch.Tensor, colmul: torch.Tensor | None = None, eps: float = 1e-8,
@@ -665,8 +685,14 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, k: int, scale_a: torch.Tensor | No
         if GEMM_EVENTS is not None and M > 0 and N > 0:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        _call(fn, _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
-              ldd, int(out_kind), M, N, int(k), _stream(dev))
+        need = int(lib().ff_gemm_i8_ws_bytes(M, N, int(k))) if fn == "ff_gemm_i8" and M > 0 and N > 0 else 0
+        if need > 0:  # skinny A: stream-K over all SMs with a split-K workspace
+            ws = _splitk_ws(dev, need)
+            _call("ff_gemm_i8_ws", _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
+                  ldd, int(out_kind), M, N, int(k), _ptr(ws), ws.numel(), _stream(dev))
+        else:
+            _call(fn, _ptr(a), lda, _ptr(b), ldb, _ptr(sa), _ptr(sb), _ptr(bb), _ptr(out),
+                  ldd, int(out_kind), M, N, int(k), _stream(dev))
         if ev is not None:
             ev[1].record()
             byts = M * int(k) + N * int(k) + M * N * out.element_size() * (2 if out_kind == FF_OUT_BF16_ACCUM else 1)

@@ -77,6 +77,13 @@ __device__ __forceinline__ void raise_status(uint32_t bits) { atomicOr(&g_status
 // ---------------------------------------------------------------------------
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: no legitimate wait here comes close
 
+// Limit of the in-kernel waits on another unit's progress (mbarrier phases of TMA copies, MMAs,
+// epilogues): kWaitLimitNs unless ff_set_wait_limit_ns lowered it, which a test does to make a
+// wait run out.  The drains after an abort keep the fixed kWaitLimitNs, so in-flight copies and
+// MMAs always finish before a CTA exits.
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns); }
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -110,9 +110,9 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
 // time-bounded wait; false (and FF_DEVICE_TIMEOUT raised) if the copies never landed
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
   if (bar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
   while (!bar_try(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       raise_status(FF_DEVICE_TIMEOUT);
       return false;
     }

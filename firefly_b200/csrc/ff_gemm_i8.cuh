@@ -154,11 +154,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort_flag = 1;
       raise_status(FF_DEVICE_TIMEOUT);
       return false;
@@ -1350,6 +1350,14 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
   }
 }
 
+}  // namespace gemm
+}  // namespace ff
+
+#include "ff_gemm_skinny.cuh"
+
+namespace ff {
+namespace gemm {
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1487,10 +1495,13 @@ inline int max_pairs_current() {
 }
 
 // One GEMM, any layout of B: BMN == false -> B is N x K (ldb), BMN == true -> B is K x N (ldb).
+// Skinny problems (M <= 128, K-major B) given a workspace of at least skinny_ws_bytes(M, N) bytes
+// take the stream-K kernel of ff_gemm_skinny.cuh.
 template <bool BMN>
 inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
                          const float* scale_a, const float* scale_b, const float* bias, void* D, int64_t ldd,
-                         int out_kind, int64_t M, int64_t N, int64_t K, void* stream) {
+                         int out_kind, int64_t M, int64_t N, int64_t K, void* stream, void* ws = nullptr,
+                         int64_t ws_bytes = 0) {
   FF_REQUIRE(M >= 0 && N >= 0 && K >= 1, FF_ERR_INVALID_ARG, "%s: M=%lld N=%lld K=%lld", name, (long long)M,
              (long long)N, (long long)K);
   FF_REQUIRE(out_kind >= FF_OUT_S32 && out_kind <= FF_OUT_BF16_ACCUM, FF_ERR_INVALID_ARG, "%s: bad out_kind %d", name,
@@ -1519,6 +1530,30 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
   ep.M = M;
   ep.N = N;
   ep.vec = aligned(D, 16) && ((ldd * es) % 16 == 0);
+  if constexpr (!BMN) {
+    if (ws && M <= 128) {
+      const int mp = sk_mp(M);
+      const int64_t tiles = (N + SK_BN - 1) / SK_BN;
+      FF_REQUIRE(ws_bytes >= sk_ws_bytes(tiles, mp) && aligned(ws, 16), FF_ERR_INVALID_ARG,
+                 "%s: workspace of %lld bytes (16-byte aligned) needed, got %lld", name,
+                 (long long)sk_ws_bytes(tiles, mp), (long long)ws_bytes);
+      rc = make_map(&mb, B, N, K, ldb, SK_BN);
+      if (rc) return rc;
+      CUtensorMap mas;
+      rc = make_map(&mas, A, M, K, lda, mp);
+      if (rc) return rc;
+      const int64_t total = tiles * ((K + BK - 1) / BK);
+      const int grid = (int)min64((int64_t)num_sms_current(), max64(1, total / 2));
+      int32_t* part = static_cast<int32_t*>(ws);
+      uint32_t* cnt = reinterpret_cast<uint32_t*>(part + tiles * mp * SK_BN);
+      switch (out_kind) {
+        case FF_OUT_S32: return launch_skinny_mp<FF_OUT_S32>(mp, mas, mb, K, (int)tiles, ep, grid, part, cnt, st);
+        case FF_OUT_F32: return launch_skinny_mp<FF_OUT_F32>(mp, mas, mb, K, (int)tiles, ep, grid, part, cnt, st);
+        case FF_OUT_BF16: return launch_skinny_mp<FF_OUT_BF16>(mp, mas, mb, K, (int)tiles, ep, grid, part, cnt, st);
+        default: return launch_skinny_mp<FF_OUT_BF16_ACCUM>(mp, mas, mb, K, (int)tiles, ep, grid, part, cnt, st);
+      }
+    }
+  }
   // Tile configuration by a small cost model: waves x work per SM per tile / relative
   // efficiency, for 256 x 256 tiles on CTA pairs (cta_group::2), 128 x 256 tiles and
   // 128 x 64 tiles (the narrow tiles spread small and skinny problems over the SMs; not
@@ -1596,6 +1631,18 @@ extern "C" int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t
                           int64_t N, int64_t K, void* stream) {
   return ff::gemm::gemm_dispatch<false>("ff_gemm_i8", A, lda, B, ldb, scale_a, scale_b, bias, D, ldd, out_kind, M, N,
                                         K, stream);
+}
+
+extern "C" int64_t ff_gemm_i8_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || M > 128 || N < 1 || K < 1) return 0;
+  return ff::gemm::sk_ws_bytes((N + ff::gemm::SK_BN - 1) / ff::gemm::SK_BN, ff::gemm::sk_mp(M));
+}
+
+extern "C" int ff_gemm_i8_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,
+                             const float* scale_b, const float* bias, void* D, int64_t ldd, int out_kind, int64_t M,
+                             int64_t N, int64_t K, void* ws, int64_t ws_bytes, void* stream) {
+  return ff::gemm::gemm_dispatch<false>("ff_gemm_i8_ws", A, lda, B, ldb, scale_a, scale_b, bias, D, ldd, out_kind, M,
+                                        N, K, stream, ws, ws_bytes);
 }
 
 extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, const float* scale_a,

@@ -37,6 +37,12 @@ extern "C" int ff_device_status(uint32_t* out, int clear) {
   return FF_OK;
 }
 
+extern "C" int ff_set_wait_limit_ns(uint64_t ns) {
+  const uint64_t v = ns ? ns : ff::kWaitLimitNs;
+  FF_CUDA_TRY(cudaMemcpyToSymbol(ff::g_wait_limit_ns, &v, sizeof(v)), "ff_set_wait_limit_ns");
+  return FF_OK;
+}
+
 // ---------------------------------------------------------------------------
 // ff_quant_dual_i8_noalloc: ff_quant_dual_i8 with its absmax workspace in a
 // static device array of this library instead of caller-provided memory.

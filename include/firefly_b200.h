@@ -100,6 +100,15 @@ FF_API int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t cols
                      int8_t* q_cols_t, int64_t ldqt, float* s_cols,
                      float* absmax_ws, void* stream);
 
+/*
+ * Test hook for the failure path (no counterpart in the reference, which has no device code):
+ * sets the limit, in nanoseconds, of the in-kernel waits of later launches on the current
+ * device (0 restores the default of 2 s).  A wait that runs out sets FF_DEVICE_TIMEOUT in
+ * the device status word, the kernel drains its in-flight copies and MMAs and returns, and
+ * the context stays usable.  Synchronous; for tests only.
+ */
+FF_API int ff_set_wait_limit_ns(uint64_t ns);
+
 /* Largest rows + cols that ff_quant_dual_i8_noalloc accepts (its scratch: 1 MiB of fp32). */
 #define FF_NOALLOC_DUAL_MAX_ELEMS 262144
 
@@ -326,6 +335,28 @@ FF_API int ff_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb
                const float* scale_a, const float* scale_b, const float* bias,
                void* D, int64_t ldd, int out_kind, int64_t M, int64_t N, int64_t K,
                void* stream);
+
+/*
+ * Bytes of the split-K workspace that ff_gemm_i8_ws uses for an M x N x K problem, or 0
+ * when that shape takes no workspace (M > 128).  No counterpart in the reference (its
+ * GEMM went through bitsandbytes / cuBLASLt, fireflykernels.py:132-156, :164-176).
+ */
+FF_API int64_t ff_gemm_i8_ws_bytes(int64_t M, int64_t N, int64_t K);
+
+/*
+ * ff_gemm_i8 (same arguments and results, bit for bit) with a split-K workspace for skinny
+ * problems (M <= 128 rows of A, which are a stream over B): the k-range of every 128-row tile
+ * of B is divided over all SMs (stream-K) and the int32 partial sums are added in the
+ * workspace, the last contributor of a tile applying the epilogue.  ws: at least
+ * ff_gemm_i8_ws_bytes(M, N, K) bytes, 16-byte aligned, all zeros before the first call; every
+ * call leaves it all zeros again (after a device timeout, FF_DEVICE_TIMEOUT, zero it before
+ * reuse).  Calls that share a workspace must be ordered on one stream.  With M > 128 the
+ * workspace is not used and the call is ff_gemm_i8.
+ */
+FF_API int ff_gemm_i8_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                  const float* scale_a, const float* scale_b, const float* bias,
+                  void* D, int64_t ldd, int out_kind, int64_t M, int64_t N, int64_t K,
+                  void* ws, int64_t ws_bytes, void* stream);
 
 /*
  * ff_gemm_i8 with B given as a K x N row-major matrix (N contiguous, leading dim ldb >= N,

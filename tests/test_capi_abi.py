@@ -71,3 +71,13 @@ def test_noalloc_size_limit_checked_on_the_host_without_overflow():
                                           None, 16, None, None, 16, None, None)
         assert rc == _capi.FF_ERR_UNSUPPORTED, (rows, cols)
         assert b"exceeds the built-in scratch" in lib.ff_last_error()
+
+
+def test_gemm_workspace_size_and_argument_checks():
+    """The split-K workspace size (no GPU needed), and the host-side refusal of a short one."""
+    lib = _capi.lib()
+    assert lib.ff_gemm_i8_ws_bytes(129, 8192, 8192) == 0
+    assert lib.ff_gemm_i8_ws_bytes(0, 8192, 8192) == 0
+    assert lib.ff_gemm_i8_ws_bytes(16, 8192, 8192) == 64 * 16 * 128 * 4 + 64 * 4
+    assert lib.ff_gemm_i8_ws_bytes(128, 100, 64) == 1 * 128 * 128 * 4 + 4
+    assert lib.ff_gemm_i8_ws_bytes(17, 8192, 64) == 64 * 32 * 128 * 4 + 64 * 4

@@ -149,3 +149,40 @@ def test_gemm_kn_layout_bit_exact(M, N, K):
     d16 = _capi.gemm_i8(a.to(DEV), b.to(DEV), K, sa.to(DEV), out_kind=_capi.FF_OUT_BF16, b_kn_cols=N)
     np.testing.assert_array_equal(bf16_bits(d16), O.f32_to_bf16_bits(O.dequant(acc, sa.numpy())))
     assert _capi.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 8192, 8192), (128, 8192, 8192), (33, 1000, 3000), (100, 130, 640),
+                                   (64, 256, 128)])
+def test_skinny_split_k_equals_oracle_and_leaves_workspace_zero(M, N, K):
+    """Skinny A (M <= 128) runs stream-K with a split-K workspace: int32 results bit-exact, the
+    scaled epilogues identical to the unsplit kernel (ff_gemm_i8 without a workspace), and the
+    workspace all zeros again after every call, so a second call gives the same results."""
+    import ctypes
+
+    a, b, sa, sb, bias = _operands(M, N, K, seed=7 * M + N)
+    ad, bd = a.to(DEV), b.to(DEV)
+    lib = _capi.lib()
+    need = lib.ff_gemm_i8_ws_bytes(M, N, K)
+    assert need == -(-N // 128) * (16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128) * 128 * 4 \
+        + -(-N // 128) * 4
+    ws = torch.zeros(need + 16, dtype=torch.uint8, device=DEV)
+    want = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
+    lda = a.shape[1]
+    for kind in (_capi.FF_OUT_S32, _capi.FF_OUT_F32, _capi.FF_OUT_BF16):
+        odt = {_capi.FF_OUT_S32: torch.int32, _capi.FF_OUT_F32: torch.float32, _capi.FF_OUT_BF16: torch.bfloat16}[kind]
+        ref = torch.empty(M, N, dtype=odt, device=DEV)
+        sa_d, sb_d, bias_d = sa.to(DEV), sb.to(DEV), bias.to(DEV)
+        args = (ctypes.c_void_p(ad.data_ptr()), lda, ctypes.c_void_p(bd.data_ptr()), lda,
+                ctypes.c_void_p(sa_d.data_ptr()), ctypes.c_void_p(sb_d.data_ptr()), ctypes.c_void_p(bias_d.data_ptr()))
+        assert lib.ff_gemm_i8(*args, ctypes.c_void_p(ref.data_ptr()), N, kind, M, N, K, None) == 0
+        for _ in range(2):
+            got = torch.full((M, N), 7, dtype=odt, device=DEV)
+            rc = lib.ff_gemm_i8_ws(*args, ctypes.c_void_p(got.data_ptr()), N, kind, M, N, K,
+                                   ctypes.c_void_p(ws.data_ptr()), need, None)
+            assert rc == 0, lib.ff_last_error()
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), kind
+            assert int(ws.count_nonzero()) == 0
+        if kind == _capi.FF_OUT_S32:
+            np.testing.assert_array_equal(got.cpu().numpy().astype(np.int64), want)
+    assert _capi.device_status() == 0
