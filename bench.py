@@ -417,7 +417,16 @@ def gemm_sweep(dev):
 
     from firefly_b200 import _capi
 
+    # L2 flush between timed launches: write a buffer twice the size of L2, then read another one,
+    # so that L2 holds only clean lines of unrelated data (no write-back of the flush's own dirty
+    # lines lands on the timed kernel)
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    clean_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+
+    def l2_flush():
+        flush_buf.zero_()
+        clean_buf.sum()
+
     res = []
     shapes = [(n, n, n) for n in (1024, 2048, 4096, 8192)] + [(16, 8192, 8192), (128, 8192, 8192)]
     for M, N, K in shapes:
@@ -428,7 +437,7 @@ def gemm_sweep(dev):
         sb = torch.empty(N, device=dev).uniform_(1e-3, 1e-2)
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         t = _time_cuda(lambda: _capi.gemm_i8(a, b, K, sa, sb, out_kind=_capi.FF_OUT_BF16, out=out), 10,
-                       flush=lambda: flush_buf.zero_())
+                       flush=l2_flush)
         ops = 2 * M * N * K
         byts = M * K + N * K + 2 * M * N + 4 * (M + N)
         res.append({"M": M, "N": N, "K": K, "us": round(t * 1e6, 2), "tops": round(ops / t / 1e12, 1),
@@ -438,14 +447,14 @@ def gemm_sweep(dev):
         try:
             bt = b.t()
             if M >= 17:
-                tl = _time_cuda(lambda: torch._int_mm(a, bt), 10, flush=lambda: flush_buf.zero_())
+                tl = _time_cuda(lambda: torch._int_mm(a, bt), 10, flush=l2_flush)
                 res[-1]["comparator"] = "cuBLASLt int8 via torch._int_mm (substitute for bitsandbytes igemmlt)"
                 res[-1]["torch_int_mm_us"] = round(tl * 1e6, 2)
                 res[-1]["torch_int_mm_tops"] = round(ops / tl / 1e12, 1)
         except Exception as e:  # noqa: BLE001
             res[-1]["torch_int_mm"] = f"unavailable: {type(e).__name__}"
         del a, b, out
-    del flush_buf
+    del flush_buf, clean_buf
     torch.cuda.empty_cache()
     return res
 
