@@ -73,7 +73,8 @@ def parse_args():
                     help="ZeRO-1 gradient bucket size (MB of bf16); 0 = one bucket")
     ap.add_argument("--zero-overlap", type=int, choices=[0, 1], default=1,
                     help="start each bucket's reduce-scatter from the backward pass")
-    ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "gemm_skinny128", "gemm2048", "adamw",
+    ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "gemm_skinny128", "gemm2048", "gemm4096",
+                                              "gemm_narrow", "adamw",
                                               "quant", "quant_rows", "swiglu", "swiglu_bwd", "swiglu_gemm",
                                               "swiglu_bwd_gemm", "gelu_gemm", "gelu_bwd_gemm", "layernorm",
                                               "colsum", "dense_adamw", "mlp", "decoder4"],
@@ -91,8 +92,10 @@ def kernel_case(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     if args.kernel_case.startswith("gemm"):
+        # gemm_narrow: 128 x 64 tiles on one CTA each (the shape spreads best over the SMs that way)
         M, N, K = {"gemm8192": (8192, 8192, 8192), "gemm_skinny16": (16, 8192, 8192),
-                   "gemm_skinny128": (128, 8192, 8192), "gemm2048": (2048, 2048, 2048)}[args.kernel_case]
+                   "gemm_skinny128": (128, 8192, 8192), "gemm2048": (2048, 2048, 2048),
+                   "gemm4096": (4096, 4096, 4096), "gemm_narrow": (4096, 512, 4096)}[args.kernel_case]
         a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
         b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
         sa, sb = torch.rand(M, device=dev) * 1e-2, torch.rand(N, device=dev) * 1e-2
