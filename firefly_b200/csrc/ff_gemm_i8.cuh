@@ -957,8 +957,8 @@ constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 256 + 8 
 // GELU: 4 stages, the SwiGLU layout's buffers, then the table of gelu (bf16) or gelu' (fp32)
 constexpr int C2_SMEM_BYTES_GELU = C2_STAGES_GELU * C2_STAGE_BYTES + 1024 + 512 + 8 * 2 * C2_SW_BUF_FLOATS * 4 +
                                    8 * 2 * 2048 + kGeluTabEntries * 4;
-// bf16 output: per epilogue warp two 32 x 32 bf16 staging buffers for the TMA stores
-constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 4 * 2 * 2048;
+// bf16 output: per epilogue warp (8) two 32 x 32 bf16 staging buffers for the TMA stores
+constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 8 * 2 * 2048;
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
   return is_gelu(OUT) ? C2_STAGES_GELU : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
@@ -968,11 +968,11 @@ __host__ __device__ constexpr int c2_smem_bytes() {
   return is_gelu(OUT) ? C2_SMEM_BYTES_GELU
                       : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
 }
-// threads of the 2-CTA kernel: TMA warp, MMA warp, then 4 epilogue warps (8 for the SwiGLU
-// epilogue: two per TMEM lane quarter, each on half of the tile's features)
+// threads of the 2-CTA kernel: TMA warp, MMA warp, then 8 epilogue warps (two per TMEM lane
+// quarter, each on half of the tile's columns), so a tile's epilogue takes half as long
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return is_fused_act(OUT) ? 320 : NUM_THREADS;
+  return 320;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -1027,7 +1027,8 @@ template <int OUT, bool BMN>
 __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     gemm_i8_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmH, int64_t K,
-                        int tiles_m, int tiles_n, EpiParams ep) {
+                        int tiles_m, int tiles_n, EpiParams ep, const __grid_constant__ CUtensorMap tmB2,
+                        int split) {
   constexpr int NST = c2_stages<OUT>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1054,6 +1055,28 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
   const int num_kb = (int)((K + BK - 1) / BK);
   const int total_tiles = tiles_m * tiles_n;
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  // This pair's j-th tile: with `split` (plain epilogues, K-major B, a last wave at most half
+  // full) the tiles of the last partial wave are cut into 256 x 128 halves, one per pair, so
+  // that wave takes half the time; otherwise tile pair + j * num_pairs.  half = -1: whole tile.
+  const int full_waves = split ? total_tiles / num_pairs : 0;
+  const int rest = total_tiles - full_waves * num_pairs;
+  auto item = [&](int j, int& tm, int& tn, int& half) -> bool {
+    int t;
+    half = -1;
+    if (!split) {
+      t = pair + j * num_pairs;
+      if (t >= total_tiles) return false;
+    } else if (j < full_waves) {
+      t = pair + j * num_pairs;
+    } else if (j == full_waves && pair < 2 * rest) {
+      t = full_waves * num_pairs + (pair >> 1);
+      half = pair & 1;
+    } else {
+      return false;
+    }
+    tile_coords(t, tiles_m, tiles_n, tm, tn);
+    return true;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -1098,18 +1121,21 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
-        int tm, tn;
-        tile_coords(t, tiles_m, tiles_n, tm, tn);
+      int tm, tn, half;
+      for (int j = 0; ok && item(j, tm, tn, half); ++j) {
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
           const uint32_t lbar = mapa_shared(full_bar(stage), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C2_STAGE_BYTES);
+          if (rank == 0)
+            mbar_arrive_expect_tx(full_bar(stage), half < 0 ? 2 * C2_STAGE_BYTES : 2 * (C2_A_BYTES + C2_B_BYTES / 2));
           tma_load_2d_pair(sA + stage * C2_A_BYTES, &tmA, kb * BK, tm * (2 * C2_BM) + (int)rank * C2_BM, lbar);
-          if constexpr (OUT == kOutSwigluFwd) {  // gate rows of the tile's features, then the up rows
+          if (half >= 0) {  // this CTA's 64 rows of the half tile's 128 columns
+            tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB2, kb * BK,
+                             tn * C2_BN + half * (C2_BN / 2) + (int)rank * (C2_BN_CTA / 2), lbar);
+          } else if constexpr (OUT == kOutSwigluFwd) {  // gate rows of the tile's features, then the up rows
             tma_load_2d_pair(sB + stage * C2_B_BYTES, &tmB, kb * BK,
                              tn * kSwigluFeat + (rank ? (int)ep.F : 0), lbar);
           } else if constexpr (!BMN) {
@@ -1134,7 +1160,9 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
+      constexpr uint32_t idesc_half = idesc_i8(2 * C2_BM, C2_BN / 2);
+      int tm_, tn_, half;
+      for (int j = 0; ok && item(j, tm_, tn_, half); ++j) {
         if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C2_BN);
@@ -1149,7 +1177,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           for (int k = 0; k < BK / UMMA_K; ++k) {
             const uint64_t bdesc = BMN ? smem_desc_mn_sw128(b0 + k * UMMA_K * 128, 128 * BK)
                                        : smem_desc_k_sw128(b0 + k * UMMA_K);
-            tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), bdesc, idesc, (kb | k) != 0);
+            tc_mma_i8_pair(d_tmem, smem_desc_k_sw128(a0 + k * UMMA_K), bdesc, half < 0 ? idesc : idesc_half,
+                           (kb | k) != 0);
           }
           tc_commit_pair(empty_bar(stage));  // frees the stage in both CTAs
           if (++stage == NST) {
@@ -1184,9 +1213,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     uint8_t* st_stage = ctrl + st_off + (warp - 2) * 2 * 2048;
     const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
-    for (int t = pair; t < total_tiles; t += num_pairs) {
-      int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, tm, tn);
+    int tm, tn, half;
+    for (int j = 0; item(j, tm, tn, half); ++j) {
       float4 st_s, st_b;  // loaded before the accumulator wait, stored after it
       uint4 pg[4], pu[4];  // SwiGLU backward: g and u of the next chunk, loaded ahead
       if constexpr (OUT == kOutSwigluBwd) {
@@ -1305,21 +1333,23 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         }
         if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
       } else {
-        const int64_t ncol_tile = min64(C2_BN, ep.N - (int64_t)tn * C2_BN);
+        const int64_t col0 = (int64_t)tn * C2_BN + (half < 0 ? 0 : half * (C2_BN / 2));
+        const int64_t ncol_tile = min64(half < 0 ? C2_BN : C2_BN / 2, ep.N - col0);
+        // this warp's half of the tile's 32-column chunks
+        const int nchunk = (half < 0 ? C2_BN : C2_BN / 2) / 64;
 #pragma unroll 1
-        for (int c = 0; c < C2_BN / 32; ++c) {
+        for (int c = eh * nchunk; c < (eh + 1) * nchunk; ++c) {
           if ((int64_t)c * 32 >= ncol_tile) break;
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tmem_wait_ld();
           if constexpr (OUT == FF_OUT_BF16) {
             if (ep.tma_store) {
-              epilogue_chunk_tma(r, (int64_t)tn * C2_BN + c * 32, row - lane, ep, &tmD, sa, lane, st_stage,
-                                 st_stage_addr, st_count);
+              epilogue_chunk_tma(r, col0 + c * 32, row - lane, ep, &tmD, sa, lane, st_stage, st_stage_addr, st_count);
               continue;
             }
           }
-          epilogue_chunk<OUT>(r, row, (int64_t)tn * C2_BN + c * 32, ep, sa, lane);
+          epilogue_chunk<OUT>(r, row, col0 + c * 32, ep, sa, lane);
         }
       }
       tc_fence_before();
@@ -1437,7 +1467,8 @@ constexpr int NARROW_STAGES = 8;
 
 template <int OUT, bool BMN>
 inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mh,
-                       int64_t K, int tiles_m, int tiles_n, const EpiParams& ep, int max_pairs, cudaStream_t st) {
+                       int64_t K, int tiles_m, int tiles_n, const EpiParams& ep, int max_pairs, cudaStream_t st,
+                       const CUtensorMap* mb2 = nullptr) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1460,7 +1491,12 @@ inline int launch_2cta(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, md, mh, K, tiles_m, tiles_n, ep),
+  // the last wave of tiles cut into halves when it is at most half full (plain epilogues, K-major B)
+  const int total = tiles_m * tiles_n, rest = total % pairs;
+  const int split = (mb2 != nullptr && !BMN && OUT <= FF_OUT_BF16_ACCUM && total > pairs && rest > 0 &&
+                     2 * rest <= pairs) ? 1 : 0;
+  FF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_i8_2cta_kernel<OUT, BMN>, ma, mb, md, mh, K, tiles_m, tiles_n, ep,
+                                 mb2 ? *mb2 : mb, split),
               "ff_gemm_i8 2-CTA launch");
   return check_launch("ff_gemm_i8 (2-CTA)");
 }
@@ -1475,7 +1511,7 @@ inline int max_pairs_current() {
                          c2_smem_bytes<FF_OUT_BF16>());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
-    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.blockDim = dim3(c2_threads<FF_OUT_BF16>());
     cfg.dynamicSmemBytes = c2_smem_bytes<FF_OUT_BF16>();
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1564,7 +1600,14 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
   const int64_t wide_tiles = tm64 * tn64;
   const int64_t narrow_tiles = tm64 * ((N + 63) / 64);
   auto waves = [](int64_t tiles, int64_t slots) { return (double)((tiles + slots - 1) / slots); };
-  const double cost_pair = max_pairs > 0 ? waves(pair_tiles, max_pairs) * 4.0 : 1e300;
+  // pair tiles: a last wave at most half full is cut into half-width tiles (plain epilogues, K-major
+  // B), so it costs half a wave
+  auto pair_waves = [&]() {
+    const int64_t full = pair_tiles / max_pairs, rest = pair_tiles % max_pairs;
+    if (!BMN && full > 0 && rest > 0 && 2 * rest <= max_pairs) return (double)full + 0.5;
+    return waves(pair_tiles, max_pairs);
+  };
+  const double cost_pair = max_pairs > 0 ? pair_waves() * 4.0 : 1e300;
   const double cost_wide = waves(wide_tiles, nsm) * 4.0 / 0.9;
   const double cost_narrow = BMN ? 1e300 : waves(narrow_tiles, nsm) * 1.0 / 0.6;
   // B maps: K-major boxes are (128 K bytes) x (rows of N); MN-major boxes are (128 N bytes) x (128 K rows)
@@ -1582,11 +1625,19 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
       if (rc) return rc;
       ep.tma_store = 1;
     }
+    CUtensorMap mb2;  // 64-row boxes of B for the half-width tiles of a short last wave
+    const CUtensorMap* pmb2 = nullptr;
+    if constexpr (!BMN) {
+      rc = make_map(&mb2, B, N, K, ldb, C2_BN_CTA / 2);
+      if (rc) return rc;
+      pmb2 = &mb2;
+    }
     switch (out_kind) {
-      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
-      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
-      default: return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+      case FF_OUT_S32: return launch_2cta<FF_OUT_S32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st, pmb2);
+      case FF_OUT_F32: return launch_2cta<FF_OUT_F32, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st, pmb2);
+      case FF_OUT_BF16: return launch_2cta<FF_OUT_BF16, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st, pmb2);
+      default:
+        return launch_2cta<FF_OUT_BF16_ACCUM, BMN>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st, pmb2);
     }
   }
   if (cost_wide <= cost_narrow) {  // 128 x 256 tiles, one CTA each

@@ -44,6 +44,8 @@ SHAPES = [
     (2600, 2600, 1000),   # 256 x 256 tiles on CTA pairs, ragged M, N and K
     (16, 8192, 8192),     # the skinny sizes of the GEMM sweep (HBM-bound: B streamed once)
     (128, 8192, 8192),
+    (2560, 2048, 256),    # pair tiles with a short last wave, cut into 256 x 128 halves
+    (2600, 1800, 384),    # the same with ragged M and N (one half tile entirely past N)
 ]
 
 
@@ -57,7 +59,7 @@ def test_gemm_s32_bit_exact(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 1, 1), (200, 300, 1000), (256, 1024, 1024), (129, 257, 4096),
-                                   (130, 18944, 512), (2600, 2600, 1000)])
+                                   (130, 18944, 512), (2600, 2600, 1000), (2600, 1800, 384)])
 def test_gemm_f32_and_bf16_epilogue(M, N, K):
     a, b, sa, sb, bias = _operands(M, N, K, seed=3 * M + K)
     acc = O.gemm_i8(a[:, :K].numpy(), b[:, :K].numpy())
