@@ -126,6 +126,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major, 128 B swizzle, 8-row core-matrix
@@ -227,6 +236,34 @@ constexpr int kSwigluFeat = 128;  // features per tile
 // quantiser of [dg | du].  dh itself is not written.
 constexpr int kOutSwigluBwd = 17;
 __host__ __device__ constexpr bool is_swiglu(int out) { return out == kOutSwigluFwd || out == kOutSwigluBwd; }
+// The SwiGLU backward epilogue runs kSwbWpq warps per TMEM lane quarter; the tile's 256 features
+// are 16 chunks of kSwbChunk, and warp e of a quarter takes chunks e, e + kSwbWpq, ...  g and u
+// pass through shared memory: per epilogue warp a ring of kSwbBufs buffers, each one chunk of
+// the warp's 32 rows of g and of u, loaded by TMA (32 x 32 B boxes, 32-byte swizzle: the 16-byte
+// half k of row r sits at half k ^ ((r >> 2) & 1), so the lanes' row reads and writes hit distinct
+// banks).  dg and du are written over g and u in the same buffer and leave by TMA stores from
+// there; a buffer is loaded again once its stores have read it, kSwbBufs - 1 chunks ahead of its
+// use.
+constexpr int kSwbChunk = 16;
+#ifndef FF_SWB_WPQ
+#define FF_SWB_WPQ 3
+#endif
+#ifndef FF_SWB_BUFS
+#define FF_SWB_BUFS 3
+#endif
+constexpr int kSwbWpq = FF_SWB_WPQ;
+constexpr int kSwbWarps = 4 * kSwbWpq;
+constexpr int kSwbBufs = FF_SWB_BUFS;
+constexpr int kSwbBoxBytes = 32 * kSwbChunk * 2;  // 32 rows x 16 bf16
+constexpr int kSwbBufBytes = 2 * kSwbBoxBytes;    // g box, then u box
+// after the barriers (256 B): per warp one buffer of the tile's 256 gate and 256 up column
+// multipliers, then the rings (256-byte aligned for the swizzle), then the rings' barriers
+constexpr uint32_t kSwbCmOff = 256;
+constexpr uint32_t kSwbCmBytes = 2 * 256 * 4;
+constexpr uint32_t kSwbRingOff = kSwbCmOff + kSwbWarps * kSwbCmBytes;
+constexpr uint32_t kSwbBarOff = kSwbRingOff + kSwbWarps * kSwbBufs * kSwbBufBytes;
+constexpr uint32_t kSwbCtrlBytes = kSwbBarOff + kSwbWarps * kSwbBufs * 8;
+static_assert(kSwbRingOff % 256 == 0, "the rings must be 256-byte aligned for the 32-byte swizzle");
 // Epilogue kind of the up GEMM of a GELU MLP block: u (bf16, as FF_OUT_BF16 forms it) and
 // h = gelu(u) (tanh form) written by TMA, |h| folded into the row and column maxima: the first
 // pass of the dual quantiser of h.
@@ -409,7 +446,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const uint32_t (&acc)[32], in
     }
     w[q] = pack_bf16x2(mk2(t2[0], t2[1]));
   }
-  staged_store(w, tmD, (int32_t)col0, (int32_t)row0, lane, stage, stage_addr, n);
+  staged_store<true>(w, tmD, (int32_t)col0, (int32_t)row0, lane, stage, stage_addr, n);
 }
 
 // 32 features of the SwiGLU forward epilogue for one row (one thread): accumulators of the
@@ -468,9 +505,9 @@ __device__ __forceinline__ void swiglu_fwd_chunk(const uint32_t (&ag)[32], const
   }
   // g, u (columns fb and F + fb of gu) and h: TMA tile stores of the warp's 32 rows (clipped at M)
   const int32_t row0 = (int32_t)(row - lane);
-  staged_store(wg, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
-  staged_store(wu, tmD, (int32_t)(p.F + fb), row0, lane, stage, stage_addr, nst);
-  staged_store(wh, tmH, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  staged_store<true>(wg, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
+  staged_store<true>(wu, tmD, (int32_t)(p.F + fb), row0, lane, stage, stage_addr, nst);
+  staged_store<true>(wh, tmH, (int32_t)fb, row0, lane, stage, stage_addr, nst);
   // maxima of |h| (rows past M hold no data: excluded)
   uint32_t a[16];
 #pragma unroll
@@ -537,84 +574,111 @@ __device__ __forceinline__ uint32_t warp_colmax_bits(uint32_t (&a)[16], int lane
   return (lane & 1) ? (a[0] & 0xFFFF0000u) : (a[0] << 16);
 }
 
-// g and u of one row's 32 features (64 B each), zeros for rows past M
-__device__ __forceinline__ void swiglu_bwd_load(const EpiParams& p, int64_t row, int64_t fb, uint4 (&gq)[4],
-                                                uint4 (&uq)[4]) {
-  if (row < p.M) {
-    const uint4* gp = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + fb);
-    const uint4* up = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + p.F + fb);
+// reduce-scatter of 8 bf16x2 words (16 features) over the warp's 32 rows: the maximum of feature
+// 8*b4 + 4*b3 + 2*b2 + b0 over all 32 lanes (b_i = bit i of the lane), as float bits; lanes with
+// bit 1 set hold a copy of their neighbour's feature
+__device__ __forceinline__ uint32_t warp_colmax16_bits(uint32_t (&a)[8], int lane) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      gq[k] = __ldg(gp + k);
-      uq[k] = __ldg(up + k);
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) gq[k] = uq[k] = make_uint4(0u, 0u, 0u, 0u);
+  for (int q = 0; q < 4; ++q) {
+    const bool up = lane & 16;
+    const uint32_t send = up ? a[q] : a[q + 4], keep = up ? a[q + 4] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 16));
   }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool up = lane & 8;
+    const uint32_t send = up ? a[q] : a[q + 2], keep = up ? a[q + 2] : a[q];
+    a[q] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  {
+    const bool up = lane & 4;
+    const uint32_t send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
+    a[0] = max_bf16x2(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  a[0] = max_bf16x2(a[0], __shfl_xor_sync(0xffffffffu, a[0], 2));
+  a[0] = max_bf16x2(a[0], __shfl_xor_sync(0xffffffffu, a[0], 1));  // word 4*b4 + 2*b3 + b2, all 32 rows
+  return (lane & 1) ? (a[0] & 0xFFFF0000u) : (a[0] << 16);
+}
+__device__ __forceinline__ int colmax16_feature(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + (lane & 1);
 }
 
-// 32 features of the SwiGLU backward epilogue for one row (one thread): dh = bf16(acc * sa)
-// (as FF_OUT_BF16 forms it) with the row's g and u (gq, uq) gives dg = bf16(silu_backward(
-// bf16(dh * u), g)) and du = bf16(dh * bf16(silu(g))), stored by TMA at columns fb and F + fb of
-// D; folds |dg * colmul|, |du * colmul| into rmax and |dg|, |du| into the column maxima.  `cm`
-// points at this chunk's staged column multipliers: gate at [0, 32), up at [128, 160).
-__device__ __forceinline__ void swiglu_bwd_chunk(const uint32_t (&acc)[32], const uint4 (&gq)[4],
-                                                 const uint4 (&uq)[4], int64_t row, int64_t fb, const EpiParams& p,
-                                                 float sa, int lane, const float* cm, float& rmax,
-                                                 const CUtensorMap* tmD, uint8_t* stage, uint32_t stage_addr,
-                                                 uint32_t& nst) {
-  const bool live = row < p.M;
-  uint32_t gw[16], uw[16], dw[16];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    gw[4 * k] = gq[k].x; gw[4 * k + 1] = gq[k].y; gw[4 * k + 2] = gq[k].z; gw[4 * k + 3] = gq[k].w;
-    uw[4 * k] = uq[k].x; uw[4 * k + 1] = uq[k].y; uw[4 * k + 2] = uq[k].z; uw[4 * k + 3] = uq[k].w;
-  }
+// kSwbChunk (16) features of the SwiGLU backward epilogue for one row (one thread): dh = bf16(acc *
+// sa) (as FF_OUT_BF16 forms it) with the row's g and u (from the ring buffer `buf`, shared address
+// buf_addr) gives dg = bf16(silu_backward(bf16(dh * u), g)) and du = bf16(dh * bf16(silu(g))); they
+// are written over g and u and stored by TMA at columns fb and F + fb of D (lane 0 issues the
+// stores as one bulk group).  Folds |dg * colmul|, |du * colmul| into rmax and |dg|, |du| into the
+// column maxima.  `cg`, `cu`: this chunk's 16 gate and 16 up column multipliers.
+__device__ __forceinline__ void swiglu_bwd_chunk16(const uint32_t (&acc)[16], uint8_t* buf, uint32_t buf_addr,
+                                                   int64_t row, int64_t fb, const EpiParams& p, float sa, int lane,
+                                                   const float* cg, const float* cu, float& rmax,
+                                                   const CUtensorMap* tmD) {
+  const int sw = (lane >> 2) & 1;
+  uint4* gp = reinterpret_cast<uint4*>(buf + lane * 32);
+  uint4* up = reinterpret_cast<uint4*>(buf + kSwbBoxBytes + lane * 32);
+  const uint4 g0 = gp[sw], g1 = gp[sw ^ 1], u0 = up[sw], u1 = up[sw ^ 1];
+  const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
   const f2 sa2 = splat(sa);
+  uint32_t dw[8];
 #pragma unroll
-  for (int q = 0; q < 16; ++q)
+  for (int q = 0; q < 8; ++q)
     dw[q] = pack_bf16x2(mul2(mk2(__int2float_rn((int)acc[2 * q]), __int2float_rn((int)acc[2 * q + 1])), sa2));
-  uint32_t wdg[16], wdu[16];
-  bool rare = false;
+  uint32_t wdg[8], wdu[8];
+  uint32_t gmag = 0u;  // halfwise maximum of |g| (bf16 bits)
   const f2 one = splat(1.f);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
+  for (int q = 0; q < 8; ++q) {
     const f2 x = unpack_bf16x2(gw[q]), d = unpack_bf16x2(dw[q]);
-    const SwigluMath2 m = swiglu_fast2(__uint_as_float(gw[q] << 16), __uint_as_float(gw[q] & 0xFFFF0000u), rare);
+    gmag = max_u16x2(gmag, abs_bf16x2(gw[q]));
+    const SwigluMath2 m = swiglu_fast2_in_range(__uint_as_float(gw[q] << 16), __uint_as_float(gw[q] & 0xFFFF0000u));
     const f2 ds = unpack_bf16x2(pack_bf16x2(mul2(d, unpack_bf16x2(uw[q]))));
     wdg[q] = pack_bf16x2(mul2(mul2(ds, m.s), fma2(x, sub2(one, m.s), one)));
     wdu[q] = pack_bf16x2(mul2(d, unpack_bf16x2(pack_bf16x2(m.q))));
   }
-  if (__builtin_expect(rare, 0)) {
+  if (__builtin_expect(bf16x2_outside_64(gmag), 0)) {  // some |g| >= 64: the IEEE path for the chunk
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const uint2 e = swiglu_bwd_exact_word(gw[q], dw[q], uw[q]);
       wdg[q] = e.x;
       wdu[q] = e.y;
     }
   }
-  const int32_t row0 = (int32_t)(row - lane);
-  staged_store(wdg, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
-  staged_store(wdu, tmD, (int32_t)(p.F + fb), row0, lane, stage, stage_addr, nst);
-  uint32_t ag[16], au[16];
+  gp[sw] = make_uint4(wdg[0], wdg[1], wdg[2], wdg[3]);
+  gp[sw ^ 1] = make_uint4(wdg[4], wdg[5], wdg[6], wdg[7]);
+  up[sw] = make_uint4(wdu[0], wdu[1], wdu[2], wdu[3]);
+  up[sw ^ 1] = make_uint4(wdu[4], wdu[5], wdu[6], wdu[7]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int32_t row0 = (int32_t)(row - lane);
+    tma_store_2d(tmD, buf_addr, (int32_t)fb, row0);
+    tma_store_2d(tmD, buf_addr + kSwbBoxBytes, (int32_t)(p.F + fb), row0);
+    bulk_commit_group();
+  }
+  // rows past M have zero dh, g and u (TMA fills them with zeros), so their dg and du are zeros
+  uint32_t ag[8], au[8];
   uint32_t rw = 0u;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    ag[q] = live ? abs_bf16x2(wdg[q]) : 0u;
-    au[q] = live ? abs_bf16x2(wdu[q]) : 0u;
+  for (int q = 0; q < 8; ++q) {
+    ag[q] = abs_bf16x2(wdg[q]);
+    au[q] = abs_bf16x2(wdu[q]);
     if (p.colmul) {  // |v| * colmul (colmul >= 0) in fp32, as the row quantiser takes it
       float a0, a1, b0, b1;
-      un2(mul2(unpack_bf16x2(ag[q]), mk2(cm[2 * q], cm[2 * q + 1])), a0, a1);
-      un2(mul2(unpack_bf16x2(au[q]), mk2(cm[kSwigluFeat + 2 * q], cm[kSwigluFeat + 2 * q + 1])), b0, b1);
+      un2(mul2(unpack_bf16x2(ag[q]), mk2(cg[2 * q], cg[2 * q + 1])), a0, a1);
+      un2(mul2(unpack_bf16x2(au[q]), mk2(cu[2 * q], cu[2 * q + 1])), b0, b1);
       rmax = fmaxf(rmax, fmaxf(fmaxf(a0, a1), fmaxf(b0, b1)));
     } else {
       rw = max_bf16x2(rw, max_bf16x2(ag[q], au[q]));
     }
   }
   if (!p.colmul) rmax = fmaxf(rmax, fmaxf(__uint_as_float(rw << 16), __uint_as_float(rw & 0xFFFF0000u)));
-  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(ag, lane));
-  atomicMax(p.col_amax + p.F + fb + lane, warp_colmax_bits(au, lane));
+  const uint32_t mg = warp_colmax16_bits(ag, lane), mu = warp_colmax16_bits(au, lane);
+  if (!(lane & 2)) {
+    const int f = colmax16_feature(lane);
+    atomicMax(p.col_amax + fb + f, mg);
+    atomicMax(p.col_amax + p.F + fb + f, mu);
+  }
 }
 
 // 32 features of the GELU forward epilogue for one row (one thread): u exactly as the
@@ -889,7 +953,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
-      if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
+      if (!__all_sync(0xffffffffu, wait_bar(tfull_bar(acc), acc_phase, abort_flag))) break;  // warp-uniform exit
       tc_fence_after();
       const int64_t row = (int64_t)tm * BM + lg * 32 + lane;
       float sa = 1.f;
@@ -952,27 +1016,40 @@ constexpr int C2_SMEM_BYTES = C2_STAGES * C2_STAGE_BYTES + 1024 + 256;
 // SwiGLU epilogue: per epilogue warp, two buffers (by accumulator) of the column scales and
 // bias of its 64 features: gate scales, up scales, gate bias, up bias (4 x 64 floats)
 constexpr int C2_SW_BUF_FLOATS = 2 * kSwigluFeat;  // per warp and buffer: its 64 features x 4 arrays
-// SwiGLU: 5 stages, then 8 warps x (2 scale/bias buffers + 2 output staging buffers)
-constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 256 + 8 * 2 * C2_SW_BUF_FLOATS * 4 + 8 * 2 * 2048;
+// SwiGLU: 5 stages, then 8 warps x (2 scale/bias buffers + 2 output staging buffers, 512-byte aligned)
+constexpr int C2_SMEM_BYTES_SW = C2_STAGES_SW * C2_STAGE_BYTES + 1024 + 512 + 8 * 2 * C2_SW_BUF_FLOATS * 4 + 8 * 2 * 2048;
 // GELU: 4 stages, the SwiGLU layout's buffers, then the table of gelu (bf16) or gelu' (fp32)
 constexpr int C2_SMEM_BYTES_GELU = C2_STAGES_GELU * C2_STAGE_BYTES + 1024 + 512 + 8 * 2 * C2_SW_BUF_FLOATS * 4 +
                                    8 * 2 * 2048 + kGeluTabEntries * 4;
-// bf16 output: per epilogue warp (8) two 32 x 32 bf16 staging buffers for the TMA stores
-constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 8 * 2 * 2048;
+// bf16 output: per epilogue warp (8) two 32 x 32 bf16 staging buffers for the TMA stores (from
+// byte 512 of the control area: 512-byte aligned for the 64-byte swizzle)
+constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 256 + 8 * 2 * 2048;
+static_assert(C2_SMEM_BYTES_ST <= 232448, "bf16-output kernel exceeds the shared memory of a CTA");
+// SwiGLU backward: 4 stages, then the column multipliers and the g/u rings (kSwbCtrlBytes)
+#ifndef FF_SWB_STAGES
+#define FF_SWB_STAGES 4
+#endif
+constexpr int C2_STAGES_SWB = FF_SWB_STAGES;
+constexpr int C2_SMEM_BYTES_SWB = C2_STAGES_SWB * C2_STAGE_BYTES + 1024 + (int)kSwbCtrlBytes;
+static_assert(C2_SMEM_BYTES_SWB <= 232448, "SwiGLU backward kernel exceeds the shared memory of a CTA");
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
-  return is_gelu(OUT) ? C2_STAGES_GELU : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
+  return OUT == kOutSwigluBwd ? C2_STAGES_SWB
+         : is_gelu(OUT)       ? C2_STAGES_GELU
+                              : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
 }
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return is_gelu(OUT) ? C2_SMEM_BYTES_GELU
-                      : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
+  return OUT == kOutSwigluBwd ? C2_SMEM_BYTES_SWB
+         : is_gelu(OUT)       ? C2_SMEM_BYTES_GELU
+                              : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 8 epilogue warps (two per TMEM lane
-// quarter, each on half of the tile's columns), so a tile's epilogue takes half as long
+// quarter, each on half of the tile's columns), so a tile's epilogue takes half as long; the
+// SwiGLU backward epilogue runs kSwbWpq warps per quarter
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return 320;
+  return OUT == kOutSwigluBwd ? 64 + 32 * kSwbWarps : 320;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -1089,6 +1166,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     }
     mbar_init(drain, 1);
     mbar_init(done_bar, 1);
+    if constexpr (OUT == kOutSwigluBwd)
+      for (int i = 0; i < kSwbWarps * kSwbBufs; ++i) mbar_init(cbase + kSwbBarOff + 8u * i, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmA);
@@ -1203,29 +1282,71 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     const int eh = (warp - 2) >> 2;    // SwiGLU: which half of the tile's features (0 or 1)
     int acc = 0;
     uint32_t acc_phase = 0;
-    // SwiGLU: this warp's two staging buffers of its features' column scales and bias
-    float* sw_buf = reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * 2 * C2_SW_BUF_FLOATS;
-    // this warp's two TMA-store staging buffers (32 rows x 64 B each); with the SwiGLU epilogue
-    // they follow the 8 warps' scale/bias buffers
-    // (the GELU epilogues' buffers start 512-byte aligned, for the 64-byte swizzle)
-    constexpr uint32_t st_off = 256u + (is_fused_act(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u) +
-                                (is_gelu(OUT) ? 256u : 0u);
+    // SwiGLU: this warp's two staging buffers of its features' column scales and bias (the
+    // backward epilogue: one buffer of its column multipliers)
+    constexpr int sw_bufs = OUT == kOutSwigluBwd ? 1 : 2;
+    float* sw_buf = OUT == kOutSwigluBwd
+                        ? reinterpret_cast<float*>(ctrl + kSwbCmOff + (warp - 2) * kSwbCmBytes)
+                        : reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * sw_bufs * C2_SW_BUF_FLOATS;
+    // this warp's two TMA-store staging buffers (32 rows x 64 B each, 512-byte aligned for the
+    // 64-byte swizzle); with the activation epilogues they follow the 8 warps' scale/bias buffers
+    constexpr uint32_t st_off = 512u + (is_fused_act(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
     uint8_t* st_stage = ctrl + st_off + (warp - 2) * 2 * 2048;
     const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
     int tm, tn, half;
+    // SwiGLU backward: this warp's ring of g/u chunks (kSwbChunk).  The warp's chunks (those of
+    // its chunk indices that lie below F) in schedule order; lane 0 keeps the cursor of the next
+    // chunk to load (item sj, chunk sc at tile sm, sn) and the count of chunks loaded.
+    [[maybe_unused]] const uint32_t swb_ring = cbase + kSwbRingOff + (uint32_t)(warp - 2) * kSwbBufs * kSwbBufBytes;
+    [[maybe_unused]] uint8_t* swb_ring_p = ctrl + kSwbRingOff + (warp - 2) * kSwbBufs * kSwbBufBytes;
+    [[maybe_unused]] const uint32_t swb_bar = cbase + kSwbBarOff + (uint32_t)(warp - 2) * kSwbBufs * 8;
+    // chunks of tile column tn below F (16, or 8 for a last tile of 128 features: F % 128 == 0)
+    auto swb_chunks = [&](int tn_) { return (int)min64(C2_BN / kSwbChunk, (ep.F - (int64_t)tn_ * C2_BN) / kSwbChunk); };
+    int sj = 0, sc = 0, sm = 0, sn = 0, swb_loaded = 0, swb_used = 0;
+    bool s_ok = false;
+    auto swb_seek = [&](int from) {  // the first item >= from with a chunk of this warp
+      int h_;
+      for (sj = from; item(sj, sm, sn, h_); ++sj)
+        if (swb_chunks(sn) > eh) {
+          sc = eh;
+          s_ok = true;
+          return;
+        }
+      s_ok = false;
+    };
+    auto swb_load = [&]() {  // lane 0: TMA loads of the cursor's chunk into its ring buffer
+      const int b = swb_loaded % kSwbBufs;
+      const int32_t x = (int32_t)((int64_t)sn * C2_BN + sc * kSwbChunk);
+      const int32_t y = (int32_t)((int64_t)sm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32);
+      const uint32_t bar = swb_bar + 8u * (uint32_t)b, dst = swb_ring + (uint32_t)(b * kSwbBufBytes);
+      mbar_arrive_expect_tx(bar, kSwbBufBytes);
+      tma_load_2d(dst, &tmH, x, y, bar);
+      tma_load_2d(dst + kSwbBoxBytes, &tmH, (int32_t)ep.F + x, y, bar);
+      ++swb_loaded;
+      sc += kSwbWpq;
+      if (sc >= swb_chunks(sn)) swb_seek(sj + 1);
+    };
+    if constexpr (OUT == kOutSwigluBwd) {
+      if (lane == 0) {
+        swb_seek(0);
+        while (s_ok && swb_loaded < kSwbBufs) swb_load();
+      }
+    }
+    bool swb_abort = false;
     for (int j = 0; item(j, tm, tn, half); ++j) {
       float4 st_s, st_b;  // loaded before the accumulator wait, stored after it
-      uint4 pg[4], pu[4];  // SwiGLU backward: g and u of the next chunk, loaded ahead
+      uint4 pu[4];        // GELU backward: u of the next chunk, loaded ahead
+      [[maybe_unused]] float4 st_s2, st_b2;  // SwiGLU backward: the multipliers of features 128..255
       if constexpr (OUT == kOutSwigluBwd) {
-        // this warp's 128 features of the tile: lane l holds gate multipliers 4l..4l+3, up likewise
-        const int64_t col = (int64_t)tn * C2_BN + eh * 128 + lane * 4;
-        const bool in = ep.colmul && col < ep.F;
-        st_s = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
-        st_b = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + ep.F + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
-        const int64_t fb0 = (int64_t)tn * C2_BN + eh * 128;
-        const int64_t prow = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
-        if (fb0 < ep.F) swiglu_bwd_load(ep, prow, fb0, pg, pu);
+        // the tile's 256 features: lane l holds gate multipliers 4l..4l+3 and 128+4l..128+4l+3, up likewise
+        const int64_t col = (int64_t)tn * C2_BN + lane * 4;
+        const bool in = ep.colmul && col < ep.F, in2 = ep.colmul && col + 128 < ep.F;
+        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
+        st_s = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col)) : one4;
+        st_b = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + ep.F + col)) : one4;
+        st_s2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col + 128)) : one4;
+        st_b2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + ep.F + col + 128)) : one4;
       }
       if constexpr (OUT == kOutGeluFwd || OUT == kOutGeluBwd) {
         // this warp's 128 features of the tile: lane l holds features 4l..4l+3 (forward: column
@@ -1247,12 +1368,19 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         st_s = ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
         st_b = ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag)) break;
+      if (!__all_sync(0xffffffffu, wait_bar(tfull_bar(acc), acc_phase, abort_flag))) break;  // warp-uniform exit
       tc_fence_after();
       if constexpr (is_fused_act(OUT)) {
-        float* buf = sw_buf + acc * C2_SW_BUF_FLOATS;
-        reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
-        reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
+        float* buf = sw_buf + (sw_bufs == 2 ? acc : 0) * C2_SW_BUF_FLOATS;
+        if constexpr (OUT == kOutSwigluBwd) {  // [gate 256 | up 256]
+          reinterpret_cast<float4*>(buf)[lane] = st_s;
+          reinterpret_cast<float4*>(buf + 128)[lane] = st_s2;
+          reinterpret_cast<float4*>(buf + 256)[lane] = st_b;
+          reinterpret_cast<float4*>(buf + 384)[lane] = st_b2;
+        } else {
+          reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
+          reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
+        }
         __syncwarp();
       }
       const int64_t row = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
@@ -1312,26 +1440,36 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         }
         if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
       } else if constexpr (OUT == kOutSwigluBwd) {
-        float rmax = 0.f;
+        const int nchunks = swb_chunks(tn);
+        if (nchunks > eh) {
+          float rmax = 0.f;
+          const float* cmb = sw_buf;  // [gate 256 | up 256] multipliers of the tile's features
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
-          const int fc = eh * 128 + c * 32;
-          const int64_t fb = (int64_t)tn * C2_BN + fc;
-          if (fb >= ep.F) break;
-          uint4 cg[4], cu[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            cg[k] = pg[k];
-            cu[k] = pu[k];
+          for (int c = eh; c < nchunks; c += kSwbWpq, ++swb_used) {
+            const int b = swb_used % kSwbBufs;
+            // warp-uniform: lanes that saw the phase complete leave with those that saw the abort
+            if (!__all_sync(0xffffffffu, wait_bar(swb_bar + 8u * (uint32_t)b, (uint32_t)(swb_used / kSwbBufs) & 1u,
+                                                  abort_flag))) {
+              swb_abort = true;
+              break;
+            }
+            uint32_t r[16];
+            tmem_ld16(tbase + c * kSwbChunk, r);
+            tmem_wait_ld();
+            swiglu_bwd_chunk16(r, swb_ring_p + b * kSwbBufBytes, swb_ring + (uint32_t)(b * kSwbBufBytes), row,
+                               (int64_t)tn * C2_BN + c * kSwbChunk, ep, sa, lane, cmb + c * kSwbChunk,
+                               cmb + 256 + c * kSwbChunk, rmax, &tmD);
+            // the previous chunk's buffer (its stores were issued one chunk ago) takes the chunk
+            // kSwbBufs - 1 ahead of the next
+            if (lane == 0 && swb_used >= 1 && s_ok) {
+              bulk_wait_read_1();
+              swb_load();
+            }
+            __syncwarp();
           }
-          if (c + 1 < 4 && fb + 32 < ep.F) swiglu_bwd_load(ep, row, fb + 32, pg, pu);  // next chunk
-          uint32_t r[32];
-          tmem_ld32(tbase + fc, r);
-          tmem_wait_ld();
-          swiglu_bwd_chunk(r, cg, cu, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32, rmax, &tmD,
-                           st_stage, st_stage_addr, st_count);
+          if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
         }
-        if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
+        if (swb_abort) break;
       } else {
         const int64_t col0 = (int64_t)tn * C2_BN + (half < 0 ? 0 : half * (C2_BN / 2));
         const int64_t ncol_tile = min64(half < 0 ? C2_BN : C2_BN / 2, ep.N - col0);
@@ -1360,7 +1498,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         acc_phase ^= 1u;
       }
     }
-    if (st_count && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
+    if ((st_count || OUT == kOutSwigluBwd) && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
     __syncwarp();
   }
 
@@ -1417,19 +1555,25 @@ inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t col
   return FF_OK;
 }
 
-// bf16 output [rows, cols] (leading dim ld) for TMA tile stores of 32 x 32 boxes
-inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, bool swz64 = false) {
+// bf16 matrix [rows, cols] (leading dim ld) for TMA boxes of box_cols x box_rows elements
+inline int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                         int box_rows, CUtensorMapSwizzle swizzle,
+                         CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_NONE) {
   auto fn = encode_fn();
   if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swz64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
   return FF_OK;
+}
+
+// bf16 output [rows, cols] (leading dim ld) for TMA tile stores of 32 x 32 boxes
+inline int make_map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, bool swz64 = false) {
+  return make_map_bf16(m, ptr, rows, cols, ld, 32, 32, swz64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 inline int num_sms_current() {
@@ -1621,7 +1765,7 @@ inline int gemm_dispatch(const char* name, const int8_t* A, int64_t lda, const i
     CUtensorMap md;
     memset(&md, 0, sizeof(md));
     if (out_kind == FF_OUT_BF16 && ep.vec) {  // 16-byte aligned output rows: TMA tile stores
-      rc = make_map_out_bf16(&md, D, M, N, ldd);
+      rc = make_map_out_bf16(&md, D, M, N, ldd, true);
       if (rc) return rc;
       ep.tma_store = 1;
     }
@@ -1747,9 +1891,9 @@ extern "C" int ff_swiglu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, 
   ep.col_amax = ep.row_amax + M;
   const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)(F / kSwigluFeat);
   CUtensorMap md, mh;  // gu and h, written by TMA tile stores
-  rc = make_map_out_bf16(&md, gu, M, 2 * F, ldgu);
+  rc = make_map_out_bf16(&md, gu, M, 2 * F, ldgu, true);
   if (rc) return rc;
-  rc = make_map_out_bf16(&mh, h, M, F, ldh);
+  rc = make_map_out_bf16(&mh, h, M, F, ldh, true);
   if (rc) return rc;
   rc = launch_2cta<kOutSwigluFwd, false>(ma, mb, md, mh, K, t2m, t2n, ep, max_pairs, st);
   if (rc != FF_OK) return rc;
@@ -1787,12 +1931,15 @@ extern "C" int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t*
   FF_REQUIRE(max_pairs > 0, FF_ERR_UNSUPPORTED, "%s: the 2-CTA GEMM cannot be resident on this device", name);
   cudaStream_t st = as_stream(stream);
   FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(M + 2 * F), st), name);
-  CUtensorMap ma, mb, md;
+  CUtensorMap ma, mb, md, mg;
   rc = make_map(&ma, A, M, K, lda, BM);
   if (rc) return rc;
   rc = make_map(&mb, B, K, F, ldb, BK);  // B is K x F row-major: read MN-major
   if (rc) return rc;
-  rc = make_map_out_bf16(&md, dgu, M, 2 * F, lddgu);
+  // g/u loads and dg/du stores: boxes of one epilogue chunk (kSwbChunk features x 32 rows)
+  rc = make_map_bf16(&md, dgu, M, 2 * F, lddgu, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  rc = make_map_bf16(&mg, gu, M, 2 * F, ldgu, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
   if (rc) return rc;
   EpiParams ep{};
   ep.scale_a = scale_a;
@@ -1808,7 +1955,7 @@ extern "C" int ff_swiglu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t*
   ep.ldg_in = ldgu;
   ep.colmul = colmul;
   const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((F + C2_BN - 1) / C2_BN);
-  rc = launch_2cta<kOutSwigluBwd, true>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+  rc = launch_2cta<kOutSwigluBwd, true>(ma, mb, md, mg, K, t2m, t2n, ep, max_pairs, st);
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(dgu), M, 2 * F, lddgu, colmul,
                                       eps, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);

@@ -40,15 +40,6 @@ __host__ __device__ constexpr int sk_tmem_cols(int mp) { return 2 * mp < 32 ? 32
 inline int64_t sk_ws_bytes(int64_t tiles, int mp) { return tiles * mp * SK_BN * 4 + tiles * 4; }
 inline int sk_mp(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
 // the CTA whose k-iteration range holds iteration i (ranges [c*total/G, (c+1)*total/G))
 __device__ __forceinline__ int64_t sk_owner(int64_t i, int64_t total, int64_t G) { return ((i + 1) * G + total - 1) / total - 1; }
 

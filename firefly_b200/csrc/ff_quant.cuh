@@ -199,6 +199,34 @@ __device__ __forceinline__ SwigluMath2 swiglu_fast2(float x0, float x1, bool& ra
   rare |= !(d0 < 0x1p126f) || !(d1 < 0x1p126f) || !(x0 < INFINITY) || !(x1 < INFINITY);
   return m;
 }
+// swiglu_fast2 without its range flag, for callers that route inputs with |x| >= 64 (bf16 bit
+// patterns with magnitude >= 0x4280, non-finite ones included) to the IEEE path themselves: every
+// x with |x| < 64 lies inside the fast path's range (1 + exp(-x) < 2^93)
+__device__ __forceinline__ SwigluMath2 swiglu_fast2_in_range(float x0, float x1) {
+  const f2 x = mk2(x0, x1), one = splat(1.f);
+  const f2 e = mk2(expf(-x0), expf(-x1));
+  const f2 nden = sub2(splat(-1.f), e);
+  float d0, d1;
+  un2(add2(one, e), d0, d1);
+  const f2 y = mk2(rcp_approx_ftz(d0), rcp_approx_ftz(d1));
+  SwigluMath2 m;
+  m.s = fma2(fma2(nden, y, one), y, y);
+  const f2 q0 = mul2(x, m.s);
+  float q0a, q0b;
+  un2(fma2(fma2(nden, q0, x), m.s, q0), q0a, q0b);
+  m.q = mk2(sign_of(q0a, x0), sign_of(q0b, x1));
+  return m;
+}
+// halfwise unsigned maximum of two words of 16-bit halves
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// true if either bf16 half of the packed magnitudes `mag` (sign bits cleared) is >= 64 or not finite
+__device__ __forceinline__ bool bf16x2_outside_64(uint32_t mag) {
+  return (mag & 0xFFFFu) >= 0x4280u || (mag >> 16) >= 0x4280u;
+}
 __device__ __forceinline__ SwigluMath swiglu_exact(float x) {
   SwigluMath m;
   m.den = __fadd_rn(1.f, expf(-x));
