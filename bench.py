@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--decoder-warmup", type=int, default=2)
     ap.add_argument("--zero-bucket-mb", type=float, default=256.0,
                     help="ZeRO-1 gradient bucket size (MB of bf16); 0 = one bucket")
+    ap.add_argument("--zero-peer", choices=["auto", "0", "1"], default="auto",
+                    help="ZeRO-1 peer mode (the update kernel reads and writes the other ranks' arenas over "
+                         "NVLink): auto = where the ranks can map each other's memory")
     ap.add_argument("--zero-overlap", type=int, choices=[0, 1], default=1,
                     help="start each bucket's reduce-scatter from the backward pass")
     ap.add_argument("--kernel-case", choices=["gemm8192", "gemm_skinny16", "gemm_skinny128", "gemm2048", "gemm4096",
@@ -518,6 +521,8 @@ def zero1_parity_check(dev, world: int, rank: int, steps: int = 3) -> dict:
     torch.manual_seed(0)
     mods = [BitLinear(k, o).to(dev) for o, k in ZERO1_CHECK_SHAPES]
     opt = ZeroFireFlyOptim(mods, lr=1e-3, weight_decay=0.01, seed=5, bucket_mb=0.05, overlap=True)
+    opt.keep_reduced_grad = True  # peer mode: the averaged gradient of each shard, for the replay
+    path = "peer" if opt.peer else "collectives"
     plan = opt.plan
     gen = torch.Generator(device=dev).manual_seed(123 + rank)
     averaged = []
@@ -550,14 +555,19 @@ def zero1_parity_check(dev, world: int, rank: int, steps: int = 3) -> dict:
         for k, v in got.items():
             w = want[k]
             ok = ok and (torch.equal(v, w.cpu()) if torch.is_tensor(v) else v == w)
-    return {"ok": bool(ok), "world": world, "steps": steps, "buckets": len(plan.buckets),
-            "what": ("ZeRO-1 over NCCL (sharded DQT update, overlapped bucketed reduce-scatters, all-gathers) vs "
-                     "an unsharded FireFlyOptim replay on the same averaged gradients: int8 weights and "
-                     "gathered bit_state bit-identical")}
+    return {"ok": bool(ok), "world": world, "steps": steps, "buckets": len(plan.buckets), "path": path,
+            "what": ("ZeRO-1 (peer: one kernel per shard reads every rank's gradient and writes every rank's "
+                     "weights over NVLink; collectives: overlapped bucketed NCCL reduce-scatters, sharded DQT "
+                     "update, all-gathers) vs an unsharded FireFlyOptim replay on the same averaged gradients: "
+                     "int8 weights and gathered bit_state bit-identical")}
+
+
+def zero_peer(args):
+    return None if args.zero_peer == "auto" else args.zero_peer == "1"
 
 
 def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: int = 64, seq: int = 2048,
-                     micro: int = 8, bucket_mb: float = 256.0, overlap: bool = True):
+                     micro: int = 8, bucket_mb: float = 256.0, overlap: bool = True, peer: bool | None = None):
     """Data-parallel training step of the 1.3B BitLinear decoder (24 layers, d 2048, 16 heads,
     ffn 8192 GELU, vocab 32000) on a global batch of ``seqs`` sequences of ``seq`` tokens split
     over the ranks (strong scaling), micro-batches of ``micro`` sequences, ZeRO-1 8-bit optimizer.
@@ -575,7 +585,7 @@ def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: 
     per_rank = seqs // world
     model = build_decoder(cfg, dev, seed=0)
     opt = ZeroFireFlyOptim(model.bit_modules(), params=model.dense_parameters(), lr=1e-4, betas=(0.9, 0.999),
-                           eps=1e-8, weight_decay=0.01, seed=11, bucket_mb=bucket_mb, overlap=overlap)
+                           eps=1e-8, weight_decay=0.01, seed=11, bucket_mb=bucket_mb, overlap=overlap, peer=peer)
     batches = synthetic_batches(cfg, per_rank, seq, min(micro, per_rank), dev, seed=1000 + rank)
     for _ in range(max(warmup, 1)):
         train_step(model, opt, batches)
@@ -893,7 +903,7 @@ def main():
     model.init_normal_(0.02, generator=torch.Generator(device=dev).manual_seed(42))
     mods = [model.gate_up, model.down]
     opt = ZeroFireFlyOptim(mods, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, seed=7,
-                           bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap))
+                           bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap), peer=zero_peer(args))
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     # the block input is an activation of the model: it needs a gradient (dX is part of the step)
     # two resident input batches used alternately, so that every step quantises a new input
@@ -927,6 +937,7 @@ def main():
     _capi.GEMM_EVENTS = []
     _capi.FUSED_GEMM_EVENTS = []
     launches0 = _capi.LAUNCHES
+    opt.comm_events = [] if world > 1 else None
     barrier()
     torch.cuda.synchronize()
     clocks.mark()
@@ -951,6 +962,25 @@ def main():
     g_ms = [a.elapsed_time(b) for a, b, _, _ in gemm_events]
     g_ops = [o for _, _, o, _ in gemm_events]
     alg_bytes = sum(b for _, _, _, b in gemm_events)
+    comm = None
+    if world > 1:  # the compute stream's waits for the collectives (their exposed part), per step
+        phases = ["reduce_scatter_wait", "dense_all_reduce_wait", "all_gather_wait", "peer_fence_wait",
+                  "peer_update", "optimizer_step"]
+        per = {k: 0.0 for k in phases}
+        for k, a, b in opt.comm_events:
+            per[k] += a.elapsed_time(b) / args.steps
+        opt.comm_events = None
+        pt = torch.tensor([per[k] for k in phases], dtype=torch.float64, device=dev)
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        per = dict(zip(phases, pt.tolist()))
+        comm = {"zero1_path": "peer" if opt.peer else "collectives",
+                "exposed_ms_per_step": (per["reduce_scatter_wait"] + per["dense_all_reduce_wait"] + per["all_gather_wait"]
+                                        + per["peer_fence_wait"]),
+                "by_phase_ms_per_step": per,
+                "method": "CUDA events on the compute stream around each wait for a collective in the optimizer "
+                          "step (time the stream stood still for communication), mean per step, max over ranks; "
+                          "peer_update = the fused update kernels of peer mode (their NVLink reads and writes "
+                          "overlap the update arithmetic); optimizer_step = the whole step() on the device"}
 
     # ---- e2e: every step's data batch x copied from pinned host memory, the loss read back.
     # The loss is L = sum(y * R) for a fixed projection R resident on the device (the block's
@@ -1011,7 +1041,8 @@ def main():
     torch.cuda.empty_cache()
     if not args.no_decoder:  # every rank: the data-parallel step
         sub["decoder_1p3b_dp"] = decoder_dp_bench(dev, world, rank, args.decoder_steps, args.decoder_warmup,
-                                                  bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap))
+                                                  bucket_mb=args.zero_bucket_mb, overlap=bool(args.zero_overlap),
+                                                  peer=zero_peer(args))
     if world > 1:
         sub["zero1_parity"] = zero1_parity_check(dev, world, rank)
     if rank == 0 and world == 1 and not args.no_sub:
@@ -1058,13 +1089,14 @@ def main():
             "workload": f"swiglu_mlp_train_step T={T}/GPU d={d} f={f} (BitLinear fwd+bwd + 8-bit DQT AdamW)",
             "tokens_per_gpu": T, "global_batch_tokens": T * world,
             "parallelism": f"dp{world}" + ("+zero1" if world > 1 else ""),
-            "zero1": {"bucket_mb": args.zero_bucket_mb, "overlap": bool(args.zero_overlap)},
+            "zero1": {"bucket_mb": args.zero_bucket_mb, "overlap": bool(args.zero_overlap), "peer": args.zero_peer},
             "l2": "inputs larger than L2 (step working set > 126 MB)",
         },
         "e2e": {"value": T * world * e2e_steps / e2e_sec, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(xh.numel() * xh.element_size()), "d2h_bytes_per_step": 4,
                 "host_cpus_per_rank": bound_cpus},
         "gpu_launches": launches,
+        "comm": comm,
         "roofline": {
             "kernel": "ff_gemm_i8 (tcgen05 kind::i8)", "bound": "tensor",
             "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s", "frac": achieved / int8_peak if achieved else None,

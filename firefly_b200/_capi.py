@@ -71,6 +71,13 @@ SIGNATURES = {
     "ff_colsum_bf16": (_I, [_P, _I64, _I64, _I64, _P, _P, _P]),
     "ff_dqt_adamw8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
                            _D, _D, _D, _D, _D, _D, _D, _D, _U64, _U64, _I64, _P, _P, _P, _P]),
+    "ff_dqt_adamw8_peers": (_I, [_P, _P, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
+                                 _D, _D, _D, _D, _D, _D, _D, _D, _U64, _U64, _I64, _P, _P, _P]),
+    "ff_ipc_alloc": (_I, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "ff_ipc_free": (_I, [_P]),
+    "ff_ipc_get_handle": (_I, [_P, ctypes.c_char_p]),
+    "ff_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "ff_ipc_close": (_I, [_P]),
     "ff_update_int8_weight": (_I, [_P, _P, _I64, _P]),
     "ff_adamw8_blockwise": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I64, _D, _D, _D, _D, _D, _I64, _P, _P, _P]),
 }
@@ -90,7 +97,7 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_gelu_eval": 1, "ff_gelu_gemm_i8": 2, "ff_gelu_bwd_gemm_i8": 2,
                      "ff_layernorm_i8": 2, "ff_layernorm_bwd": 3,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1, "ff_gemm_i8_ws": 1,
-                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_update_int8_weight": 1,
+                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_dqt_adamw8_peers": 1, "ff_update_int8_weight": 1,
                      "ff_adamw8_blockwise": 1}
 
 
@@ -742,6 +749,111 @@ def dqt_adamw8(q: torch.Tensor, wscale: torch.Tensor, row_len: int, g: torch.Ten
               float(lr), float(beta1), float(beta2), float(eps), float(wd), bc1, bc2, float(sr_bias),
               int(seed) & (2**64 - 1), int(step), int(rng_offset), _ptr(u), _ptr(dec_s), _ptr(dec_u),
               _stream(dev))
+
+
+DQT_MAX_SOURCES = 8
+IPC_HANDLE_BYTES = 64
+
+
+def dqt_adamw8_peers(q: torch.Tensor, wscale: torch.Tensor, row_len: int, g_ptrs: list[int], q_ptrs: list[int],
+                     m_q: torch.Tensor, m_absmax: torch.Tensor, v_q: torch.Tensor, v_absmax: torch.Tensor,
+                     r_q: torch.Tensor, r_absmax: torch.Tensor, *, lr: float, beta1: float, beta2: float,
+                     eps: float, wd: float, step: int, sr_bias: float, seed: int, rng_offset: int = 0,
+                     elem_base: int = 0, g_out: torch.Tensor | None = None, dec_s: torch.Tensor,
+                     dec_u: torch.Tensor, block: int = 256) -> None:
+    """``dqt_adamw8`` of one rank of a data-parallel job (``ff_dqt_adamw8_peers``): the gradient is
+    the average of the bf16 arrays at the device addresses ``g_ptrs`` (every rank's gradient of
+    these ``q.numel()`` elements, in rank order) and the new weights go to every address of
+    ``q_ptrs`` (every rank's copy, ``q`` among them).  ``g_out`` (optional, bf16) receives the
+    averaged gradient."""
+    dev = _require_cuda(q, wscale, m_q, m_absmax, v_q, v_absmax, r_q, r_absmax, g_out, dec_s, dec_u)
+    numel = q.numel()
+    for name, t, dt in (("q", q, torch.int8), ("m_q", m_q, torch.uint8), ("v_q", v_q, torch.uint8),
+                        ("r_q", r_q, torch.uint8)) + ((("g_out", g_out, torch.bfloat16),) if g_out is not None else ()):
+        if t.dtype != dt or t.numel() != numel or not t.is_contiguous():
+            raise ValueError(f"dqt_adamw8_peers: {name} must be a contiguous {dt} tensor of {numel} elements")
+    for name, t in (("m_absmax", m_absmax), ("v_absmax", v_absmax), ("r_absmax", r_absmax)):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < (numel + block - 1) // block:
+            raise ValueError(f"dqt_adamw8_peers: {name} must be contiguous fp32 with one entry per block")
+    if not 1 <= len(g_ptrs) <= DQT_MAX_SOURCES or not 1 <= len(q_ptrs) <= DQT_MAX_SOURCES:
+        raise ValueError(f"dqt_adamw8_peers: 1 to {DQT_MAX_SOURCES} gradient sources and weight destinations")
+    if q.data_ptr() not in q_ptrs:
+        raise ValueError("dqt_adamw8_peers: q must be one of the weight destinations")
+    gs = (ctypes.c_void_p * len(g_ptrs))(*[int(x) for x in g_ptrs])
+    qs = (ctypes.c_void_p * len(q_ptrs))(*[int(x) for x in q_ptrs])
+    ws = wscale.to(torch.float32).contiguous()
+    bc1 = 1.0 - beta1 ** step
+    bc2 = 1.0 - beta2 ** step
+    with torch.cuda.device(dev):
+        _call("ff_dqt_adamw8_peers", _ptr(q), _ptr(ws), int(row_len), int(elem_base), ctypes.cast(gs, _P),
+              len(g_ptrs), ctypes.cast(qs, _P), len(q_ptrs), _ptr(g_out), _ptr(m_q), _ptr(m_absmax), _ptr(v_q),
+              _ptr(v_absmax), _ptr(r_q), _ptr(r_absmax), numel, block, float(lr), float(beta1), float(beta2),
+              float(eps), float(wd), bc1, bc2, float(sr_bias), int(seed) & (2**64 - 1), int(step),
+              int(rng_offset), _ptr(dec_s), _ptr(dec_u), _stream(dev))
+
+
+class IpcBuffer:
+    """A device allocation of this process that other processes of the node can map (CUDA IPC).
+
+    ``tensor(dtype)`` views it as a flat tensor; ``handle()`` gives the bytes another process
+    passes to ``IpcMapping``.  The allocation is freed when the object and every tensor view of it
+    are gone."""
+
+    def __init__(self, nbytes: int, device: torch.device):
+        self.nbytes, self.device = int(nbytes), device
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _call("ff_ipc_alloc", self.nbytes, ctypes.byref(ptr))
+        self.ptr = int(ptr.value)
+        self._lib = lib()
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        with torch.cuda.device(self.device):
+            _call("ff_ipc_get_handle", self.ptr, buf)
+        return buf.raw
+
+    def tensor(self, dtype: torch.dtype) -> torch.Tensor:
+        """The whole allocation as a flat tensor of ``dtype`` (it keeps this object alive)."""
+        iface = {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False), "version": 3,
+                 "strides": None}
+        holder = type("_IpcView", (), {"__cuda_array_interface__": iface, "owner": self})()
+        return torch.as_tensor(holder, device=self.device).view(dtype)
+
+    def __del__(self):
+        try:
+            with torch.cuda.device(self.device):
+                self._lib.ff_ipc_free(ctypes.c_void_p(self.ptr))
+        except Exception:
+            pass
+
+
+class IpcMapping:
+    """Another process's ``IpcBuffer`` mapped into this process (``ptr``: its device address here)."""
+
+    def __init__(self, handle: bytes, device: torch.device):
+        if len(handle) != IPC_HANDLE_BYTES:
+            raise ValueError(f"IpcMapping: a handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+        self.device = device
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _call("ff_ipc_open", handle, ctypes.byref(ptr))
+        self.ptr = int(ptr.value)
+        self._lib = lib()
+
+    def close(self) -> None:
+        if self.ptr:
+            with torch.cuda.device(self.device):
+                _call("ff_ipc_close", self.ptr)
+            self.ptr = 0
+
+    def __del__(self):
+        try:
+            if self.ptr:
+                with torch.cuda.device(self.device):
+                    self._lib.ff_ipc_close(ctypes.c_void_p(self.ptr))
+        except Exception:
+            pass
 
 
 def update_int8_weight(w: torch.Tensor, dq: torch.Tensor) -> None:

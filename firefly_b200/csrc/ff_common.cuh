@@ -10,6 +10,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/firefly_b200.h"
@@ -239,6 +240,17 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
   f2 r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
   return r;
+}
+
+// bf16x2 words: element 2k in the low half, 2k+1 in the high half
+__device__ __forceinline__ uint32_t pack_bf16x2(f2 v) {
+  float a, b;
+  un2(v, a, b);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ f2 unpack_bf16x2(uint32_t w) {
+  return mk2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
 // low bytes of four words packed into one word (byte k = low byte of the k-th argument)

@@ -56,6 +56,13 @@ constexpr int kTabBytes = 256 * 256;  // 256 codes x (32 signed + 32 unsigned co
 constexpr int kStageOffQ = 512, kStageOffM = 768, kStageOffV = 1024, kStageOffR = 1280, kStageOffU = 1536;
 __host__ __device__ constexpr int stage_bytes(bool has_u) { return has_u ? 2560 : 1536; }
 __host__ __device__ constexpr int smem_bytes(bool has_u) { return kTabBytes + kWarps * 2 * stage_bytes(has_u) + kWarps * 2 * 8; }
+// Data-parallel mode (several gradient sources): the stage holds one 512-byte gradient block per
+// source, in source order, then q, m, v, r (256 bytes each)
+constexpr int kMaxSources = FF_DQT_MAX_SOURCES;
+__host__ __device__ constexpr int stage_bytes_multi(int nsrc) { return 512 * nsrc + 1024; }
+__host__ __device__ constexpr int smem_bytes_multi(int nsrc) {
+  return kTabBytes + kWarps * 2 * stage_bytes_multi(nsrc) + kWarps * 2 * 8;
+}
 constexpr float kMagic = 12582912.0f;     // 1.5 * 2^23
 // rows with lr / max(ws, eps) above this take the step-by-step chain (see exact_pair)
 constexpr float kFastRatio = 16.f;
@@ -86,6 +93,14 @@ struct Params {
   const float* u;
   const float* dec_s;
   const float* dec_u;
+  // data-parallel mode: the gradient is the average of the nsrc bf16 arrays gsrc[0..nsrc) (summed in
+  // fp32 in that order, times inv_nsrc, rounded to bf16); the new weights go to the nqdst arrays
+  // qdst[0..nqdst) (q itself among them); gout (or null) receives the averaged gradient
+  const uint16_t* gsrc[kMaxSources];
+  int8_t* qdst[kMaxSources];
+  uint16_t* gout;
+  int nsrc, nqdst;
+  float inv_nsrc;
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -328,27 +343,58 @@ __device__ __forceinline__ float ld_tab(uint32_t base, uint32_t off) {
 // The per-block work of one warp (8 elements per lane).  ROWS: 0 = row_len a multiple of 8 (a
 // lane's 8 elements share one weight row), 1 = row_len >= 8 (they span at most two rows),
 // 2 = row_len < 8.  TAB: the shared address of the decode rows when known at compile time (the
-// kernel dispatches on the usual values), else -1.
-template <bool HAS_U, int ROWS, int TAB>
+// kernel dispatches on the usual values), else -1.  MULTI: data-parallel mode (gradient sources
+// gsrc, weight destinations qdst; the stage layout of stage_bytes_multi).
+template <bool HAS_U, int ROWS, int TAB, bool MULTI>
 __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
-  constexpr int kStage = stage_bytes(HAS_U);
+  static_assert(!(HAS_U && MULTI), "supplied uniforms and several gradient sources are not combined");
+  const int kStage = MULTI ? stage_bytes_multi(p.nsrc) : stage_bytes(HAS_U);
+  const int offQ = MULTI ? 512 * p.nsrc : kStageOffQ;  // q, m, v, r follow the gradient blocks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* my_stage = smem + kTabBytes + warp * 2 * kStage;
   const uint32_t bar0 = smem_addr(smem + kTabBytes + kWarps * 2 * kStage) + warp * 16;
   const uint32_t tab_base = smem_addr(smem);
   const uint32_t lane4 = 4u * lane;
-  const uint32_t stage_bytes_tx = 512 + 4 * 256 + (HAS_U ? 1024 : 0);
+  const uint32_t stage_bytes_tx = MULTI ? (uint32_t)stage_bytes_multi(p.nsrc) : 512 + 4 * 256 + (HAS_U ? 1024 : 0);
   // lane 0 stages block b (a full block) into stage s
   auto prefetch = [&](int64_t b, int s) {
     const uint32_t dst = smem_addr(my_stage + s * kStage), bar = bar0 + 8 * s;
     const int64_t e = b * kBlock;
     bar_expect(bar, stage_bytes_tx);
-    bulk_g2s(dst, p.g + e, 512, bar);
-    bulk_g2s(dst + kStageOffQ, p.q + e, 256, bar);
-    bulk_g2s(dst + kStageOffM, p.m_q + e, 256, bar);
-    bulk_g2s(dst + kStageOffV, p.v_q + e, 256, bar);
-    bulk_g2s(dst + kStageOffR, p.r_q + e, 256, bar);
+    if constexpr (MULTI) {  // every source's gradient block (peers' over NVLink, no multicast)
+#pragma unroll
+      for (int k = 0; k < kMaxSources; ++k)
+        if (k < p.nsrc) bulk_g2s(dst + 512 * k, p.gsrc[k] + e, 512, bar);
+    } else {
+      bulk_g2s(dst, p.g + e, 512, bar);
+    }
+    bulk_g2s(dst + offQ, p.q + e, 256, bar);
+    bulk_g2s(dst + offQ + 256, p.m_q + e, 256, bar);
+    bulk_g2s(dst + offQ + 512, p.v_q + e, 256, bar);
+    bulk_g2s(dst + offQ + 768, p.r_q + e, 256, bar);
     if constexpr (HAS_U) bulk_g2s(dst + kStageOffU, p.u + e, 1024, bar);
+  };
+  // data-parallel mode: the averaged gradient of a lane's 8 elements from the sources' words
+  // (src(k) returns source k's 4 words), fp32 sums in source order, rounded to bf16
+  auto average = [&](auto src, uint32_t (&gw)[4]) {
+    f2 acc[4];
+    {
+      const uint4 w = src(0);
+      acc[0] = unpack_bf16x2(w.x); acc[1] = unpack_bf16x2(w.y); acc[2] = unpack_bf16x2(w.z); acc[3] = unpack_bf16x2(w.w);
+    }
+#pragma unroll
+    for (int k = 1; k < kMaxSources; ++k) {
+      if (k < p.nsrc) {
+        const uint4 w = src(k);
+        acc[0] = add2(acc[0], unpack_bf16x2(w.x));
+        acc[1] = add2(acc[1], unpack_bf16x2(w.y));
+        acc[2] = add2(acc[2], unpack_bf16x2(w.z));
+        acc[3] = add2(acc[3], unpack_bf16x2(w.w));
+      }
+    }
+    const f2 inv = splat(p.inv_nsrc);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) gw[k] = pack_bf16x2(mul2(acc[k], inv));
   };
   const int64_t full_blocks = p.numel / kBlock;  // blocks [0, full_blocks) have 256 elements
   const int64_t nblocks = (p.numel + kBlock - 1) / kBlock;
@@ -522,13 +568,24 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     }
     if (nvalid == 8) {
       // generic-proxy stores; the bulk copies only ever read other blocks
-      *reinterpret_cast<uint2*>(p.q + e0) = make_uint2(pack_magic4(cq[0], cq[1], cq[2], cq[3]), pack_magic4(cq[4], cq[5], cq[6], cq[7]));
+      const uint2 qv = make_uint2(pack_magic4(cq[0], cq[1], cq[2], cq[3]), pack_magic4(cq[4], cq[5], cq[6], cq[7]));
+      if constexpr (MULTI) {  // every rank's copy of the weights (peers' over NVLink)
+#pragma unroll
+        for (int k = 0; k < kMaxSources; ++k)
+          if (k < p.nqdst) *reinterpret_cast<uint2*>(p.qdst[k] + e0) = qv;
+      } else {
+        *reinterpret_cast<uint2*>(p.q + e0) = qv;
+      }
       *reinterpret_cast<uint2*>(p.m_q + e0) = make_uint2(pack_magic4(cm[0], cm[1], cm[2], cm[3]), pack_magic4(cm[4], cm[5], cm[6], cm[7]));
       *reinterpret_cast<uint2*>(p.v_q + e0) = make_uint2(pack_magic4(cv[0], cv[1], cv[2], cv[3]), pack_magic4(cv[4], cv[5], cv[6], cv[7]));
       *reinterpret_cast<uint2*>(p.r_q + e0) = make_uint2(pack_magic4(cr[0], cr[1], cr[2], cr[3]), pack_magic4(cr[4], cr[5], cr[6], cr[7]));
     } else {
       for (int j = 0; j < nvalid; ++j) {
-        p.q[e0 + j] = (int8_t)__float_as_uint(cq[j]);
+        if constexpr (MULTI) {
+          for (int k = 0; k < p.nqdst; ++k) p.qdst[k][e0 + j] = (int8_t)__float_as_uint(cq[j]);
+        } else {
+          p.q[e0 + j] = (int8_t)__float_as_uint(cq[j]);
+        }
         p.m_q[e0 + j] = (uint8_t)__float_as_uint(cm[j]);
         p.v_q[e0 + j] = (uint8_t)__float_as_uint(cv[j]);
         p.r_q[e0 + j] = (uint8_t)__float_as_uint(cr[j]);
@@ -574,12 +631,18 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
     if (!bar_wait(bar0 + 8 * stg, (it >> 1) & 1)) return;  // copies lost: status raised
     const uint8_t* sb = my_stage + stg * kStage;
-    const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
-    const uint2 q2 = *reinterpret_cast<const uint2*>(sb + kStageOffQ + lane * 8);
-    const uint2 m2 = *reinterpret_cast<const uint2*>(sb + kStageOffM + lane * 8);
-    const uint2 v2 = *reinterpret_cast<const uint2*>(sb + kStageOffV + lane * 8);
-    const uint2 r2 = *reinterpret_cast<const uint2*>(sb + kStageOffR + lane * 8);
-    const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+    uint32_t gw[4];
+    if constexpr (MULTI) {
+      average([&](int k) { return *reinterpret_cast<const uint4*>(sb + 512 * k + lane * 16); }, gw);
+      if (p.gout) *reinterpret_cast<uint4*>(p.gout + blk * kBlock + lane * 8) = make_uint4(gw[0], gw[1], gw[2], gw[3]);
+    } else {
+      const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
+      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
+    }
+    const uint2 q2 = *reinterpret_cast<const uint2*>(sb + offQ + lane * 8);
+    const uint2 m2 = *reinterpret_cast<const uint2*>(sb + offQ + 256 + lane * 8);
+    const uint2 v2 = *reinterpret_cast<const uint2*>(sb + offQ + 512 + lane * 8);
+    const uint2 r2 = *reinterpret_cast<const uint2*>(sb + offQ + 768 + lane * 8);
     const uint32_t qw[2] = {q2.x, q2.y}, mw[2] = {m2.x, m2.y}, vw[2] = {v2.x, v2.y}, rw[2] = {r2.x, r2.y};
     float u[HAS_U ? 8 : 1];
     if constexpr (HAS_U) {
@@ -604,12 +667,16 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     uint32_t gw[4], qw[2], mw[2], vw[2], rw[2];
     float u[HAS_U ? 8 : 1];
     if (nvalid == 8) {
-      const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(p.g + e0));
+      if constexpr (MULTI) {  // plain loads: the peers' arrays are not read-only data of this kernel
+        average([&](int k) { return *reinterpret_cast<const uint4*>(p.gsrc[k] + e0); }, gw);
+      } else {
+        const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(p.g + e0));
+        gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
+      }
       const uint2 q2 = *reinterpret_cast<const uint2*>(p.q + e0);
       const uint2 m2 = *reinterpret_cast<const uint2*>(p.m_q + e0);
       const uint2 v2 = *reinterpret_cast<const uint2*>(p.v_q + e0);
       const uint2 r2 = *reinterpret_cast<const uint2*>(p.r_q + e0);
-      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
       qw[0] = q2.x; qw[1] = q2.y; mw[0] = m2.x; mw[1] = m2.y;
       vw[0] = v2.x; vw[1] = v2.y; rw[0] = r2.x; rw[1] = r2.y;
       if constexpr (HAS_U) {
@@ -627,13 +694,25 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
       for (int j = 0; j < 8; ++j) {
         if (j < nvalid) {
           const int sh = 8 * (j & 3), w = j >> 2;
-          gw[j >> 1] |= (uint32_t)p.g[e0 + j] << (16 * (j & 1));
+          if constexpr (!MULTI) gw[j >> 1] |= (uint32_t)p.g[e0 + j] << (16 * (j & 1));
           qw[w] |= ((uint32_t)(uint8_t)p.q[e0 + j]) << sh;
           mw[w] = (mw[w] & ~(0xFFu << sh)) | ((uint32_t)p.m_q[e0 + j] << sh);
           vw[w] |= (uint32_t)p.v_q[e0 + j] << sh;
           rw[w] = (rw[w] & ~(0xFFu << sh)) | ((uint32_t)p.r_q[e0 + j] << sh);
         }
         if constexpr (HAS_U) u[j] = j < nvalid ? __ldg(p.u + e0 + j) : 2.f;
+      }
+      if constexpr (MULTI) {  // the same average, missing elements 0 in every source
+        average([&](int k) {
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          for (int j = 0; j < nvalid; ++j) w[j >> 1] |= (uint32_t)p.gsrc[k][e0 + j] << (16 * (j & 1));
+          return make_uint4(w[0], w[1], w[2], w[3]);
+        }, gw);
+      }
+    }
+    if constexpr (MULTI) {
+      if (p.gout) {
+        for (int j = 0; j < nvalid; ++j) p.gout[e0 + j] = (uint16_t)(gw[j >> 1] >> (16 * (j & 1)));
       }
     }
     const int64_t ge = p.elem_base + min64(e0, p.numel - 1);
@@ -647,10 +726,10 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
   }
 }
 
-template <bool HAS_U, int ROWS>
+template <bool HAS_U, int ROWS, bool MULTI>
 __global__ void __launch_bounds__(kThreads, HAS_U ? 1 : kCtasPerSm) dqt_adamw8_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];  // decode rows, then staging, then barriers
-  constexpr int kStage = stage_bytes(HAS_U);
+  const int kStage = MULTI ? stage_bytes_multi(p.nsrc) : stage_bytes(HAS_U);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // decode rows: word 64*c + l = signed entry of code c, word 64*c + 32 + l = unsigned entry
   {
@@ -669,42 +748,64 @@ __global__ void __launch_bounds__(kThreads, HAS_U ? 1 : kCtasPerSm) dqt_adamw8_k
   __syncthreads();
   const uint32_t base = smem_addr(smem);
   if (base == 0)
-    dqt_run<HAS_U, ROWS, 0>(p, smem);
+    dqt_run<HAS_U, ROWS, 0, MULTI>(p, smem);
   else if (base == 1024)
-    dqt_run<HAS_U, ROWS, 1024>(p, smem);
+    dqt_run<HAS_U, ROWS, 1024, MULTI>(p, smem);
   else
-    dqt_run<HAS_U, ROWS, -1>(p, smem);
+    dqt_run<HAS_U, ROWS, -1, MULTI>(p, smem);
+  // the weights stored into the peers' memory are visible to them once the kernel has ended (the
+  // host orders the peers' next reads after it with a collective)
+  if constexpr (MULTI) __threadfence_system();
 }
 
 }  // namespace optim
 }  // namespace ff
 
-extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base, const uint16_t* g,
-                             uint8_t* m_q, float* m_absmax, uint8_t* v_q, float* v_absmax, uint8_t* r_q,
-                             float* r_absmax, int64_t numel, int64_t block, double lr, double beta1,
-                             double beta2, double eps, double wd, double bc1, double bc2, double sr_bias,
-                             uint64_t seed, uint64_t step,
-                             int64_t rng_offset, const float* u, const float* dec_s, const float* dec_u,
-                             void* stream) {
-  using namespace ff;
-  using namespace ff::optim;
-  FF_REQUIRE(numel >= 0 && row_len >= 1 && elem_base >= 0 && rng_offset >= 0, FF_ERR_INVALID_ARG,
-             "ff_dqt_adamw8: bad sizes");
-  FF_REQUIRE(block == kBlock, FF_ERR_UNSUPPORTED, "ff_dqt_adamw8: block must be %d (got %lld)", kBlock,
-             (long long)block);
+
+namespace ff {
+namespace optim {
+
+// One launch of the update over `numel` elements.  nsrc == 0: the single-source kernel (g; u for
+// supplied uniforms); nsrc >= 1: the data-parallel kernel (gradient sources gsrc, weight
+// destinations qdst, optional averaged-gradient output gout).
+inline int dqt_launch(const char* name, int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base,
+                      const uint16_t* g, uint8_t* m_q, float* m_absmax, uint8_t* v_q, float* v_absmax, uint8_t* r_q,
+                      float* r_absmax, int64_t numel, int64_t block, double lr, double beta1, double beta2,
+                      double eps, double wd, double bc1, double bc2, double sr_bias, uint64_t seed, uint64_t step,
+                      int64_t rng_offset, const float* u, const float* dec_s, const float* dec_u,
+                      const uint16_t* const* gsrc, int nsrc, int8_t* const* qdst, int nqdst, uint16_t* gout,
+                      void* stream) {
+  const bool multi = nsrc > 0;
+  FF_REQUIRE(numel >= 0 && row_len >= 1 && elem_base >= 0 && rng_offset >= 0, FF_ERR_INVALID_ARG, "%s: bad sizes",
+             name);
+  FF_REQUIRE(block == kBlock, FF_ERR_UNSUPPORTED, "%s: block must be %d (got %lld)", name, kBlock, (long long)block);
+  FF_REQUIRE(nsrc >= 0 && nsrc <= kMaxSources && (!multi || (nqdst >= 1 && nqdst <= kMaxSources)),
+             FF_ERR_INVALID_ARG, "%s: %d gradient sources and %d weight destinations (1 to %d each)", name, nsrc,
+             nqdst, kMaxSources);
   if (numel == 0) return FF_OK;
-  FF_REQUIRE(q && wscale && g && m_q && m_absmax && v_q && v_absmax && r_q && r_absmax && dec_s && dec_u,
-             FF_ERR_INVALID_ARG, "ff_dqt_adamw8: null pointer");
-  FF_REQUIRE(aligned(g, 16) && aligned(q, 8) && aligned(m_q, 8) && aligned(v_q, 8) && aligned(r_q, 8),
-             FF_ERR_UNSUPPORTED, "ff_dqt_adamw8: g needs 16-byte and code arrays 8-byte alignment");
-  FF_REQUIRE(rng_offset % 8 == 0, FF_ERR_UNSUPPORTED, "ff_dqt_adamw8: rng_offset must be a multiple of 8");
-  FF_REQUIRE(bc1 > 0.0 && bc2 > 0.0, FF_ERR_INVALID_ARG, "ff_dqt_adamw8: bias corrections must be > 0");
+  FF_REQUIRE(q && wscale && (multi || g) && m_q && m_absmax && v_q && v_absmax && r_q && r_absmax && dec_s && dec_u,
+             FF_ERR_INVALID_ARG, "%s: null pointer", name);
+  FF_REQUIRE((multi || aligned(g, 16)) && aligned(q, 8) && aligned(m_q, 8) && aligned(v_q, 8) && aligned(r_q, 8),
+             FF_ERR_UNSUPPORTED, "%s: g needs 16-byte and code arrays 8-byte alignment", name);
+  for (int k = 0; k < nsrc; ++k) {
+    FF_REQUIRE(gsrc[k], FF_ERR_INVALID_ARG, "%s: null gradient source %d", name, k);
+    FF_REQUIRE(aligned(gsrc[k], 16), FF_ERR_UNSUPPORTED, "%s: gradient source %d needs 16-byte alignment", name, k);
+  }
+  for (int k = 0; multi && k < nqdst; ++k) {
+    FF_REQUIRE(qdst[k], FF_ERR_INVALID_ARG, "%s: null weight destination %d", name, k);
+    FF_REQUIRE(aligned(qdst[k], 8), FF_ERR_UNSUPPORTED, "%s: weight destination %d needs 8-byte alignment", name, k);
+  }
+  FF_REQUIRE(!gout || aligned(gout, 16), FF_ERR_UNSUPPORTED, "%s: the averaged-gradient output needs 16-byte alignment",
+             name);
+  FF_REQUIRE(!(multi && u), FF_ERR_UNSUPPORTED, "%s: supplied uniforms take a single gradient source", name);
+  FF_REQUIRE(rng_offset % 8 == 0, FF_ERR_UNSUPPORTED, "%s: rng_offset must be a multiple of 8", name);
+  FF_REQUIRE(bc1 > 0.0 && bc2 > 0.0, FF_ERR_INVALID_ARG, "%s: bias corrections must be > 0", name);
   Params p;
   p.q = q;
   p.wscale = wscale;
   p.row_len = row_len;
   p.elem_base = elem_base;
-  p.g = g;
+  p.g = multi ? gsrc[0] : g;
   p.m_q = m_q;
   p.m_absmax = m_absmax;
   p.v_q = v_q;
@@ -743,44 +844,97 @@ extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, in
   p.u = u;
   p.dec_s = dec_s;
   p.dec_u = dec_u;
+  for (int k = 0; k < kMaxSources; ++k) {
+    p.gsrc[k] = k < nsrc ? gsrc[k] : nullptr;
+    p.qdst[k] = multi && k < nqdst ? qdst[k] : nullptr;
+  }
+  p.gout = gout;
+  p.nsrc = nsrc;
+  p.nqdst = multi ? nqdst : 0;
+  p.inv_nsrc = multi ? (float)(1.0 / nsrc) : 1.f;
+  // bulk staging needs every staged array 16-byte aligned (the sources were checked above)
   p.bulk = aligned(q, 16) && aligned(m_q, 16) && aligned(v_q, 16) && aligned(r_q, 16) && (!u || aligned(u, 16));
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    const void* fns_u[] = {(const void*)dqt_adamw8_kernel<true, 0>, (const void*)dqt_adamw8_kernel<true, 1>,
-                           (const void*)dqt_adamw8_kernel<true, 2>};
-    const void* fns[] = {(const void*)dqt_adamw8_kernel<false, 0>, (const void*)dqt_adamw8_kernel<false, 1>,
-                         (const void*)dqt_adamw8_kernel<false, 2>};
+    const void* fns_u[] = {(const void*)dqt_adamw8_kernel<true, 0, false>, (const void*)dqt_adamw8_kernel<true, 1, false>,
+                           (const void*)dqt_adamw8_kernel<true, 2, false>};
+    const void* fns[] = {(const void*)dqt_adamw8_kernel<false, 0, false>, (const void*)dqt_adamw8_kernel<false, 1, false>,
+                         (const void*)dqt_adamw8_kernel<false, 2, false>};
+    const void* fns_m[] = {(const void*)dqt_adamw8_kernel<false, 0, true>, (const void*)dqt_adamw8_kernel<false, 1, true>,
+                           (const void*)dqt_adamw8_kernel<false, 2, true>};
     for (const void* fn : fns_u)
       FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(true)),
                   "ff_dqt_adamw8 smem attribute");
     for (const void* fn : fns)
       FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(false)),
                   "ff_dqt_adamw8 smem attribute");
+    for (const void* fn : fns_m)
+      FF_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes_multi(kMaxSources)),
+                  "ff_dqt_adamw8 smem attribute");
     attr_set[dev] = true;
   }
   const int64_t nblocks = (numel + kBlock - 1) / kBlock;
   int nsm = 148;
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  int smem_sm = 0;
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  const int smem = u ? smem_bytes(true) : multi ? smem_bytes_multi(nsrc) : smem_bytes(false);
+  // CTAs per SM: two unless their shared memory (plus the 1 KiB the runtime reserves per CTA) does not fit
+  const int per_sm = u ? 1 : (2 * (smem + 1024) <= smem_sm ? kCtasPerSm : 1);
   const int64_t want = (nblocks + kWarps - 1) / kWarps;
-  const int grid = (int)min64(want, (int64_t)nsm * (u ? 1 : kCtasPerSm));
+  const int grid = (int)min64(want, (int64_t)nsm * per_sm);
   const int64_t stride_elems = (int64_t)grid * kWarps * kBlock;
   p.row_step = stride_elems / row_len;
   p.in_row_step = stride_elems % row_len;
   cudaStream_t st = as_stream(stream);
   // a lane's 8 elements start at a multiple of 8 of the weight when elem_base is one
   const int rows_mode = (row_len % 8 == 0 && elem_base % 8 == 0) ? 0 : (row_len >= 8 ? 1 : 2);
-#define FF_DQT_LAUNCH(HU, RM) dqt_adamw8_kernel<HU, RM><<<grid, kThreads, smem_bytes(HU), st>>>(p)
+#define FF_DQT_LAUNCH(HU, RM, MU) dqt_adamw8_kernel<HU, RM, MU><<<grid, kThreads, smem, st>>>(p)
   if (u) {
-    if (rows_mode == 0) FF_DQT_LAUNCH(true, 0);
-    else if (rows_mode == 1) FF_DQT_LAUNCH(true, 1);
-    else FF_DQT_LAUNCH(true, 2);
+    if (rows_mode == 0) FF_DQT_LAUNCH(true, 0, false);
+    else if (rows_mode == 1) FF_DQT_LAUNCH(true, 1, false);
+    else FF_DQT_LAUNCH(true, 2, false);
+  } else if (multi) {
+    if (rows_mode == 0) FF_DQT_LAUNCH(false, 0, true);
+    else if (rows_mode == 1) FF_DQT_LAUNCH(false, 1, true);
+    else FF_DQT_LAUNCH(false, 2, true);
   } else {
-    if (rows_mode == 0) FF_DQT_LAUNCH(false, 0);
-    else if (rows_mode == 1) FF_DQT_LAUNCH(false, 1);
-    else FF_DQT_LAUNCH(false, 2);
+    if (rows_mode == 0) FF_DQT_LAUNCH(false, 0, false);
+    else if (rows_mode == 1) FF_DQT_LAUNCH(false, 1, false);
+    else FF_DQT_LAUNCH(false, 2, false);
   }
 #undef FF_DQT_LAUNCH
-  return check_launch("ff_dqt_adamw8");
+  return check_launch(name);
+}
+
+}  // namespace optim
+}  // namespace ff
+
+extern "C" int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base, const uint16_t* g,
+                             uint8_t* m_q, float* m_absmax, uint8_t* v_q, float* v_absmax, uint8_t* r_q,
+                             float* r_absmax, int64_t numel, int64_t block, double lr, double beta1,
+                             double beta2, double eps, double wd, double bc1, double bc2, double sr_bias,
+                             uint64_t seed, uint64_t step,
+                             int64_t rng_offset, const float* u, const float* dec_s, const float* dec_u,
+                             void* stream) {
+  return ff::optim::dqt_launch("ff_dqt_adamw8", q, wscale, row_len, elem_base, g, m_q, m_absmax, v_q, v_absmax, r_q,
+                               r_absmax, numel, block, lr, beta1, beta2, eps, wd, bc1, bc2, sr_bias, seed, step,
+                               rng_offset, u, dec_s, dec_u, nullptr, 0, nullptr, 0, nullptr, stream);
+}
+
+extern "C" int ff_dqt_adamw8_peers(int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base,
+                                   const uint16_t* const* g_srcs, int n_srcs, int8_t* const* q_dsts, int n_dsts,
+                                   uint16_t* g_out, uint8_t* m_q, float* m_absmax, uint8_t* v_q, float* v_absmax,
+                                   uint8_t* r_q, float* r_absmax, int64_t numel, int64_t block, double lr,
+                                   double beta1, double beta2, double eps, double wd, double bc1, double bc2,
+                                   double sr_bias, uint64_t seed, uint64_t step, int64_t rng_offset,
+                                   const float* dec_s, const float* dec_u, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(g_srcs && q_dsts && n_srcs >= 1, FF_ERR_INVALID_ARG, "ff_dqt_adamw8_peers: no gradient sources");
+  return ff::optim::dqt_launch("ff_dqt_adamw8_peers", q, wscale, row_len, elem_base, nullptr, m_q, m_absmax, v_q,
+                               v_absmax, r_q, r_absmax, numel, block, lr, beta1, beta2, eps, wd, bc1, bc2, sr_bias,
+                               seed, step, rng_offset, nullptr, dec_s, dec_u, g_srcs, n_srcs, q_dsts, n_dsts, g_out,
+                               stream);
 }

@@ -77,3 +77,46 @@ extern "C" int ff_quant_dual_i8_noalloc(const void* x, int dtype, int64_t rows, 
   return ff_quant_dual_i8(x, dtype, rows, cols, ldx, row_colmul, eps, q_rows, ldq, s_rows, q_cols_t, ldqt,
                           s_cols, static_cast<float*>(addr), stream);
 }
+
+// ---------------------------------------------------------------------------
+// Device memory shared between the processes of one node (CUDA IPC): the data-parallel
+// optimizer's weight and gradient arenas, which every rank's update kernel reads and writes
+// over NVLink.  ff_ipc_alloc returns a whole cudaMalloc allocation (IPC handles name
+// allocations); the handle (FF_IPC_HANDLE_BYTES bytes) is opened in another process with
+// ff_ipc_open, which maps the allocation there and enables peer access.
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == FF_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int ff_ipc_alloc(int64_t bytes, void** ptr) {
+  FF_REQUIRE(ptr && bytes > 0, FF_ERR_INVALID_ARG, "ff_ipc_alloc: bytes=%lld", (long long)bytes);
+  *ptr = nullptr;
+  FF_CUDA_TRY(cudaMalloc(ptr, (size_t)bytes), "ff_ipc_alloc");
+  return FF_OK;
+}
+
+extern "C" int ff_ipc_free(void* ptr) {
+  if (ptr) FF_CUDA_TRY(cudaFree(ptr), "ff_ipc_free");
+  return FF_OK;
+}
+
+extern "C" int ff_ipc_get_handle(void* ptr, uint8_t* handle) {
+  FF_REQUIRE(ptr && handle, FF_ERR_INVALID_ARG, "ff_ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  FF_CUDA_TRY(cudaIpcGetMemHandle(&h, ptr), "ff_ipc_get_handle");
+  memcpy(handle, &h, sizeof(h));
+  return FF_OK;
+}
+
+extern "C" int ff_ipc_open(const uint8_t* handle, void** ptr) {
+  FF_REQUIRE(handle && ptr, FF_ERR_INVALID_ARG, "ff_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  FF_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ff_ipc_open");
+  return FF_OK;
+}
+
+extern "C" int ff_ipc_close(void* ptr) {
+  if (ptr) FF_CUDA_TRY(cudaIpcCloseMemHandle(ptr), "ff_ipc_close");
+  return FF_OK;
+}

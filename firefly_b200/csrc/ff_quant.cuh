@@ -146,16 +146,6 @@ __device__ __forceinline__ float rcp_approx_ftz(float x) {
   return y;
 }
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-// bf16x2 words: element 2k in the low half, 2k+1 in the high half
-__device__ __forceinline__ uint32_t pack_bf16x2(f2 v) {
-  float a, b;
-  un2(v, a, b);
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ f2 unpack_bf16x2(uint32_t w) {
-  return mk2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-}
 __device__ __forceinline__ uint32_t abs_bf16x2(uint32_t w) { return w & 0x7FFF7FFFu; }
 __device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   uint32_t d;

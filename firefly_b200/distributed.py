@@ -164,7 +164,8 @@ class BitArena:
     """
 
     def __init__(self, modules: Sequence[BitLinear], world_size: int = 1, rank: int = 0,
-                 device: torch.device | None = None, bucket_elems: int = 0):
+                 device: torch.device | None = None, bucket_elems: int = 0,
+                 alloc: Callable[[int], tuple[torch.Tensor, torch.Tensor]] | None = None):
         self.modules = list(modules)
         if not self.modules:
             raise ValueError("BitArena needs at least one BitLinear")
@@ -172,8 +173,13 @@ class BitArena:
         self.plan = ShardPlan([m.int_weight.numel() for m in self.modules], world_size, rank,
                               bucket_elems=bucket_elems)
         assert self.plan.rng_offsets == bit_rng_offsets(self.modules)
-        self.q = torch.zeros(self.plan.total, dtype=torch.int8, device=device)
-        self.g = torch.zeros(self.plan.total, dtype=torch.bfloat16, device=device)
+        if alloc is None:
+            self.q = torch.zeros(self.plan.total, dtype=torch.int8, device=device)
+            self.g = torch.zeros(self.plan.total, dtype=torch.bfloat16, device=device)
+        else:  # caller-provided memory (int8 and bf16 arrays of plan.total elements), zeroed here
+            self.q, self.g = alloc(self.plan.total)
+            self.q.zero_()
+            self.g.zero_()
         self.g_views = []
         for m, off in zip(self.modules, self.plan.offsets):
             n = m.int_weight.numel()
@@ -246,7 +252,7 @@ class ZeroFireFlyOptim:
     def __init__(self, bit_modules: Sequence[BitLinear], params=(), lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
                  weight_decay=0.1, block_size=256, sr_bias_scale=0.15, process_group=None,
                  update_fn: Callable | None = None, seed: int | None = None, bucket_mb: float = 256.0,
-                 overlap: bool = True):
+                 overlap: bool = True, peer: bool | None = None):
         if int(block_size) != BLOCK:
             raise ValueError(f"block_size must be {BLOCK} on this build")
         self.group = process_group
@@ -259,7 +265,37 @@ class ZeroFireFlyOptim:
         self.lr, self.betas, self.eps, self.wd = float(lr), tuple(betas), float(eps), float(weight_decay)
         self.sr_bias_scale = float(sr_bias_scale)
         bucket_elems = int(bucket_mb * 2**20) // 2 if bucket_mb and bucket_mb > 0 else 0
-        self.arena = BitArena(self.modules, self.world, self.rank, bucket_elems=bucket_elems)
+        self._nccl = self.world > 1 and dist.get_backend(self.group) == "nccl"
+        # host-side agreement on which modules have gradients (no GPU synchronisation)
+        self._host_group = None
+        if self.world > 1:
+            if dist.get_backend(self.group) == "gloo":
+                self._host_group = self.group
+            else:
+                ranks = None if self.group is None else dist.get_process_group_ranks(self.group)
+                self._host_group = dist.new_group(ranks=ranks, backend="gloo")
+        # peer mode: the ranks of one node read each other's gradient arena and write each other's
+        # weight arena from the update kernel (ff_dqt_adamw8_peers) instead of the collectives
+        want_peer = (peer is None or peer) and self._nccl and 2 <= self.world <= _capi.DQT_MAX_SOURCES and \
+            update_fn is None
+        if peer and not want_peer:
+            raise ValueError("peer=True needs an NCCL process group of 2 to 8 ranks and the kernel update")
+        self._ipc = None
+        alloc = None
+        if want_peer:
+            dev0 = self.modules[0].int_weight.device
+
+            def alloc(total, dev0=dev0):  # raises RuntimeError when the allocation fails
+                qb, gb = _capi.IpcBuffer(total, dev0), _capi.IpcBuffer(2 * total, dev0)
+                self._ipc = [qb, gb]
+                return qb.tensor(torch.int8), gb.tensor(torch.bfloat16)
+        try:
+            self.arena = BitArena(self.modules, self.world, self.rank, bucket_elems=bucket_elems, alloc=alloc)
+        except (RuntimeError, ValueError):
+            if alloc is None:
+                raise
+            self._ipc = None  # no shareable memory here: the collectives path
+            self.arena = BitArena(self.modules, self.world, self.rank, bucket_elems=bucket_elems)
         self.plan = self.arena.plan
         dev = self.arena.q.device
         n = self.plan.shard
@@ -290,20 +326,21 @@ class ZeroFireFlyOptim:
                 dist.broadcast(p.data, src=0, group=self.group)
         for m in self.modules:
             _invalidate_weight_cache(m._registered_handle)
-        # overlapped gradient reduction
-        self._nccl = self.world > 1 and dist.get_backend(self.group) == "nccl"
-        # host-side agreement on which modules have gradients (no GPU synchronisation)
-        self._host_group = None
-        if self.world > 1:
-            if dist.get_backend(self.group) == "gloo":
-                self._host_group = self.group
-            else:
-                ranks = None if self.group is None else dist.get_process_group_ranks(self.group)
-                self._host_group = dist.new_group(ranks=ranks, backend="gloo")
+        self.peer = False
+        self._peer_maps: list = []
+        if want_peer:
+            self.peer = self._connect_peers()
+            if peer and not self.peer:
+                raise RuntimeError("peer=True: the ranks could not map each other's arenas")
+        # with peer mode: the averaged gradient of this rank's shard is also written to g_shard
+        self.keep_reduced_grad = False
         self._sync = True
+        # None, or a list to which step() appends (phase, start event, end event) triples timing on
+        # the current stream each wait for a collective (its exposed part) and the whole step
+        self.comm_events: list | None = None
         self._module_of = {m._registered_handle: i for i, m in enumerate(self.modules)}
         self._reset_pending()
-        self.overlap = bool(overlap) and self.world > 1
+        self.overlap = bool(overlap) and self.world > 1 and not self.peer  # peer mode reduces in the update
         if self.overlap:
             # the hooks hold the optimizer weakly: a discarded optimizer stops reducing
             ref = weakref.ref(self)
@@ -318,11 +355,84 @@ class ZeroFireFlyOptim:
 
     def close(self) -> None:
         """Remove this optimizer's gradient hooks from its modules (later backward passes no
-        longer start reductions for it)."""
+        longer start reductions for it) and unmap the other ranks' arenas (every rank closes)."""
         if self.overlap:
             for m in self.modules:
                 set_grad_ready_hook(m._registered_handle, None)
             self.overlap = False
+        if self.peer:
+            torch.cuda.synchronize(self.arena.q.device)  # no update kernel still reads or writes a peer
+            for mp in self._peer_maps:
+                mp.close()
+            self._peer_maps = []
+            self.peer = False
+
+    # -- peer mode -----------------------------------------------------------------
+    def _connect_peers(self) -> bool:
+        """Map every other rank's weight and gradient arenas into this process (CUDA IPC), when all
+        ranks run on this node and have shareable arenas; all ranks agree on the outcome."""
+        import socket
+
+        dev = self.arena.q.device
+        mine = None
+        if self._ipc:
+            try:
+                mine = (socket.gethostname(), self._ipc[0].handle(), self._ipc[1].handle())
+            except (RuntimeError, ValueError):
+                mine = None
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=self._host_group)
+        ok = all(v is not None for v in every) and len({v[0] for v in every}) == 1
+        q_ptrs, g_ptrs, maps = [], [], []
+        if ok:
+            try:
+                for r, v in enumerate(every):
+                    if r == self.rank:
+                        q_ptrs.append(self.arena.q.data_ptr())
+                        g_ptrs.append(self.arena.g.data_ptr())
+                        continue
+                    mq, mg = _capi.IpcMapping(v[1], dev), _capi.IpcMapping(v[2], dev)
+                    maps += [mq, mg]
+                    q_ptrs.append(mq.ptr)
+                    g_ptrs.append(mg.ptr)
+            except (RuntimeError, ValueError):
+                ok = False
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self._host_group)
+        if int(flag.item()) == 0:
+            for mp in maps:
+                mp.close()
+            return False
+        self._peer_maps, self._q_ptrs, self._g_ptrs = maps, q_ptrs, g_ptrs
+        self._fence_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        return True
+
+    def _peer_fence(self) -> None:
+        """Order this rank's stream after every rank's work issued so far: a one-element NCCL
+        all-reduce on the stream completes only once every rank's stream has reached it."""
+        t = self._mark()
+        dist.all_reduce(self._fence_t, group=self.group)
+        self._timed("peer_fence_wait", t)
+
+    def _update_bucket_peer(self, b: int, has_grad: list[bool]) -> None:
+        """This rank's slice of bucket b from every rank's gradient, its new weights written to every
+        rank's arena (ff_dqt_adamw8_peers): the reduce-scatter and all-gather inside the update."""
+        plan = self.plan
+        dec_s, dec_u = _tables_on(self.arena.q.device)
+        for seg in self._segments_of[b]:
+            if not has_grad[seg.module]:
+                continue
+            m = self.modules[seg.module]
+            a, e = seg.local, seg.local + seg.hi - seg.lo
+            ba, bb = plan.local_blocks(seg)
+            _capi.dqt_adamw8_peers(
+                self.arena.q[seg.lo:seg.hi], m.weight_scale, m.in_features,
+                [ptr + 2 * seg.lo for ptr in self._g_ptrs], [ptr + seg.lo for ptr in self._q_ptrs],
+                self.m_q[a:e], self.m_absmax[ba:bb], self.v_q[a:e], self.v_absmax[ba:bb], self.r_q[a:e],
+                self.r_absmax[ba:bb], lr=self.lr, beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, wd=self.wd,
+                step=self.steps[seg.module], sr_bias=self.sr_bias_scale, seed=self.rng_seed, rng_offset=seg.rng,
+                elem_base=seg.elem_base, g_out=self.g_shard[a:e] if self.keep_reduced_grad else None,
+                dec_s=dec_s, dec_u=dec_u)
 
     # -- overlapped reduction ----------------------------------------------------
     def _reset_pending(self) -> None:
@@ -430,36 +540,66 @@ class ZeroFireFlyOptim:
             self._segs_cache = segs
         return segs
 
+    def _mark(self):
+        if self.comm_events is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def _timed(self, phase: str, start) -> None:
+        if start is not None:
+            self.comm_events.append((phase, start, self._mark()))
+
     @torch.no_grad()
     def step(self) -> None:
         plan = self.plan
+        t_step = self._mark()
         clear_activation_cache()  # the next step's inputs are quantised afresh
         has_grad = self.arena.collect_grads()
         if self.world > 1:
-            # buckets not reduced during the backward (no overlap, or a module without a
-            # gradient, whose slot now holds zeros) are reduced now, in the same fixed order
-            for b in range(self._next_reduce, -1, -1):
-                self._launch_reduce(b)
-            self._next_reduce = -1
+            if not self.peer:
+                # buckets not reduced during the backward (no overlap, or a module without a
+                # gradient, whose slot now holds zeros) are reduced now, in the same fixed order
+                for b in range(self._next_reduce, -1, -1):
+                    self._launch_reduce(b)
+                self._next_reduce = -1
             # a module with a gradient on any rank is updated on every rank
             flags = torch.tensor(has_grad, dtype=torch.int32)
             dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self._host_group)
             has_grad = [bool(v) for v in flags.tolist()]
         for i, h in enumerate(has_grad):
             self.steps[i] += int(h)
-        if self.world > 1:
+        if self.peer:
+            dense = self._launch_dense_reduce()
+            self._peer_fence()  # every rank's gradients are complete
+            t = self._mark()
+            for b in range(len(plan.buckets)):
+                self._update_bucket_peer(b, has_grad)
+            self._timed("peer_update", t)
+            self._peer_fence()  # every rank's new weights are written and its gradients read
+            t = self._mark()
+            self._finish_dense_reduce(dense)
+            self._timed("dense_all_reduce_wait", t)
+        elif self.world > 1:
             dense = self._launch_dense_reduce()
             gathers = []
             for b in list(self._rs_order):
+                t = self._mark()
                 self._finish_reduce(b)
+                self._timed("reduce_scatter_wait", t)
                 self._update_bucket(b, self.g_shard, has_grad)
                 bk = plan.buckets[b]
                 lo, hi = plan.rank_slice(b)
                 gathers.append(dist.all_gather_into_tensor(self.arena.q[bk.lo:bk.lo + bk.size], self.arena.q[lo:hi],
                                                            group=self.group, async_op=True))
+            t = self._mark()
             self._finish_dense_reduce(dense)
+            self._timed("dense_all_reduce_wait", t)
+            t = self._mark()
             for w in gathers:
                 w.wait()  # the next forward reads the gathered weights
+            self._timed("all_gather_wait", t)
         else:
             for b in range(len(plan.buckets)):
                 self._update_bucket(b, self.arena.g, has_grad)
@@ -468,6 +608,7 @@ class ZeroFireFlyOptim:
             self.dense_opt.step()
         for m in self.modules:
             _invalidate_weight_cache(m._registered_handle)
+        self._timed("optimizer_step", t_step)
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         if self.dense_opt is not None:

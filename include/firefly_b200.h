@@ -430,6 +430,44 @@ FF_API int ff_dqt_adamw8(int8_t* q, const float* wscale, int64_t row_len, int64_
                   const float* dec_u, void* stream);
 
 /*
+ * ff_dqt_adamw8 for one rank of a data-parallel job, with the gradient reduction and the
+ * weight gather in the same kernel (no reference counterpart: the reference trains on one
+ * GPU).  The gradient of element i is the average of the n_srcs bf16 arrays g_srcs[k][i]
+ * (every rank's gradient of the same elements, the other ranks' read over NVLink: device
+ * pointers of this process, e.g. from ff_ipc_open), summed in fp32 in the order k = 0..n_srcs-1,
+ * multiplied by 1/n_srcs and rounded to bf16; the new weight of element i is written to
+ * q_dsts[k][i] for every k < n_dsts (every rank's copy of the weights; q itself is read for the
+ * current weight and must be one of them).  g_out (or NULL) receives the averaged gradient.
+ * 1 <= n_srcs, n_dsts <= FF_DQT_MAX_SOURCES; g_srcs 16-byte aligned, q_dsts 8-byte aligned.
+ * The other arguments are ff_dqt_adamw8's (uniforms always from Philox).  The kernel does not
+ * wait for the other ranks: the caller orders it after every rank's gradient is complete and
+ * orders every rank's next use of the weights or gradients after it (e.g. a collective on the
+ * stream before and after).
+ */
+#define FF_DQT_MAX_SOURCES 8
+FF_API int ff_dqt_adamw8_peers(int8_t* q, const float* wscale, int64_t row_len, int64_t elem_base,
+                               const uint16_t* const* g_srcs, int n_srcs, int8_t* const* q_dsts, int n_dsts,
+                               uint16_t* g_out, uint8_t* m_q, float* m_absmax, uint8_t* v_q, float* v_absmax,
+                               uint8_t* r_q, float* r_absmax, int64_t numel, int64_t block, double lr,
+                               double beta1, double beta2, double eps, double wd, double bc1, double bc2,
+                               double sr_bias, uint64_t seed, uint64_t step, int64_t rng_offset,
+                               const float* dec_s, const float* dec_u, void* stream);
+
+/*
+ * Device memory shared between the processes of one node (CUDA IPC), for the data-parallel
+ * arenas that ff_dqt_adamw8_peers reads and writes.  ff_ipc_alloc: one device allocation of the
+ * current device (freed by ff_ipc_free); ff_ipc_get_handle writes its FF_IPC_HANDLE_BYTES-byte
+ * handle; ff_ipc_open maps another process's allocation from its handle (peer access enabled),
+ * ff_ipc_close unmaps it.
+ */
+#define FF_IPC_HANDLE_BYTES 64
+FF_API int ff_ipc_alloc(int64_t bytes, void** ptr);
+FF_API int ff_ipc_free(void* ptr);
+FF_API int ff_ipc_get_handle(void* ptr, uint8_t* handle);
+FF_API int ff_ipc_open(const uint8_t* handle, void** ptr);
+FF_API int ff_ipc_close(void* ptr);
+
+/*
  * update_int8_weight_ (fireflykernels.py:218-223): w = clamp(int16(w) + dq, -127, 127).
  * dq: int32[n].
  */

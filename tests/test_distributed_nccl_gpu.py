@@ -1,10 +1,11 @@
 """ZeRO-1 data parallelism on real GPUs over NCCL (skipped with fewer than two GPUs).
 
 Two ranks run a small BitLinear model on the same tokens, so their averaged gradients equal each
-rank's own; the sharded, bucketed update (the DQT kernel on each rank's slice, reduce-scatters
-issued from the backward, per-bucket all-gathers) must then give bit for bit the weights and the
-gathered 8-bit states of the same three steps on one GPU: the stochastic-rounding uniforms are
-keyed by the global element index, not by the rank.
+rank's own; the sharded, bucketed update must then give bit for bit the weights and the gathered
+8-bit states of the same three steps on one GPU: the stochastic-rounding uniforms are keyed by the
+global element index, not by the rank.  Both paths: the collectives (the DQT kernel on each rank's
+slice, reduce-scatters issued from the backward, per-bucket all-gathers) and peer mode (one kernel
+per slice reads both ranks' gradient arenas and writes both ranks' weight arenas over NVLink).
 """
 import os
 import socket
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _train(rank, world, port, out_path):
+def _train(rank, world, port, out_path, peer=False):
     import datetime
 
     import torch.distributed as dist
@@ -40,7 +41,9 @@ def _train(rank, world, port, out_path):
     torch.manual_seed(0)
     mods = [BitLinear(k, o).to(dev) for o, k in SHAPES]
     # two buckets, so that a reduce-scatter starts from the backward before the last one
-    opt = ZeroFireFlyOptim(mods, lr=1e-3, weight_decay=0.01, seed=5, bucket_mb=0.05, overlap=True)
+    opt = ZeroFireFlyOptim(mods, lr=1e-3, weight_decay=0.01, seed=5, bucket_mb=0.05, overlap=True,
+                           peer=bool(peer) if world > 1 else None)
+    assert opt.peer == (bool(peer) and world > 1)
     g = torch.Generator(device=dev).manual_seed(123)  # the same tokens on every rank
     for step in range(3):
         # the BitLinear weights are buffers: the input carries the autograd graph
@@ -49,6 +52,7 @@ def _train(rank, world, port, out_path):
         y.float().pow(2).mean().backward()
         opt.step()
     bits = opt.gather_bit_state()
+    opt.close()
     if rank == 0:
         torch.save({"q": [m.int_weight.cpu() for m in mods], "bits": bits, "buckets": len(opt.plan.buckets)},
                    out_path)
@@ -59,14 +63,15 @@ def _train(rank, world, port, out_path):
 
 @pytest.mark.timeout(600)
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_zero1_two_gpus_equal_one_gpu(tmp_path):
+@pytest.mark.parametrize("peer", [False, True], ids=["collectives", "peer"])
+def test_zero1_two_gpus_equal_one_gpu(tmp_path, peer):
     one, two = tmp_path / "one.pt", tmp_path / "two.pt"
     ctx = mp.get_context("spawn")  # a fresh process for each run (no CUDA state inherited)
     p = ctx.Process(target=_train, args=(0, 1, 0, str(one)))
     p.start()
     p.join(300)
     assert p.exitcode == 0
-    mp.start_processes(_train, args=(2, _free_port(), str(two)), nprocs=2, start_method="spawn")
+    mp.start_processes(_train, args=(2, _free_port(), str(two), peer), nprocs=2, start_method="spawn")
     a, b = torch.load(one, weights_only=False), torch.load(two, weights_only=False)
     assert b["buckets"] > 1
     for qa, qb in zip(a["q"], b["q"]):

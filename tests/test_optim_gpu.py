@@ -177,3 +177,77 @@ def test_zero_state_matches_reference_encoding():
     o = O.init_state((5, 100))
     for k in KEYS:
         np.testing.assert_array_equal(st[k].cpu().numpy(), o[k])
+
+
+@pytest.mark.parametrize("O_,K,nsrc,offset", [(64, 512, 2, 0), (33, 70, 3, 0), (40, 96, 2, 8), (8, 1024, 8, 0)])
+def test_multi_source_update_equals_update_on_the_averaged_gradient(O_, K, nsrc, offset):
+    """ff_dqt_adamw8_peers with every source and destination on this GPU (stand-ins for the other
+    ranks' arenas): the same result as ff_dqt_adamw8 on the gradient averaged the way the kernel
+    defines it (fp32 sums in source order, times 1/nsrc, rounded to bf16), the new weights in every
+    destination, the averaged gradient in g_out.  offset 8 makes the arrays 8-byte but not 16-byte
+    aligned (no bulk staging: the per-element path); 33 x 70 ends in a ragged block."""
+    q, ws, _, st, rng = _random_case(O_, K, seed=O_ * K + nsrc)
+    n = O_ * K
+    grads = [torch.from_numpy(rng.standard_normal(n).astype(np.float32) * 1e-3).to(DEV).to(torch.bfloat16)
+             for _ in range(nsrc)]
+    acc = grads[0].float()
+    for g in grads[1:]:
+        acc = acc + g.float()
+    g_avg = (acc * torch.tensor(1.0 / nsrc, dtype=torch.float32, device=DEV)).to(torch.bfloat16)
+    dec_s, dec_u = _tables_on(DEV)
+    wsd = torch.from_numpy(np.ascontiguousarray(ws)).to(DEV)
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01, step=int(st["step"]) + 1, sr_bias=0.15,
+              seed=77, rng_offset=512, dec_s=dec_s, dec_u=dec_u)
+
+    def arrays(extra):  # q and the states, each starting `extra` bytes into a larger buffer
+        def put(a, dtype):
+            t = torch.from_numpy(np.ascontiguousarray(a).ravel()).to(DEV)
+            buf = torch.zeros(t.numel() * t.element_size() + 64, dtype=torch.uint8, device=DEV)
+            v = buf[extra:extra + t.numel() * t.element_size()].view(dtype)
+            v.copy_(t.view(dtype))
+            return v
+        out = {"q": put(q, torch.int8)}
+        for k in KEYS:
+            out[k] = put(st[k], torch.float32 if "absmax" in k else torch.uint8)
+        return out
+
+    ref = arrays(0)
+    _capi.dqt_adamw8(ref["q"], wsd, K, g_avg, ref["m_q"], ref["m_absmax"], ref["v_q"], ref["v_absmax"], ref["r_q"],
+                     ref["r_absmax"], **kw)
+    got = arrays(offset)
+    q2 = torch.zeros_like(got["q"])  # a second rank's copy of the weights
+    gsrc = []
+    for g in grads:
+        buf = torch.zeros(n * 2 + 64, dtype=torch.uint8, device=DEV)
+        v = buf[16:16 + 2 * n].view(torch.bfloat16)
+        v.copy_(g)
+        gsrc.append(v)
+    g_out = torch.empty(n, dtype=torch.bfloat16, device=DEV)
+    _capi.dqt_adamw8_peers(got["q"], wsd, K, [t.data_ptr() for t in gsrc], [got["q"].data_ptr(), q2.data_ptr()],
+                           got["m_q"], got["m_absmax"], got["v_q"], got["v_absmax"], got["r_q"], got["r_absmax"],
+                           g_out=g_out, **kw)
+    torch.cuda.synchronize()
+    assert _capi.device_status() == 0
+    assert torch.equal(g_out, g_avg)
+    assert torch.equal(got["q"], ref["q"])
+    assert torch.equal(q2, ref["q"])
+    for k in KEYS:
+        assert torch.equal(got[k], ref[k]), k
+
+
+def test_multi_source_argument_checks():
+    q = torch.zeros(256, dtype=torch.int8, device=DEV)
+    st = {k: torch.zeros(256 if k.endswith("_q") else 1, dtype=torch.uint8 if k.endswith("_q") else torch.float32,
+                         device=DEV) for k in KEYS}
+    dec_s, dec_u = _tables_on(DEV)
+    g = torch.zeros(256, dtype=torch.bfloat16, device=DEV)
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01, step=1, sr_bias=0.15, seed=1, dec_s=dec_s,
+              dec_u=dec_u)
+    args = (torch.ones(1, device=DEV), 256)
+    states = (st["m_q"], st["m_absmax"], st["v_q"], st["v_absmax"], st["r_q"], st["r_absmax"])
+    with pytest.raises(ValueError):  # q must be among the destinations
+        _capi.dqt_adamw8_peers(q, *args, [g.data_ptr()], [g.data_ptr()], *states, **kw)
+    with pytest.raises(ValueError):  # at most 8 sources
+        _capi.dqt_adamw8_peers(q, *args, [g.data_ptr()] * 9, [q.data_ptr()], *states, **kw)
+    with pytest.raises(ValueError):  # sources 16-byte aligned (checked by the library)
+        _capi.dqt_adamw8_peers(q, *args, [g.data_ptr() + 2], [q.data_ptr()], *states, **kw)
