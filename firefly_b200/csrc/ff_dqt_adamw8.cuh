@@ -53,16 +53,23 @@ constexpr int kBlock = 256;
 constexpr int kTabBytes = 256 * 256;  // 256 codes x (32 signed + 32 unsigned copies)
 // per warp, two stages of one block's inputs, filled by 1-D bulk (TMA) copies:
 // g (512 B) | q (256) | m (256) | v (256) | r (256) | u (1024, supplied-uniform mode only)
-constexpr int kStageOffQ = 512, kStageOffM = 768, kStageOffV = 1024, kStageOffR = 1280, kStageOffU = 1536;
-__host__ __device__ constexpr int stage_bytes(bool has_u) { return has_u ? 2560 : 1536; }
-__host__ __device__ constexpr int smem_bytes(bool has_u) { return kTabBytes + kWarps * 2 * stage_bytes(has_u) + kWarps * 2 * 8; }
-// Data-parallel mode (several gradient sources): the stage holds one 512-byte gradient block per
-// source, in source order, then q, m, v, r (256 bytes each)
+// Every warp of a CTA updates one block per iteration (the CTA's kCons consecutive blocks, a
+// "chunk"); the chunks' inputs are staged into a ring of CTA stages one chunk ahead, one bulk copy
+// per array, by lane 0 of warp i % kCons for the CTA's i-th chunk, so that the staging work is
+// spread evenly over the warps (three per scheduler: the warps of a CTA split evenly)
+constexpr int kCons = kWarps;
 constexpr int kMaxSources = FF_DQT_MAX_SOURCES;
-__host__ __device__ constexpr int stage_bytes_multi(int nsrc) { return 512 * nsrc + 1024; }
-__host__ __device__ constexpr int smem_bytes_multi(int nsrc) {
-  return kTabBytes + kWarps * 2 * stage_bytes_multi(nsrc) + kWarps * 2 * 8;
+// bytes one block takes in a stage: ng gradient blocks (512 B each; ng = the number of gradient
+// sources), q, m, v, r (256 B each), and the uniforms (1 KiB) when they are supplied
+__host__ __device__ constexpr int block_stage_bytes(int ng, bool has_u) { return 512 * ng + 1024 + (has_u ? 1024 : 0); }
+// stages of the chunk ring (two CTAs of two stages fit an SM)
+__host__ __device__ constexpr int num_stages(bool) { return 2; }
+// the decode rows, the stages of one chunk each, the stages' full and empty barriers
+__host__ __device__ constexpr int smem_bytes_for(int ng, bool has_u, bool multi) {
+  return kTabBytes + num_stages(multi) * kCons * block_stage_bytes(ng, has_u) + 2 * num_stages(multi) * 8;
 }
+__host__ __device__ constexpr int smem_bytes(bool has_u) { return smem_bytes_for(1, has_u, false); }
+__host__ __device__ constexpr int smem_bytes_multi(int nsrc) { return smem_bytes_for(nsrc, false, true); }
 constexpr float kMagic = 12582912.0f;     // 1.5 * 2^23
 // rows with lr / max(ws, eps) above this take the step-by-step chain (see exact_pair)
 constexpr float kFastRatio = 16.f;
@@ -82,6 +89,7 @@ struct Params {
   int64_t numel;
   float neg_lr, beta1, beta2, eps, wd, sr_bias;
   float omb1, omb2, ibc1, ibc2, bc1, bc2;
+  float den_k, den_c;  // bc1 * sqrt(1/bc2) and bc1 * eps (fp32, correctly rounded sqrt): a's denominator
   uint32_t seed_lo, seed_hi, step_lo, step_hi;
   int64_t rng_offset;
   int64_t row_step, in_row_step;  // grid-stride advance in (rows, elements within a row)
@@ -106,8 +114,11 @@ struct Params {
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void bar_init(uint32_t bar) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar));
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void bar_expect(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
@@ -348,32 +359,19 @@ __device__ __forceinline__ float ld_tab(uint32_t base, uint32_t off) {
 template <bool HAS_U, int ROWS, int TAB, bool MULTI>
 __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
   static_assert(!(HAS_U && MULTI), "supplied uniforms and several gradient sources are not combined");
-  const int kStage = MULTI ? stage_bytes_multi(p.nsrc) : stage_bytes(HAS_U);
-  const int offQ = MULTI ? 512 * p.nsrc : kStageOffQ;  // q, m, v, r follow the gradient blocks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* my_stage = smem + kTabBytes + warp * 2 * kStage;
-  const uint32_t bar0 = smem_addr(smem + kTabBytes + kWarps * 2 * kStage) + warp * 16;
+  // a stage holds one chunk (kCons blocks) as regions: the gradient blocks of each source
+  // (kCons x 512 B each), then q, m, v, r (kCons x 256 B each), then u (kCons x 1 KiB)
+  const int ng = MULTI ? p.nsrc : 1;
+  const int chunk_bytes = kCons * block_stage_bytes(ng, HAS_U);
+  const int oQ = kCons * 512 * ng, oM = oQ + kCons * 256, oV = oM + kCons * 256, oR = oV + kCons * 256,
+            oU = oR + kCons * 256;
+  constexpr int NST = num_stages(MULTI);
+  uint8_t* stage_p = smem + kTabBytes;
+  const uint32_t stage0 = smem_addr(stage_p);
+  const uint32_t full0 = stage0 + NST * chunk_bytes, empty0 = full0 + 8 * NST;  // full[NST], empty[NST]
   const uint32_t tab_base = smem_addr(smem);
   const uint32_t lane4 = 4u * lane;
-  const uint32_t stage_bytes_tx = MULTI ? (uint32_t)stage_bytes_multi(p.nsrc) : 512 + 4 * 256 + (HAS_U ? 1024 : 0);
-  // lane 0 stages block b (a full block) into stage s
-  auto prefetch = [&](int64_t b, int s) {
-    const uint32_t dst = smem_addr(my_stage + s * kStage), bar = bar0 + 8 * s;
-    const int64_t e = b * kBlock;
-    bar_expect(bar, stage_bytes_tx);
-    if constexpr (MULTI) {  // every source's gradient block (peers' over NVLink, no multicast)
-#pragma unroll
-      for (int k = 0; k < kMaxSources; ++k)
-        if (k < p.nsrc) bulk_g2s(dst + 512 * k, p.gsrc[k] + e, 512, bar);
-    } else {
-      bulk_g2s(dst, p.g + e, 512, bar);
-    }
-    bulk_g2s(dst + offQ, p.q + e, 256, bar);
-    bulk_g2s(dst + offQ + 256, p.m_q + e, 256, bar);
-    bulk_g2s(dst + offQ + 512, p.v_q + e, 256, bar);
-    bulk_g2s(dst + offQ + 768, p.r_q + e, 256, bar);
-    if constexpr (HAS_U) bulk_g2s(dst + kStageOffU, p.u + e, 1024, bar);
-  };
   // data-parallel mode: the averaged gradient of a lane's 8 elements from the sources' words
   // (src(k) returns source k's 4 words), fp32 sums in source order, rounded to bf16
   auto average = [&](auto src, uint32_t (&gw)[4]) {
@@ -399,7 +397,7 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
   const int64_t full_blocks = p.numel / kBlock;  // blocks [0, full_blocks) have 256 elements
   const int64_t nblocks = (p.numel + kBlock - 1) / kBlock;
   const int64_t staged_blocks = p.bulk ? full_blocks : 0;
-  const int64_t wstride = (int64_t)gridDim.x * kWarps;
+  const int64_t wstride = (int64_t)gridDim.x * kCons;  // blocks between a warp's iterations
   const float eps = p.eps;
   const int64_t last_row = (p.elem_base + p.numel - 1) / p.row_len;
   const Hyper hy{p.neg_lr, p.beta1, p.beta2, eps, p.wd, p.sr_bias, p.omb1, p.omb2, p.bc1, p.bc2, p.ibc1, p.ibc2};
@@ -455,7 +453,7 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     f2 mn[4], vn[4], rn[4], qn[4];
     if (!exact) {
       const f2 am2 = splat(am * p.beta1), av2 = splat(av * p.beta2), ar2 = splat(ar);
-      const f2 den_k = splat(p.bc1 * sqrtf(p.ibc2)), den_c = splat(p.bc1 * eps);  // bc1*sqrt(v/bc2) + bc1*eps
+      const f2 den_k = splat(p.den_k), den_c = splat(p.den_c);  // bc1*sqrt(v/bc2) + bc1*eps
 #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         const int j0 = 2 * pp, j1 = 2 * pp + 1;
@@ -598,9 +596,38 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     }
   };
 
-  // ---- staged loop: full blocks whose inputs arrive by bulk copies into the warp's two stages
-  int64_t blk = (int64_t)blockIdx.x * kWarps + warp;
-  if (lane == 0 && blk < staged_blocks) prefetch(blk, 0);
+  // ---- staged loop: chunks of kCons consecutive full blocks; iteration it of this CTA is chunk
+  // blockIdx.x + it * gridDim.x, staged into stage it % NST
+  const int64_t staged_chunks = p.bulk ? (full_blocks + kCons - 1) / kCons : 0;
+  // lane 0 of warp it % kCons: stage the chunk of iteration it (if any) into stage it % NST once
+  // every warp has read that stage's previous chunk (iteration it - NST); false if that wait gave up
+  auto produce = [&](int it) -> bool {
+    const int64_t c = (int64_t)blockIdx.x + (int64_t)it * gridDim.x;
+    if (c >= staged_chunks) return true;
+    const int st = it % NST;
+    if (it >= NST && !bar_wait(empty0 + 8 * st, ((it / NST) & 1) ^ 1)) return false;
+    const int64_t b0 = c * kCons;
+    const int nb = (int)min64(kCons, full_blocks - b0);
+    const uint32_t dst = stage0 + st * chunk_bytes, bar = full0 + 8 * st;
+    const int64_t e = b0 * kBlock;
+    bar_expect(bar, (uint32_t)(nb * block_stage_bytes(ng, HAS_U)));
+    if constexpr (MULTI) {  // every source's gradient blocks (peers' over NVLink, no multicast)
+#pragma unroll
+      for (int k = 0; k < kMaxSources; ++k)
+        if (k < p.nsrc) bulk_g2s(dst + k * kCons * 512, p.gsrc[k] + e, nb * 512, bar);
+    } else {
+      bulk_g2s(dst, p.g + e, nb * 512, bar);
+    }
+    bulk_g2s(dst + oQ, p.q + e, nb * 256, bar);
+    bulk_g2s(dst + oM, p.m_q + e, nb * 256, bar);
+    bulk_g2s(dst + oV, p.v_q + e, nb * 256, bar);
+    bulk_g2s(dst + oR, p.r_q + e, nb * 256, bar);
+    if constexpr (HAS_U) bulk_g2s(dst + oU, p.u + e, nb * 1024, bar);
+    return true;
+  };
+  for (int k = 0; k < NST - 1; ++k)
+    if (lane == 0 && warp == k % kCons) produce(k);
+  int64_t blk = (int64_t)blockIdx.x * kCons + warp;
   // weight row of this lane's first element, advanced incrementally (no division per block)
   int64_t row, in_row;
   {
@@ -609,18 +636,21 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     in_row = ge - row * p.row_len;
   }
   float am = 0.f, av = 0.f, ar = 0.f;
-  if (blk < staged_blocks) {
+  if (blk < full_blocks && staged_chunks > 0) {
     am = __ldg(p.m_absmax + blk);
     av = __ldg(p.v_absmax + blk);
     ar = __ldg(p.r_absmax + blk);
   }
-  for (int it = 0; blk < staged_blocks; blk += wstride, ++it) {
-    const int stg = it & 1;
+  for (int it = 0;; ++it) {
+    const int64_t c = (int64_t)blockIdx.x + (int64_t)it * gridDim.x;
+    if (c >= staged_chunks) break;
+    if (lane == 0 && warp == (it + NST - 1) % kCons && !produce(it + NST - 1)) return;  // NST - 1 chunks ahead
+    const int st = it % NST;
+    blk = c * kCons + warp;
+    const bool mine = blk < full_blocks;  // only the last chunk can hold fewer than kCons blocks
     const int64_t nxt = blk + wstride;
-    // stage the next block while this one is computed (its stage was consumed last iteration)
-    if (lane == 0 && nxt < staged_blocks) prefetch(nxt, stg ^ 1);
     const float am_c = am, av_c = av, ar_c = ar;
-    if (nxt < staged_blocks) {  // the next block's absmax, one iteration ahead
+    if (nxt < full_blocks) {  // the next block's absmax, one iteration ahead
       am = __ldg(p.m_absmax + nxt);
       av = __ldg(p.v_absmax + nxt);
       ar = __ldg(p.r_absmax + nxt);
@@ -629,29 +659,35 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
     const int jsw = ROWS != 1 ? 8 : (int)min64(8, p.row_len - in_row);  // j >= jsw: next row
     const float wsa = fmaxf(__ldg(p.wscale + ra), eps);
     const float wsb = jsw < 8 ? fmaxf(__ldg(p.wscale + rb), eps) : wsa;
-    if (!bar_wait(bar0 + 8 * stg, (it >> 1) & 1)) return;  // copies lost: status raised
-    const uint8_t* sb = my_stage + stg * kStage;
-    uint32_t gw[4];
-    if constexpr (MULTI) {
-      average([&](int k) { return *reinterpret_cast<const uint4*>(sb + 512 * k + lane * 16); }, gw);
-      if (p.gout) *reinterpret_cast<uint4*>(p.gout + blk * kBlock + lane * 8) = make_uint4(gw[0], gw[1], gw[2], gw[3]);
-    } else {
-      const uint4 g4 = *reinterpret_cast<const uint4*>(sb + lane * 16);
-      gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
-    }
-    const uint2 q2 = *reinterpret_cast<const uint2*>(sb + offQ + lane * 8);
-    const uint2 m2 = *reinterpret_cast<const uint2*>(sb + offQ + 256 + lane * 8);
-    const uint2 v2 = *reinterpret_cast<const uint2*>(sb + offQ + 512 + lane * 8);
-    const uint2 r2 = *reinterpret_cast<const uint2*>(sb + offQ + 768 + lane * 8);
-    const uint32_t qw[2] = {q2.x, q2.y}, mw[2] = {m2.x, m2.y}, vw[2] = {v2.x, v2.y}, rw[2] = {r2.x, r2.y};
+    uint32_t gw[4], qw[2], mw[2], vw[2], rw[2];
     float u[HAS_U ? 8 : 1];
-    if constexpr (HAS_U) {
-      const float4 u0 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32);
-      const float4 u1 = *reinterpret_cast<const float4*>(sb + kStageOffU + lane * 32 + 16);
-      u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w;
-      u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
+    if (mine) {
+      if (!bar_wait(full0 + 8 * st, (it / NST) & 1)) return;  // copies lost: status raised
+      const uint8_t* sb = stage_p + st * chunk_bytes;
+      if constexpr (MULTI) {
+        average([&](int k) { return *reinterpret_cast<const uint4*>(sb + k * kCons * 512 + warp * 512 + lane * 16); },
+                gw);
+        if (p.gout) *reinterpret_cast<uint4*>(p.gout + blk * kBlock + lane * 8) = make_uint4(gw[0], gw[1], gw[2], gw[3]);
+      } else {
+        const uint4 g4 = *reinterpret_cast<const uint4*>(sb + warp * 512 + lane * 16);
+        gw[0] = g4.x; gw[1] = g4.y; gw[2] = g4.z; gw[3] = g4.w;
+      }
+      const uint2 q2 = *reinterpret_cast<const uint2*>(sb + oQ + warp * 256 + lane * 8);
+      const uint2 m2 = *reinterpret_cast<const uint2*>(sb + oM + warp * 256 + lane * 8);
+      const uint2 v2 = *reinterpret_cast<const uint2*>(sb + oV + warp * 256 + lane * 8);
+      const uint2 r2 = *reinterpret_cast<const uint2*>(sb + oR + warp * 256 + lane * 8);
+      qw[0] = q2.x; qw[1] = q2.y; mw[0] = m2.x; mw[1] = m2.y;
+      vw[0] = v2.x; vw[1] = v2.y; rw[0] = r2.x; rw[1] = r2.y;
+      if constexpr (HAS_U) {
+        const float4 u0 = *reinterpret_cast<const float4*>(sb + oU + warp * 1024 + lane * 32);
+        const float4 u1 = *reinterpret_cast<const float4*>(sb + oU + warp * 1024 + lane * 32 + 16);
+        u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w;
+        u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
+      }
     }
-    __syncwarp();  // every lane has its inputs: the stage may be refilled next iteration
+    __syncwarp();  // every lane has its inputs: this warp's part of the stage may be refilled
+    if (lane == 0) bar_arrive(empty0 + 8 * st);
+    if (!mine) break;  // the last chunk, and this warp has no block in it
     process(blk, gw, qw, mw, vw, rw, u, wsa, wsb, jsw, am_c, av_c, ar_c, 8);
     row += p.row_step;
     in_row += p.in_row_step;
@@ -660,6 +696,7 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
       ++row;
     }
   }
+  blk = (p.bulk ? full_blocks : 0) + (int64_t)blockIdx.x * kCons + warp;
   // ---- the rest: the ragged last block, or every block when the arrays are not 16-byte aligned
   for (; blk < nblocks; blk += wstride) {
     const int64_t e0 = blk * kBlock + lane * 8;
@@ -728,9 +765,7 @@ __device__ __forceinline__ void dqt_run(const Params& p, uint8_t* smem) {
 
 template <bool HAS_U, int ROWS, bool MULTI>
 __global__ void __launch_bounds__(kThreads, HAS_U ? 1 : kCtasPerSm) dqt_adamw8_kernel(Params p) {
-  extern __shared__ __align__(1024) uint8_t smem[];  // decode rows, then staging, then barriers
-  const int kStage = MULTI ? stage_bytes_multi(p.nsrc) : stage_bytes(HAS_U);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ __align__(1024) uint8_t smem[];  // decode rows, then the two stages, then barriers
   // decode rows: word 64*c + l = signed entry of code c, word 64*c + 32 + l = unsigned entry
   {
     float* tw = reinterpret_cast<float*>(smem);
@@ -739,10 +774,14 @@ __global__ void __launch_bounds__(kThreads, HAS_U ? 1 : kCtasPerSm) dqt_adamw8_k
       tw[i] = (i & 32) ? __ldg(p.dec_u + c) : __ldg(p.dec_s + c);
     }
   }
-  if (lane == 0) {
-    const uint32_t bar0 = smem_addr(smem + kTabBytes + kWarps * 2 * kStage) + warp * 16;
-    bar_init(bar0);
-    bar_init(bar0 + 8);
+  if (threadIdx.x == 0) {  // full[]: the producer's arrival with the bytes; empty[]: one arrival per consumer warp
+    constexpr int NST = num_stages(MULTI);
+    const int chunk_bytes = kCons * block_stage_bytes(MULTI ? p.nsrc : 1, HAS_U);
+    const uint32_t full0 = smem_addr(smem + kTabBytes + NST * chunk_bytes);
+    for (int k = 0; k < NST; ++k) {
+      bar_init(full0 + 8 * k, 1);
+      bar_init(full0 + 8 * (NST + k), kCons);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -826,6 +865,12 @@ inline int dqt_launch(const char* name, int8_t* q, const float* wscale, int64_t 
   p.bc2 = (float)bc2;
   p.ibc1 = (float)(1.0 / (double)p.bc1);
   p.ibc2 = (float)(1.0 / (double)p.bc2);
+  // the same fp32 roundings as the device expression p.bc1 * sqrtf(p.ibc2), p.bc1 * p.eps
+  {
+    volatile float sq = sqrtf(p.ibc2);  // IEEE sqrt, correctly rounded as on the device
+    p.den_k = (float)(p.bc1 * sq);
+    p.den_c = (float)(p.bc1 * p.eps);
+  }
   p.seed_lo = (uint32_t)seed;
   p.seed_hi = (uint32_t)(seed >> 32);
   p.step_lo = (uint32_t)step;
@@ -883,9 +928,9 @@ inline int dqt_launch(const char* name, int8_t* q, const float* wscale, int64_t 
   const int smem = u ? smem_bytes(true) : multi ? smem_bytes_multi(nsrc) : smem_bytes(false);
   // CTAs per SM: two unless their shared memory (plus the 1 KiB the runtime reserves per CTA) does not fit
   const int per_sm = u ? 1 : (2 * (smem + 1024) <= smem_sm ? kCtasPerSm : 1);
-  const int64_t want = (nblocks + kWarps - 1) / kWarps;
+  const int64_t want = (nblocks + kCons - 1) / kCons;
   const int grid = (int)min64(want, (int64_t)nsm * per_sm);
-  const int64_t stride_elems = (int64_t)grid * kWarps * kBlock;
+  const int64_t stride_elems = (int64_t)grid * kCons * kBlock;
   p.row_step = stride_elems / row_len;
   p.in_row_step = stride_elems % row_len;
   cudaStream_t st = as_stream(stream);
