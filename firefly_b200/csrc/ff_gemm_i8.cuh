@@ -35,7 +35,10 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int ACC_STAGES = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
-constexpr int GROUP_M = 8;
+#ifndef FF_GROUP_M
+#define FF_GROUP_M 16
+#endif
+constexpr int GROUP_M = FF_GROUP_M;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
 // ---------------------------------------------------------------------------
@@ -1094,11 +1097,6 @@ __device__ __forceinline__ void tc_mma_i8_pair(uint32_t d_tmem, uint64_t adesc, 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void spin_ns(uint64_t ns) {
-  const uint64_t t0 = globaltimer_ns();
-  while (globaltimer_ns() - t0 < ns) {
-  }
-}
 
 template <int OUT, bool BMN>
 __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
@@ -1529,18 +1527,6 @@ namespace gemm {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1552,22 +1538,6 @@ inline int make_map(CUtensorMap* m, const int8_t* ptr, int64_t rows, int64_t col
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FF_OK;
-}
-
-// bf16 matrix [rows, cols] (leading dim ld) for TMA boxes of box_cols x box_rows elements
-inline int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
-                         int box_rows, CUtensorMapSwizzle swizzle,
-                         CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_NONE) {
-  auto fn = encode_fn();
-  if (!fn) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FF_ERR_CUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
   return FF_OK;
 }
 
