@@ -239,14 +239,14 @@ constexpr int kSwigluFeat = 128;  // features per tile
 // quantiser of [dg | du].  dh itself is not written.
 constexpr int kOutSwigluBwd = 17;
 __host__ __device__ constexpr bool is_swiglu(int out) { return out == kOutSwigluFwd || out == kOutSwigluBwd; }
-// The SwiGLU backward epilogue runs kSwbWpq warps per TMEM lane quarter; the tile's 256 features
-// are 16 chunks of kSwbChunk, and warp e of a quarter takes chunks e, e + kSwbWpq, ...  g and u
-// pass through shared memory: per epilogue warp a ring of kSwbBufs buffers, each one chunk of
-// the warp's 32 rows of g and of u, loaded by TMA (32 x 32 B boxes, 32-byte swizzle: the 16-byte
-// half k of row r sits at half k ^ ((r >> 2) & 1), so the lanes' row reads and writes hit distinct
-// banks).  dg and du are written over g and u in the same buffer and leave by TMA stores from
-// there; a buffer is loaded again once its stores have read it, kSwbBufs - 1 chunks ahead of its
-// use.
+// The ring epilogues (SwiGLU backward: g and u in, dg and du out; GELU backward: u in, du out) run
+// kSwbWpq warps per TMEM lane quarter; the tile's 256 features are 16 chunks of kSwbChunk, and warp
+// e of a quarter takes chunks e, e + kSwbWpq, ...  The inputs pass through shared memory: per
+// epilogue warp a ring of kSwbBufs buffers, each one chunk of the warp's 32 rows of every input
+// array, loaded by TMA (32 x 32 B boxes, 32-byte swizzle: the 16-byte half k of row r sits at half
+// k ^ ((r >> 2) & 1), so the lanes' row reads and writes hit distinct banks).  The outputs are
+// written over the inputs in the same buffer and leave by TMA stores from there; a buffer is loaded
+// again once its stores have read it, kSwbBufs - 1 chunks ahead of its use.
 constexpr int kSwbChunk = 16;
 #ifndef FF_SWB_WPQ
 #define FF_SWB_WPQ 3
@@ -258,15 +258,9 @@ constexpr int kSwbWpq = FF_SWB_WPQ;
 constexpr int kSwbWarps = 4 * kSwbWpq;
 constexpr int kSwbBufs = FF_SWB_BUFS;
 constexpr int kSwbBoxBytes = 32 * kSwbChunk * 2;  // 32 rows x 16 bf16
-constexpr int kSwbBufBytes = 2 * kSwbBoxBytes;    // g box, then u box
-// after the barriers (256 B): per warp one buffer of the tile's 256 gate and 256 up column
-// multipliers, then the rings (256-byte aligned for the swizzle), then the rings' barriers
+// after the barriers (256 B): per warp one buffer of the column multipliers of the tile's 256
+// features for every output array
 constexpr uint32_t kSwbCmOff = 256;
-constexpr uint32_t kSwbCmBytes = 2 * 256 * 4;
-constexpr uint32_t kSwbRingOff = kSwbCmOff + kSwbWarps * kSwbCmBytes;
-constexpr uint32_t kSwbBarOff = kSwbRingOff + kSwbWarps * kSwbBufs * kSwbBufBytes;
-constexpr uint32_t kSwbCtrlBytes = kSwbBarOff + kSwbWarps * kSwbBufs * 8;
-static_assert(kSwbRingOff % 256 == 0, "the rings must be 256-byte aligned for the 32-byte swizzle");
 // Epilogue kind of the up GEMM of a GELU MLP block: u (bf16, as FF_OUT_BF16 forms it) and
 // h = gelu(u) (tanh form) written by TMA, |h| folded into the row and column maxima: the first
 // pass of the dual quantiser of h.
@@ -288,6 +282,24 @@ constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
 __device__ __forceinline__ uint32_t gelu_tab_bits(int i) {
   return (i >= kGeluTabSpan ? 0x8000u : 0u) | (uint32_t)((i % kGeluTabSpan) + (kGeluTabExpLo << 7));
 }
+// Ring epilogue layout after the pipeline stages: barriers (256 B), the warps' column multipliers,
+// the rings (256-byte aligned for the swizzle), the rings' barriers, then (GELU backward) the
+// table of gelu'.
+__host__ __device__ constexpr bool is_ring(int out) { return out == kOutSwigluBwd || out == kOutGeluBwd; }
+__host__ __device__ constexpr int ring_arrays(int out) { return out == kOutSwigluBwd ? 2 : 1; }  // boxes per chunk
+__host__ __device__ constexpr int ring_buf_bytes(int out) { return ring_arrays(out) * kSwbBoxBytes; }
+__host__ __device__ constexpr uint32_t ring_cm_bytes(int out) { return (uint32_t)ring_arrays(out) * 256u * 4u; }
+__host__ __device__ constexpr uint32_t ring_off(int out) { return kSwbCmOff + kSwbWarps * ring_cm_bytes(out); }
+__host__ __device__ constexpr uint32_t ring_bar_off(int out) {
+  return ring_off(out) + (uint32_t)(kSwbWarps * kSwbBufs * ring_buf_bytes(out));
+}
+__host__ __device__ constexpr uint32_t ring_tab_off(int out) { return ring_bar_off(out) + kSwbWarps * kSwbBufs * 8; }
+__host__ __device__ constexpr uint32_t ring_ctrl_bytes(int out) {
+  return ring_tab_off(out) + (out == kOutGeluBwd ? (uint32_t)kGeluTabEntries * 4u : 0u);
+}
+static_assert(ring_off(kOutSwigluBwd) % 256 == 0 && ring_off(kOutGeluBwd) % 256 == 0,
+              "the rings must be 256-byte aligned for the 32-byte swizzle");
+
 // table entry of a bf16 bit pattern, or -1 outside the table
 __device__ __forceinline__ int gelu_tab_index(uint32_t b16) {
   const int t = (int)(b16 & 0x7FFFu) - (kGeluTabExpLo << 7);
@@ -741,37 +753,24 @@ __device__ __forceinline__ void gelu_fwd_chunk(const uint32_t (&acc)[32], int64_
   atomicMax(p.col_amax + fb + lane, warp_colmax_bits(a, lane));
 }
 
-// u of one row's 32 features (64 B), zeros for rows past M
-__device__ __forceinline__ void gelu_bwd_load(const EpiParams& p, int64_t row, int64_t fb, uint4 (&uq)[4]) {
-  if (row < p.M) {
-    const uint4* up = reinterpret_cast<const uint4*>(p.g_in + row * p.ldg_in + fb);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) uq[k] = __ldg(up + k);
-  } else {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) uq[k] = make_uint4(0u, 0u, 0u, 0u);
-  }
-}
-
-// 32 features of the GELU backward epilogue for one row (one thread): dh = bf16(acc * sa) (as
-// FF_OUT_BF16 forms it) and the row's u (uq) give du = bf16(dh * gelu'(u)), stored by TMA at
-// column fb of D; |du * colmul| is folded into rmax and |du| into the column maxima.  `cm`:
-// this chunk's column multipliers at [0, 32).
-__device__ __forceinline__ void gelu_bwd_chunk(const uint32_t (&acc)[32], const uint4 (&uq)[4], int64_t row,
-                                               int64_t fb, const EpiParams& p, float sa, int lane, const float* cm,
-                                               uint32_t tab, float& rmax, const CUtensorMap* tmD,
-                                               uint8_t* stage, uint32_t stage_addr, uint32_t& nst) {
-  const bool live = row < p.M;
-  uint32_t uw[16], wdu[16];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uw[4 * k] = uq[k].x; uw[4 * k + 1] = uq[k].y; uw[4 * k + 2] = uq[k].z; uw[4 * k + 3] = uq[k].w;
-  }
+// kSwbChunk (16) features of the GELU backward epilogue for one row (one thread): dh = bf16(acc * sa)
+// (as FF_OUT_BF16 forms it) and the row's u (from the ring buffer `buf`, shared address buf_addr) give
+// du = bf16(dh * gelu'(u)) (gelu' from the shared table at `tab`, the arithmetic itself outside it),
+// written over u and stored by TMA at column fb of D (lane 0 issues the store as one bulk group).
+// Folds |du * colmul| into rmax and |du| into the column maxima.  `cm`: this chunk's 16 multipliers.
+// Rows past M have zero dh and u (TMA fills them with zeros), so their du is zero.
+__device__ __forceinline__ void gelu_bwd_chunk16(const uint32_t (&acc)[16], uint8_t* buf, uint32_t buf_addr,
+                                                 int64_t row, int64_t fb, const EpiParams& p, float sa, int lane,
+                                                 const float* cm, uint32_t tab, float& rmax, const CUtensorMap* tmD) {
+  const int sw = (lane >> 2) & 1;
+  uint4* up = reinterpret_cast<uint4*>(buf + lane * 32);
+  const uint4 u0 = up[sw], u1 = up[sw ^ 1];
+  const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
   const f2 sa2 = splat(sa);
-  uint32_t dwv[16];
+  uint32_t dwv[8], wdu[8];
   bool rare = false;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
+  for (int q = 0; q < 8; ++q) {
     dwv[q] = pack_bf16x2(mul2(mk2(__int2float_rn((int)acc[2 * q]), __int2float_rn((int)acc[2 * q + 1])), sa2));
     const int i0 = gelu_tab_index(uw[q] & 0xFFFFu), i1 = gelu_tab_index(uw[q] >> 16);
     rare |= (i0 | i1) < 0;
@@ -780,7 +779,7 @@ __device__ __forceinline__ void gelu_bwd_chunk(const uint32_t (&acc)[32], const 
   }
   if (__builtin_expect(rare, 0)) {  // inputs outside the table: the arithmetic itself
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const uint32_t b0 = uw[q] & 0xFFFFu, b1 = uw[q] >> 16;
       if ((gelu_tab_index(b0) | gelu_tab_index(b1)) < 0) {
         const int i0 = gelu_tab_index(b0), i1 = gelu_tab_index(b1);
@@ -790,13 +789,19 @@ __device__ __forceinline__ void gelu_bwd_chunk(const uint32_t (&acc)[32], const 
       }
     }
   }
-  const int32_t row0 = (int32_t)(row - lane);
-  staged_store<true>(wdu, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
-  uint32_t a[16];
+  up[sw] = make_uint4(wdu[0], wdu[1], wdu[2], wdu[3]);
+  up[sw ^ 1] = make_uint4(wdu[4], wdu[5], wdu[6], wdu[7]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmD, buf_addr, (int32_t)fb, (int32_t)(row - lane));
+    bulk_commit_group();
+  }
+  uint32_t a[8];
   uint32_t rw = 0u;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    a[q] = live ? abs_bf16x2(wdu[q]) : 0u;
+  for (int q = 0; q < 8; ++q) {
+    a[q] = abs_bf16x2(wdu[q]);
     if (p.colmul) {  // |v| * colmul (colmul >= 0) in fp32, as the row quantiser takes it
       float a0, a1;
       un2(mul2(unpack_bf16x2(a[q]), mk2(cm[2 * q], cm[2 * q + 1])), a0, a1);
@@ -806,7 +811,8 @@ __device__ __forceinline__ void gelu_bwd_chunk(const uint32_t (&acc)[32], const 
     }
   }
   if (!p.colmul) rmax = fmaxf(rmax, fmaxf(__uint_as_float(rw << 16), __uint_as_float(rw & 0xFFFF0000u)));
-  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(a, lane));
+  const uint32_t m = warp_colmax16_bits(a, lane);
+  if (!(lane & 2)) atomicMax(p.col_amax + fb + colmax16_feature(lane), m);
 }
 
 template <int OUT, int BN_, int STAGES_, bool BMN>
@@ -1028,31 +1034,34 @@ constexpr int C2_SMEM_BYTES_GELU = C2_STAGES_GELU * C2_STAGE_BYTES + 1024 + 512 
 // byte 512 of the control area: 512-byte aligned for the 64-byte swizzle)
 constexpr int C2_SMEM_BYTES_ST = C2_SMEM_BYTES + 256 + 8 * 2 * 2048;
 static_assert(C2_SMEM_BYTES_ST <= 232448, "bf16-output kernel exceeds the shared memory of a CTA");
-// SwiGLU backward: 4 stages, then the column multipliers and the g/u rings (kSwbCtrlBytes)
+// ring epilogues: 4 stages, then the ring layout (ring_ctrl_bytes)
 #ifndef FF_SWB_STAGES
 #define FF_SWB_STAGES 4
 #endif
 constexpr int C2_STAGES_SWB = FF_SWB_STAGES;
-constexpr int C2_SMEM_BYTES_SWB = C2_STAGES_SWB * C2_STAGE_BYTES + 1024 + (int)kSwbCtrlBytes;
-static_assert(C2_SMEM_BYTES_SWB <= 232448, "SwiGLU backward kernel exceeds the shared memory of a CTA");
+__host__ __device__ constexpr int c2_smem_ring(int out) {
+  return C2_STAGES_SWB * C2_STAGE_BYTES + 1024 + (int)ring_ctrl_bytes(out);
+}
+static_assert(c2_smem_ring(kOutSwigluBwd) <= 232448 && c2_smem_ring(kOutGeluBwd) <= 232448,
+              "a ring-epilogue kernel exceeds the shared memory of a CTA");
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
-  return OUT == kOutSwigluBwd ? C2_STAGES_SWB
-         : is_gelu(OUT)       ? C2_STAGES_GELU
+  return is_ring(OUT)   ? C2_STAGES_SWB
+         : is_gelu(OUT) ? C2_STAGES_GELU
                               : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
 }
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return OUT == kOutSwigluBwd ? C2_SMEM_BYTES_SWB
-         : is_gelu(OUT)       ? C2_SMEM_BYTES_GELU
+  return is_ring(OUT)   ? c2_smem_ring(OUT)
+         : is_gelu(OUT) ? C2_SMEM_BYTES_GELU
                               : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 8 epilogue warps (two per TMEM lane
 // quarter, each on half of the tile's columns), so a tile's epilogue takes half as long; the
-// SwiGLU backward epilogue runs kSwbWpq warps per quarter
+// ring epilogues run kSwbWpq warps per quarter
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return OUT == kOutSwigluBwd ? 64 + 32 * kSwbWarps : 320;
+  return is_ring(OUT) ? 64 + 32 * kSwbWarps : 320;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -1164,8 +1173,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     }
     mbar_init(drain, 1);
     mbar_init(done_bar, 1);
-    if constexpr (OUT == kOutSwigluBwd)
-      for (int i = 0; i < kSwbWarps * kSwbBufs; ++i) mbar_init(cbase + kSwbBarOff + 8u * i, 1);
+    if constexpr (is_ring(OUT))
+      for (int i = 0; i < kSwbWarps * kSwbBufs; ++i) mbar_init(cbase + ring_bar_off(OUT) + 8u * i, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmA);
@@ -1177,7 +1186,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  constexpr uint32_t gelu_tab_off = 512u + 8u * 2u * C2_SW_BUF_FLOATS * 4u + 8u * 2u * 2048u;
+  constexpr uint32_t gelu_tab_off =
+      is_ring(OUT) ? ring_tab_off(OUT) : 512u + 8u * 2u * C2_SW_BUF_FLOATS * 4u + 8u * 2u * 2048u;
   if constexpr (is_gelu(OUT)) {  // the CTA's GELU table, by all threads
     for (int i = threadIdx.x; i < kGeluTabEntries; i += c2_threads<OUT>()) {
       const uint32_t b16 = gelu_tab_bits(i);
@@ -1282,10 +1292,9 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     uint32_t acc_phase = 0;
     // SwiGLU: this warp's two staging buffers of its features' column scales and bias (the
     // backward epilogue: one buffer of its column multipliers)
-    constexpr int sw_bufs = OUT == kOutSwigluBwd ? 1 : 2;
-    float* sw_buf = OUT == kOutSwigluBwd
-                        ? reinterpret_cast<float*>(ctrl + kSwbCmOff + (warp - 2) * kSwbCmBytes)
-                        : reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * sw_bufs * C2_SW_BUF_FLOATS;
+    constexpr int sw_bufs = is_ring(OUT) ? 1 : 2;
+    float* sw_buf = is_ring(OUT) ? reinterpret_cast<float*>(ctrl + kSwbCmOff + (warp - 2) * ring_cm_bytes(OUT))
+                                 : reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * sw_bufs * C2_SW_BUF_FLOATS;
     // this warp's two TMA-store staging buffers (32 rows x 64 B each, 512-byte aligned for the
     // 64-byte swizzle); with the activation epilogues they follow the 8 warps' scale/bias buffers
     constexpr uint32_t st_off = 512u + (is_fused_act(OUT) ? 8u * 2u * C2_SW_BUF_FLOATS * 4u : 0u);
@@ -1293,12 +1302,13 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     const uint32_t st_stage_addr = cbase + st_off + (uint32_t)(warp - 2) * 2 * 2048;
     uint32_t st_count = 0;
     int tm, tn, half;
-    // SwiGLU backward: this warp's ring of g/u chunks (kSwbChunk).  The warp's chunks (those of
+    // ring epilogues: this warp's ring of input chunks (kSwbChunk).  The warp's chunks (those of
     // its chunk indices that lie below F) in schedule order; lane 0 keeps the cursor of the next
     // chunk to load (item sj, chunk sc at tile sm, sn) and the count of chunks loaded.
-    [[maybe_unused]] const uint32_t swb_ring = cbase + kSwbRingOff + (uint32_t)(warp - 2) * kSwbBufs * kSwbBufBytes;
-    [[maybe_unused]] uint8_t* swb_ring_p = ctrl + kSwbRingOff + (warp - 2) * kSwbBufs * kSwbBufBytes;
-    [[maybe_unused]] const uint32_t swb_bar = cbase + kSwbBarOff + (uint32_t)(warp - 2) * kSwbBufs * 8;
+    constexpr int kRingBuf = ring_buf_bytes(OUT);
+    [[maybe_unused]] const uint32_t swb_ring = cbase + ring_off(OUT) + (uint32_t)(warp - 2) * kSwbBufs * kRingBuf;
+    [[maybe_unused]] uint8_t* swb_ring_p = ctrl + ring_off(OUT) + (warp - 2) * kSwbBufs * kRingBuf;
+    [[maybe_unused]] const uint32_t swb_bar = cbase + ring_bar_off(OUT) + (uint32_t)(warp - 2) * kSwbBufs * 8;
     // chunks of tile column tn below F (16, or 8 for a last tile of 128 features: F % 128 == 0)
     auto swb_chunks = [&](int tn_) { return (int)min64(C2_BN / kSwbChunk, (ep.F - (int64_t)tn_ * C2_BN) / kSwbChunk); };
     int sj = 0, sc = 0, sm = 0, sn = 0, swb_loaded = 0, swb_used = 0;
@@ -1317,15 +1327,15 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       const int b = swb_loaded % kSwbBufs;
       const int32_t x = (int32_t)((int64_t)sn * C2_BN + sc * kSwbChunk);
       const int32_t y = (int32_t)((int64_t)sm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32);
-      const uint32_t bar = swb_bar + 8u * (uint32_t)b, dst = swb_ring + (uint32_t)(b * kSwbBufBytes);
-      mbar_arrive_expect_tx(bar, kSwbBufBytes);
-      tma_load_2d(dst, &tmH, x, y, bar);
-      tma_load_2d(dst + kSwbBoxBytes, &tmH, (int32_t)ep.F + x, y, bar);
+      const uint32_t bar = swb_bar + 8u * (uint32_t)b, dst = swb_ring + (uint32_t)(b * kRingBuf);
+      mbar_arrive_expect_tx(bar, kRingBuf);
+      tma_load_2d(dst, &tmH, x, y, bar);  // SwiGLU: g; GELU: u
+      if constexpr (OUT == kOutSwigluBwd) tma_load_2d(dst + kSwbBoxBytes, &tmH, (int32_t)ep.F + x, y, bar);  // u
       ++swb_loaded;
       sc += kSwbWpq;
       if (sc >= swb_chunks(sn)) swb_seek(sj + 1);
     };
-    if constexpr (OUT == kOutSwigluBwd) {
+    if constexpr (is_ring(OUT)) {
       if (lane == 0) {
         swb_seek(0);
         while (s_ok && swb_loaded < kSwbBufs) swb_load();
@@ -1334,8 +1344,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     bool swb_abort = false;
     for (int j = 0; item(j, tm, tn, half); ++j) {
       float4 st_s, st_b;  // loaded before the accumulator wait, stored after it
-      uint4 pu[4];        // GELU backward: u of the next chunk, loaded ahead
-      [[maybe_unused]] float4 st_s2, st_b2;  // SwiGLU backward: the multipliers of features 128..255
+      [[maybe_unused]] float4 st_s2, st_b2;  // ring epilogues: the multipliers of features 128..255
       if constexpr (OUT == kOutSwigluBwd) {
         // the tile's 256 features: lane l holds gate multipliers 4l..4l+3 and 128+4l..128+4l+3, up likewise
         const int64_t col = (int64_t)tn * C2_BN + lane * 4;
@@ -1346,19 +1355,20 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         st_s2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col + 128)) : one4;
         st_b2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + ep.F + col + 128)) : one4;
       }
-      if constexpr (OUT == kOutGeluFwd || OUT == kOutGeluBwd) {
-        // this warp's 128 features of the tile: lane l holds features 4l..4l+3 (forward: column
-        // scales and bias; backward: the row quantiser's column multipliers)
+      if constexpr (OUT == kOutGeluBwd) {
+        // the tile's 256 features: lane l holds the multipliers of features 4l..4l+3 and 128+4l..128+4l+3
+        const int64_t col = (int64_t)tn * C2_BN + lane * 4;
+        const bool in = ep.colmul && col < ep.F, in2 = ep.colmul && col + 128 < ep.F;
+        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
+        st_s = in ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col)) : one4;
+        st_s2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col + 128)) : one4;
+      }
+      if constexpr (OUT == kOutGeluFwd) {
+        // this warp's 128 features of the tile: lane l holds the column scales and bias of features 4l..4l+3
         const int64_t col = (int64_t)tn * C2_BN + eh * 128 + lane * 4;
         const bool in = col < ep.F;
-        const float* s4 = OUT == kOutGeluFwd ? ep.scale_b : ep.colmul;
-        st_s = in && s4 ? __ldg(reinterpret_cast<const float4*>(s4 + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
-        st_b = in && OUT == kOutGeluFwd && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col))
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-        if constexpr (OUT == kOutGeluBwd) {
-          const int64_t prow = (int64_t)tm * (2 * C2_BM) + (int64_t)rank * C2_BM + lg * 32 + lane;
-          if (col - lane * 4 < ep.F) gelu_bwd_load(ep, prow, col - lane * 4, pu);
-        }
+        st_s = in && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        st_b = in && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       if constexpr (OUT == kOutSwigluFwd) {
         // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
@@ -1375,6 +1385,9 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           reinterpret_cast<float4*>(buf + 128)[lane] = st_s2;
           reinterpret_cast<float4*>(buf + 256)[lane] = st_b;
           reinterpret_cast<float4*>(buf + 384)[lane] = st_b2;
+        } else if constexpr (OUT == kOutGeluBwd) {  // [256]
+          reinterpret_cast<float4*>(buf)[lane] = st_s;
+          reinterpret_cast<float4*>(buf + 128)[lane] = st_s2;
         } else {
           reinterpret_cast<float4*>(buf)[lane] = st_s;       // [gate 64 | up 64]
           reinterpret_cast<float4*>(buf + 128)[lane] = st_b;  // [gate bias 64 | up bias 64]
@@ -1419,29 +1432,11 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         if (row < ep.M)
           atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
                                                                __uint_as_float(rmax & 0xFFFF0000u))));
-      } else if constexpr (OUT == kOutGeluBwd) {
-        float rmax = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
-          const int fc = eh * 128 + c * 32;
-          const int64_t fb = (int64_t)tn * C2_BN + fc;
-          if (fb >= ep.F) break;
-          uint4 cu[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) cu[k] = pu[k];
-          if (c + 1 < 4 && fb + 32 < ep.F) gelu_bwd_load(ep, row, fb + 32, pu);  // next chunk
-          uint32_t r[32];
-          tmem_ld32(tbase + fc, r);
-          tmem_wait_ld();
-          gelu_bwd_chunk(r, cu, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32,
-                         cbase + gelu_tab_off, rmax, &tmD, st_stage, st_stage_addr, st_count);
-        }
-        if (row < ep.M) atomicMax(ep.row_amax + row, __float_as_uint(rmax));
-      } else if constexpr (OUT == kOutSwigluBwd) {
+      } else if constexpr (is_ring(OUT)) {
         const int nchunks = swb_chunks(tn);
         if (nchunks > eh) {
           float rmax = 0.f;
-          const float* cmb = sw_buf;  // [gate 256 | up 256] multipliers of the tile's features
+          const float* cmb = sw_buf;  // the multipliers of the tile's features ([gate 256 | up 256], or [256])
 #pragma unroll 1
           for (int c = eh; c < nchunks; c += kSwbWpq, ++swb_used) {
             const int b = swb_used % kSwbBufs;
@@ -1454,9 +1449,13 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
             uint32_t r[16];
             tmem_ld16(tbase + c * kSwbChunk, r);
             tmem_wait_ld();
-            swiglu_bwd_chunk16(r, swb_ring_p + b * kSwbBufBytes, swb_ring + (uint32_t)(b * kSwbBufBytes), row,
-                               (int64_t)tn * C2_BN + c * kSwbChunk, ep, sa, lane, cmb + c * kSwbChunk,
-                               cmb + 256 + c * kSwbChunk, rmax, &tmD);
+            const int64_t fb = (int64_t)tn * C2_BN + c * kSwbChunk;
+            if constexpr (OUT == kOutSwigluBwd)
+              swiglu_bwd_chunk16(r, swb_ring_p + b * kRingBuf, swb_ring + (uint32_t)(b * kRingBuf), row, fb, ep, sa,
+                                 lane, cmb + c * kSwbChunk, cmb + 256 + c * kSwbChunk, rmax, &tmD);
+            else
+              gelu_bwd_chunk16(r, swb_ring_p + b * kRingBuf, swb_ring + (uint32_t)(b * kRingBuf), row, fb, ep, sa, lane,
+                               cmb + c * kSwbChunk, cbase + gelu_tab_off, rmax, &tmD);
             // the previous chunk's buffer (its stores were issued one chunk ago) takes the chunk
             // kSwbBufs - 1 ahead of the next
             if (lane == 0 && swb_used >= 1 && s_ok) {
@@ -1496,7 +1495,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         acc_phase ^= 1u;
       }
     }
-    if ((st_count || OUT == kOutSwigluBwd) && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
+    if ((st_count || is_ring(OUT)) && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
     __syncwarp();
   }
 
@@ -2024,7 +2023,11 @@ extern "C" int ff_gelu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B
   if (rc) return rc;
   rc = make_map(&mb, B, K, F, ldb, BK);  // B is K x F row-major: read MN-major
   if (rc) return rc;
-  rc = make_map_out_bf16(&md, du, M, F, lddu, true);
+  // du stores and u loads: boxes of one epilogue chunk (kSwbChunk features x 32 rows)
+  CUtensorMap mu;
+  rc = make_map_bf16(&md, du, M, F, lddu, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  rc = make_map_bf16(&mu, u, M, F, ldu, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
   if (rc) return rc;
   EpiParams ep{};
   ep.scale_a = scale_a;
@@ -2041,7 +2044,7 @@ extern "C" int ff_gelu_bwd_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B
   ep.colmul = colmul;
   ep.act_variant = variant;
   const int t2m = (int)((M + 2 * C2_BM - 1) / (2 * C2_BM)), t2n = (int)((F + C2_BN - 1) / C2_BN);
-  rc = launch_2cta<kOutGeluBwd, true>(ma, mb, md, md, K, t2m, t2n, ep, max_pairs, st);
+  rc = launch_2cta<kOutGeluBwd, true>(ma, mb, md, mu, K, t2m, t2n, ep, max_pairs, st);
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>(name, reinterpret_cast<const __nv_bfloat16*>(du), M, F, lddu, colmul, eps,
                                       q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
