@@ -282,23 +282,32 @@ constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
 __device__ __forceinline__ uint32_t gelu_tab_bits(int i) {
   return (i >= kGeluTabSpan ? 0x8000u : 0u) | (uint32_t)((i % kGeluTabSpan) + (kGeluTabExpLo << 7));
 }
-// Ring epilogue layout after the pipeline stages: barriers (256 B), the warps' column multipliers,
-// the rings (256-byte aligned for the swizzle), the rings' barriers, then (GELU backward) the
-// table of gelu'.
+// The wide epilogues run kSwbWpq warps per TMEM lane quarter on interleaved 16-feature chunks:
+// the ring epilogues (SwiGLU backward, GELU backward, whose inputs come through the rings) and the
+// GELU forward one (no inputs: u and h leave through two staging buffers per warp).  Layout after
+// the pipeline stages: barriers (256 B), the warps' column parameters, the buffers (256-byte
+// aligned for the swizzle), the rings' barriers, then the GELU table (gelu' or gelu).
 __host__ __device__ constexpr bool is_ring(int out) { return out == kOutSwigluBwd || out == kOutGeluBwd; }
-__host__ __device__ constexpr int ring_arrays(int out) { return out == kOutSwigluBwd ? 2 : 1; }  // boxes per chunk
+__host__ __device__ constexpr bool is_wide(int out) { return is_ring(out) || out == kOutGeluFwd; }
+__host__ __device__ constexpr int ring_arrays(int out) { return out == kOutGeluBwd ? 1 : 2; }  // boxes per chunk
+__host__ __device__ constexpr int ring_bufs(int out) { return out == kOutGeluFwd ? 2 : kSwbBufs; }
 __host__ __device__ constexpr int ring_buf_bytes(int out) { return ring_arrays(out) * kSwbBoxBytes; }
+// per warp: two 256-feature arrays (SwiGLU: gate and up multipliers; GELU forward: column scales
+// and bias) or one (GELU backward: the multipliers)
 __host__ __device__ constexpr uint32_t ring_cm_bytes(int out) { return (uint32_t)ring_arrays(out) * 256u * 4u; }
 __host__ __device__ constexpr uint32_t ring_off(int out) { return kSwbCmOff + kSwbWarps * ring_cm_bytes(out); }
 __host__ __device__ constexpr uint32_t ring_bar_off(int out) {
-  return ring_off(out) + (uint32_t)(kSwbWarps * kSwbBufs * ring_buf_bytes(out));
+  return ring_off(out) + (uint32_t)(kSwbWarps * ring_bufs(out) * ring_buf_bytes(out));
 }
-__host__ __device__ constexpr uint32_t ring_tab_off(int out) { return ring_bar_off(out) + kSwbWarps * kSwbBufs * 8; }
+__host__ __device__ constexpr uint32_t ring_tab_off(int out) {
+  return ring_bar_off(out) + (uint32_t)(kSwbWarps * ring_bufs(out) * 8);
+}
 __host__ __device__ constexpr uint32_t ring_ctrl_bytes(int out) {
-  return ring_tab_off(out) + (out == kOutGeluBwd ? (uint32_t)kGeluTabEntries * 4u : 0u);
+  return ring_tab_off(out) +
+         (out == kOutGeluBwd ? (uint32_t)kGeluTabEntries * 4u : out == kOutGeluFwd ? (uint32_t)kGeluTabEntries * 2u : 0u);
 }
-static_assert(ring_off(kOutSwigluBwd) % 256 == 0 && ring_off(kOutGeluBwd) % 256 == 0,
-              "the rings must be 256-byte aligned for the 32-byte swizzle");
+static_assert(ring_off(kOutSwigluBwd) % 256 == 0 && ring_off(kOutGeluBwd) % 256 == 0 && ring_off(kOutGeluFwd) % 256 == 0,
+              "the buffers must be 256-byte aligned for the 32-byte swizzle");
 
 // table entry of a bf16 bit pattern, or -1 outside the table
 __device__ __forceinline__ int gelu_tab_index(uint32_t b16) {
@@ -696,28 +705,21 @@ __device__ __forceinline__ void swiglu_bwd_chunk16(const uint32_t (&acc)[16], ui
   }
 }
 
-// 32 features of the GELU forward epilogue for one row (one thread): u exactly as the
-// FF_OUT_BF16 epilogue forms it (((acc * sa) * sb) (+ bias) -> bf16, stored at column fb of D)
-// and h = bf16(gelu(u)) (column fb of H); |h| is folded into the row maximum rmax (bf16x2 word)
-// and the column maxima.  `cb`: this chunk's column scales at [0, 32), bias at [128, 160).
-__device__ __forceinline__ void gelu_fwd_chunk(const uint32_t (&acc)[32], int64_t row, int64_t fb,
-                                               const EpiParams& p, float sa, int lane, const float* cb,
-                                               uint32_t tab, uint32_t& rmax, const CUtensorMap* tmD,
-                                               const CUtensorMap* tmH, uint8_t* stage, uint32_t stage_addr,
-                                               uint32_t& nst) {
+// kSwbChunk (16) features of the GELU forward epilogue for one row (one thread): u exactly as the
+// FF_OUT_BF16 epilogue forms it (((acc * sa) * sb) (+ bias) -> bf16) and h = bf16(gelu(u)) (from the
+// shared table at `tab`, the arithmetic itself outside it) are written to the staging buffer `buf`
+// (shared address buf_addr: the u box, then the h box, 32-byte swizzle) and stored by TMA at column
+// fb of D and H (lane 0 issues both stores as one bulk group); |h| is folded into the row maximum
+// rmax (bf16x2 word) and the column maxima.  `sb`, `bb`: this chunk's 16 column scales and biases.
+__device__ __forceinline__ void gelu_fwd_chunk16(const uint32_t (&acc)[16], uint8_t* buf, uint32_t buf_addr,
+                                                 int64_t row, int64_t fb, const EpiParams& p, float sa, int lane,
+                                                 const float* sb, const float* bb, uint32_t tab, uint32_t& rmax,
+                                                 const CUtensorMap* tmD, const CUtensorMap* tmH) {
   const bool live = row < p.M;
-  float sb[32], bb[32];
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) {  // shared-memory broadcasts: every lane reads the same values
-    const float4 a = *reinterpret_cast<const float4*>(cb + j);
-    sb[j] = a.x; sb[j + 1] = a.y; sb[j + 2] = a.z; sb[j + 3] = a.w;
-    const float4 c = *reinterpret_cast<const float4*>(cb + 128 + j);
-    bb[j] = c.x; bb[j + 1] = c.y; bb[j + 2] = c.z; bb[j + 3] = c.w;
-  }
-  uint32_t wu[16], wh[16];
+  uint32_t wu[8], wh[8];
   bool rare = false;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
+  for (int q = 0; q < 8; ++q) {
     float t2[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -735,22 +737,35 @@ __device__ __forceinline__ void gelu_fwd_chunk(const uint32_t (&acc)[32], int64_
   }
   if (__builtin_expect(rare, 0)) {  // inputs outside the table: the arithmetic itself
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const uint32_t b0 = wu[q] & 0xFFFFu, b1 = wu[q] >> 16;
       if (gelu_tab_index(b0) < 0) wh[q] = (wh[q] & 0xFFFF0000u) | gelu_fwd_bits_slow(b0, p.act_variant);
       if (gelu_tab_index(b1) < 0) wh[q] = (wh[q] & 0xFFFFu) | (gelu_fwd_bits_slow(b1, p.act_variant) << 16);
     }
   }
-  const int32_t row0 = (int32_t)(row - lane);
-  staged_store<true>(wu, tmD, (int32_t)fb, row0, lane, stage, stage_addr, nst);
-  staged_store<true>(wh, tmH, (int32_t)fb, row0, lane, stage, stage_addr, nst);
-  uint32_t a[16];
+  const int sw = (lane >> 2) & 1;
+  uint4* ud = reinterpret_cast<uint4*>(buf + lane * 32);
+  uint4* hd = reinterpret_cast<uint4*>(buf + kSwbBoxBytes + lane * 32);
+  ud[sw] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+  ud[sw ^ 1] = make_uint4(wu[4], wu[5], wu[6], wu[7]);
+  hd[sw] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+  hd[sw ^ 1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int32_t row0 = (int32_t)(row - lane);
+    tma_store_2d(tmD, buf_addr, (int32_t)fb, row0);
+    tma_store_2d(tmH, buf_addr + kSwbBoxBytes, (int32_t)fb, row0);
+    bulk_commit_group();
+  }
+  uint32_t a[8];
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    a[q] = live ? abs_bf16x2(wh[q]) : 0u;  // rows past M hold no data
+  for (int q = 0; q < 8; ++q) {
+    a[q] = live ? abs_bf16x2(wh[q]) : 0u;  // rows past M hold no data (their h is gelu(bias))
     rmax = max_bf16x2(rmax, a[q]);
   }
-  atomicMax(p.col_amax + fb + lane, warp_colmax_bits(a, lane));
+  const uint32_t m = warp_colmax16_bits(a, lane);
+  if (!(lane & 2)) atomicMax(p.col_amax + fb + colmax16_feature(lane), m);
 }
 
 // kSwbChunk (16) features of the GELU backward epilogue for one row (one thread): dh = bf16(acc * sa)
@@ -1042,26 +1057,27 @@ constexpr int C2_STAGES_SWB = FF_SWB_STAGES;
 __host__ __device__ constexpr int c2_smem_ring(int out) {
   return C2_STAGES_SWB * C2_STAGE_BYTES + 1024 + (int)ring_ctrl_bytes(out);
 }
-static_assert(c2_smem_ring(kOutSwigluBwd) <= 232448 && c2_smem_ring(kOutGeluBwd) <= 232448,
-              "a ring-epilogue kernel exceeds the shared memory of a CTA");
+static_assert(c2_smem_ring(kOutSwigluBwd) <= 232448 && c2_smem_ring(kOutGeluBwd) <= 232448 &&
+                  c2_smem_ring(kOutGeluFwd) <= 232448,
+              "a wide-epilogue kernel exceeds the shared memory of a CTA");
 template <int OUT>
 __host__ __device__ constexpr int c2_stages() {
-  return is_ring(OUT)   ? C2_STAGES_SWB
+  return is_wide(OUT)   ? C2_STAGES_SWB
          : is_gelu(OUT) ? C2_STAGES_GELU
                               : (is_fused_act(OUT) ? C2_STAGES_SW : C2_STAGES);
 }
 template <int OUT>
 __host__ __device__ constexpr int c2_smem_bytes() {
-  return is_ring(OUT)   ? c2_smem_ring(OUT)
+  return is_wide(OUT)   ? c2_smem_ring(OUT)
          : is_gelu(OUT) ? C2_SMEM_BYTES_GELU
                               : (is_fused_act(OUT) ? C2_SMEM_BYTES_SW : (OUT == FF_OUT_BF16 ? C2_SMEM_BYTES_ST : C2_SMEM_BYTES));
 }
 // threads of the 2-CTA kernel: TMA warp, MMA warp, then 8 epilogue warps (two per TMEM lane
 // quarter, each on half of the tile's columns), so a tile's epilogue takes half as long; the
-// ring epilogues run kSwbWpq warps per quarter
+// wide epilogues run kSwbWpq warps per quarter
 template <int OUT>
 __host__ __device__ constexpr int c2_threads() {
-  return is_ring(OUT) ? 64 + 32 * kSwbWarps : 320;
+  return is_wide(OUT) ? 64 + 32 * kSwbWarps : 320;
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -1187,7 +1203,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   constexpr uint32_t gelu_tab_off =
-      is_ring(OUT) ? ring_tab_off(OUT) : 512u + 8u * 2u * C2_SW_BUF_FLOATS * 4u + 8u * 2u * 2048u;
+      is_wide(OUT) ? ring_tab_off(OUT) : 512u + 8u * 2u * C2_SW_BUF_FLOATS * 4u + 8u * 2u * 2048u;
   if constexpr (is_gelu(OUT)) {  // the CTA's GELU table, by all threads
     for (int i = threadIdx.x; i < kGeluTabEntries; i += c2_threads<OUT>()) {
       const uint32_t b16 = gelu_tab_bits(i);
@@ -1292,8 +1308,8 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     uint32_t acc_phase = 0;
     // SwiGLU: this warp's two staging buffers of its features' column scales and bias (the
     // backward epilogue: one buffer of its column multipliers)
-    constexpr int sw_bufs = is_ring(OUT) ? 1 : 2;
-    float* sw_buf = is_ring(OUT) ? reinterpret_cast<float*>(ctrl + kSwbCmOff + (warp - 2) * ring_cm_bytes(OUT))
+    constexpr int sw_bufs = is_wide(OUT) ? 1 : 2;
+    float* sw_buf = is_wide(OUT) ? reinterpret_cast<float*>(ctrl + kSwbCmOff + (warp - 2) * ring_cm_bytes(OUT))
                                  : reinterpret_cast<float*>(ctrl + 256) + (warp - 2) * sw_bufs * C2_SW_BUF_FLOATS;
     // this warp's two TMA-store staging buffers (32 rows x 64 B each, 512-byte aligned for the
     // 64-byte swizzle); with the activation epilogues they follow the 8 warps' scale/bias buffers
@@ -1306,9 +1322,10 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
     // its chunk indices that lie below F) in schedule order; lane 0 keeps the cursor of the next
     // chunk to load (item sj, chunk sc at tile sm, sn) and the count of chunks loaded.
     constexpr int kRingBuf = ring_buf_bytes(OUT);
-    [[maybe_unused]] const uint32_t swb_ring = cbase + ring_off(OUT) + (uint32_t)(warp - 2) * kSwbBufs * kRingBuf;
-    [[maybe_unused]] uint8_t* swb_ring_p = ctrl + ring_off(OUT) + (warp - 2) * kSwbBufs * kRingBuf;
-    [[maybe_unused]] const uint32_t swb_bar = cbase + ring_bar_off(OUT) + (uint32_t)(warp - 2) * kSwbBufs * 8;
+    constexpr int kRingBufs = ring_bufs(OUT);
+    [[maybe_unused]] const uint32_t swb_ring = cbase + ring_off(OUT) + (uint32_t)(warp - 2) * kRingBufs * kRingBuf;
+    [[maybe_unused]] uint8_t* swb_ring_p = ctrl + ring_off(OUT) + (warp - 2) * kRingBufs * kRingBuf;
+    [[maybe_unused]] const uint32_t swb_bar = cbase + ring_bar_off(OUT) + (uint32_t)(warp - 2) * kRingBufs * 8;
     // chunks of tile column tn below F (16, or 8 for a last tile of 128 features: F % 128 == 0)
     auto swb_chunks = [&](int tn_) { return (int)min64(C2_BN / kSwbChunk, (ep.F - (int64_t)tn_ * C2_BN) / kSwbChunk); };
     int sj = 0, sc = 0, sm = 0, sn = 0, swb_loaded = 0, swb_used = 0;
@@ -1364,11 +1381,15 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         st_s2 = in2 ? __ldg(reinterpret_cast<const float4*>(ep.colmul + col + 128)) : one4;
       }
       if constexpr (OUT == kOutGeluFwd) {
-        // this warp's 128 features of the tile: lane l holds the column scales and bias of features 4l..4l+3
-        const int64_t col = (int64_t)tn * C2_BN + eh * 128 + lane * 4;
-        const bool in = col < ep.F;
-        st_s = in && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : make_float4(1.f, 1.f, 1.f, 1.f);
-        st_b = in && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        // the tile's 256 features: lane l holds the column scales and biases of features 4l..4l+3 and
+        // 128+4l..128+4l+3
+        const int64_t col = (int64_t)tn * C2_BN + lane * 4;
+        const bool in = col < ep.F, in2 = col + 128 < ep.F;
+        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f), zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        st_s = in && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : one4;
+        st_s2 = in2 && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col + 128)) : one4;
+        st_b = in && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : zero4;
+        st_b2 = in2 && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col + 128)) : zero4;
       }
       if constexpr (OUT == kOutSwigluFwd) {
         // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
@@ -1380,7 +1401,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
       tc_fence_after();
       if constexpr (is_fused_act(OUT)) {
         float* buf = sw_buf + (sw_bufs == 2 ? acc : 0) * C2_SW_BUF_FLOATS;
-        if constexpr (OUT == kOutSwigluBwd) {  // [gate 256 | up 256]
+        if constexpr (OUT == kOutSwigluBwd || OUT == kOutGeluFwd) {  // [gate 256 | up 256], [scale 256 | bias 256]
           reinterpret_cast<float4*>(buf)[lane] = st_s;
           reinterpret_cast<float4*>(buf + 128)[lane] = st_s2;
           reinterpret_cast<float4*>(buf + 256)[lane] = st_b;
@@ -1417,21 +1438,28 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
           atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
                                                                __uint_as_float(rmax & 0xFFFF0000u))));
       } else if constexpr (OUT == kOutGeluFwd) {
-        uint32_t rmax = 0u;
+        const int nchunks = swb_chunks(tn);
+        if (nchunks > eh) {
+          uint32_t rmax = 0u;
+          const float* cmb = sw_buf;  // [scale 256 | bias 256] of the tile's features
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {  // this warp's 128 features: four chunks of 32
-          const int fc = eh * 128 + c * 32;
-          const int64_t fb = (int64_t)tn * C2_BN + fc;
-          if (fb >= ep.F) break;
-          uint32_t r[32];
-          tmem_ld32(tbase + fc, r);
-          tmem_wait_ld();
-          gelu_fwd_chunk(r, row, fb, ep, sa, lane, sw_buf + acc * C2_SW_BUF_FLOATS + c * 32,
-                         cbase + gelu_tab_off, rmax, &tmD, &tmH, st_stage, st_stage_addr, st_count);
+          for (int c = eh; c < nchunks; c += kSwbWpq, ++swb_used) {
+            const int b = swb_used & 1;
+            if (swb_used >= 2) {  // this buffer's stores (two chunks ago) must have read it
+              if (lane == 0) bulk_wait_read_1();
+              __syncwarp();
+            }
+            uint32_t r[16];
+            tmem_ld16(tbase + c * kSwbChunk, r);
+            tmem_wait_ld();
+            gelu_fwd_chunk16(r, swb_ring_p + b * kRingBuf, swb_ring + (uint32_t)(b * kRingBuf), row,
+                             (int64_t)tn * C2_BN + c * kSwbChunk, ep, sa, lane, cmb + c * kSwbChunk,
+                             cmb + 256 + c * kSwbChunk, cbase + gelu_tab_off, rmax, &tmD, &tmH);
+          }
+          if (row < ep.M)
+            atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
+                                                                 __uint_as_float(rmax & 0xFFFF0000u))));
         }
-        if (row < ep.M)
-          atomicMax(ep.row_amax + row, __float_as_uint(fmaxf(__uint_as_float(rmax << 16),
-                                                               __uint_as_float(rmax & 0xFFFF0000u))));
       } else if constexpr (is_ring(OUT)) {
         const int nchunks = swb_chunks(tn);
         if (nchunks > eh) {
@@ -1495,7 +1523,7 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         acc_phase ^= 1u;
       }
     }
-    if ((st_count || is_ring(OUT)) && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
+    if ((st_count || is_wide(OUT)) && lane == 0) bulk_wait_all();  // TMA stores complete before the CTA exits
     __syncwarp();
   }
 
@@ -1964,9 +1992,10 @@ extern "C" int ff_gelu_gemm_i8(const int8_t* A, int64_t lda, const int8_t* B, in
   if (rc) return rc;
   rc = make_map(&mb, B, F, K, ldb, C2_BN_CTA);
   if (rc) return rc;
-  rc = make_map_out_bf16(&md, u, M, F, ldu, true);
+  // u and h stores: boxes of one epilogue chunk (kSwbChunk features x 32 rows)
+  rc = make_map_bf16(&md, u, M, F, ldu, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
-  rc = make_map_out_bf16(&mh, h, M, F, ldh, true);
+  rc = make_map_bf16(&mh, h, M, F, ldh, kSwbChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   EpiParams ep{};
   ep.scale_a = scale_a;
