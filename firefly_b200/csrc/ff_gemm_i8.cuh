@@ -720,15 +720,13 @@ __device__ __forceinline__ void gelu_fwd_chunk16(const uint32_t (&acc)[16], uint
   bool rare = false;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
+    // ((acc * sa) * sb) + bias, each step rounded (never contracted), with the missing factors 1 and
+    // the missing bias -0 (exact identities)
     float t2[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int j = 2 * q + e;
-      float t = __int2float_rn((int)acc[j]);
-      if (p.scale_a) t = __fmul_rn(t, sa);
-      if (p.scale_b) t = __fmul_rn(t, sb[j]);
-      if (p.bias) t = __fadd_rn(t, bb[j]);
-      t2[e] = t;
+      t2[e] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn((int)acc[j]), sa), sb[j]), bb[j]);
     }
     wu[q] = pack_bf16x2(mk2(t2[0], t2[1]));
     const int i0 = gelu_tab_index(wu[q] & 0xFFFFu), i1 = gelu_tab_index(wu[q] >> 16);
@@ -1385,11 +1383,12 @@ __global__ void __launch_bounds__(c2_threads<OUT>(), 1)
         // 128+4l..128+4l+3
         const int64_t col = (int64_t)tn * C2_BN + lane * 4;
         const bool in = col < ep.F, in2 = col + 128 < ep.F;
-        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f), zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        // missing scales are 1 and a missing bias -0: x * 1 and x + (-0) give x exactly, signed zeros included
+        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f), nzero4 = make_float4(-0.f, -0.f, -0.f, -0.f);
         st_s = in && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col)) : one4;
         st_s2 = in2 && ep.scale_b ? __ldg(reinterpret_cast<const float4*>(ep.scale_b + col + 128)) : one4;
-        st_b = in && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : zero4;
-        st_b2 = in2 && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col + 128)) : zero4;
+        st_b = in && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col)) : nzero4;
+        st_b2 = in2 && ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + col + 128)) : nzero4;
       }
       if constexpr (OUT == kOutSwigluFwd) {
         // lanes 0-15: the 64 gate features of this warp, lanes 16-31: the same 64 up features
