@@ -69,6 +69,8 @@ SIGNATURES = {
     "ff_gemm_i8_kn": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "ff_colsum_ws_elems": (_I64, [_I64, _I64]),
     "ff_colsum_bf16": (_I, [_P, _I64, _I64, _I64, _P, _P, _P]),
+    "ff_quant_dual_db_ws_elems": (_I64, [_I64, _I64]),
+    "ff_quant_dual_i8_db": (_I, [_P, _I64, _I64, _I64, _P, _F, _P, _I64, _P, _P, _I64, _P, _P, _P, _P, _P]),
     "ff_dqt_adamw8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
                            _D, _D, _D, _D, _D, _D, _D, _D, _U64, _U64, _I64, _P, _P, _P, _P]),
     "ff_dqt_adamw8_peers": (_I, [_P, _P, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
@@ -97,7 +99,7 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_gelu_eval": 1, "ff_gelu_gemm_i8": 2, "ff_gelu_bwd_gemm_i8": 2,
                      "ff_layernorm_i8": 2, "ff_layernorm_bwd": 3,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1, "ff_gemm_i8_ws": 1,
-                     "ff_colsum_bf16": 2, "ff_dqt_adamw8": 1, "ff_dqt_adamw8_peers": 1, "ff_update_int8_weight": 1,
+                     "ff_colsum_bf16": 2, "ff_quant_dual_i8_db": 3, "ff_dqt_adamw8": 1, "ff_dqt_adamw8_peers": 1, "ff_update_int8_weight": 1,
                      "ff_adamw8_blockwise": 1}
 
 
@@ -241,11 +243,14 @@ def quant_rows(x: torch.Tensor, colmul: torch.Tensor | None = None, eps: float =
 
 
 def quant_dual(x: torch.Tensor, row_colmul: torch.Tensor | None = None, eps: float = 1e-8,
-               rows: bool = True, cols: bool = True):
+               rows: bool = True, cols: bool = True, colsum: bool = False):
     """Row codes ``[R, ldq]`` (ldq = round_up(C,16)) and transposed column codes
     ``[C, ldqt]`` (ldqt = round_up(R,16)) with their scales.  Either part may be skipped
-    (returned as ``None``)."""
+    (returned as ``None``).  ``colsum=True`` (bf16 ``x`` only) appends a fifth output, the
+    bf16 column sums of ``x`` (``colsum_bf16(x)``'s values), taken in the same read of x."""
     dev = _require_cuda(x, row_colmul)
+    if colsum and x.dtype != torch.bfloat16:
+        raise ValueError(f"quant_dual(colsum=True) needs a bf16 input, got {x.dtype}")
     x, ldx = _rows_view(x)
     R, C = x.shape
     if C == 0:
@@ -261,6 +266,13 @@ def quant_dual(x: torch.Tensor, row_colmul: torch.Tensor | None = None, eps: flo
     ws = torch.empty((R + C,), dtype=torch.float32, device=dev)
     if row_colmul is not None:
         row_colmul = row_colmul.to(torch.float32).contiguous()
+    if colsum:
+        db = torch.empty((C,), dtype=torch.bfloat16, device=dev)
+        db_ws = torch.empty((int(lib().ff_quant_dual_db_ws_elems(R, C)),), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _call("ff_quant_dual_i8_db", _ptr(x), R, C, ldx, _ptr(row_colmul), float(eps), _ptr(q_rows), ldq,
+                  _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols), _ptr(ws), _ptr(db), _ptr(db_ws), _stream(dev))
+        return q_rows, s_rows, q_cols, s_cols, db
     with torch.cuda.device(dev):
         _call("ff_quant_dual_i8", _ptr(x), _dtype_code(x.dtype), R, C, ldx, _ptr(row_colmul),
               float(eps), _ptr(q_rows), ldq, _ptr(s_rows), _ptr(q_cols), ldqt, _ptr(s_cols),

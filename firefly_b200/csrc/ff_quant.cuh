@@ -5,6 +5,8 @@
 //   q = clamp(rint(v / s), -127, 127)  (IEEE divide, round half to even)
 // Integer codes are bit-exact with the reference's torch CPU path.
 #pragma once
+#include <type_traits>
+
 #include "ff_common.cuh"
 
 namespace ff {
@@ -469,12 +471,16 @@ template <class Src>
 __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_kernel(
     Src src, int64_t rows, int64_t cols, const float* __restrict__ colmul, bool want_rows, bool want_cols,
     uint32_t* __restrict__ row_amax, uint32_t* __restrict__ col_amax, __nv_bfloat16* __restrict__ store,
-    int64_t lds) {
+    int64_t lds, float* __restrict__ colsum) {
   constexpr int NO = Src::NOUT;
   constexpr int U = Src::kRowsInFlight;
   constexpr bool W = Src::kWords;
+  // colsum (plain bf16 sources only): this CTA's column sums of its 128 rows, fp32, the even
+  // rows' sum plus the odd rows' (each in row order), at colsum[blockIdx.y * cols + c]
+  constexpr bool kSums = std::is_same_v<Src, PlainSrc<FF_DTYPE_BF16>>;
   __shared__ float red[kDualARows][5];    // per row: 4 warps' partial maxima
   __shared__ float cred[NO][kDualACols];  // odd-row half's column maxima
+  __shared__ float csred[kSums ? kDualACols : 1];  // odd-row half's column sums
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = tid >> 7, ct = tid & 127;
   const int64_t c0 = (int64_t)blockIdx.x * kDualACols + ct * 8;
@@ -501,6 +507,7 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
     for (int j = 0; j < (W ? 1 : 8); ++j) cmax[o][j] = 0.f;
   }
   const int nr = (int)min64(kDualARows, rows - r0);
+  f2 csum2[4] = {splat(0.f), splat(0.f), splat(0.f), splat(0.f)};
 #pragma unroll 1
   for (int i0 = half; i0 < kDualARows; i0 += 2 * U) {
     typename Src::Raw v[U];
@@ -517,6 +524,12 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
       if constexpr (W) {
         uint32_t wv[NO][4];
         src.eval_words(v[u], wv);  // columns past the end were loaded as zeros: value 0
+        if constexpr (kSums) {
+          if (colsum && i < nr) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) csum2[q] = add2(csum2[q], unpack_bf16x2(wv[0][q]));
+          }
+        }
         uint32_t rmw = 0u;
 #pragma unroll
         for (int o = 0; o < NO; ++o)
@@ -587,7 +600,24 @@ __global__ void __launch_bounds__(kDualAThreads, Src::kMinBlocks) dual_absmax_ke
 #pragma unroll
       for (int j = 0; j < 8; ++j) cred[o][ct * 8 + j] = cfin[o][j];
   }
+  if constexpr (kSums) {
+    if (colsum && half == 1) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) un2(csum2[q], csred[ct * 8 + 2 * q], csred[ct * 8 + 2 * q + 1]);
+    }
+  }
   __syncthreads();
+  if constexpr (kSums) {
+    if (colsum && half == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float a0, a1;
+        un2(add2(csum2[q], mk2(csred[ct * 8 + 2 * q], csred[ct * 8 + 2 * q + 1])), a0, a1);
+        if (c0 + 2 * q < cols) colsum[(int64_t)blockIdx.y * cols + c0 + 2 * q] = a0;
+        if (c0 + 2 * q + 1 < cols) colsum[(int64_t)blockIdx.y * cols + c0 + 2 * q + 1] = a1;
+      }
+    }
+  }
   if (want_cols && half == 0) {
 #pragma unroll
     for (int o = 0; o < NO; ++o)
@@ -847,13 +877,13 @@ namespace ff {
 template <class Src>
 int launch_pass_a(const char* name, const Src& src, int64_t rows, int64_t cols, const float* colmul,
                   bool do_rows, bool do_cols, float* absmax_ws, __nv_bfloat16* store, int64_t lds,
-                  cudaStream_t st) {
+                  cudaStream_t st, float* colsum = nullptr) {
   uint32_t* row_amax = reinterpret_cast<uint32_t*>(absmax_ws);
   FF_CUDA_TRY(cudaMemsetAsync(absmax_ws, 0, sizeof(float) * (size_t)(rows + Src::NOUT * cols), st), name);
   dim3 gA((unsigned)((cols + kDualACols - 1) / kDualACols), (unsigned)((rows + kDualARows - 1) / kDualARows));
   FF_REQUIRE(gA.y < 65536, FF_ERR_UNSUPPORTED, "%s: too many rows", name);
   dual_absmax_kernel<Src><<<gA, kDualAThreads, 0, st>>>(src, rows, cols, colmul, do_rows, do_cols, row_amax,
-                                                         row_amax + rows, store, lds);
+                                                         row_amax + rows, store, lds, colsum);
   return check_launch(name);
 }
 
@@ -920,6 +950,43 @@ extern "C" int ff_quant_dual_i8(const void* x, int dtype, int64_t rows, int64_t 
   if (dtype == FF_DTYPE_BF16) FF_DQ(FF_DTYPE_BF16)
   FF_DQ(FF_DTYPE_F16)
 #undef FF_DQ
+}
+
+extern "C" int64_t ff_quant_dual_db_ws_elems(int64_t rows, int64_t cols) {
+  const int64_t nch = (rows + ff::kDualARows - 1) / ff::kDualARows;
+  return (nch > 0 ? nch : 1) * (cols > 0 ? cols : 1);
+}
+
+extern "C" int ff_quant_dual_i8_db(const uint16_t* x, int64_t rows, int64_t cols, int64_t ldx,
+                                   const float* row_colmul, float eps, int8_t* q_rows, int64_t ldq,
+                                   float* s_rows, int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                                   float* absmax_ws, uint16_t* db, float* db_ws, void* stream) {
+  using namespace ff;
+  FF_REQUIRE(rows >= 0 && cols >= 1 && ldx >= cols, FF_ERR_INVALID_ARG,
+             "ff_quant_dual_i8_db: rows=%lld cols=%lld ldx=%lld", (long long)rows, (long long)cols,
+             (long long)ldx);
+  FF_REQUIRE(q_rows || q_cols_t, FF_ERR_INVALID_ARG, "ff_quant_dual_i8_db: nothing to do");
+  FF_REQUIRE(db && db_ws, FF_ERR_INVALID_ARG, "ff_quant_dual_i8_db: null db or db workspace");
+  cudaStream_t st = as_stream(stream);
+  if (rows == 0) {
+    FF_CUDA_TRY(cudaMemsetAsync(db, 0, sizeof(uint16_t) * cols, st), "ff_quant_dual_i8_db memset");
+    return FF_OK;
+  }
+  FF_REQUIRE(x, FF_ERR_INVALID_ARG, "ff_quant_dual_i8_db: null input");
+  int rc = check_dual_outputs("ff_quant_dual_i8_db", rows, cols, q_rows, ldq, s_rows, q_cols_t, ldqt, s_cols,
+                              absmax_ws);
+  if (rc != FF_OK) return rc;
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  rc = launch_pass_a("ff_quant_dual_i8_db", PlainSrc<FF_DTYPE_BF16>{xb, ldx}, rows, cols, row_colmul,
+                     q_rows != nullptr, q_cols_t != nullptr, absmax_ws, nullptr, 0, st, db_ws);
+  if (rc != FF_OK) return rc;
+  const int64_t nch = (rows + kDualARows - 1) / kDualARows;
+  colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(db_ws, nch, cols,
+                                                                reinterpret_cast<__nv_bfloat16*>(db));
+  rc = check_launch("ff_quant_dual_i8_db");
+  if (rc != FF_OK) return rc;
+  return launch_pass_b<FF_DTYPE_BF16>("ff_quant_dual_i8_db", xb, rows, cols, ldx, row_colmul, eps, q_rows, ldq,
+                                      s_rows, q_cols_t, ldqt, s_cols, absmax_ws, st);
 }
 
 extern "C" int ff_swiglu_quant_i8(const uint16_t* g, const uint16_t* u, int64_t ld, int64_t rows, int64_t cols,

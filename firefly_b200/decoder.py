@@ -176,11 +176,11 @@ class GeluMLPFn(torch.autograd.Function):
             return dx, None, None, None, None, None, db, None
         dy = grad_out.to(torch.bfloat16).contiguous()
         # down projection: dH = dY·W_d (GELU backward and du's absmax in its epilogue), dW_d = dYᵀ·H
-        q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=d_ws)
+        q_g, s_g, q_dyt, s_dy, *db = _capi.quant_dual(dy, row_colmul=d_ws, colsum=ctx.has_bias)
         q_d, s_d, q_dt, s_dc, _ = _capi.gelu_bwd_gemm(q_g, _weight_operand(d_handle, d_weight), O, s_g, u,
                                                       colmul=up_ws, rows=need_dx)
         _weight_grad_gemm(d_handle, q_dyt, s_dy, q_ht, s_hc, O, Fh, T, dev)
-        db = _capi.colsum_bf16(dy).to(grad_out.dtype) if ctx.has_bias else None
+        db = db[0].to(grad_out.dtype) if ctx.has_bias else None
         dx = None
         if need_dx:
             dx = _capi.gemm_i8(q_d, _weight_operand(up_handle, up_weight), Fu, scale_a=s_d,

@@ -265,14 +265,16 @@ class Int8LinearFn(torch.autograd.Function):
                 grad_in = torch.zeros((0, K), dtype=grad_out.dtype, device=dy.device)
             db = torch.zeros((O,), dtype=grad_out.dtype, device=dy.device) if ctx.has_bias else None
             return grad_in, None, None, db, None
-        q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=ws, rows=need_dx, cols=True)
+        # db = Σ_rows dY (fireflykernels.py:200) comes out of the same read of dY
+        q_g, s_g, q_dyt, s_dy, *db = _capi.quant_dual(dy, row_colmul=ws, rows=need_dx, cols=True,
+                                                      colsum=ctx.has_bias)
         if need_dx:
             # dX = dY·W contracts over O: W [O, K] is read directly as the K x N operand
             w_op = _weight_operand(ctx.handle, int_weight)
             grad_in = _capi.gemm_i8(q_g, w_op, O, scale_a=s_g, out_kind=_capi.FF_OUT_BF16, b_kn_cols=K)
         # dW = dYᵀ X, accumulated in the epilogue (fireflykernels.py:193-198)
         _weight_grad_gemm(ctx.handle, q_dyt, s_dy, q_xt, s_xc, O, K, T, dy.device)
-        grad_bias = _capi.colsum_bf16(dy) if ctx.has_bias else None
+        grad_bias = db[0] if ctx.has_bias else None
         if grad_bias is not None and grad_bias.dtype != grad_out.dtype:
             grad_bias = grad_bias.to(grad_out.dtype)
         if grad_in is not None and grad_in.dtype != grad_out.dtype:

@@ -94,7 +94,7 @@ class SwiGLUMLPFn(torch.autograd.Function):
             return dx, None, None, None, None, None, db, None
         dy = grad_out.to(torch.bfloat16).contiguous()
         # down projection: dH = dY·W_d, dW_d = dYᵀ·H, db = Σ dY
-        q_g, s_g, q_dyt, s_dy = _capi.quant_dual(dy, row_colmul=d_ws)
+        q_g, s_g, q_dyt, s_dy, *db = _capi.quant_dual(dy, row_colmul=d_ws, colsum=ctx.has_bias)
         w_d = _weight_operand(d_handle, d_weight)
         if Fh % 128 == 0:  # dH, the SwiGLU backward and [dg | du]'s absmax in one GEMM epilogue
             q_d, s_d, q_dt, s_dc, _ = _capi.swiglu_bwd_gemm(q_g, w_d, O, s_g, gu, colmul=gu_ws, rows=need_dx)
@@ -102,7 +102,7 @@ class SwiGLUMLPFn(torch.autograd.Function):
             dh = _capi.gemm_i8(q_g, w_d, O, scale_a=s_g, out_kind=_capi.FF_OUT_BF16, b_kn_cols=Fh)
             q_d, s_d, q_dt, s_dc, _ = _capi.swiglu_bwd_quant(dh, gu, colmul=gu_ws, rows=need_dx)
         _weight_grad_gemm(d_handle, q_dyt, s_dy, q_ht, s_hc, O, Fh, T, dev)
-        db = _capi.colsum_bf16(dy).to(grad_out.dtype) if ctx.has_bias else None
+        db = db[0].to(grad_out.dtype) if ctx.has_bias else None
         dx = None
         if need_dx:
             dx = _capi.gemm_i8(q_d, _weight_operand(gu_handle, gu_weight), F2, scale_a=s_d,

@@ -380,6 +380,23 @@ FF_API int ff_colsum_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t
                    uint16_t* out, float* ws, void* stream);
 
 /*
+ * ff_quant_dual_i8 of a bf16 matrix (the output gradient dY) that also writes the bias
+ * gradient db[c] = bf16(sum_r x[r,c]) from the same read of x: the column sums are
+ * accumulated in fp32 inside the absmax pass (per 128-row block, even and odd rows each in
+ * row order, then the two added) and a second small kernel adds the blocks in order and
+ * rounds to bf16.  Deterministic.  db_ws: fp32 workspace of ff_quant_dual_db_ws_elems(rows,
+ * cols) elements; the other arguments as ff_quant_dual_i8 (dtype bf16).  rows == 0 writes
+ * db = 0.  Replaces the operand preparation of go_bf16 (fireflykernels.py:185) together
+ * with go_bf16.sum(dim=0) (fireflykernels.py:200).
+ */
+FF_API int64_t ff_quant_dual_db_ws_elems(int64_t rows, int64_t cols);
+FF_API int ff_quant_dual_i8_db(const uint16_t* x, int64_t rows, int64_t cols, int64_t ldx,
+                               const float* row_colmul, float eps,
+                               int8_t* q_rows, int64_t ldq, float* s_rows,
+                               int8_t* q_cols_t, int64_t ldqt, float* s_cols,
+                               float* absmax_ws, uint16_t* db, float* db_ws, void* stream);
+
+/*
  * Block-wise 8-bit AdamW step of a dense (non-BitLinear) parameter, in place.
  * Replaces bitsandbytes' AdamW8bit, which steps the reference's dense parameters
  * (fireflyoptim.py:83, :124); the algorithm is the published one (Dettmers et al., ICLR

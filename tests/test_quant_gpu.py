@@ -139,6 +139,36 @@ def test_colsum_bf16():
     np.testing.assert_array_equal(gb, _capi.colsum_bf16(x).cpu().view(torch.int16).numpy().view(np.uint16))
 
 
+@pytest.mark.parametrize("shape,colmul,rows", [((1000, 77), False, True), ((1, 5), False, True),
+                                               ((129, 1030), True, True), ((300, 2050), True, False),
+                                               ((4096, 512), False, True), ((0, 24), False, True)])
+def test_quant_dual_with_column_sums(shape, colmul, rows):
+    """quant_dual(colsum=True): the same codes and scales as quant_dual, plus the bias
+    gradient Σ_r x[r, :] within 1 bf16 ulp of the exact sum, deterministic."""
+    from tests._util import bf16_ulp_diff
+    R, C = shape
+    x = _rand(shape, torch.bfloat16, seed=R * 3 + C).to(DEV)
+    cm = (torch.rand(C, generator=torch.Generator().manual_seed(C)) + 0.5).to(DEV) if colmul else None
+    got = _capi.quant_dual(x, row_colmul=cm, rows=rows, colsum=True)
+    if R:
+        want = _capi.quant_dual(x, row_colmul=cm, rows=rows)
+        for a, b in zip(got[:4], want):
+            assert (a is None) == (b is None)
+            if a is not None:
+                np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+    exact = O.f32_to_bf16_bits(x.float().cpu().numpy().astype(np.float64).sum(0).astype(np.float32))
+    db = got[4].cpu().view(torch.int16).numpy().view(np.uint16)
+    assert db.shape == (C,)
+    assert bf16_ulp_diff(db, exact).max() <= 1
+    again = _capi.quant_dual(x, row_colmul=cm, rows=rows, colsum=True)[4]
+    np.testing.assert_array_equal(db, again.cpu().view(torch.int16).numpy().view(np.uint16))
+
+
+def test_quant_dual_column_sums_need_bf16():
+    with pytest.raises(ValueError):
+        _capi.quant_dual(torch.zeros((4, 8), dtype=torch.float32, device=DEV), colsum=True)
+
+
 def test_update_int8_weight():
     g = torch.Generator().manual_seed(9)
     w = torch.randint(-127, 128, (50, 60), generator=g, dtype=torch.int8)
