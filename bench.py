@@ -594,15 +594,30 @@ def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: 
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    opt.comm_events = []  # device time of the optimizer step and of its communication phases
+    host_step = 0.0
     e0.record()
     for _ in range(steps):
+        h0 = time.perf_counter()
         loss = train_step(model, opt, batches)
+        host_step += time.perf_counter() - h0
     e1.record()
     torch.cuda.synchronize()
     sec = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(sec, op=dist.ReduceOp.MAX)
     sec = float(sec.item())
+    phases = ["optimizer_step", "peer_update", "peer_fence_wait", "dense_all_reduce_wait", "reduce_scatter_wait",
+              "all_gather_wait"]
+    per = {k: 0.0 for k in phases}
+    for k, a, b in opt.comm_events:
+        per[k] += a.elapsed_time(b) / steps
+    opt.comm_events = None
+    per["host_train_step"] = host_step / steps * 1e3
+    pt = torch.tensor([per[k] for k in per], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+    per = {k: round(v, 3) for k, v in zip(per, pt.tolist())}
     tokens = seqs * seq * steps
     out = {
         "workload": (f"decoder_1p3b_dp_train_step: {cfg.layers} layers, d {cfg.d_model}, {cfg.heads} heads, ffn "
@@ -614,6 +629,12 @@ def decoder_dp_bench(dev, world: int, rank: int, steps: int, warmup: int, seqs: 
         "int8_gemm_tops_effective": cfg.int8_ops_per_token() * tokens / sec / 1e12,
         "attention_tflops_effective": attention_flops_per_sequence(cfg, seq) * seqs * steps / sec / 1e12,
         "final_loss": float(loss), "data": "synthetic token ids uniform over the vocabulary; weights N(0,0.02)",
+        "zero1_path": "peer" if getattr(opt, "peer", False) else ("collectives" if world > 1 else "local"),
+        "phases_ms_per_step": per,
+        "phases_method": ("CUDA events on the compute stream, mean per step, max over ranks: optimizer_step = "
+                          "the whole step() on the device (the rest of ms_per_step is the micro-batches' forward "
+                          "and backward), the other device phases are parts of it; host_train_step = host wall "
+                          "time of one train_step call (launch side)"),
     }
     del model, opt, batches
     torch.cuda.empty_cache()

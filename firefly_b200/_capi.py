@@ -82,7 +82,15 @@ SIGNATURES = {
     "ff_ipc_close": (_I, [_P]),
     "ff_update_int8_weight": (_I, [_P, _P, _I64, _P]),
     "ff_adamw8_blockwise": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I64, _D, _D, _D, _D, _D, _I64, _P, _P, _P]),
+    "ff_adamw32_multi": (_I, [_P, ctypes.c_int32, _F, ctypes.c_int32, _F, _F, _F, _F, _P]),
 }
+
+
+class Adamw32Tensor(ctypes.Structure):
+    """``FfAdamw32Tensor``: one dense parameter of ``ff_adamw32_multi``."""
+    _fields_ = [("param", _P), ("grad", _P), ("exp_avg", _P), ("exp_avg_sq", _P), ("numel", ctypes.c_int64),
+                ("param_dtype", ctypes.c_int32), ("grad_dtype", ctypes.c_int32), ("eps_term", _F),
+                ("step_scale", _F)]
 
 _lib = None
 
@@ -100,7 +108,8 @@ _KERNELS_PER_CALL = {"ff_quant_rows_i8": 1, "ff_quant_dual_i8": 2, "ff_quant_dua
                      "ff_layernorm_i8": 2, "ff_layernorm_bwd": 3,
                      "ff_transpose_i8": 1, "ff_gemm_i8": 1, "ff_gemm_i8_kn": 1, "ff_gemm_i8_ws": 1,
                      "ff_colsum_bf16": 2, "ff_quant_dual_i8_db": 3, "ff_dqt_adamw8": 1, "ff_dqt_adamw8_peers": 1, "ff_update_int8_weight": 1,
-                     "ff_adamw8_blockwise": 1}
+                     "ff_adamw8_blockwise": 1,
+                     "ff_adamw32_multi": 1}
 
 
 def lib() -> ctypes.CDLL:
@@ -897,3 +906,31 @@ def adamw8_blockwise(p: torch.Tensor, g: torch.Tensor, m_q: torch.Tensor, m_absm
         _call("ff_adamw8_blockwise", _ptr(p), _dtype_code(p.dtype), _ptr(g), _dtype_code(g.dtype), _ptr(m_q),
               _ptr(m_absmax), _ptr(v_q), _ptr(v_absmax), n, float(lr), float(beta1), float(beta2), float(eps),
               float(wd), int(step), _ptr(qmap_s.contiguous()), _ptr(qmap_u.contiguous()), _stream(dev))
+
+
+def adamw32_multi(items, *, lr: float, beta1: float, beta2: float, eps: float, wd: float) -> None:
+    """In-place fp32-moment AdamW step of many small dense parameters in one launch (per 64).
+
+    ``items``: ``(p, g, exp_avg, exp_avg_sq, step)`` per parameter, all on one CUDA device, contiguous,
+    p and g fp32 or bf16, the moments fp32; ``step`` is the parameter's step count after this step.
+    The scalars are rounded to fp32 exactly as torch rounds python-float operands."""
+    items = list(items)
+    if not items:
+        return
+    dev = _require_cuda(*[t for it in items for t in it[:4]])
+    arr = (Adamw32Tensor * len(items))()
+    for k, (p, g, m, v, step) in enumerate(items):
+        n = p.numel()
+        for name, t in (("param", p), ("grad", g), ("exp_avg", m), ("exp_avg_sq", v)):
+            if t.numel() != n or not t.is_contiguous() or t.device != dev:
+                raise ValueError(f"adamw32_multi: {name} of item {k} must be contiguous on {dev} with {n} elements")
+        if m.dtype != torch.float32 or v.dtype != torch.float32:
+            raise ValueError("adamw32_multi: the moments must be fp32")
+        if p.dtype not in (torch.float32, torch.bfloat16) or g.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"adamw32_multi: fp32 or bf16 parameters and gradients, got {p.dtype}/{g.dtype}")
+        bc1, bc2 = 1.0 - beta1 ** step, 1.0 - beta2 ** step
+        arr[k] = Adamw32Tensor(_ptr(p), _ptr(g), _ptr(m), _ptr(v), n, _dtype_code(p.dtype), _dtype_code(g.dtype),
+                               eps * bc2 ** 0.5, lr * bc2 ** 0.5 / bc1)
+    with torch.cuda.device(dev):
+        _call("ff_adamw32_multi", ctypes.cast(arr, _P), len(items), 1.0 - lr * wd, int(wd != 0.0), beta1,
+              1.0 - beta1, beta2, 1.0 - beta2, _stream(dev))

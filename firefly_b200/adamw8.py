@@ -13,7 +13,9 @@ al., "8-bit Optimizers via Block-wise Quantization", ICLR 2022) on the B200 kern
   length e selects the decade 10^-e, an indicator bit, and the remaining bits as a linear
   fraction in (0.1, 1];
 * parameters with fewer than ``min_8bit_size`` elements (biases, norm scales), and
-  parameters not on a CUDA device, keep fp32 moments (plain AdamW on the same formula).
+  parameters not on a CUDA device, keep fp32 moments (plain AdamW on the same formula);
+  the CUDA ones of a parameter group are stepped together by one multi-tensor kernel
+  (``ff_adamw32_multi``) rather than a dozen small kernels each.
 
 State per parameter: ``step`` and either ``m_q``/``m_absmax``/``v_q``/``v_absmax`` (8-bit)
 or ``exp_avg``/``exp_avg_sq`` (fp32).  The maps and the rounding of the update are this
@@ -80,6 +82,7 @@ class AdamW8bitDense(torch.optim.Optimizer):
                 loss = closure()
         for group in self.param_groups:
             lr, (b1, b2), eps, wd = group["lr"], group["betas"], group["eps"], group["weight_decay"]
+            fused: dict[torch.device, list] = {}  # small CUDA parameters: one multi-tensor launch per device
             for p in group["params"]:
                 if p.grad is None:
                     continue
@@ -88,8 +91,18 @@ class AdamW8bitDense(torch.optim.Optimizer):
                 state = self.state[p]
                 if self._eight_bit(p):
                     self._step_8bit(p, state, lr, b1, b2, eps, wd)
+                elif p.is_cuda and p.is_contiguous() and p.dtype in (torch.float32, torch.bfloat16):
+                    self._init_32bit(p, state)
+                    state["step"] += 1
+                    g = p.grad
+                    if g.dtype not in (torch.float32, torch.bfloat16):
+                        g = g.float()
+                    fused.setdefault(p.device, []).append(
+                        (p, g.contiguous(), state["exp_avg"], state["exp_avg_sq"], int(state["step"])))
                 else:
                     self._step_32bit(p, state, lr, b1, b2, eps, wd)
+            for items in fused.values():
+                _capi.adamw32_multi(items, lr=lr, beta1=b1, beta2=b2, eps=eps, wd=wd)
         return loss
 
     def _step_8bit(self, p, state, lr, b1, b2, eps, wd):
@@ -114,11 +127,17 @@ class AdamW8bitDense(torch.optim.Optimizer):
                                qmap_s=qs, qmap_u=qu)
 
     @staticmethod
-    def _step_32bit(p, state, lr, b1, b2, eps, wd):
+    def _init_32bit(p, state):
         if "exp_avg" not in state:
             state["step"] = 0
-            state["exp_avg"] = torch.zeros_like(p, dtype=torch.float32)
-            state["exp_avg_sq"] = torch.zeros_like(p, dtype=torch.float32)
+            state["exp_avg"] = torch.zeros_like(p, dtype=torch.float32, memory_format=torch.contiguous_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, dtype=torch.float32, memory_format=torch.contiguous_format)
+
+    @staticmethod
+    def _step_32bit(p, state, lr, b1, b2, eps, wd):
+        """fp32-moment AdamW in torch ops: parameters off the GPU, or of other dtypes or layouts
+        (CUDA fp32/bf16 parameters take the fused ``ff_adamw32_multi`` with the same roundings)."""
+        AdamW8bitDense._init_32bit(p, state)
         state["step"] += 1
         t = int(state["step"])
         g = p.grad.float()
@@ -134,10 +153,11 @@ class AdamW8bitDense(torch.optim.Optimizer):
 
     def load_state_dict(self, state_dict):
         # torch casts floating state tensors to the parameter's dtype; the block absmax
-        # arrays stay fp32
+        # arrays and the fp32 moments stay fp32
         saved = {}
         for pid, st in state_dict["state"].items():
-            saved[pid] = {k: v.clone() for k, v in st.items() if k in ("m_absmax", "v_absmax")}
+            saved[pid] = {k: v.clone() for k, v in st.items()
+                          if k in ("m_absmax", "v_absmax", "exp_avg", "exp_avg_sq")}
         super().load_state_dict(state_dict)
         params = [p for group in self.param_groups for p in group["params"]]
         for pid, p in enumerate(params):

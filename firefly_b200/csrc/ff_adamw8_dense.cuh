@@ -317,8 +317,102 @@ __global__ void __launch_bounds__(kThreads) adamw8_dense_kernel(Params p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// fp32-moment AdamW of many small parameters in one launch (the parameters below the 8-bit
+// size threshold: norm scales, biases).  The same per-element chain as above without the
+// 8-bit codes: the moments are read and written as fp32.  Up to kMultiMax tensors per launch,
+// their descriptors passed by value; CTA b works on chunk b - chunk0[t] of tensor t.
+// ---------------------------------------------------------------------------
+constexpr int kMultiMax = 64;
+constexpr int kMultiChunk = 4096;
+constexpr int kMultiThreads = 256;
+
+struct MultiParams {
+  FfAdamw32Tensor t[kMultiMax];
+  int32_t chunk0[kMultiMax + 1];  // first CTA of each tensor; chunk0[count] = the grid size
+  int32_t count;
+  int32_t use_decay;
+  float decay, b1, omb1, b2, omb2;
+};
+static_assert(sizeof(MultiParams) <= 4096, "kernel parameters of the multi-tensor AdamW");
+
+__global__ void __launch_bounds__(kMultiThreads) adamw32_multi_kernel(const __grid_constant__ MultiParams p) {
+  const int b = (int)blockIdx.x;
+  int lo = 0, hi = p.count - 1;  // the last tensor whose first CTA is <= b
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.chunk0[mid] <= b) lo = mid;
+    else hi = mid - 1;
+  }
+  const FfAdamw32Tensor& d = p.t[lo];
+  const int64_t i0 = (int64_t)(b - p.chunk0[lo]) * kMultiChunk;
+  const int64_t i1 = min64(i0 + kMultiChunk, d.numel);
+  const bool pbf = d.param_dtype == FF_DTYPE_BF16, gbf = d.grad_dtype == FF_DTYPE_BF16;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += kMultiThreads) {
+    const float g = gbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(d.grad)[i])
+                        : reinterpret_cast<const float*>(d.grad)[i];
+    float w = pbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(d.param)[i])
+                  : reinterpret_cast<const float*>(d.param)[i];
+    if (p.use_decay) w = __fmul_rn(w, p.decay);
+    const float m = __fadd_rn(__fmul_rn(d.exp_avg[i], p.b1), __fmul_rn(g, p.omb1));
+    const float v = __fadd_rn(__fmul_rn(d.exp_avg_sq[i], p.b2), __fmul_rn(__fmul_rn(g, p.omb2), g));
+    d.exp_avg[i] = m;
+    d.exp_avg_sq[i] = v;
+    w = __fsub_rn(w, __fmul_rn(__fdiv_rn(m, __fadd_rn(__fsqrt_rn(v), d.eps_term)), d.step_scale));
+    if (pbf) reinterpret_cast<__nv_bfloat16*>(d.param)[i] = __float2bfloat16_rn(w);
+    else reinterpret_cast<float*>(d.param)[i] = w;
+  }
+}
+
 }  // namespace dense
 }  // namespace ff
+
+extern "C" int ff_adamw32_multi(const FfAdamw32Tensor* tensors, int32_t count, float decay, int32_t use_decay,
+                                float beta1, float one_minus_beta1, float beta2, float one_minus_beta2,
+                                void* stream) {
+  using namespace ff;
+  using namespace ff::dense;
+  FF_REQUIRE(count >= 0, FF_ERR_INVALID_ARG, "ff_adamw32_multi: count=%d", count);
+  if (count == 0) return FF_OK;
+  FF_REQUIRE(tensors, FF_ERR_INVALID_ARG, "ff_adamw32_multi: null descriptor array");
+  for (int32_t i = 0; i < count; ++i) {
+    const FfAdamw32Tensor& d = tensors[i];
+    FF_REQUIRE(d.numel >= 0, FF_ERR_INVALID_ARG, "ff_adamw32_multi: tensor %d numel=%lld", i, (long long)d.numel);
+    FF_REQUIRE(d.numel == 0 || (d.param && d.grad && d.exp_avg && d.exp_avg_sq), FF_ERR_INVALID_ARG,
+               "ff_adamw32_multi: tensor %d has a null pointer", i);
+    FF_REQUIRE((d.param_dtype == FF_DTYPE_F32 || d.param_dtype == FF_DTYPE_BF16) &&
+                   (d.grad_dtype == FF_DTYPE_F32 || d.grad_dtype == FF_DTYPE_BF16),
+               FF_ERR_UNSUPPORTED, "ff_adamw32_multi: tensor %d dtypes %d/%d (fp32 or bf16)", i, d.param_dtype,
+               d.grad_dtype);
+    FF_REQUIRE(d.numel <= (int64_t)kMultiChunk * 65535, FF_ERR_UNSUPPORTED,
+               "ff_adamw32_multi: tensor %d has %lld elements", i, (long long)d.numel);
+  }
+  cudaStream_t st = as_stream(stream);
+  for (int32_t base = 0; base < count; base += kMultiMax) {
+    MultiParams prm;
+    prm.count = 0;
+    int32_t grid = 0;
+    for (int32_t i = base; i < count && i < base + kMultiMax; ++i) {
+      if (tensors[i].numel == 0) continue;
+      prm.t[prm.count] = tensors[i];
+      prm.chunk0[prm.count] = grid;
+      grid += (int32_t)((tensors[i].numel + kMultiChunk - 1) / kMultiChunk);
+      ++prm.count;
+    }
+    if (prm.count == 0) continue;
+    prm.chunk0[prm.count] = grid;
+    prm.use_decay = use_decay != 0;
+    prm.decay = decay;
+    prm.b1 = beta1;
+    prm.omb1 = one_minus_beta1;
+    prm.b2 = beta2;
+    prm.omb2 = one_minus_beta2;
+    adamw32_multi_kernel<<<grid, kMultiThreads, 0, st>>>(prm);
+    const int rc = check_launch("ff_adamw32_multi");
+    if (rc != FF_OK) return rc;
+  }
+  return FF_OK;
+}
 
 extern "C" int ff_adamw8_blockwise(void* p, int p_dtype, const void* g, int g_dtype, uint8_t* m_q, float* m_absmax,
                                    uint8_t* v_q, float* v_absmax, int64_t n, double lr, double beta1, double beta2,

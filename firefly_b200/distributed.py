@@ -220,6 +220,10 @@ class BitArena:
         return has
 
 
+# dense gradients with at least this many elements are all-reduced in place, not flattened
+_DENSE_INPLACE_NUMEL = 1 << 20
+
+
 class ZeroFireFlyOptim:
     """FireFlyOptim's BitLinear update, data-parallel with ZeRO-1 sharded 8-bit states.
 
@@ -490,21 +494,34 @@ class ZeroFireFlyOptim:
         groups: dict[torch.dtype, list[torch.Tensor]] = {}
         for p in self.dense:
             if p.grad is not None:
-                groups.setdefault(p.grad.dtype, []).append(p.grad)
+                groups.setdefault(p.grad.dtype, []).append(p)
         pending = []
-        for grads in groups.values():
-            flat = torch._utils._flatten_dense_tensors(grads)
-            op = dist.ReduceOp.AVG if self._nccl else dist.ReduceOp.SUM
-            pending.append((grads, flat, dist.all_reduce(flat, op=op, group=self.group, async_op=True)))
+        op = dist.ReduceOp.AVG if self._nccl else dist.ReduceOp.SUM
+        for params in groups.values():
+            # large gradients (embeddings) are reduced where they lie; the small ones in one flat buffer
+            small = []
+            for p in params:
+                if p.grad.numel() >= _DENSE_INPLACE_NUMEL and p.grad.is_contiguous():
+                    pending.append(([p], None, dist.all_reduce(p.grad, op=op, group=self.group, async_op=True)))
+                else:
+                    small.append(p)
+            if small:
+                flat = torch._utils._flatten_dense_tensors([p.grad for p in small])
+                pending.append((small, flat, dist.all_reduce(flat, op=op, group=self.group, async_op=True)))
         return pending
 
     def _finish_dense_reduce(self, pending) -> None:
-        for grads, flat, work in pending:
+        for params, flat, work in pending:
             work.wait()
+            if flat is None:
+                if not self._nccl:
+                    params[0].grad.div_(self.world)
+                continue
             if not self._nccl:
                 flat.div_(self.world)
-            for g, f in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
-                g.copy_(f)
+            # each gradient becomes its slice of the reduced buffer (no copy back)
+            for p, f in zip(params, torch._utils._unflatten_dense_tensors(flat, [p.grad for p in params])):
+                p.grad = f
 
     # -- the per-segment update ------------------------------------------------
     def _kernel_update(self, *, q, wscale, row_len, elem_base, g, m_q, m_absmax, v_q, v_absmax, r_q, r_absmax,
@@ -571,8 +588,8 @@ class ZeroFireFlyOptim:
         for i, h in enumerate(has_grad):
             self.steps[i] += int(h)
         if self.peer:
-            dense = self._launch_dense_reduce()
             self._peer_fence()  # every rank's gradients are complete
+            dense = self._launch_dense_reduce()  # on the collective stream, under the updates
             t = self._mark()
             for b in range(len(plan.buckets)):
                 self._update_bucket_peer(b, has_grad)

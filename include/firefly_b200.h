@@ -416,6 +416,32 @@ FF_API int ff_adamw8_blockwise(void* p, int p_dtype, const void* g, int g_dtype,
                                double eps, double weight_decay, int64_t step, const float* qmap_s,
                                const float* qmap_u, void* stream);
 
+/* One dense parameter of ff_adamw32_multi (all pointers device memory, numel elements each). */
+typedef struct FfAdamw32Tensor {
+  void* param;          /* FF_DTYPE_F32 or FF_DTYPE_BF16 (param_dtype), updated in place */
+  const void* grad;     /* FF_DTYPE_F32 or FF_DTYPE_BF16 (grad_dtype) */
+  float* exp_avg;       /* fp32 first moment, updated in place */
+  float* exp_avg_sq;    /* fp32 second moment, updated in place */
+  int64_t numel;
+  int32_t param_dtype;
+  int32_t grad_dtype;
+  float eps_term;       /* fp32(eps * sqrt(1 - beta2^step)) of this parameter's step */
+  float step_scale;     /* fp32(lr * sqrt(1 - beta2^step) / (1 - beta1^step)) */
+} FfAdamw32Tensor;
+
+/*
+ * AdamW with fp32 moments of `count` dense parameters in ceil(count / 64) launches: the
+ * parameters that bitsandbytes' AdamW8bit keeps in 32 bits (fewer than min_8bit_size
+ * elements: norm scales, biases; fireflyoptim.py:83, :124).  Per element, fp32, each
+ * operation rounded once, in the order of the torch ops it replaces:
+ *   p *= decay (if use_decay; decay = fp32(1 - lr*wd));
+ *   m = m*beta1 + g*one_minus_beta1;  v = v*beta2 + (g*one_minus_beta2)*g;
+ *   p -= (m / (sqrt(v) + eps_term)) * step_scale.
+ * `tensors` is a HOST array of `count` descriptors (read during the call).
+ */
+FF_API int ff_adamw32_multi(const FfAdamw32Tensor* tensors, int32_t count, float decay, int32_t use_decay,
+                            float beta1, float one_minus_beta1, float beta2, float one_minus_beta2, void* stream);
+
 /*
  * Fused DQT-SR 8-bit AdamW update of one int8 weight tensor (one BitLinear).
  * Replaces FireFlyOptim.step's bit-module loop body fireflyoptim.py:137-209

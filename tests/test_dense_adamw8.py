@@ -85,6 +85,45 @@ def test_small_params_keep_fp32_moments_and_checkpoint_roundtrip():
     assert opt2.state[big]["m_absmax"].dtype == torch.float32  # not cast to the bf16 parameter's dtype
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("wd", [0.0, 0.1])
+def test_small_params_fused_step_equals_the_torch_chain(wd):
+    """The small parameters' multi-tensor kernel (70 parameters: two launches) gives, bit for bit,
+    the fp32-moment AdamW of torch ops (AdamW8bitDense._step_32bit), with fp32 and bf16
+    parameters (gradients of the same dtype) and per-parameter step counts (one parameter
+    skips a step)."""
+    gen = torch.Generator().manual_seed(5)
+    sizes = [int(s) for s in torch.randint(1, 4096, (70,), generator=gen)] + [4095, 1]
+    dts = [torch.float32, torch.bfloat16]
+    ps = [torch.nn.Parameter((torch.randn(n, generator=gen) * 0.1).to(dts[i % 2]).to(DEV))
+          for i, n in enumerate(sizes)]
+    ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+    opt = AdamW8bitDense(ps, lr=3e-3, betas=(0.9, 0.99), eps=1e-6, weight_decay=wd)
+    states = [{} for _ in ref]
+    for step in range(3):
+        for i, (p, r) in enumerate(zip(ps, ref)):
+            if step == 1 and i == 3:
+                p.grad = r.grad = None
+                continue
+            g = torch.randn(p.shape, generator=gen).to(p.dtype).to(DEV)
+            p.grad, r.grad = g, g.clone()
+        opt.step()
+        with torch.no_grad():
+            for r, st in zip(ref, states):
+                if r.grad is not None:
+                    AdamW8bitDense._step_32bit(r, st, 3e-3, 0.9, 0.99, 1e-6, wd)
+    for i, (p, r, st) in enumerate(zip(ps, ref, states)):
+        assert opt.state[p]["step"] == st["step"] == (2 if i == 3 else 3)
+        assert torch.equal(p.detach(), r.detach()), i
+        assert torch.equal(opt.state[p]["exp_avg"], st["exp_avg"]), i
+        assert torch.equal(opt.state[p]["exp_avg_sq"], st["exp_avg_sq"]), i
+    # checkpoint round trip keeps the fp32 moments of bf16 parameters in fp32
+    opt2 = AdamW8bitDense(ps, lr=3e-3, betas=(0.9, 0.99), eps=1e-6, weight_decay=wd)
+    opt2.load_state_dict(opt.state_dict())
+    assert opt2.state[ps[1]]["exp_avg"].dtype == torch.float32
+    assert torch.equal(opt2.state[ps[1]]["exp_avg_sq"], opt.state[ps[1]]["exp_avg_sq"])
+
+
 def _encode_probe_grads(n, seed=0):
     """Gradients whose values hit every map entry, every midpoint between neighbours and the
     floats just either side of both, with 1.0 first in each block (so the block absmax of m is

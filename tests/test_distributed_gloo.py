@@ -147,6 +147,58 @@ def _run(rank, world, port, out_dir, buckets=False):
         dist.destroy_process_group()
 
 
+def _dense_grads(rank, step):
+    g = torch.Generator().manual_seed(900 + 10 * step + rank)
+    return [torch.randn(1100, 1000, generator=g), torch.randn(300, generator=g), torch.randn(7, 3, generator=g)]
+
+
+def _run_dense(rank, world, port, out_dir):
+    """Two steps with dense parameters beside the BitLinears: one large enough to be all-reduced
+    in place, two that share a flat buffer; each rank has its own dense gradients."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from firefly_b200.distributed import _DENSE_INPLACE_NUMEL, ZeroFireFlyOptim
+    from firefly_b200.fireflykernels import _BIT_GRAD_CACHE
+
+    mods = _make_modules()
+    g = torch.Generator().manual_seed(77)
+    dense = [torch.nn.Parameter(torch.randn(1100, 1000, generator=g)), torch.nn.Parameter(torch.randn(300, generator=g)),
+             torch.nn.Parameter(torch.randn(7, 3, generator=g))]
+    assert dense[0].numel() >= _DENSE_INPLACE_NUMEL > dense[1].numel()
+    opt = ZeroFireFlyOptim(mods, params=dense, lr=LR, weight_decay=WD, seed=SEED, update_fn=_oracle_update([], SEED))
+    for step in range(2):
+        for m, gb in zip(mods, _grads(step)):
+            _BIT_GRAD_CACHE[m._registered_handle] = gb.clone()
+        for p, gd in zip(dense, _dense_grads(rank, step)):
+            p.grad = gd
+        opt.step()
+    torch.save([p.detach().clone() for p in dense], os.path.join(out_dir, f"dense_rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_zero1_dense_parameters_step_on_the_averaged_gradient(tmp_path):
+    """Dense parameters are stepped by the dense optimizer on the rank average of their
+    gradients (large ones reduced in place, small ones through a flat buffer): both ranks hold
+    the parameters of a local AdamW step on (g0 + g1) / 2."""
+    from firefly_b200.adamw8 import AdamW8bitDense
+
+    mp.start_processes(_run_dense, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    got = [torch.load(tmp_path / f"dense_rank{r}.pt", weights_only=False) for r in range(2)]
+    g = torch.Generator().manual_seed(77)
+    ref = [torch.randn(1100, 1000, generator=g), torch.randn(300, generator=g), torch.randn(7, 3, generator=g)]
+    states = [{} for _ in ref]
+    with torch.no_grad():
+        for step in range(2):
+            for i, (p, st) in enumerate(zip(ref, states)):
+                p.grad = (_dense_grads(0, step)[i] + _dense_grads(1, step)[i]) / 2
+                AdamW8bitDense._step_32bit(p, st, LR, 0.9, 0.999, 1e-8, WD)
+    for r in range(2):
+        for a, b in zip(got[r], ref):
+            assert torch.equal(a, b)
+
+
 @pytest.mark.timeout(300)
 def test_zero1_two_ranks_equal_single_rank(tmp_path):
     """Identical gradients on both ranks: averaging is exact, so the sharded update must
