@@ -80,7 +80,8 @@ def parse_args():
                                               "gemm_narrow", "adamw",
                                               "quant", "quant_rows", "swiglu", "swiglu_bwd", "swiglu_gemm",
                                               "swiglu_bwd_gemm", "gelu_gemm", "gelu_bwd_gemm", "layernorm",
-                                              "colsum", "dense_adamw", "mlp", "decoder4"],
+                                              "colsum", "quant_db", "adamw_peers", "small", "dense_adamw", "mlp",
+                                              "decoder4"],
                     help="run one launch of one kernel (for ncu captures) and exit")
     return ap.parse_args()
 
@@ -126,6 +127,35 @@ def kernel_case(args):
         y, mean, rstd, _ = _capi.layernorm_quant(x, gamma, beta)
         dy = torch.randn(16384, 2048, device=dev, generator=g).to(torch.bfloat16)
         _capi.layernorm_bwd(dy, x, mean, rstd, gamma)
+    elif args.kernel_case == "quant_db":  # dY's backward codes with db from the same read (T=8192, O=4096)
+        x = torch.randn(8192, 4096, device=dev, generator=g).to(torch.bfloat16)
+        _capi.quant_dual(x, row_colmul=torch.rand(4096, device=dev) * 1e-3, colsum=True)
+    elif args.kernel_case == "adamw_peers":
+        # the multi-source update of peer mode, two sources (both local here) and two weight copies:
+        # 134 M parameters (rows of 4096)
+        n = 134217728
+        q = torch.randint(-127, 128, (n,), dtype=torch.int8, device=dev, generator=g)
+        q2 = q.clone()
+        grads = [torch.empty(n, dtype=torch.bfloat16, device=dev).normal_(0, 1e-3, generator=g) for _ in range(2)]
+        c = [torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g) for _ in range(3)]
+        am = [torch.empty(n // 256, device=dev).uniform_(1e-4, 1e-2, generator=g) for _ in range(3)]
+        ws = torch.empty(n // 4096, device=dev).uniform_(1e-4, 1e-3, generator=g)
+        dec_s, dec_u = _tables_on(dev)
+        _capi.dqt_adamw8_peers(q, ws, 4096, [t.data_ptr() for t in grads], [q.data_ptr(), q2.data_ptr()], c[0],
+                               am[0], c[1], am[1], c[2], am[2], lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8,
+                               wd=0.01, step=3, sr_bias=0.15, seed=1, dec_s=dec_s, dec_u=dec_u)
+    elif args.kernel_case == "small":
+        # the fp32-moment AdamW of the 1.3B decoder's 98 LayerNorm parameters (2048 each), the int8
+        # transpose of a 8192 x 4096 weight, and the int8 weight update of 64 M parameters
+        ps = [torch.randn(2048, device=dev, generator=g) for _ in range(98)]
+        items = [(p_, torch.randn(2048, device=dev, generator=g), torch.zeros(2048, device=dev),
+                  torch.zeros(2048, device=dev), 1) for p_ in ps]
+        _capi.adamw32_multi(items, lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.01)
+        w = torch.randint(-127, 128, (8192, 4096), dtype=torch.int8, device=dev, generator=g)
+        _capi.transpose_i8(w)
+        w2 = torch.randint(-127, 128, (1 << 26,), dtype=torch.int8, device=dev, generator=g)
+        dq = torch.randint(-3, 4, (1 << 26,), dtype=torch.int32, device=dev, generator=g)
+        _capi.update_int8_weight(w2, dq)
     elif args.kernel_case == "colsum":  # db of a BitLinear with a bias (T=8192, O=11008)
         x = torch.randn(8192, 11008, device=dev, generator=g).to(torch.bfloat16)
         _capi.colsum_bf16(x)

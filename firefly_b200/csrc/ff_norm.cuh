@@ -217,18 +217,33 @@ __global__ void __launch_bounds__(kThreads) ln_wgrad_stage1(const __nv_bfloat16*
   *reinterpret_cast<float4*>(wg + cols + col + 4) = make_float4(ab[4], ab[5], ab[6], ab[7]);
 }
 
-// stage 2: the row blocks' partial sums added in block order
+// stage 2: per column, the row blocks' partial sums in a fixed order: warp w of the CTA adds the
+// w-th eighth of the blocks in block order, then the eight range sums are added in warp order.
+// A CTA takes 32 columns of dgamma (blockIdx.y = 0) or dbeta (1); a warp reads 128 B per block.
+constexpr int kS2Cols = 32;
 __global__ void __launch_bounds__(kThreads) ln_wgrad_stage2(const float* __restrict__ ws, int64_t nblocks, int cols,
                                                            float* __restrict__ dgamma, float* __restrict__ dbeta) {
-  const int c = blockIdx.x * kThreads + threadIdx.x;
-  if (c >= cols) return;
-  float g = 0.f, b = 0.f;
-  for (int64_t k = 0; k < nblocks; ++k) {
-    g += ws[(size_t)k * 2 * cols + c];
-    b += ws[(size_t)k * 2 * cols + cols + c];
+  constexpr int kSlices = kThreads / kS2Cols;
+  __shared__ float part[kSlices][kS2Cols];
+  const int lane = threadIdx.x % kS2Cols, slice = threadIdx.x / kS2Cols;
+  const int c = blockIdx.x * kS2Cols + lane;
+  float* out = blockIdx.y == 0 ? dgamma : dbeta;
+  if (out == nullptr) return;  // uniform over the CTA
+  const int64_t per = (nblocks + kSlices - 1) / kSlices;
+  const int64_t k0 = min64(nblocks, slice * per), k1 = min64(nblocks, k0 + per);
+  float acc = 0.f;
+  if (c < cols) {
+    const float* src = ws + (blockIdx.y == 0 ? 0 : cols) + c;
+    for (int64_t k = k0; k < k1; ++k) acc += src[(size_t)k * 2 * cols];
   }
-  if (dgamma) dgamma[c] = g;
-  if (dbeta) dbeta[c] = b;
+  part[slice][lane] = acc;
+  __syncthreads();
+  if (slice == 0 && c < cols) {
+    float t = part[0][lane];
+#pragma unroll
+    for (int s = 1; s < kSlices; ++s) t += part[s][lane];
+    out[c] = t;
+  }
 }
 
 template <int MAXCH>
@@ -331,8 +346,8 @@ extern "C" int ff_layernorm_bwd(const uint16_t* dy, int64_t lddy, const uint16_t
     FF_REQUIRE(nb < 65536, FF_ERR_UNSUPPORTED, "%s: too many rows", name);
     const dim3 g1((unsigned)((cols / 8 + kThreads - 1) / kThreads), (unsigned)nb);
     ln_wgrad_stage1<<<g1, kThreads, 0, st>>>(dyb, lddy, xb, ldx, rows, (int)cols, mean, rstd, ws);
-    ln_wgrad_stage2<<<(unsigned)((cols + kThreads - 1) / kThreads), kThreads, 0, st>>>(ws, nb, (int)cols, dgamma,
-                                                                                       dbeta);
+    ln_wgrad_stage2<<<dim3((unsigned)((cols + kS2Cols - 1) / kS2Cols), 2), kThreads, 0, st>>>(ws, nb, (int)cols,
+                                                                                              dgamma, dbeta);
   }
   return check_launch(name);
 }

@@ -816,13 +816,29 @@ __global__ void colsum_stage1(const __nv_bfloat16* __restrict__ x, int64_t rows,
   ws[ch * cols + c] = acc;
 }
 
-__global__ void colsum_stage2(const float* __restrict__ ws, int64_t nchunks, int64_t cols,
-                              __nv_bfloat16* __restrict__ out) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// per column, the chunks' partial sums in a fixed order: warp w of the CTA adds the w-th eighth of
+// the chunks in chunk order, then the eight range sums are added in warp order (32 columns per CTA)
+constexpr int kColsumS2Cols = 32;
+constexpr int kColsumS2Threads = 256;
+__global__ void __launch_bounds__(kColsumS2Threads) colsum_stage2(const float* __restrict__ ws, int64_t nchunks,
+                                                                 int64_t cols, __nv_bfloat16* __restrict__ out) {
+  constexpr int kSlices = kColsumS2Threads / kColsumS2Cols;
+  __shared__ float part[kSlices][kColsumS2Cols];
+  const int lane = threadIdx.x % kColsumS2Cols, slice = threadIdx.x / kColsumS2Cols;
+  const int64_t c = (int64_t)blockIdx.x * kColsumS2Cols + lane;
+  const int64_t per = (nchunks + kSlices - 1) / kSlices;
+  const int64_t k0 = min64(nchunks, slice * per), k1 = min64(nchunks, k0 + per);
   float acc = 0.f;
-  for (int64_t k = 0; k < nchunks; ++k) acc += ws[k * cols + c];
-  out[c] = __float2bfloat16_rn(acc);
+  if (c < cols)
+    for (int64_t k = k0; k < k1; ++k) acc += ws[k * cols + c];
+  part[slice][lane] = acc;
+  __syncthreads();
+  if (slice == 0 && c < cols) {
+    float t = part[0][lane];
+#pragma unroll
+    for (int s = 1; s < kSlices; ++s) t += part[s][lane];
+    out[c] = __float2bfloat16_rn(t);
+  }
 }
 
 __global__ void update_int8_weight_kernel(int8_t* __restrict__ w, const int32_t* __restrict__ dq, int64_t n) {
@@ -981,8 +997,8 @@ extern "C" int ff_quant_dual_i8_db(const uint16_t* x, int64_t rows, int64_t cols
                      q_rows != nullptr, q_cols_t != nullptr, absmax_ws, nullptr, 0, st, db_ws);
   if (rc != FF_OK) return rc;
   const int64_t nch = (rows + kDualARows - 1) / kDualARows;
-  colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(db_ws, nch, cols,
-                                                                reinterpret_cast<__nv_bfloat16*>(db));
+  const unsigned g2 = (unsigned)((cols + kColsumS2Cols - 1) / kColsumS2Cols);
+  colsum_stage2<<<g2, kColsumS2Threads, 0, st>>>(db_ws, nch, cols, reinterpret_cast<__nv_bfloat16*>(db));
   rc = check_launch("ff_quant_dual_i8_db");
   if (rc != FF_OK) return rc;
   return launch_pass_b<FF_DTYPE_BF16>("ff_quant_dual_i8_db", xb, rows, cols, ldx, row_colmul, eps, q_rows, ldq,
@@ -1096,8 +1112,8 @@ extern "C" int ff_colsum_bf16(const uint16_t* x, int64_t rows, int64_t cols, int
   FF_REQUIRE(nch < 65536, FF_ERR_UNSUPPORTED, "ff_colsum_bf16: too many rows");
   dim3 g1((unsigned)((cols + 255) / 256), (unsigned)nch);
   colsum_stage1<<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, ldx, ws);
-  colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(ws, nch, cols,
-                                                                reinterpret_cast<__nv_bfloat16*>(out));
+  const unsigned g2 = (unsigned)((cols + kColsumS2Cols - 1) / kColsumS2Cols);
+  colsum_stage2<<<g2, kColsumS2Threads, 0, st>>>(ws, nch, cols, reinterpret_cast<__nv_bfloat16*>(out));
   return check_launch("ff_colsum_bf16");
 }
 
